@@ -1,0 +1,186 @@
+/*
+ * tinygiant.h — C ABI of the B200 drop-in libtinygiant.so.
+ *
+ * The first block is the reference's ABI: the 21 symbols that the reference
+ * loader tinygiant/_lib.py:39-93 registers with ctypes, with the same names,
+ * argument lists, return types and accumulate (+=) semantics as
+ * csrc/libtinygiant.c.  Every pointer is a HOST pointer, exactly as the
+ * reference engine passes numpy arrays and mmap views; weight bytes are
+ * uploaded to HBM on first use and stay resident (see tg_cuda_register).
+ * All calls are synchronous: results are in the caller's buffers on return.
+ *
+ * Errors: the reference functions return void and validate nothing.  Here a
+ * call that cannot run (no GPU, an unsupported format, a bad shape, a CUDA
+ * failure) leaves its outputs untouched, prints one line to stderr and
+ * records the error for tg_cuda_last_error(); there is no CPU fallback.
+ *
+ * Format codes (libtinygiant.c:594): 0 Q4_K, 1 F16, 2 Q6_K, 3 MXFP4, 4 Q8_0.
+ * Activation codes (libtinygiant.c:1248): 0 SiLU, 1 gpt-oss.
+ */
+#ifndef TINYGIANT_H
+#define TINYGIANT_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- Reference ABI ------------------------------------------------------ */
+
+/* out[D] += w * down(silu(gate.x) * up.x) for one all-Q4_K expert stored
+ * contiguously as [gate | up | down] (libtinygiant.c:1040-1080). */
+void tg_expert_forward(const uint8_t *q4_data, const float *input, float *output, float weight,
+                       int embed_dim, int inter_dim);
+
+/* As tg_expert_forward with separate Q4_K gate/up and a down matrix in
+ * format 1 (F16), 2 (Q6_K) or anything else (Q4_K) (libtinygiant.c:1084-1128). */
+void tg_expert_forward_mixed(const uint8_t *gate_q4, const uint8_t *up_q4, const void *down_data,
+                             int down_format, const float *input, float *output, float weight,
+                             int embed_dim, int inter_dim);
+
+/* out[nrows] = Q4_K matrix . Q8(x) (libtinygiant.c:375-378). */
+void tg_matmul_q4k(const uint8_t *q4_matrix, const float *input, float *output, int nrows, int ncols);
+
+/* out[nrows] = Q6_K matrix . Q8(x) (libtinygiant.c:498-501). */
+void tg_matmul_q6k(const uint8_t *q6_matrix, const float *input, float *output, int nrows, int ncols);
+
+/* out = x / sqrt(mean(x^2) + eps) * w (libtinygiant.c:680-698). */
+void tg_rms_norm(const float *x, const float *weight, float *out, int dim, float eps);
+
+/* out[nrows] = A (fp32, row-major) . x (libtinygiant.c:662-676). */
+void tg_f32_matvec(const float *A, const float *x, float *out, int nrows, int ncols);
+
+/* out[nrows] = A (fp16, row-major) . x (libtinygiant.c:655-658). */
+void tg_f16_matvec(const uint16_t *A, const float *x, float *out, int nrows, int ncols);
+
+/* Single-row GQA attention decode step, fp32 weights (libtinygiant.c:723-814). */
+void tg_attention_decode(const float *wq, const float *wk, const float *wv, const float *wo,
+                         const float *q_norm_w, const float *k_norm_w, float *kv_k, float *kv_v,
+                         int kv_len, int kv_max, const float *rope_cos, const float *rope_sin,
+                         const float *input, float *output, int embed_dim, int n_heads, int n_kv_heads,
+                         int head_dim, int pos);
+
+/* Same with Q4_K q/k/o and fp16 v projections (libtinygiant.c:985-1036). */
+void tg_attention_decode_q4(const uint8_t *wq_q4, const uint8_t *wk_q4, const uint16_t *wv_f16,
+                            const uint8_t *wo_q4, const float *q_norm_w, const float *k_norm_w,
+                            float *kv_k, float *kv_v, int kv_len, int kv_max, const float *rope_cos,
+                            const float *rope_sin, const float *input, float *output, int embed_dim,
+                            int n_heads, int n_kv_heads, int head_dim, int pos);
+
+/* Host page-cache hints (libtinygiant.c:1550-1571). */
+void tg_prefetch(const void *addr, size_t len);
+void tg_prefetch_batch(const void **addrs, const size_t *lens, int count);
+int tg_mlock(const void *addr, size_t len);
+
+/* Generic attention decode step: any weight format per projection,
+ * optional biases, QK norm, sinks and sliding window (libtinygiant.c:939-983). */
+void tg_attention_v2(int fmt_q, int fmt_k, int fmt_v, int fmt_o, const void *wq, const void *wk,
+                     const void *wv, const void *wo, const float *bq, const float *bk, const float *bv,
+                     const float *bo, const float *q_norm_w, const float *k_norm_w, const float *sinks,
+                     float *kv_k, float *kv_v, int kv_len, int kv_max, int window, const float *rope_cos,
+                     const float *rope_sin, const float *input, float *output, int embed_dim, int n_heads,
+                     int n_kv_heads, int head_dim, int pos, float eps);
+
+/* The MoE layer the engine calls (libtinygiant.c:1386-1437, engine.py:336-340):
+ * for each of n_experts experts, the rows r with row_weights[e*k + r] != 0
+ * run gate/up (gate_fmt), the activation, down (down_fmts[e]) and
+ * output[r] += w * (down.h + down_bias); experts combine in the given order.
+ * Bias arrays are per-expert pointer arrays or NULL (gate_bias implies up_bias). */
+void tg_moe_forward_rows_v2(const uint8_t *const *gate_ptrs, const uint8_t *const *up_ptrs,
+                            const void *const *down_ptrs, int gate_fmt, const int *down_fmts,
+                            const float *const *gate_bias, const float *const *up_bias,
+                            const float *const *down_bias, int act, int n_experts, const float *row_weights,
+                            const float *inputs, float *output, int k, int embed_dim, int inter_dim);
+
+/* out[nrows] = mat(fmt) . x + (bias ? bias : 0) (libtinygiant.c:925-931). */
+void tg_matmul(int fmt, const void *mat, const float *bias, const float *input, float *output, int nrows,
+               int ncols);
+
+/* Bytes of one row of ncols values in format fmt (libtinygiant.c:596-606). */
+size_t tg_row_bytes(int fmt, int ncols);
+
+/* CPU thread-pool size of the reference (libtinygiant.c:85-104).  Recorded
+ * and reported back; the GPU path does not use host threads. */
+void tg_set_threads(int n);
+int tg_get_threads(void);
+
+/* k rows through one expert with Q4_K gate/up (libtinygiant.c:1182-1231). */
+void tg_expert_forward_rows(const uint8_t *gate_q4, const uint8_t *up_q4, const void *down_data,
+                            int down_format, const float *inputs, float *output, const float *weights,
+                            int k, int embed_dim, int inter_dim);
+
+/* tg_moe_forward_rows_v2 with Q4_K gate, SiLU and no biases (libtinygiant.c:1439-1448). */
+void tg_moe_forward_rows(const uint8_t *const *gate_ptrs, const uint8_t *const *up_ptrs,
+                         const void *const *down_ptrs, const int *down_fmts, int n_experts,
+                         const float *row_weights, const float *inputs, float *output, int k, int embed_dim,
+                         int inter_dim);
+
+/* Zeroes output, then adds weights[e] * expert_e(x) for all-Q4_K experts
+ * (libtinygiant.c:1452-1460). */
+void tg_moe_forward(const uint8_t **expert_ptrs, const float *weights, int n_experts, const float *input,
+                    float *output, int embed_dim, int inter_dim);
+
+/* Whole decoder layer with fp32 attention and pre-routed experts
+ * (libtinygiant.c:1467-1507). */
+void tg_transformer_layer(const float *wq, const float *wk, const float *wv, const float *wo,
+                          const float *attn_norm_w, const float *q_norm_w, const float *k_norm_w,
+                          const float *ffn_norm_w, float *kv_k, float *kv_v, int kv_len, int kv_max,
+                          const float *rope_cos, const float *rope_sin, const uint8_t **gate_ptrs,
+                          const uint8_t **up_ptrs, const void **down_ptrs, const int *down_is_f16,
+                          const float *expert_weights, int n_active, float *x, int embed_dim, int inter_dim,
+                          int n_heads, int n_kv_heads, int head_dim, int pos);
+
+/* ---- Extensions (no counterpart in the reference) ----------------------- */
+
+/* Error of the most recent failed call (0 = none) with its message copied
+ * into buf (NUL-terminated, truncated to len); reading clears it. */
+int tg_cuda_last_error(char *buf, size_t len);
+
+/* CUDA device used by this process (default: the current device, else 0).
+ * Must be called before the first compute call to take effect. */
+int tg_cuda_set_device(int device);
+
+/* Runs all later work on the given cudaStream_t (NULL: the library's own
+ * stream).  Host-pointer calls still synchronise that stream before return. */
+void tg_cuda_set_stream(void *stream);
+
+/* Uploads [host_ptr, host_ptr + nbytes) of raw weight bytes to HBM now, so a
+ * later call that names any matrix inside it does not pay the upload.  The
+ * registry treats registered bytes as immutable; after changing them call
+ * tg_cuda_unregister or tg_cuda_registry_clear.  Returns 0 on success. */
+int tg_cuda_register(const void *host_ptr, size_t nbytes);
+int tg_cuda_unregister(const void *host_ptr);
+void tg_cuda_registry_clear(void);
+/* Bytes of HBM the registry holds. */
+size_t tg_cuda_registry_bytes(void);
+
+/* Number of kernels this library has launched since load. */
+uint64_t tg_cuda_launch_count(void);
+
+/* Number of CUDA devices visible to this process (0 without a GPU). */
+int tg_cuda_device_count(void);
+
+/* Test hooks exposing the intermediates that must match the reference bit
+ * for bit.  tg_cuda_debug_quantize_q8 writes nrows x ceil(ncols/256) blocks
+ * in the reference's 296-byte q8_block layout (libtinygiant.c:159-164).
+ * tg_cuda_debug_row_isums writes every row's int32 sub-block sums of a
+ * quantized matrix against one input given as such blocks (per row: Q4_K 8
+ * per block, Q6_K 16 per block, MXFP4 / Q8_0 1 per 32 values) and returns
+ * the count per row, or -1. */
+int tg_cuda_debug_quantize_q8(const float *x, int nrows, int ncols, void *out_blocks);
+int tg_cuda_debug_row_isums(int fmt, const void *mat, int nrows, int ncols, const void *xq_blocks, int32_t *out);
+
+/* Q4_K / Q6_K packers (host, multi-threaded): rows x cols fp32 (cols a
+ * multiple of 256) -> rows * tg_row_bytes(fmt, cols) bytes.  A per-sub-block
+ * min/max affine fit (Q4_K) or signed max-abs fit (Q6_K) with 6-/8-bit
+ * sub-block scales; the block layouts are the ones the kernels decode. */
+void tg_pack_q4k(const float *w, int rows, int cols, uint8_t *out);
+void tg_pack_q6k(const float *w, int rows, int cols, uint8_t *out);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TINYGIANT_H */

@@ -1,0 +1,47 @@
+// tg_plan.cuh — the device-side description of one MoE call.
+//
+// A call (tg_moe_forward_rows_v2 and the entries built on it) selects
+// n_slots experts, in the caller's order.  Slot s uses rows[row_off ..
+// row_off + n_rows) of the k input rows with weights wts[...]; this is the
+// reference's per-expert gather of active rows (csrc/libtinygiant.c:1411-1423),
+// laid out flat so every kernel indexes it without host help.
+#pragma once
+#include "tg_common.cuh"
+
+namespace tg {
+
+struct SlotDesc {
+  WDesc gate, up, down;
+  const float* gb;   // gate bias [inter] or null
+  const float* ub;   // up bias [inter] or null
+  const float* db;   // down bias [embed] or null
+  int n_rows;        // active input rows of this expert
+  int row_off;       // offset of this slot's rows in the flat arrays
+  int pad[2];
+};
+
+struct MoePlan {
+  const SlotDesc* slots;  // [n_slots]
+  const int* rows;        // [total_rows] input row of each active (slot, j)
+  const float* wts;       // [total_rows] combine weight of each active (slot, j)
+  int n_slots;
+  int total_rows;
+  int k;                  // input rows of the call
+  int embed_dim;          // D
+  int inter_dim;          // I
+  int act;                // Act
+  int assoc_rule;         // AssocRule
+  int bias_term;          // 1: part = w * (v + (db ? db[r] : 0.f)); 0: part = w * v
+};
+
+// Whether active row j (0-based within its slot of n rows) is computed with
+// the x4 association.
+__host__ __device__ __forceinline__ bool use_x4(int rule, int j, int n, int k) {
+  if (rule == ASSOC_X1) return false;
+  if (rule == ASSOC_ROWS) return k > 1;
+  int g0 = j & ~3;
+  int m = n - g0 < 4 ? n - g0 : 4;
+  return m > 1;
+}
+
+}  // namespace tg

@@ -1,0 +1,891 @@
+// tg_runtime.cu — host side of libtinygiant.so: device context, the
+// host-pointer -> HBM weight registry, per-call staging, and the C ABI.
+//
+// The reference engine passes host pointers (numpy arrays, mmap views of the
+// expert files) to every call and reads the results right after.  Here each
+// weight matrix is uploaded once, repacked into the aligned HBM layout, and
+// found again by its host address; per call only activations cross PCIe:
+// one host->device copy of [plan | inputs | output], the kernels, one
+// device->host copy of the output.
+#include <sys/mman.h>
+#include <unistd.h>
+
+#include <algorithm>
+#include <atomic>
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <string>
+#include <tuple>
+#include <vector>
+
+#include "../../include/tinygiant.h"
+#include "tg_kernels.h"
+#include "tg_runtime.h"
+
+namespace tg {
+
+// ---------------------------------------------------------------------
+// Errors.
+
+static std::mutex g_err_mu;
+static int g_err_code = 0;
+static std::string g_err_msg;
+
+void set_host_error(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  {
+    std::lock_guard<std::mutex> lk(g_err_mu);
+    g_err_code = code;
+    g_err_msg = buf;
+  }
+  fprintf(stderr, "libtinygiant(cuda): %s\n", buf);
+  if (getenv("TG_CUDA_ABORT_ON_ERROR")) abort();
+}
+
+static bool cuda_ok(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return true;
+  set_host_error(100 + (int)e, "%s: %s", what, cudaGetErrorString(e));
+  return false;
+}
+
+std::atomic<uint64_t> g_launches{0};
+
+// ---------------------------------------------------------------------
+// Growable device / pinned buffers.
+
+struct DevBuf {
+  void* p = nullptr;
+  size_t n = 0;
+  bool reserve(size_t need) {
+    if (need <= n) return true;
+    size_t cap = std::max(need, n * 2);
+    cap = (cap + 4095) & ~(size_t)4095;
+    if (p) cudaFree(p);
+    p = nullptr;
+    n = 0;
+    if (!cuda_ok(cudaMalloc(&p, cap), "cudaMalloc(scratch)")) return false;
+    n = cap;
+    return true;
+  }
+};
+
+struct PinBuf {
+  void* p = nullptr;
+  size_t n = 0;
+  bool reserve(size_t need) {
+    if (need <= n) return true;
+    size_t cap = std::max(need, n * 2);
+    cap = (cap + 4095) & ~(size_t)4095;
+    if (p) cudaFreeHost(p);
+    p = nullptr;
+    n = 0;
+    if (!cuda_ok(cudaMallocHost(&p, cap), "cudaMallocHost(staging)")) return false;
+    n = cap;
+    return true;
+  }
+};
+
+// ---------------------------------------------------------------------
+// Context.
+
+struct Ctx {
+  std::recursive_mutex mu;
+  bool inited = false;
+  bool init_failed = false;
+  int device = -1;
+  cudaStream_t own_stream = nullptr;
+  cudaStream_t user_stream = nullptr;
+  bool user_stream_set = false;
+  DevStatus* d_status = nullptr;
+  DevStatus* h_status = nullptr;  // pinned
+  DevBuf d_stage, d_xq8, d_hidden, d_hq8, d_tmp;
+  PinBuf h_up, h_down;
+  int threads = 1;
+};
+
+static Ctx g;
+
+cudaStream_t stream() { return g.user_stream_set ? g.user_stream : g.own_stream; }
+
+bool ensure_init() {
+  if (g.inited) return true;
+  if (g.init_failed) {
+    set_host_error(1, "no usable CUDA device (initialisation failed earlier)");
+    return false;
+  }
+  int n = 0;
+  cudaError_t e = cudaGetDeviceCount(&n);
+  if (e != cudaSuccess || n == 0) {
+    g.init_failed = true;
+    set_host_error(1, "no CUDA device available (%s); this library has no CPU path",
+                   e == cudaSuccess ? "0 devices" : cudaGetErrorString(e));
+    return false;
+  }
+  if (g.device < 0) {
+    int cur = 0;
+    if (cudaGetDevice(&cur) != cudaSuccess) cur = 0;
+    g.device = cur;
+  }
+  if (!cuda_ok(cudaSetDevice(g.device), "cudaSetDevice")) {
+    g.init_failed = true;
+    return false;
+  }
+  if (!cuda_ok(cudaStreamCreateWithFlags(&g.own_stream, cudaStreamNonBlocking), "cudaStreamCreate") ||
+      !cuda_ok(cudaMalloc(&g.d_status, sizeof(DevStatus)), "cudaMalloc(status)") ||
+      !cuda_ok(cudaMallocHost(&g.h_status, sizeof(DevStatus)), "cudaMallocHost(status)") ||
+      !cuda_ok(cudaMemset(g.d_status, 0, sizeof(DevStatus)), "cudaMemset(status)")) {
+    g.init_failed = true;
+    return false;
+  }
+  g.inited = true;
+  return true;
+}
+
+// Synchronises the stream and turns a device-side error record into a host error.
+bool finish(const char* what) {
+  cudaStream_t s = stream();
+  if (!cuda_ok(cudaMemcpyAsync(g.h_status, g.d_status, sizeof(DevStatus), cudaMemcpyDeviceToHost, s), what))
+    return false;
+  if (!cuda_ok(cudaStreamSynchronize(s), what)) return false;
+  if (g.h_status->code != 0) {
+    DevStatus st = *g.h_status;
+    cudaMemsetAsync(g.d_status, 0, sizeof(DevStatus), s);
+    cudaStreamSynchronize(s);
+    set_host_error(200 + st.code, "%s: device error %d at site %d (%d, %d)", what, st.code, st.where, st.a, st.b);
+    return false;
+  }
+  return true;
+}
+
+// ---------------------------------------------------------------------
+// Weight registry.
+
+static size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+size_t host_row_bytes(int fmt, int ncols) {
+  switch (fmt) {
+    case FMT_Q4K: return (size_t)(ncols / QK) * Q4K_BYTES;
+    case FMT_Q6K: return (size_t)(ncols / QK) * Q6K_BYTES;
+    case FMT_MXFP4: return (size_t)(ncols / 32) * MXFP4_BYTES;
+    case FMT_Q80: return (size_t)(ncols / 32) * Q80_BYTES;
+    default: return (size_t)ncols * 2;
+  }
+}
+
+// Bump allocator over large cudaMalloc chunks; every sub-allocation is
+// 256-byte aligned and padded so bulk copies may round a tile up to 16 bytes.
+struct Slab {
+  std::vector<std::pair<uint8_t*, size_t>> chunks;
+  size_t used = 0, cap = 0, total = 0;
+  uint8_t* cur = nullptr;
+  uint8_t* alloc(size_t n) {
+    n = align_up(n + 64, 256);
+    if (!cur || used + n > cap) {
+      size_t sz = std::max(n, (size_t)256 << 20);
+      uint8_t* p = nullptr;
+      if (!cuda_ok(cudaMalloc(&p, sz), "cudaMalloc(weights)")) return nullptr;
+      chunks.push_back({p, sz});
+      cur = p;
+      used = 0;
+      cap = sz;
+      total += sz;
+    }
+    uint8_t* r = cur + used;
+    used += n;
+    return r;
+  }
+  void clear() {
+    for (auto& c : chunks) cudaFree(c.first);
+    chunks.clear();
+    cur = nullptr;
+    used = cap = total = 0;
+  }
+};
+
+struct Sample {
+  size_t off[3];
+  uint8_t bytes[3][32];
+  int len[3];
+};
+
+static void take_sample(const uint8_t* h, size_t n, Sample& s) {
+  size_t offs[3] = {0, n / 2, n > 32 ? n - 32 : 0};
+  for (int i = 0; i < 3; i++) {
+    s.off[i] = offs[i];
+    s.len[i] = (int)std::min<size_t>(32, n - std::min(n, offs[i]));
+    memcpy(s.bytes[i], h + offs[i], s.len[i]);
+  }
+}
+
+static bool sample_matches(const uint8_t* h, const Sample& s) {
+  for (int i = 0; i < 3; i++)
+    if (memcmp(s.bytes[i], h + s.off[i], s.len[i]) != 0) return false;
+  return true;
+}
+
+struct Entry {
+  WDesc w;
+  size_t raw_bytes;
+  Sample sample;
+};
+
+// A registered raw byte range (tg_cuda_register): matrices inside it are
+// found by address and are not re-checked.
+struct Range {
+  size_t nbytes;
+};
+
+static Slab g_slab;
+static std::map<std::tuple<uintptr_t, int, int, int>, Entry> g_mats;
+static std::map<uintptr_t, Range> g_ranges;
+
+static bool in_registered_range(uintptr_t p, size_t n) {
+  auto it = g_ranges.upper_bound(p);
+  if (it == g_ranges.begin()) return false;
+  --it;
+  return p >= it->first && p + n <= it->first + it->second.nbytes;
+}
+
+// Copies raw host bytes to HBM in the layout of WDesc w (already allocated).
+static bool upload_into(const uint8_t* h, size_t raw, const WDesc& w) {
+  cudaStream_t s = stream();
+  const long nblk = w.fmt == FMT_Q6K ? (long)w.rows * (w.cols / QK)
+                  : (w.fmt == FMT_MXFP4 || w.fmt == FMT_Q80) ? (long)w.rows * (w.cols / 32) : 0;
+  if (nblk == 0) {
+    if (!cuda_ok(cudaMemcpyAsync((void*)w.main, h, raw, cudaMemcpyHostToDevice, s), "upload weights")) return false;
+  } else {
+    if (!g.d_tmp.reserve(raw)) return false;
+    if (!cuda_ok(cudaMemcpyAsync(g.d_tmp.p, h, raw, cudaMemcpyHostToDevice, s), "upload weights")) return false;
+    launch_repack((const uint8_t*)g.d_tmp.p, w.fmt, nblk, (uint8_t*)w.main, (uint8_t*)w.aux1, (uint8_t*)w.aux2, s);
+    g_launches++;
+  }
+  return cuda_ok(cudaStreamSynchronize(s), "upload weights");
+}
+
+// Device descriptor of a rows x cols matrix in format fmt at host address h
+// (fmt -1: fp32 values, fmt -2: fp32 vector of `rows` values).
+bool lookup_matrix(const void* hp, int fmt, int rows, int cols, WDesc* out) {
+  const uint8_t* h = (const uint8_t*)hp;
+  if (!h) {
+    set_host_error(2, "NULL weight pointer");
+    return false;
+  }
+  size_t raw = fmt == -1 ? (size_t)rows * cols * 4 : fmt == -2 ? (size_t)rows * 4 : (size_t)rows * host_row_bytes(fmt, cols);
+  auto key = std::make_tuple((uintptr_t)h, fmt, rows, cols);
+  auto it = g_mats.find(key);
+  if (it != g_mats.end()) {
+    if (!in_registered_range((uintptr_t)h, raw) && !sample_matches(h, it->second.sample)) {
+      take_sample(h, raw, it->second.sample);
+      if (!upload_into(h, raw, it->second.w)) return false;
+    }
+    *out = it->second.w;
+    return true;
+  }
+  Entry e{};
+  e.raw_bytes = raw;
+  e.w.fmt = fmt;
+  e.w.rows = rows;
+  e.w.cols = cols;
+  if (fmt == FMT_Q6K) {
+    size_t nb = (size_t)rows * (cols / QK);
+    uint8_t* m = g_slab.alloc(nb * 192);
+    uint8_t* a1 = g_slab.alloc(nb * 16);
+    uint8_t* a2 = g_slab.alloc(nb * 2);
+    if (!m || !a1 || !a2) return false;
+    e.w.main = m; e.w.aux1 = a1; e.w.aux2 = a2;
+  } else if (fmt == FMT_MXFP4) {
+    size_t nb = (size_t)rows * (cols / 32);
+    uint8_t* m = g_slab.alloc(nb * 16);
+    uint8_t* a1 = g_slab.alloc(nb);
+    if (!m || !a1) return false;
+    e.w.main = m; e.w.aux1 = a1;
+  } else if (fmt == FMT_Q80) {
+    size_t nb = (size_t)rows * (cols / 32);
+    uint8_t* m = g_slab.alloc(nb * 32);
+    uint8_t* a2 = g_slab.alloc(nb * 2);
+    if (!m || !a2) return false;
+    e.w.main = m; e.w.aux2 = a2;
+  } else {
+    uint8_t* m = g_slab.alloc(raw);
+    if (!m) return false;
+    e.w.main = m;
+  }
+  take_sample(h, raw, e.sample);
+  if (!upload_into(h, raw, e.w)) return false;
+  g_mats[key] = e;
+  *out = e.w;
+  return true;
+}
+
+const float* lookup_vector(const float* h, int n) {
+  if (!h) return nullptr;
+  WDesc w;
+  if (!lookup_matrix(h, -2, n, 1, &w)) return nullptr;
+  return (const float*)w.main;
+}
+
+// ---------------------------------------------------------------------
+// Per-call staging.
+
+struct Stage {
+  size_t off = 0;
+  size_t take(size_t n) {
+    size_t o = off;
+    off = align_up(off + n, 256);
+    return o;
+  }
+};
+
+// ---------------------------------------------------------------------
+// The MoE driver shared by every expert entry point.
+
+struct HostSlot {
+  WDesc gate, up, down;
+  const float *gb = nullptr, *ub = nullptr, *db = nullptr;
+  std::vector<int> rows;
+  std::vector<float> wts;
+};
+
+// Runs the plan: output[k][D] (host) accumulates.  `zero_output` clears it first.
+bool run_moe(std::vector<HostSlot>& slots, int gate_fmt, int act, int rule, int bias_term, const float* inputs,
+             float* output, int k, int D, int I, bool zero_output) {
+  const char* what = "tg_moe_forward";
+  if (zero_output) memset(output, 0, sizeof(float) * (size_t)k * D);
+  // Drop experts with no active rows: the reference skips them entirely.
+  std::vector<HostSlot*> act_slots;
+  int total = 0;
+  for (auto& s : slots)
+    if (!s.rows.empty()) {
+      act_slots.push_back(&s);
+      total += (int)s.rows.size();
+    }
+  if (act_slots.empty() || k == 0) return true;
+  const int n = (int)act_slots.size();
+  const int gbpr = (D + QK - 1) / QK, dbpr = (I + QK - 1) / QK;
+
+  Stage st;
+  size_t o_slots = st.take(sizeof(SlotDesc) * n);
+  size_t o_rows = st.take(sizeof(int) * total);
+  size_t o_wts = st.take(sizeof(float) * total);
+  size_t o_rslot = st.take(sizeof(int) * total);
+  size_t o_in = st.take(sizeof(float) * (size_t)k * D);
+  size_t o_out = st.take(sizeof(float) * (size_t)k * D);
+  size_t bytes = st.off;
+  if (!g.h_up.reserve(bytes) || !g.d_stage.reserve(bytes) || !g.h_down.reserve(sizeof(float) * (size_t)k * D) ||
+      !g.d_xq8.reserve(sizeof(Q8Dev) * (size_t)k * gbpr) || !g.d_hidden.reserve(sizeof(float) * (size_t)total * I) ||
+      !g.d_hq8.reserve(sizeof(Q8Dev) * (size_t)total * dbpr))
+    return false;
+  uint8_t* hb = (uint8_t*)g.h_up.p;
+  uint8_t* db = (uint8_t*)g.d_stage.p;
+  SlotDesc* hs = (SlotDesc*)(hb + o_slots);
+  int* hrows = (int*)(hb + o_rows);
+  float* hwts = (float*)(hb + o_wts);
+  int* hrs = (int*)(hb + o_rslot);
+  int off = 0;
+  for (int i = 0; i < n; i++) {
+    HostSlot& s = *act_slots[i];
+    SlotDesc d{};
+    d.gate = s.gate;
+    d.up = s.up;
+    d.down = s.down;
+    d.gb = s.gb;
+    d.ub = s.ub;
+    d.db = s.db;
+    d.n_rows = (int)s.rows.size();
+    d.row_off = off;
+    hs[i] = d;
+    for (size_t j = 0; j < s.rows.size(); j++) {
+      hrows[off] = s.rows[j];
+      hwts[off] = s.wts[j];
+      hrs[off] = i;
+      off++;
+    }
+  }
+  memcpy(hb + o_in, inputs, sizeof(float) * (size_t)k * D);
+  memcpy(hb + o_out, output, sizeof(float) * (size_t)k * D);
+
+  cudaStream_t s = stream();
+  if (!cuda_ok(cudaMemcpyAsync(db, hb, bytes, cudaMemcpyHostToDevice, s), what)) return false;
+  MoePlan plan{};
+  plan.slots = (const SlotDesc*)(db + o_slots);
+  plan.rows = (const int*)(db + o_rows);
+  plan.wts = (const float*)(db + o_wts);
+  plan.n_slots = n;
+  plan.total_rows = total;
+  plan.k = k;
+  plan.embed_dim = D;
+  plan.inter_dim = I;
+  plan.act = act;
+  plan.assoc_rule = rule;
+  plan.bias_term = bias_term;
+  const float* d_in = (const float*)(db + o_in);
+  float* d_out = (float*)(db + o_out);
+  Q8Dev* xq8 = (Q8Dev*)g.d_xq8.p;
+  float* hidden = (float*)g.d_hidden.p;
+  Q8Dev* hq8 = (Q8Dev*)g.d_hq8.p;
+
+  launch_quantize_rows(d_in, k, D, D, xq8, s);
+  if (!cuda_ok(launch_moe_gateup(plan, gate_fmt, xq8, gbpr, hidden, g.d_status, s), what)) return false;
+  launch_quantize_rows(hidden, total, I, I, hq8, s);
+  if (!cuda_ok(launch_moe_down(plan, (const int*)(db + o_rslot), hq8, dbpr, hidden, d_out, g.d_status, s), what))
+    return false;
+  g_launches += 4;
+  if (!cuda_ok(cudaMemcpyAsync(g.h_down.p, d_out, sizeof(float) * (size_t)k * D, cudaMemcpyDeviceToHost, s), what))
+    return false;
+  if (!finish(what)) return false;
+  memcpy(output, g.h_down.p, sizeof(float) * (size_t)k * D);
+  return true;
+}
+
+bool fmt_quantized(int f) { return f == FMT_Q4K || f == FMT_Q6K || f == FMT_MXFP4 || f == FMT_Q80; }
+
+// Validates a quantized matrix shape: ncols a multiple of the format's block.
+bool check_cols(int fmt, int ncols, const char* what) {
+  int blk = (fmt == FMT_Q4K || fmt == FMT_Q6K) ? QK : (fmt == FMT_MXFP4 || fmt == FMT_Q80) ? 32 : 1;
+  if (ncols <= 0 || ncols % blk != 0) {
+    set_host_error(3, "%s: %d columns is not a positive multiple of %d for format %d", what, ncols, blk, fmt);
+    return false;
+  }
+  return true;
+}
+
+}  // namespace tg
+
+using namespace tg;
+
+// ---------------------------------------------------------------------
+// C ABI.
+
+extern "C" {
+
+int tg_cuda_last_error(char* buf, size_t len) {
+  std::lock_guard<std::mutex> lk(g_err_mu);
+  int c = g_err_code;
+  if (buf && len) {
+    snprintf(buf, len, "%s", g_err_msg.c_str());
+  }
+  g_err_code = 0;
+  g_err_msg.clear();
+  return c;
+}
+
+int tg_cuda_set_device(int device) {
+  std::lock_guard<std::recursive_mutex> lk(g.mu);
+  if (g.inited) return device == g.device ? 0 : -1;
+  g.device = device;
+  return 0;
+}
+
+void tg_cuda_set_stream(void* s) {
+  std::lock_guard<std::recursive_mutex> lk(g.mu);
+  g.user_stream = (cudaStream_t)s;
+  g.user_stream_set = s != nullptr;
+}
+
+int tg_cuda_register(const void* host_ptr, size_t nbytes) {
+  std::lock_guard<std::recursive_mutex> lk(g.mu);
+  if (!ensure_init()) return -1;
+  if (!host_ptr || nbytes == 0) {
+    set_host_error(2, "tg_cuda_register: empty range");
+    return -1;
+  }
+  g_ranges[(uintptr_t)host_ptr] = Range{nbytes};
+  return 0;
+}
+
+int tg_cuda_unregister(const void* host_ptr) {
+  std::lock_guard<std::recursive_mutex> lk(g.mu);
+  int n = (int)g_ranges.erase((uintptr_t)host_ptr);
+  for (auto it = g_mats.begin(); it != g_mats.end();) {
+    if (std::get<0>(it->first) == (uintptr_t)host_ptr) {
+      it = g_mats.erase(it);
+      n++;
+    } else {
+      ++it;
+    }
+  }
+  return n > 0 ? 0 : -1;
+}
+
+void tg_cuda_registry_clear(void) {
+  std::lock_guard<std::recursive_mutex> lk(g.mu);
+  if (g.inited) cudaStreamSynchronize(stream());
+  g_mats.clear();
+  g_ranges.clear();
+  g_slab.clear();
+}
+
+size_t tg_cuda_registry_bytes(void) {
+  std::lock_guard<std::recursive_mutex> lk(g.mu);
+  return g_slab.total;
+}
+
+uint64_t tg_cuda_launch_count(void) { return g_launches.load(); }
+
+size_t tg_row_bytes(int fmt, int ncols) { return host_row_bytes(fmt, ncols); }
+
+void tg_set_threads(int n) {
+  std::lock_guard<std::recursive_mutex> lk(g.mu);
+  g.threads = n < 1 ? 1 : n;
+}
+
+int tg_get_threads(void) {
+  std::lock_guard<std::recursive_mutex> lk(g.mu);
+  return g.threads;
+}
+
+void tg_moe_forward_rows_v2(const uint8_t* const* gate_ptrs, const uint8_t* const* up_ptrs,
+                            const void* const* down_ptrs, int gate_fmt, const int* down_fmts,
+                            const float* const* gate_bias, const float* const* up_bias,
+                            const float* const* down_bias, int act, int n_experts, const float* row_weights,
+                            const float* inputs, float* output, int k, int embed_dim, int inter_dim) {
+  std::lock_guard<std::recursive_mutex> lk(g.mu);
+  const char* what = "tg_moe_forward_rows_v2";
+  if (n_experts <= 0 || k <= 0) return;
+  if (!fmt_quantized(gate_fmt)) {
+    set_host_error(4, "%s: gate format %d is not supported (0 Q4_K, 2 Q6_K, 3 MXFP4, 4 Q8_0)", what, gate_fmt);
+    return;
+  }
+  if (!check_cols(gate_fmt, embed_dim, what) || inter_dim <= 0 || inter_dim % 32 != 0) {
+    if (inter_dim % 32 != 0) set_host_error(3, "%s: inter_dim %d is not a multiple of 32", what, inter_dim);
+    return;
+  }
+  if (gate_bias && !up_bias) {
+    set_host_error(4, "%s: gate_bias given without up_bias", what);
+    return;
+  }
+  if (!ensure_init()) return;
+  std::vector<HostSlot> slots(n_experts);
+  for (int e = 0; e < n_experts; e++) {
+    HostSlot& s = slots[e];
+    for (int r = 0; r < k; r++) {
+      float w = row_weights[(size_t)e * k + r];
+      if (w == 0.f) continue;
+      s.rows.push_back(r);
+      s.wts.push_back(w);
+    }
+    if (s.rows.empty()) continue;
+    int dfmt = down_fmts[e];
+    if (!(fmt_quantized(dfmt) || dfmt == FMT_F16)) {
+      set_host_error(4, "%s: down format %d of expert %d is not supported", what, dfmt, e);
+      return;
+    }
+    if (dfmt != FMT_F16 && !check_cols(dfmt, inter_dim, what)) return;
+    if (!lookup_matrix(gate_ptrs[e], gate_fmt, inter_dim, embed_dim, &s.gate) ||
+        !lookup_matrix(up_ptrs[e], gate_fmt, inter_dim, embed_dim, &s.up) ||
+        !lookup_matrix(down_ptrs[e], dfmt, embed_dim, inter_dim, &s.down))
+      return;
+    if (gate_bias) {
+      s.gb = lookup_vector(gate_bias[e], inter_dim);
+      s.ub = lookup_vector(up_bias[e], inter_dim);
+      if (!s.gb || !s.ub) return;
+    }
+    if (down_bias) {
+      s.db = lookup_vector(down_bias[e], embed_dim);
+      if (!s.db) return;
+    }
+  }
+  run_moe(slots, gate_fmt, act == ACT_GPTOSS ? ACT_GPTOSS : ACT_SILU, ASSOC_MOE, 1, inputs, output, k, embed_dim,
+          inter_dim, false);
+}
+
+void tg_moe_forward_rows(const uint8_t* const* gate_ptrs, const uint8_t* const* up_ptrs, const void* const* down_ptrs,
+                         const int* down_fmts, int n_experts, const float* row_weights, const float* inputs,
+                         float* output, int k, int embed_dim, int inter_dim) {
+  tg_moe_forward_rows_v2(gate_ptrs, up_ptrs, down_ptrs, FMT_Q4K, down_fmts, nullptr, nullptr, nullptr, ACT_SILU,
+                         n_experts, row_weights, inputs, output, k, embed_dim, inter_dim);
+}
+
+// Down format codes of the single-expert entries: 1 F16, 2 Q6_K, else Q4_K.
+static int single_down_fmt(int f) { return f == 1 ? FMT_F16 : f == 2 ? FMT_Q6K : FMT_Q4K; }
+
+static void expert_rows(const char* what, const uint8_t* gate, const uint8_t* up, const void* down, int down_format,
+                        const float* inputs, float* output, const float* weights, int k, int D, int I, int rule,
+                        bool zero) {
+  if (k <= 0) return;
+  if (!check_cols(FMT_Q4K, D, what)) return;
+  int dfmt = single_down_fmt(down_format);
+  if (dfmt != FMT_F16 && !check_cols(dfmt, I, what)) return;
+  if (!ensure_init()) return;
+  std::vector<HostSlot> slots(1);
+  HostSlot& s = slots[0];
+  for (int r = 0; r < k; r++) {
+    s.rows.push_back(r);
+    s.wts.push_back(weights[r]);
+  }
+  if (!lookup_matrix(gate, FMT_Q4K, I, D, &s.gate) || !lookup_matrix(up, FMT_Q4K, I, D, &s.up) ||
+      !lookup_matrix(down, dfmt, D, I, &s.down))
+    return;
+  run_moe(slots, FMT_Q4K, ACT_SILU, rule, 0, inputs, output, k, D, I, zero);
+}
+
+void tg_expert_forward(const uint8_t* q4_data, const float* input, float* output, float weight, int embed_dim,
+                       int inter_dim) {
+  std::lock_guard<std::recursive_mutex> lk(g.mu);
+  size_t gate_bytes = (size_t)inter_dim * host_row_bytes(FMT_Q4K, embed_dim);
+  expert_rows("tg_expert_forward", q4_data, q4_data + gate_bytes, q4_data + 2 * gate_bytes, 0, input, output,
+              &weight, 1, embed_dim, inter_dim, ASSOC_X1, false);
+}
+
+void tg_expert_forward_mixed(const uint8_t* gate_q4, const uint8_t* up_q4, const void* down_data, int down_format,
+                             const float* input, float* output, float weight, int embed_dim, int inter_dim) {
+  std::lock_guard<std::recursive_mutex> lk(g.mu);
+  expert_rows("tg_expert_forward_mixed", gate_q4, up_q4, down_data, down_format, input, output, &weight, 1,
+              embed_dim, inter_dim, ASSOC_X1, false);
+}
+
+void tg_expert_forward_rows(const uint8_t* gate_q4, const uint8_t* up_q4, const void* down_data, int down_format,
+                            const float* inputs, float* output, const float* weights, int k, int embed_dim,
+                            int inter_dim) {
+  std::lock_guard<std::recursive_mutex> lk(g.mu);
+  expert_rows("tg_expert_forward_rows", gate_q4, up_q4, down_data, down_format, inputs, output, weights, k,
+              embed_dim, inter_dim, ASSOC_ROWS, false);
+}
+
+void tg_moe_forward(const uint8_t** expert_ptrs, const float* weights, int n_experts, const float* input,
+                    float* output, int embed_dim, int inter_dim) {
+  std::lock_guard<std::recursive_mutex> lk(g.mu);
+  const char* what = "tg_moe_forward";
+  memset(output, 0, sizeof(float) * (size_t)embed_dim);
+  if (n_experts <= 0) return;
+  if (!check_cols(FMT_Q4K, embed_dim, what) || !check_cols(FMT_Q4K, inter_dim, what)) return;
+  if (!ensure_init()) return;
+  size_t gate_bytes = (size_t)inter_dim * host_row_bytes(FMT_Q4K, embed_dim);
+  std::vector<HostSlot> slots(n_experts);
+  for (int e = 0; e < n_experts; e++) {
+    HostSlot& s = slots[e];
+    s.rows.push_back(0);
+    s.wts.push_back(weights[e]);
+    const uint8_t* b = expert_ptrs[e];
+    if (!lookup_matrix(b, FMT_Q4K, inter_dim, embed_dim, &s.gate) ||
+        !lookup_matrix(b + gate_bytes, FMT_Q4K, inter_dim, embed_dim, &s.up) ||
+        !lookup_matrix(b + 2 * gate_bytes, FMT_Q4K, embed_dim, inter_dim, &s.down))
+      return;
+  }
+  run_moe(slots, FMT_Q4K, ACT_SILU, ASSOC_X1, 0, input, output, 1, embed_dim, inter_dim, false);
+}
+
+// Matvec entries.
+
+static void matvec_entry(const char* what, int fmt, const void* mat, const float* bias, int bias_term,
+                         const float* input, float* output, int nrows, int ncols) {
+  if (nrows <= 0) return;
+  if (fmt != FMT_F16 && !check_cols(fmt, ncols, what)) return;
+  if (!ensure_init()) return;
+  WDesc w;
+  if (!lookup_matrix(mat, fmt, nrows, ncols, &w)) return;
+  const float* dbias = nullptr;
+  if (bias && !(dbias = lookup_vector(bias, nrows))) return;
+  const int nb = (ncols + QK - 1) / QK;
+  cudaStream_t s = stream();
+  if (!g.h_up.reserve(sizeof(float) * ncols) || !g.d_stage.reserve(sizeof(float) * ncols + 256 + sizeof(float) * nrows) ||
+      !g.d_xq8.reserve(sizeof(Q8Dev) * nb) || !g.h_down.reserve(sizeof(float) * nrows))
+    return;
+  float* d_x = (float*)g.d_stage.p;
+  float* d_out = (float*)((uint8_t*)g.d_stage.p + align_up(sizeof(float) * ncols, 256));
+  memcpy(g.h_up.p, input, sizeof(float) * ncols);
+  if (!cuda_ok(cudaMemcpyAsync(d_x, g.h_up.p, sizeof(float) * ncols, cudaMemcpyHostToDevice, s), what)) return;
+  if (fmt != FMT_F16) {
+    launch_quantize_rows(d_x, 1, ncols, ncols, (Q8Dev*)g.d_xq8.p, s);
+    g_launches++;
+  }
+  if (!cuda_ok(launch_matvec(w, (const Q8Dev*)g.d_xq8.p, d_x, dbias, bias_term, d_out, g.d_status, s), what)) return;
+  g_launches++;
+  if (!cuda_ok(cudaMemcpyAsync(g.h_down.p, d_out, sizeof(float) * nrows, cudaMemcpyDeviceToHost, s), what)) return;
+  if (!finish(what)) return;
+  memcpy(output, g.h_down.p, sizeof(float) * nrows);
+}
+
+void tg_matmul_q4k(const uint8_t* q4_matrix, const float* input, float* output, int nrows, int ncols) {
+  std::lock_guard<std::recursive_mutex> lk(g.mu);
+  matvec_entry("tg_matmul_q4k", FMT_Q4K, q4_matrix, nullptr, 0, input, output, nrows, ncols);
+}
+
+void tg_matmul_q6k(const uint8_t* q6_matrix, const float* input, float* output, int nrows, int ncols) {
+  std::lock_guard<std::recursive_mutex> lk(g.mu);
+  matvec_entry("tg_matmul_q6k", FMT_Q6K, q6_matrix, nullptr, 0, input, output, nrows, ncols);
+}
+
+// Any format code other than Q4_K/Q6_K/MXFP4/Q8_0 decodes as F16, as the
+// reference's dispatch default does (libtinygiant.c:596-620).
+void tg_matmul(int fmt, const void* mat, const float* bias, const float* input, float* output, int nrows, int ncols) {
+  std::lock_guard<std::recursive_mutex> lk(g.mu);
+  matvec_entry("tg_matmul", fmt_quantized(fmt) ? fmt : FMT_F16, mat, bias, 1, input, output, nrows, ncols);
+}
+
+static void plain_matvec(const char* what, bool f16, const void* A, const float* x, float* out, int nrows,
+                         int ncols) {
+  if (nrows <= 0) return;
+  if (!ensure_init()) return;
+  WDesc w;
+  if (!lookup_matrix(A, f16 ? FMT_F16 : -1, nrows, ncols, &w)) return;
+  cudaStream_t s = stream();
+  if (!g.h_up.reserve(sizeof(float) * ncols) || !g.d_stage.reserve(align_up(sizeof(float) * ncols, 256) + sizeof(float) * nrows) ||
+      !g.h_down.reserve(sizeof(float) * nrows))
+    return;
+  float* d_x = (float*)g.d_stage.p;
+  float* d_out = (float*)((uint8_t*)g.d_stage.p + align_up(sizeof(float) * ncols, 256));
+  memcpy(g.h_up.p, x, sizeof(float) * ncols);
+  if (!cuda_ok(cudaMemcpyAsync(d_x, g.h_up.p, sizeof(float) * ncols, cudaMemcpyHostToDevice, s), what)) return;
+  if (f16) launch_f16_matvec((const uint16_t*)w.main, d_x, d_out, nrows, ncols, s);
+  else launch_f32_matvec((const float*)w.main, d_x, d_out, nrows, ncols, s);
+  g_launches++;
+  if (!cuda_ok(cudaGetLastError(), what)) return;
+  if (!cuda_ok(cudaMemcpyAsync(g.h_down.p, d_out, sizeof(float) * nrows, cudaMemcpyDeviceToHost, s), what)) return;
+  if (!finish(what)) return;
+  memcpy(out, g.h_down.p, sizeof(float) * nrows);
+}
+
+void tg_f16_matvec(const uint16_t* A, const float* x, float* out, int nrows, int ncols) {
+  std::lock_guard<std::recursive_mutex> lk(g.mu);
+  plain_matvec("tg_f16_matvec", true, A, x, out, nrows, ncols);
+}
+
+void tg_f32_matvec(const float* A, const float* x, float* out, int nrows, int ncols) {
+  std::lock_guard<std::recursive_mutex> lk(g.mu);
+  plain_matvec("tg_f32_matvec", false, A, x, out, nrows, ncols);
+}
+
+void tg_rms_norm(const float* x, const float* weight, float* out, int dim, float eps) {
+  std::lock_guard<std::recursive_mutex> lk(g.mu);
+  const char* what = "tg_rms_norm";
+  if (dim <= 0) return;
+  if (!ensure_init()) return;
+  const float* dw = lookup_vector(weight, dim);
+  if (!dw) return;
+  cudaStream_t s = stream();
+  size_t xb = align_up(sizeof(float) * dim, 256);
+  if (!g.h_up.reserve(xb) || !g.d_stage.reserve(2 * xb) || !g.h_down.reserve(xb)) return;
+  float* d_x = (float*)g.d_stage.p;
+  float* d_out = (float*)((uint8_t*)g.d_stage.p + xb);
+  memcpy(g.h_up.p, x, sizeof(float) * dim);
+  if (!cuda_ok(cudaMemcpyAsync(d_x, g.h_up.p, sizeof(float) * dim, cudaMemcpyHostToDevice, s), what)) return;
+  launch_rms_norm(d_x, dw, d_out, dim, eps, s);
+  g_launches++;
+  if (!cuda_ok(cudaGetLastError(), what)) return;
+  if (!cuda_ok(cudaMemcpyAsync(g.h_down.p, d_out, sizeof(float) * dim, cudaMemcpyDeviceToHost, s), what)) return;
+  if (!finish(what)) return;
+  memcpy(out, g.h_down.p, sizeof(float) * dim);
+}
+
+// ---- Test hooks --------------------------------------------------------
+
+int tg_cuda_device_count(void) {
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  return n;
+}
+
+// The reference's 296-byte q8_block: scale, sum, bsums[8], qs[256].
+struct RefQ8 {
+  float scale;
+  int32_t sum;
+  int32_t bsums[8];
+  int8_t qs[256];
+};
+static_assert(sizeof(RefQ8) == 296, "q8_block");
+
+int tg_cuda_debug_quantize_q8(const float* x, int nrows, int ncols, void* out_blocks) {
+  std::lock_guard<std::recursive_mutex> lk(g.mu);
+  const char* what = "tg_cuda_debug_quantize_q8";
+  if (nrows <= 0 || ncols <= 0) return 0;
+  if (!ensure_init()) return -1;
+  const int nb = (ncols + QK - 1) / QK;
+  const size_t xb = align_up(sizeof(float) * (size_t)nrows * ncols, 256);
+  const size_t qb = sizeof(Q8Dev) * (size_t)nrows * nb;
+  if (!g.h_up.reserve(xb) || !g.d_stage.reserve(xb + qb) || !g.h_down.reserve(qb)) return -1;
+  memcpy(g.h_up.p, x, sizeof(float) * (size_t)nrows * ncols);
+  cudaStream_t s = stream();
+  float* dx = (float*)g.d_stage.p;
+  Q8Dev* dq = (Q8Dev*)((uint8_t*)g.d_stage.p + xb);
+  if (!cuda_ok(cudaMemcpyAsync(dx, g.h_up.p, sizeof(float) * (size_t)nrows * ncols, cudaMemcpyHostToDevice, s), what))
+    return -1;
+  launch_quantize_rows(dx, nrows, ncols, ncols, dq, s);
+  g_launches++;
+  if (!cuda_ok(cudaMemcpyAsync(g.h_down.p, dq, qb, cudaMemcpyDeviceToHost, s), what) || !finish(what)) return -1;
+  const Q8Dev* hq = (const Q8Dev*)g.h_down.p;
+  RefQ8* o = (RefQ8*)out_blocks;
+  for (size_t i = 0; i < (size_t)nrows * nb; i++) {
+    o[i].scale = hq[i].scale;
+    o[i].sum = hq[i].sum;
+    memcpy(o[i].bsums, hq[i].bsums, sizeof o[i].bsums);
+    memcpy(o[i].qs, hq[i].qs, sizeof o[i].qs);
+  }
+  return 0;
+}
+
+int tg_cuda_debug_row_isums(int fmt, const void* mat, int nrows, int ncols, const void* xq_blocks, int32_t* out) {
+  std::lock_guard<std::recursive_mutex> lk(g.mu);
+  const char* what = "tg_cuda_debug_row_isums";
+  if (!fmt_quantized(fmt)) {
+    set_host_error(4, "%s: format %d has no integer sums", what, fmt);
+    return -1;
+  }
+  if (nrows <= 0 || !check_cols(fmt, ncols, what)) return -1;
+  if (!ensure_init()) return -1;
+  WDesc w;
+  if (!lookup_matrix(mat, fmt, nrows, ncols, &w)) return -1;
+  const int nb = (ncols + QK - 1) / QK;
+  const int per_row = debug_isums_per_row(fmt, ncols);
+  const size_t qb = align_up(sizeof(Q8Dev) * nb, 256), ob = sizeof(int32_t) * (size_t)nrows * per_row;
+  if (!g.h_up.reserve(qb) || !g.d_stage.reserve(qb + ob) || !g.h_down.reserve(ob)) return -1;
+  Q8Dev* hq = (Q8Dev*)g.h_up.p;
+  const RefQ8* in = (const RefQ8*)xq_blocks;
+  memset(hq, 0, qb);
+  for (int b = 0; b < nb; b++) {
+    memcpy(hq[b].qs, in[b].qs, 256);
+    hq[b].scale = in[b].scale;
+    hq[b].sum = in[b].sum;
+    memcpy(hq[b].bsums, in[b].bsums, sizeof hq[b].bsums);
+  }
+  cudaStream_t s = stream();
+  Q8Dev* dq = (Q8Dev*)g.d_stage.p;
+  int32_t* dout = (int32_t*)((uint8_t*)g.d_stage.p + qb);
+  if (!cuda_ok(cudaMemcpyAsync(dq, hq, qb, cudaMemcpyHostToDevice, s), what)) return -1;
+  launch_debug_isums(w, dq, dout, s);
+  g_launches++;
+  if (!cuda_ok(cudaGetLastError(), what)) return -1;
+  if (!cuda_ok(cudaMemcpyAsync(g.h_down.p, dout, ob, cudaMemcpyDeviceToHost, s), what) || !finish(what)) return -1;
+  memcpy(out, g.h_down.p, ob);
+  return per_row;
+}
+
+// Host page-cache hints on the caller's (host) memory, as the reference
+// issues them; they do not touch the GPU.
+static void page_range(const void* addr, size_t len, void** a, size_t* n) {
+  uintptr_t pg = (uintptr_t)sysconf(_SC_PAGESIZE);
+  uintptr_t p = (uintptr_t)addr & ~(pg - 1);
+  *a = (void*)p;
+  *n = len + ((uintptr_t)addr - p);
+}
+
+void tg_prefetch(const void* addr, size_t len) {
+  void* a;
+  size_t n;
+  page_range(addr, len, &a, &n);
+  posix_madvise(a, n, POSIX_MADV_WILLNEED);
+}
+
+void tg_prefetch_batch(const void** addrs, const size_t* lens, int count) {
+  for (int i = 0; i < count; i++) tg_prefetch(addrs[i], lens[i]);
+}
+
+int tg_mlock(const void* addr, size_t len) {
+  void* a;
+  size_t n;
+  page_range(addr, len, &a, &n);
+  return mlock(a, n);
+}
+
+}  // extern "C"

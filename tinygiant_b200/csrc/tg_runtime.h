@@ -1,0 +1,17 @@
+// tg_runtime.h — host runtime internals shared by the C-ABI translation units.
+#pragma once
+#include <cuda_runtime.h>
+
+#include "tg_common.cuh"
+
+namespace tg {
+
+void set_host_error(int code, const char* fmt, ...);
+bool ensure_init();
+cudaStream_t stream();
+bool finish(const char* what);
+size_t host_row_bytes(int fmt, int ncols);
+bool lookup_matrix(const void* h, int fmt, int rows, int cols, WDesc* out);
+const float* lookup_vector(const float* h, int n);
+
+}  // namespace tg
