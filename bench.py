@@ -1,0 +1,390 @@
+"""Benchmark: MoE-layer decode tok/s and fused quant-matvec HBM GB/s on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--config c2|c3|c4|c5] [--tokens T]
+
+Default workload ("C2"): one Qwen3-30B-A3B-shaped MoE
+layer at batch 1 — 128 experts (Q4_K gate/up 768x2048, Q6_K down 2048x768),
+fp32 router [128 x 2048], top-8 softmax, weights from seed 1, x ~ N(0, 1).
+A step is one layer-token: rmsnorm -> router -> top-8 -> 8 experts on the
+GPU.  Synthetic data; every expert of every copy is HBM-resident.
+
+Timing (device): W warm-up steps, then K steps captured in one CUDA graph,
+bracketed by barrier + synchronize, CUDA events on the library's stream, max
+over ranks.  Steps cycle through R HBM copies of the layer (6.3 GB at R=16),
+so each step's 24.5 MB of experts were last touched 15 steps (~390 MB of
+traffic) earlier and are not L2-resident.
+
+e2e: the same step through the C-ABI entry tg_layer_forward with host
+buffers (x in, MoE output back), host<->device copies inside the timed region.
+
+Multi-GPU (torchrun): experts sharded by id (e % N == rank), router
+replicated, one NCCL all-reduce of the [T, D] output per step; total work is
+fixed ("strong").
+
+--impl reference: the reference's own CPU path on the host cores — its router
+(restated in synth.route, checked against tinygiant/router.py) + its
+csrc/libtinygiant.c tg_moe_forward_rows_v2 (oracle/_ref, compiled from the
+reference's source) with every host thread.
+"""
+import argparse
+import ctypes
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "MoE-layer decode tok/s; fused quant-matvec HBM GB/s vs ~8 TB/s B200 peak"
+UNIT = "tok/s"
+R_COPIES = 16
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--config", default="c2", choices=["c2", "c3", "c4", "c5"])
+    ap.add_argument("--tokens", type=int, default=None)
+    ap.add_argument("--copies", type=int, default=R_COPIES)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+# ---- workload ------------------------------------------------------------
+
+def make_layer(cfg):
+    from tinygiant_b200 import synth
+    if cfg == "c4":
+        return synth.gptoss_layer(seed=3)
+    if cfg == "c3":
+        return synth.qwen_layer(seed=2, router_bias=synth.zipf_bias(seed=2))
+    return synth.qwen_layer(seed=1)
+
+
+def workload_desc(cfg, T, R, L):
+    names = {
+        "c2": "C2: one Qwen3-30B-A3B MoE layer (128 experts, Q4_K gate/up, Q6_K down, top-8, D=2048, I=768)",
+        "c3": "C3: Qwen3-30B-A3B MoE layer with Zipf(1.1)-skewed router bias",
+        "c4": "C4: gpt-oss-120b-shaped MXFP4 MoE layer (128 experts, top-4, D=I=2880)",
+        "c5": "C5: Qwen3-30B-A3B MoE-FFN stack layer",
+    }
+    return {"workload": names[cfg], "tokens_per_step": T, "experts": L.n_experts, "top_k": L.top_k,
+            "embed_dim": L.embed_dim, "inter_dim": L.inter_dim, "layer_copies": R,
+            "l2": f"inputs larger than L2: steps cycle {R} HBM copies of the layer",
+            "step": "rmsnorm + router + top-k softmax + experts (gate/up/act/down/combine)"}
+
+
+def step_inputs(n, T, D, seed=4):
+    rng = np.random.default_rng([seed, 7])
+    return rng.standard_normal((n, T, D)).astype(np.float32)
+
+
+def algorithmic_bytes(L, xs):
+    """Per step: each distinct selected expert's weight bytes once + the fp32
+    router + x in and out; routing by the reference router."""
+    from tinygiant_b200 import synth
+    eb = L.expert_bytes(0)
+    out = []
+    for x in xs:
+        experts, _, _, _ = synth.route(L, synth.rms_norm(x))
+        out.append(len(experts) * eb + L.router_w.nbytes + 2 * x.nbytes)
+    return np.array(out, dtype=np.float64)
+
+
+# ---- clocks ------------------------------------------------------------------
+
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device):
+        self.device = device
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.device), f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.t.join(timeout=2)
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            p = [v.strip() for v in ln.split(",")]
+            if len(p) < 9:
+                continue
+            try:
+                sm.append(float(p[1]))
+                mx.append(float(p[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, p[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def measured_peak():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured (MEASURED_PEAKS.json hbm_gbs)"
+    return 6650.0, "fallback 6.65 TB/s"
+
+
+def traffic_from_profiles():
+    p = ROOT / "profiles" / "traffic.json"
+    if p.exists():
+        try:
+            return json.loads(p.read_text())
+        except ValueError:
+            return None
+    return None
+
+
+# ---- CPU baseline (reference arm / cpu_baseline) ---------------------------
+
+def cpu_reference_run(L, xs, budget_s=12.0, max_steps=None):
+    """The reference's CPU path per step: its router + its C MoE call."""
+    from oracle import oracle as O
+    from tinygiant_b200 import moe, synth
+    lib = O.load_reference()
+    kind = "reference"
+    if lib is None:
+        lib, kind = O.load_oracle(), "port"
+    cores = os.cpu_count() or 1
+    lib.tg_set_threads(cores)
+    out = np.zeros_like(xs[0])
+    moe.moe_layer_forward(lib, L, synth.rms_norm(xs[0]), out)    # warm
+    n, t0 = 0, time.perf_counter()
+    while True:
+        x = xs[n % len(xs)]
+        moe.moe_layer_forward(lib, L, synth.rms_norm(x), out)
+        n += 1
+        el = time.perf_counter() - t0
+        if (max_steps and n >= max_steps) or (not max_steps and el >= budget_s):
+            break
+    lib.tg_set_threads(1)
+    T = xs.shape[1]
+    return {"value": n * T / el, "unit": UNIT, "cores": cores, "kind": kind,
+            "sample": f"{n} steps x {T} token(s) of the same workload, {el:.1f} s; "
+                      f"{'reference csrc/libtinygiant.c built from source (NEON via oracle/neon_shim)' if kind == 'reference' else 'oracle port (tg_oracle.c)'}"
+                      f" + numpy router, all {cores} host threads"}, el / n
+
+
+def run_reference(a):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    cfg = a.config
+    T = a.tokens or 1
+    L = make_layer(cfg)
+    xs = step_inputs(max(a.warmup, 1) + a.steps, T, L.embed_dim)
+    # warm-up steps, untimed
+    from oracle import oracle as O
+    from tinygiant_b200 import moe, synth
+    lib = O.load_reference()
+    kind = "reference"
+    if lib is None:
+        lib, kind = O.load_oracle(), "port"
+    cores = os.cpu_count() or 1
+    lib.tg_set_threads(cores)
+    out = np.zeros_like(xs[0])
+    for i in range(a.warmup):
+        moe.moe_layer_forward(lib, L, synth.rms_norm(xs[i]), out)
+    t0 = time.perf_counter()
+    for i in range(a.steps):
+        moe.moe_layer_forward(lib, L, synth.rms_norm(xs[a.warmup + i]), out)
+    el = time.perf_counter() - t0
+    value = a.steps * T / el
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": a.gpus, "steps": a.steps,
+            "warmup": a.warmup, "ms_per_step": el / a.steps * 1e3, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "int8xQ4_K/Q6_K (int32 accumulate), fp32 combine", "data": "synthetic",
+            "config": workload_desc(cfg, T, 1, L),
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": kind,
+                             "sample": f"{a.steps} steps x {T} token(s); numpy router + "
+                                       f"{'csrc/libtinygiant.c (reference source, NEON via oracle/neon_shim)' if kind == 'reference' else 'oracle port'}"
+                                       f", tg_set_threads({cores})"},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ---- our arm ---------------------------------------------------------------
+
+def run_ours(a):
+    import torch
+    import torch.distributed as dist
+
+    import tinygiant_b200 as tg
+    from tinygiant_b200.layer import ResidentLayer
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != a.gpus:
+        a.gpus = world
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+    lib = tg.load()
+    lib.tg_cuda_set_device(local)
+    stream = torch.cuda.Stream()
+    lib.tg_cuda_set_stream(ctypes.c_void_p(stream.cuda_stream))
+
+    cfg = a.config
+    T = a.tokens or 1
+    L = make_layer(cfg)
+    D = L.embed_dim
+    R = max(1, a.copies)
+    base = ResidentLayer(L, max_tokens=T, lib=lib, shard=rank, n_shards=world)
+    layers = [base] + [base.clone() for _ in range(R - 1)]
+    tg.check(lib)
+
+    S = a.warmup + a.steps
+    xs_host = step_inputs(S, T, D)
+    xs = torch.from_numpy(xs_host).to(f"cuda:{local}")
+    out = torch.zeros((T, D), dtype=torch.float32, device=f"cuda:{local}")
+
+    def step(i):
+        lay = layers[i % R]
+        lib.tg_layer_forward_dev(lay.h, xs[i].data_ptr(), None, None, out.data_ptr(), T, 1, None)
+        if world > 1:
+            dist.all_reduce(out)
+
+    # warm-up (also exercises every copy once)
+    with torch.cuda.stream(stream):
+        for i in range(a.warmup):
+            step(i)
+    torch.cuda.synchronize()
+    tg.check(lib)
+
+    # capture the K timed steps in one graph
+    g = torch.cuda.CUDAGraph()
+    launches0 = lib.tg_cuda_launch_count()
+    with torch.cuda.graph(g, stream=stream):
+        for i in range(a.warmup, S):
+            step(i)
+    launches = lib.tg_cuda_launch_count() - launches0
+    tg.check(lib)
+    # one untimed replay so the graph's first-launch cost is not timed
+    g.replay()
+    torch.cuda.synchronize()
+
+    # Clocks are sampled over a ~1.5 s soak of untimed replays of the same
+    # graph and the timed replay that follows it (the timed region alone is
+    # shorter than nvidia-smi's sampling period).
+    clocks = ClockSampler(local)
+    clocks.start()
+    t_soak = time.perf_counter()
+    with torch.cuda.stream(stream):
+        while time.perf_counter() - t_soak < 1.5:
+            g.replay()
+            torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        ev0.record(stream)
+        g.replay()
+        ev1.record(stream)
+    torch.cuda.synchronize()
+    ms = ev0.elapsed_time(ev1)
+    if world > 1:
+        t = torch.tensor([ms], device=f"cuda:{local}")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    clk = clocks.stop()
+    tg.check(lib)
+
+    ms_step = ms / a.steps
+    value = a.steps * T / (ms / 1e3)
+    line = None
+    if rank == 0:
+        nbytes = algorithmic_bytes(L, xs_host[a.warmup:])
+        achieved = nbytes.sum() / (ms / 1e3) / 1e9
+        peak, peak_src = measured_peak()
+        peak *= world            # whole-job bytes against every GPU's HBM
+        tr = traffic_from_profiles()
+        roof = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                "traffic": (tr or {}).get(cfg),
+                "kernel": "fused MoE layer step (router + gate/up + down kernels), per step",
+                "algorithmic_bytes_per_step": float(nbytes.mean()), "peak_source": peak_src}
+        line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": a.steps,
+                "warmup": a.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong",
+                "vs_baseline": None, "dtype": "int8xQ4_K/Q6_K (int32 accumulate), fp32 combine",
+                "data": "synthetic (seeded weights and inputs)",
+                "config": {**workload_desc(cfg, T, R, L), "parallelism": f"ep{world}"},
+                "gbps": achieved, "clocks": clk, "roofline": roof, "gpu_launches": int(launches)}
+
+    # e2e through the C ABI with host buffers (rank 0 of a single-GPU run;
+    # with N > 1 every rank runs it and the slowest counts)
+    e2e = None
+    if world == 1:
+        xh = [np.ascontiguousarray(x) for x in xs_host]
+        outh = np.zeros((T, D), np.float32)
+        for i in range(min(a.warmup, S)):
+            layers[i % R].forward(xh[i], outh)
+        t0 = time.perf_counter()
+        for i in range(a.warmup, S):
+            lib.tg_layer_forward(layers[i % R].h, xh[i].ctypes.data, outh.ctypes.data, T, 1)
+        el = time.perf_counter() - t0
+        tg.check(lib)
+        e2e = {"value": a.steps * T / el, "unit": UNIT, "h2d_bytes_per_step": int(xh[0].nbytes),
+               "d2h_bytes_per_step": int(outh.nbytes), "api": "tg_layer_forward (C ABI, host buffers)",
+               "ms_per_step": el / a.steps * 1e3}
+    if rank == 0:
+        line["e2e"] = e2e
+        if world == 1 and not a.no_cpu_baseline:
+            cb, _ = cpu_reference_run(L, xs_host[a.warmup:], budget_s=12.0)
+            line["cpu_baseline"] = cb
+        print(json.dumps(line), flush=True)
+    del g
+    for lay in layers:
+        lay.close()
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def main():
+    a = parse()
+    if a.impl == "reference":
+        run_reference(a)
+    else:
+        run_ours(a)
+
+
+if __name__ == "__main__":
+    main()

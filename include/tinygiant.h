@@ -146,10 +146,12 @@ int tg_cuda_set_device(int device);
  * stream).  Host-pointer calls still synchronise that stream before return. */
 void tg_cuda_set_stream(void *stream);
 
-/* Uploads [host_ptr, host_ptr + nbytes) of raw weight bytes to HBM now, so a
- * later call that names any matrix inside it does not pay the upload.  The
- * registry treats registered bytes as immutable; after changing them call
- * tg_cuda_unregister or tg_cuda_registry_clear.  Returns 0 on success. */
+/* Declares [host_ptr, host_ptr + nbytes) as immutable weight bytes (e.g. a
+ * whole mmap'd expert file): matrices inside it are uploaded to HBM on first
+ * use and never re-checked.  Matrices outside any declared range are
+ * uploaded on first use too, but every later call compares a 96-byte sample
+ * of their host bytes and re-uploads on a change; a change that misses the
+ * sample needs tg_cuda_unregister / tg_cuda_registry_clear.  0 on success. */
 int tg_cuda_register(const void *host_ptr, size_t nbytes);
 int tg_cuda_unregister(const void *host_ptr);
 void tg_cuda_registry_clear(void);
@@ -158,6 +160,54 @@ size_t tg_cuda_registry_bytes(void);
 
 /* Number of kernels this library has launched since load. */
 uint64_t tg_cuda_launch_count(void);
+
+/* ---- Resident layers routed on the GPU ---------------------------------- *
+ * A layer holds all n_experts experts (uploaded through the registry), an
+ * fp32 router W_r [n_experts][embed_dim] (+ optional bias) and scratch for up
+ * to max_tokens rows.  One step = rmsnorm -> router -> top_k softmax ->
+ * plan -> experts (engine.py:281-342 + tg_moe_forward_rows_v2), all on the
+ * GPU.  Returns NULL on failure. */
+void *tg_layer_create(int n_experts, const uint8_t *const *gate_ptrs, const uint8_t *const *up_ptrs,
+                      const void *const *down_ptrs, int gate_fmt, const int *down_fmts,
+                      const float *const *gate_bias, const float *const *up_bias,
+                      const float *const *down_bias, int act, int embed_dim, int inter_dim,
+                      const float *router_w, const float *router_b, int top_k, int max_tokens);
+/* Expert-parallel shard of a layer: this GPU uploads only experts e with
+ * e % n_shards == shard (the router is replicated); its steps produce the
+ * local experts' part of the output, to be summed across GPUs. */
+void *tg_layer_create_shard(int n_experts, const uint8_t *const *gate_ptrs, const uint8_t *const *up_ptrs,
+                            const void *const *down_ptrs, int gate_fmt, const int *down_fmts,
+                            const float *const *gate_bias, const float *const *up_bias,
+                            const float *const *down_bias, int act, int embed_dim, int inter_dim,
+                            const float *router_w, const float *router_b, int top_k, int max_tokens, int shard,
+                            int n_shards);
+/* A second HBM copy of a layer's weights (for working sets beyond L2). */
+void *tg_layer_clone(void *layer);
+void tg_layer_destroy(void *layer);
+size_t tg_layer_expert_bytes(void *layer, int expert);
+/* Enqueue one step on device buffers: x' = x + add (add may be NULL);
+ * N = normalize ? rmsnorm(x') * norm_w (NULL: 1) : x'; moe_out = experts(N);
+ * x_out = x' (may be NULL).  Asynchronous on the library stream. */
+int tg_layer_forward_dev(void *layer, const float *x, const float *add, float *x_out, float *moe_out, int T,
+                         int normalize, const float *norm_w);
+/* Host buffers, synchronous: out[T][D] += experts(normalize ? rmsnorm(x) : x). */
+int tg_layer_forward(void *layer, const float *x_host, float *out_host, int T, int normalize);
+/* Selected experts and weights [T][top_k] of the layer's last step. */
+int tg_layer_last_routing(void *layer, int T, int *idx, float *w);
+/* x [T][D] (device) += experts_l(rmsnorm(x) * norm_w[l]) for l = 0..n_layers-1,
+ * in place, asynchronous. */
+int tg_stack_forward_dev(void *const *layers, int n_layers, float *x, int T, const float *const *norm_w);
+
+/* CUDA graphs over the library stream (capture the enqueued work between
+ * begin and end; launch replays it). */
+int tg_cuda_graph_begin(void);
+void *tg_cuda_graph_end(void);
+int tg_cuda_graph_launch(void *graph);
+void tg_cuda_graph_destroy(void *graph);
+/* The cudaStream_t the library enqueues on; synchronise it and report
+ * device-side errors. */
+void *tg_cuda_stream(void);
+int tg_cuda_synchronize(void);
 
 /* Number of CUDA devices visible to this process (0 without a GPU). */
 int tg_cuda_device_count(void);

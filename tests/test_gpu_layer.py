@@ -1,0 +1,134 @@
+"""The GPU-routed layer path (tg_layer_*): routing on the device against the
+reference router, expert outputs against the oracle, the residual stack and
+CUDA-graph replay.  Tolerance as in test_gpu_parity (1e-4 of max|ref|)."""
+import ctypes
+
+import numpy as np
+import pytest
+
+import tinygiant_b200 as tg
+from oracle import oracle as O
+from tinygiant_b200 import moe as M
+from tinygiant_b200 import synth
+from tinygiant_b200.layer import ResidentLayer
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-4
+
+
+def rel_err(got, ref):
+    s = float(np.max(np.abs(ref)))
+    return float(np.max(np.abs(got.astype(np.float64) - ref))) / (s if s > 0 else 1.0)
+
+
+def routing_agrees(layer, N, idx, w):
+    """Same experts in the same order and weights within 1e-5, except where
+    the reference's logits tie to within 1e-5 (fp32 order differences)."""
+    _, _, ridx, rw = synth.route(layer, N)
+    for t in range(N.shape[0]):
+        if not np.array_equal(ridx[t], idx[t]):
+            logits = layer.router_w @ N[t] + (0 if layer.router_b is None else layer.router_b)
+            gaps = np.abs(np.diff(np.sort(logits)[::-1][:layer.top_k + 1]))
+            assert gaps.min() < 1e-5, (t, ridx[t], idx[t])
+        else:
+            np.testing.assert_allclose(w[t], rw[t], rtol=1e-5, atol=1e-7)
+
+
+@pytest.fixture(scope="module")
+def qwen16(gpu):
+    L = synth.qwen_layer(seed=1, n_experts=16)
+    return L, ResidentLayer(L, max_tokens=8, lib=gpu)
+
+
+@pytest.mark.parametrize("T", [1, 3, 8])
+def test_layer_matches_reference_pipeline(gpu, oracle, qwen16, T):
+    L, R = qwen16
+    rng = np.random.default_rng(200 + T)
+    N = synth.rms_norm(rng.standard_normal((T, 2048)).astype(np.float32))
+    got = R.forward(N, normalize=False)          # route N as given, like the engine
+    idx, w = R.last_routing(T)
+    routing_agrees(L, N, idx, w)
+    want = M.moe_layer_forward(oracle, L, N)
+    assert rel_err(got, want) <= TOL
+
+
+def test_layer_rmsnorm_in_kernel(gpu, oracle, qwen16):
+    L, R = qwen16
+    x = np.random.default_rng(9).standard_normal((2, 2048)).astype(np.float32) * 3
+    got = R.forward(x, normalize=True)
+    want = M.moe_layer_forward(oracle, L, synth.rms_norm(x))
+    assert rel_err(got, want) <= TOL
+
+
+def test_layer_zipf_bias_and_clone(gpu, oracle):
+    L = synth.qwen_layer(seed=2, n_experts=16, router_bias=synth.zipf_bias(seed=2, n_experts=16))
+    R = ResidentLayer(L, max_tokens=4, lib=gpu)
+    C = R.clone()
+    N = synth.rms_norm(np.random.default_rng(3).standard_normal((4, 2048)).astype(np.float32))
+    a = R.forward(N, normalize=False)
+    b = C.forward(N, normalize=False)
+    assert np.array_equal(a, b)
+    want = M.moe_layer_forward(oracle, L, N)
+    assert rel_err(a, want) <= TOL
+    C.close()
+    R.close()
+
+
+def test_layer_gptoss_top4(gpu, oracle):
+    L = synth.gptoss_layer(seed=3, n_experts=8)
+    R = ResidentLayer(L, max_tokens=2, lib=gpu)
+    N = synth.rms_norm(np.random.default_rng(5).standard_normal((2, 2880)).astype(np.float32))
+    got = R.forward(N, normalize=False)
+    want = M.moe_layer_forward(oracle, L, N)
+    assert rel_err(got, want) <= TOL
+    R.close()
+
+
+def test_layer_shards_sum_to_whole(gpu, qwen16):
+    """Expert-parallel shards: the parts of 4 shards add up to the whole layer."""
+    L, R = qwen16
+    N = synth.rms_norm(np.random.default_rng(6).standard_normal((3, 2048)).astype(np.float32))
+    whole = R.forward(N, normalize=False)
+    parts = [ResidentLayer(L, max_tokens=8, lib=gpu, shard=s, n_shards=4) for s in range(4)]
+    total = sum(p.forward(N, normalize=False).astype(np.float64) for p in parts)
+    assert rel_err(total, whole) <= 1e-6 * 10
+    for p in parts:
+        p.close()
+
+
+def test_stack_forward_and_graph_replay(gpu, oracle):
+    torch = pytest.importorskip("torch")
+    layers = [synth.qwen_layer(seed=4, layer=l, n_experts=12) for l in range(3)]
+    res = [ResidentLayer(L, max_tokens=1, lib=gpu) for L in layers]
+    x0 = np.random.default_rng(4).standard_normal((1, 2048)).astype(np.float32)
+    # reference: x += moe(rmsnorm(x)) per layer, engine order
+    want = x0.copy()
+    for L in layers:
+        want = want + M.moe_layer_forward(oracle, L, synth.rms_norm(want))
+    stream = torch.cuda.Stream()
+    gpu.tg_cuda_set_stream(ctypes.c_void_p(stream.cuda_stream))
+    try:
+        hs = (ctypes.c_void_p * 3)(*[r.h for r in res])
+        x = torch.from_numpy(x0.copy()).cuda()
+        with torch.cuda.stream(stream):
+            assert gpu.tg_stack_forward_dev(hs, 3, ctypes.c_void_p(x.data_ptr()), 1, None) == 0
+        torch.cuda.synchronize()
+        tg.check(gpu)
+        got = x.cpu().numpy()
+        assert rel_err(got, want) <= TOL
+        # the same stack captured in a graph and replayed
+        x2 = torch.from_numpy(x0.copy()).cuda()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            gpu.tg_stack_forward_dev(hs, 3, ctypes.c_void_p(x2.data_ptr()), 1, None)
+        x2.copy_(torch.from_numpy(x0))
+        with torch.cuda.stream(stream):
+            g.replay()
+        torch.cuda.synchronize()
+        tg.check(gpu)
+        assert np.array_equal(x2.cpu().numpy(), got)
+        del g
+    finally:
+        gpu.tg_cuda_set_stream(None)
+        for r in res:
+            r.close()

@@ -40,6 +40,12 @@ ABI = {
                               CI, CI, CI, CI, CI, CI], None),
 }
 
+# Exported by the reference's C library but not registered by its loader;
+# bound here so Python callers get checked pointer arguments.
+EXTRA_ABI = {
+    "tg_moe_forward": ([VP, VP, CI, VP, VP, CI, CI], None),
+}
+
 # Extensions of this library (include/tinygiant.h).
 EXT = {
     "tg_cuda_last_error": ([ctypes.c_char_p, SZ], CI),
@@ -53,6 +59,21 @@ EXT = {
     "tg_cuda_device_count": ([], CI),
     "tg_cuda_debug_quantize_q8": ([VP, CI, CI, VP], CI),
     "tg_cuda_debug_row_isums": ([CI, VP, CI, CI, VP, VP], CI),
+    "tg_layer_create": ([CI, VP, VP, VP, CI, VP, VP, VP, VP, CI, CI, CI, VP, VP, CI, CI], VP),
+    "tg_layer_create_shard": ([CI, VP, VP, VP, CI, VP, VP, VP, VP, CI, CI, CI, VP, VP, CI, CI, CI, CI], VP),
+    "tg_layer_clone": ([VP], VP),
+    "tg_layer_destroy": ([VP], None),
+    "tg_layer_expert_bytes": ([VP, CI], SZ),
+    "tg_layer_forward_dev": ([VP, VP, VP, VP, VP, CI, CI, VP], CI),
+    "tg_layer_forward": ([VP, VP, VP, CI, CI], CI),
+    "tg_layer_last_routing": ([VP, CI, VP, VP], CI),
+    "tg_stack_forward_dev": ([VP, CI, VP, CI, VP], CI),
+    "tg_cuda_graph_begin": ([], CI),
+    "tg_cuda_graph_end": ([], VP),
+    "tg_cuda_graph_launch": ([VP], CI),
+    "tg_cuda_graph_destroy": ([VP], None),
+    "tg_cuda_stream": ([], VP),
+    "tg_cuda_synchronize": ([], CI),
     "tg_pack_q4k": ([VP, CI, CI, VP], None),
     "tg_pack_q6k": ([VP, CI, CI, VP], None),
 }
@@ -88,5 +109,6 @@ def load_tinygiant_lib(lib_path=None):
         return None
     lib = ctypes.CDLL(str(lib_path))
     _bind(lib, ABI)
+    _bind(lib, EXTRA_ABI, optional=True)
     _bind(lib, EXT, optional=True)
     return lib

@@ -115,6 +115,25 @@ __device__ __forceinline__ float act_fn(int act, float g, float u) {
   return fmul(__fdiv_rn(g, den), u);
 }
 
+// Raises a kernel's dynamic shared-memory limit only when a launch needs more
+// than was set before, so launches during CUDA-graph capture make no
+// attribute calls after the first (uncaptured) use.
+inline cudaError_t ensure_smem(const void* fn, size_t bytes) {
+  struct Entry { const void* fn; size_t bytes; };
+  static Entry table[32];
+  static int n = 0;
+  for (int i = 0; i < n; i++)
+    if (table[i].fn == fn) {
+      if (table[i].bytes >= bytes) return cudaSuccess;
+      cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+      if (e == cudaSuccess) table[i].bytes = bytes;
+      return e;
+    }
+  cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+  if (e == cudaSuccess && n < 32) table[n++] = Entry{fn, bytes};
+  return e;
+}
+
 // ---------------------------------------------------------------------
 // Device error status.  Kernels never trap: on a bad descriptor or a wait
 // that runs out they record a code here and return; the host reads it after

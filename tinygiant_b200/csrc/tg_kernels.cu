@@ -1,8 +1,7 @@
-// tg_kernels.cu — CUDA kernels of the fused quantized expert path (sm_100a).
+// tg_kernels.cu — matvec, quantizer and utility kernels (sm_100a); the MoE
+// expert phases are in tg_moe.cu and the fused router in tg_route.cu.
 //
 //   quantize_rows_kernel   fp32 rows -> Q8 blocks      (csrc/libtinygiant.c:169-208)
-//   moe_gateup_kernel      gate.x, up.x, act -> hidden (moe_phase_a, 1279-1327)
-//   moe_down_kernel        down.h * w (+bias), combine (moe_phase_b + 1428-1434)
 //   matvec_kernel          one matrix . one input      (mm_task / gmm_task, 345-364, 906-931)
 //   f16/f32 matvec, rms_norm, repack
 //
@@ -14,182 +13,21 @@
 #include "tg_dots.cuh"
 #include "tg_kernels.h"
 #include "tg_plan.cuh"
+#include "tg_q8.cuh"
 
 namespace tg {
 
 // ---------------------------------------------------------------------
 // Q8 quantizer: one CTA of 256 threads per 256-block.
 
-__device__ __forceinline__ float max_nan(float a, float b) {
-  if (a != a) return a;
-  if (b != b) return b;
-  return a > b ? a : b;
-}
-
 __global__ void __launch_bounds__(256) quantize_rows_kernel(const float* __restrict__ x, int ncols, long ldx,
                                                             Q8Dev* __restrict__ out, int nb) {
-  __shared__ float wmax[8];
-  __shared__ int wsum[8];
-  const int b = blockIdx.x, row = blockIdx.y, t = threadIdx.x, lane = t & 31, w = t >> 5;
+  __shared__ Q8Scratch sh;
+  const int b = blockIdx.x, row = blockIdx.y, t = threadIdx.x;
   const int n = min(QK, ncols - b * QK);
-  const float v = t < n ? x[(size_t)row * ldx + (size_t)b * QK + t] : 0.f;
-  float a = t < n ? fabsf(v) : 0.f;
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) a = max_nan(a, __shfl_xor_sync(0xffffffffu, a, o));
-  if (lane == 0) wmax[w] = a;
-  __syncthreads();
-  float amax = wmax[0];
-#pragma unroll
-  for (int i = 1; i < 8; i++) amax = max_nan(amax, wmax[i]);
-  const float sc = __fdiv_rn(amax, 127.f);
-  const float inv = amax > 0.f ? __fdiv_rn(127.f, amax) : 0.f;
-  int q = 0;
-  if (t < n) {
-    float s = __fmul_rn(v, inv);
-    q = (s != s) ? 0 : __float2int_rn(s);
-  }
-  int bs = q;
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) bs += __shfl_xor_sync(0xffffffffu, bs, o);
-  Q8Dev* o = out + (size_t)row * nb + b;
-  o->qs[t] = (int8_t)q;
-  if (lane == 0) {
-    wsum[w] = bs;
-    o->bsums[w] = bs;
-  }
-  __syncthreads();
-  if (t == 0) {
-    int total = 0;
-#pragma unroll
-    for (int i = 0; i < 8; i++) total += wsum[i];
-    o->scale = sc;
-    o->sum = total;
-  }
-}
-
-// ---------------------------------------------------------------------
-// Phase A: CTA = (tile of R rows of I, slot).  For each group of <= 4 active
-// rows: every (matrix, row, term) unit computes its outer terms, one thread
-// per (matrix, row, token) folds them in order, then gate/up biases and the
-// activation produce hidden[active row][r].
-
-template <int R>
-__global__ void __launch_bounds__(256) moe_gateup_kernel(MoePlan plan, const Q8Dev* __restrict__ xq8, int gbpr,
-                                                         float* __restrict__ hidden, DevStatus* st) {
-  extern __shared__ float smem[];
-  const int s = blockIdx.y;
-  const SlotDesc S = plan.slots[s];
-  const int I = plan.inter_dim, D = plan.embed_dim;
-  const int r0 = blockIdx.x * R;
-  if (r0 >= I || S.n_rows == 0) return;
-  const int nr = min(R, I - r0);
-  const int fmt = S.gate.fmt;
-  if (fmt == FMT_F16 || fmt < 0 || fmt > FMT_Q80 || S.up.fmt != fmt) {
-    if (threadIdx.x == 0) set_error(st, ERR_BAD_FORMAT, 1, fmt, s);
-    return;
-  }
-  const int P = terms_per_row(fmt, D);
-  float* terms = smem;                 // [2][R][4][P]
-  float* tot = terms + 2 * R * 4 * P;  // [2][R][4]
-  for (int g0 = 0; g0 < S.n_rows; g0 += 4) {
-    const int ng = min(4, S.n_rows - g0);
-    const bool x4 = use_x4(plan.assoc_rule, g0, S.n_rows, plan.k);
-    const Q8Dev* xrow[4];
-    for (int j = 0; j < 4; j++) xrow[j] = xq8 + (size_t)plan.rows[S.row_off + g0 + min(j, ng - 1)] * gbpr;
-    const int nunits = 2 * nr * P;
-    for (int u = threadIdx.x; u < nunits; u += blockDim.x) {
-      const int m = u / (nr * P), rem = u - m * nr * P, rho = rem / P, p = rem - rho * P;
-      float o[4];
-      row_terms(m ? S.up : S.gate, r0 + rho, p, xrow, ng, x4, o);
-      for (int j = 0; j < ng; j++) terms[((m * R + rho) * 4 + j) * P + p] = o[j];
-    }
-    __syncthreads();
-    for (int f = threadIdx.x; f < 2 * nr * ng; f += blockDim.x) {
-      const int m = f / (nr * ng), rem = f - m * nr * ng, rho = rem / ng, j = rem - rho * ng;
-      const float* tp = terms + ((m * R + rho) * 4 + j) * P;
-      float acc = 0.f;
-      for (int p = 0; p < P; p++) acc = fadd(acc, tp[p]);
-      tot[(m * R + rho) * 4 + j] = acc;
-    }
-    __syncthreads();
-    for (int f = threadIdx.x; f < nr * ng; f += blockDim.x) {
-      const int rho = f / ng, j = f - rho * ng, r = r0 + rho;
-      float gv = tot[(0 * R + rho) * 4 + j], uv = tot[(1 * R + rho) * 4 + j];
-      if (S.gb) {
-        gv = fadd(gv, S.gb[r]);
-        uv = fadd(uv, S.ub[r]);
-      }
-      hidden[(size_t)(S.row_off + g0 + j) * I + r] = act_fn(plan.act, gv, uv);
-    }
-    __syncthreads();
-  }
-}
-
-// ---------------------------------------------------------------------
-// Phase B: CTA = R consecutive output rows of D, all active (slot, row)
-// pairs.  Chunks of CH active rows: unit terms, per-(active row, row) fold,
-// part = w * (v + bias), then the combine adds parts into the output in the
-// flat active-row order, which is the reference's expert order.
-
-template <int R, int CH>
-__global__ void __launch_bounds__(256) moe_down_kernel(MoePlan plan, const int* __restrict__ row_slot,
-                                                       const Q8Dev* __restrict__ hq8, int dbpr,
-                                                       const float* __restrict__ hidden, float* __restrict__ out,
-                                                       DevStatus* st) {
-  extern __shared__ float smem[];
-  const int D = plan.embed_dim, I = plan.inter_dim;
-  const int r0 = blockIdx.x * R;
-  if (r0 >= D) return;
-  const int nr = min(R, D - r0);
-  const int Pmax = I / 32;
-  float* terms = smem;                // [CH][R][Pmax]
-  float* parts = terms + CH * R * Pmax;  // [CH][R]
-  for (int c0 = 0; c0 < plan.total_rows; c0 += CH) {
-    const int nch = min(CH, plan.total_rows - c0);
-    const int nunits = nch * nr * Pmax;
-    for (int u = threadIdx.x; u < nunits; u += blockDim.x) {
-      const int i = u / (nr * Pmax), rem = u - i * nr * Pmax, rho = rem / Pmax, p = rem - rho * Pmax;
-      const int sr = c0 + i;
-      const SlotDesc& S = plan.slots[row_slot[sr]];
-      const int fmt = S.down.fmt;
-      if (fmt == FMT_F16 || p >= terms_per_row(fmt, I)) continue;
-      const bool x4 = use_x4(plan.assoc_rule, sr - S.row_off, S.n_rows, plan.k);
-      const Q8Dev* xrow[1] = {hq8 + (size_t)sr * dbpr};
-      float o[1];
-      if (!row_terms(S.down, r0 + rho, p, xrow, 1, x4, o)) {
-        set_error(st, ERR_BAD_FORMAT, 2, fmt, row_slot[sr]);
-        o[0] = 0.f;
-      }
-      terms[(i * R + rho) * Pmax + p] = o[0];
-    }
-    __syncthreads();
-    for (int f = threadIdx.x; f < nch * nr; f += blockDim.x) {
-      const int i = f / nr, rho = f - i * nr, sr = c0 + i, r = r0 + rho;
-      const SlotDesc& S = plan.slots[row_slot[sr]];
-      float v;
-      if (S.down.fmt == FMT_F16) {
-        v = dot_f16_row(reinterpret_cast<const uint16_t*>(S.down.main) + (size_t)r * I, hidden + (size_t)sr * I, I);
-      } else {
-        const int P = terms_per_row(S.down.fmt, I);
-        const float* tp = terms + (i * R + rho) * Pmax;
-        v = 0.f;
-        for (int p = 0; p < P; p++) v = fadd(v, tp[p]);
-      }
-      const float w = plan.wts[sr];
-      float part;
-      if (plan.bias_term) part = fmul(w, fadd(v, S.db ? S.db[r] : 0.f));
-      else part = fmul(w, v);
-      parts[i * R + rho] = part;
-    }
-    __syncthreads();
-    for (int rho = threadIdx.x; rho < nr; rho += blockDim.x) {
-      for (int i = 0; i < nch; i++) {
-        float* o = out + (size_t)plan.rows[c0 + i] * D + r0 + rho;
-        *o = fadd(*o, parts[i * R + rho]);
-      }
-    }
-    __syncthreads();
-  }
+  const bool valid = t < n;
+  const float v = valid ? x[(size_t)row * ldx + (size_t)b * QK + t] : 0.f;
+  quantize_block_cta(v, valid, out + (size_t)row * nb + b, sh);
 }
 
 // ---------------------------------------------------------------------
@@ -285,6 +123,11 @@ __global__ void rms_norm_kernel(const float* __restrict__ x, const float* __rest
   for (int i = t; i < dim; i += blockDim.x) out[i] = fmul(fmul(x[i], sc), w[i]);
 }
 
+__global__ void add_kernel(const float* __restrict__ a, const float* __restrict__ b, float* out, size_t n) {
+  const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) out[i] = fadd(a[i], b[i]);
+}
+
 // Raw reference blocks -> HBM layout (tg_common.cuh WDesc).
 __global__ void repack_kernel(const uint8_t* __restrict__ raw, int fmt, long nblocks, uint8_t* __restrict__ mainp,
                               uint8_t* __restrict__ aux1, uint8_t* __restrict__ aux2) {
@@ -343,9 +186,6 @@ __global__ void debug_isums_kernel(WDesc W, const Q8Dev* __restrict__ xq, int32_
 // ---------------------------------------------------------------------
 // Launchers.
 
-static constexpr int GU_R = 16;
-static constexpr int DN_R = 16;
-static constexpr int DN_CH = 8;
 static constexpr int MV_R = 32;
 
 void launch_quantize_rows(const float* x, int nrows, int ncols, long ldx, Q8Dev* out, cudaStream_t s) {
@@ -354,41 +194,12 @@ void launch_quantize_rows(const float* x, int nrows, int ncols, long ldx, Q8Dev*
   quantize_rows_kernel<<<dim3(nb, nrows), 256, 0, s>>>(x, ncols, ldx, out, nb);
 }
 
-size_t gateup_smem_bytes(int gate_fmt, int D) {
-  const int P = terms_per_row(gate_fmt, D);
-  return sizeof(float) * (size_t)(2 * GU_R * 4 * P + 2 * GU_R * 4);
-}
-
-cudaError_t launch_moe_gateup(const MoePlan& plan, int gate_fmt, const Q8Dev* xq8, int gbpr, float* hidden,
-                              DevStatus* st, cudaStream_t s) {
-  if (plan.n_slots == 0) return cudaSuccess;
-  const size_t smem = gateup_smem_bytes(gate_fmt, plan.embed_dim);
-  auto k = moe_gateup_kernel<GU_R>;
-  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  if (e != cudaSuccess) return e;
-  dim3 grid((plan.inter_dim + GU_R - 1) / GU_R, plan.n_slots);
-  k<<<grid, 256, smem, s>>>(plan, xq8, gbpr, hidden, st);
-  return cudaGetLastError();
-}
-
-cudaError_t launch_moe_down(const MoePlan& plan, const int* row_slot, const Q8Dev* hq8, int dbpr, const float* hidden,
-                            float* out, DevStatus* st, cudaStream_t s) {
-  if (plan.total_rows == 0) return cudaSuccess;
-  const int Pmax = plan.inter_dim / 32;
-  const size_t smem = sizeof(float) * (size_t)(DN_CH * DN_R * Pmax + DN_CH * DN_R);
-  auto k = moe_down_kernel<DN_R, DN_CH>;
-  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  if (e != cudaSuccess) return e;
-  k<<<(plan.embed_dim + DN_R - 1) / DN_R, 256, smem, s>>>(plan, row_slot, hq8, dbpr, hidden, out, st);
-  return cudaGetLastError();
-}
-
 cudaError_t launch_matvec(const WDesc& W, const Q8Dev* xq8, const float* x, const float* bias, int bias_term,
                           float* out, DevStatus* st, cudaStream_t s) {
   const int P = W.fmt == FMT_F16 ? 1 : terms_per_row(W.fmt, W.cols);
   const size_t smem = sizeof(float) * (size_t)MV_R * P;
   auto k = matvec_kernel<MV_R>;
-  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  cudaError_t e = ensure_smem(reinterpret_cast<const void*>(k), smem);
   if (e != cudaSuccess) return e;
   k<<<(W.rows + MV_R - 1) / MV_R, 256, smem, s>>>(W, xq8, x, bias, bias_term, out, st);
   return cudaGetLastError();
@@ -400,6 +211,10 @@ void launch_f32_matvec(const float* A, const float* x, float* out, int nrows, in
 
 void launch_f16_matvec(const uint16_t* A, const float* x, float* out, int nrows, int ncols, cudaStream_t s) {
   f16_matvec_kernel<<<(nrows + 127) / 128, 128, 0, s>>>(A, x, out, nrows, ncols);
+}
+
+void launch_add(const float* a, const float* b, float* out, size_t n, cudaStream_t s) {
+  if (n) add_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(a, b, out, n);
 }
 
 void launch_rms_norm(const float* x, const float* w, float* out, int dim, float eps, cudaStream_t s) {

@@ -7,15 +7,11 @@
 namespace tg {
 
 void launch_quantize_rows(const float* x, int nrows, int ncols, long ldx, Q8Dev* out, cudaStream_t s);
-size_t gateup_smem_bytes(int gate_fmt, int D);
-cudaError_t launch_moe_gateup(const MoePlan& plan, int gate_fmt, const Q8Dev* xq8, int gbpr, float* hidden,
-                              DevStatus* st, cudaStream_t s);
-cudaError_t launch_moe_down(const MoePlan& plan, const int* row_slot, const Q8Dev* hq8, int dbpr, const float* hidden,
-                            float* out, DevStatus* st, cudaStream_t s);
 cudaError_t launch_matvec(const WDesc& W, const Q8Dev* xq8, const float* x, const float* bias, int bias_term,
                           float* out, DevStatus* st, cudaStream_t s);
 void launch_f32_matvec(const float* A, const float* x, float* out, int nrows, int ncols, cudaStream_t s);
 void launch_f16_matvec(const uint16_t* A, const float* x, float* out, int nrows, int ncols, cudaStream_t s);
+void launch_add(const float* a, const float* b, float* out, size_t n, cudaStream_t s);
 void launch_rms_norm(const float* x, const float* w, float* out, int dim, float eps, cudaStream_t s);
 int debug_isums_per_row(int fmt, int cols);
 void launch_debug_isums(const WDesc& W, const Q8Dev* xq, int32_t* out, cudaStream_t s);

@@ -1,0 +1,415 @@
+// tg_layer.cu — HBM-resident MoE layers and stacks, routed on the GPU.
+//
+// The reference engine keeps experts on disk / in the page cache and routes
+// in numpy before every MoE call (tinygiant/engine.py:281-342).  Here a
+// layer's experts, router and scratch live in HBM; one layer step is three
+// kernels on one stream (fused norm + router + plan build, gate/up +
+// activation + Q8, down + combine) with no host round trip, so steps and
+// whole stacks can be captured in a CUDA graph.  Expert weights come from the
+// same registry as the reference-ABI calls (uploaded once, repacked).
+#include <cstring>
+#include <vector>
+
+#include "../../include/tinygiant.h"
+#include "tg_kernels.h"
+#include "tg_moe.h"
+#include "tg_runtime.h"
+
+namespace tg {
+
+struct Layer {
+  int E = 0, D = 0, I = 0, gate_fmt = 0, act = 0, top_k = 0, max_tokens = 0;
+  int max_slots = 0, max_rows = 0;
+  std::vector<ExpertDesc> experts;  // host copy of the device table
+  std::vector<void*> owned;         // device allocations to free
+  ExpertDesc* d_experts = nullptr;
+  float* router_w = nullptr;
+  float* router_b = nullptr;
+  // scratch
+  Q8Dev* xq8 = nullptr;
+  float* logits = nullptr;
+  int* counter = nullptr;
+  PlanHdr* plan = nullptr;
+  SlotDesc* slots = nullptr;
+  int* rows = nullptr;
+  float* wts = nullptr;
+  int* row_slot = nullptr;
+  int* sel_idx = nullptr;
+  float* sel_w = nullptr;
+  float* hidden = nullptr;
+  Q8Dev* hq8 = nullptr;
+  int* counters = nullptr;
+  float* moe_out = nullptr;  // [2][max_tokens][D] for stacks and the host entry
+  float* xbuf = nullptr;     // [max_tokens][D]
+};
+
+static bool dmalloc(Layer* L, void** p, size_t n) {
+  n = (n + 255) & ~(size_t)255;
+  if (cudaMalloc(p, n) != cudaSuccess) {
+    cudaGetLastError();
+    set_host_error(101, "cudaMalloc(%zu bytes) failed for a layer", n);
+    return false;
+  }
+  L->owned.push_back(*p);
+  return cudaMemset(*p, 0, n) == cudaSuccess;
+}
+
+static bool alloc_scratch(Layer* L) {
+  const int T = L->max_tokens, D = L->D, I = L->I, E = L->E;
+  const int gbpr = (D + QK - 1) / QK, dbpr = (I + QK - 1) / QK;
+  L->max_rows = T * L->top_k;
+  L->max_slots = std::min(E, L->max_rows);
+  return dmalloc(L, (void**)&L->xq8, sizeof(Q8Dev) * (size_t)T * gbpr) &&
+         dmalloc(L, (void**)&L->logits, sizeof(float) * (size_t)T * E) &&
+         dmalloc(L, (void**)&L->counter, sizeof(int)) && dmalloc(L, (void**)&L->plan, sizeof(PlanHdr)) &&
+         dmalloc(L, (void**)&L->slots, sizeof(SlotDesc) * (size_t)L->max_slots) &&
+         dmalloc(L, (void**)&L->rows, sizeof(int) * (size_t)L->max_rows) &&
+         dmalloc(L, (void**)&L->wts, sizeof(float) * (size_t)L->max_rows) &&
+         dmalloc(L, (void**)&L->row_slot, sizeof(int) * (size_t)L->max_rows) &&
+         dmalloc(L, (void**)&L->sel_idx, sizeof(int) * (size_t)L->max_rows) &&
+         dmalloc(L, (void**)&L->sel_w, sizeof(float) * (size_t)L->max_rows) &&
+         dmalloc(L, (void**)&L->hidden, sizeof(float) * (size_t)L->max_rows * I) &&
+         dmalloc(L, (void**)&L->hq8, sizeof(Q8Dev) * (size_t)L->max_rows * dbpr) &&
+         dmalloc(L, (void**)&L->counters, sizeof(int) * moe_counter_ints(L->max_slots, I)) &&
+         dmalloc(L, (void**)&L->moe_out, sizeof(float) * 2 * (size_t)T * D) &&
+         dmalloc(L, (void**)&L->xbuf, sizeof(float) * (size_t)T * D);
+}
+
+static void free_layer(Layer* L) {
+  for (void* p : L->owned) cudaFree(p);
+  delete L;
+}
+
+// Enqueues one layer step: x' = x + add (if add), N = rmsnorm(x') or x',
+// moe_out = 0, moe_out += experts(N); x_out = x' (if x_out).
+static bool layer_enqueue(Layer* L, const float* x, const float* add, float* x_out, float* moe_out, int T,
+                          int normalize, const float* norm_w, cudaStream_t s, const char* what) {
+  if (T < 1 || T > L->max_tokens) {
+    set_host_error(3, "%s: %d rows exceed the layer's max_tokens %d", what, T, L->max_tokens);
+    return false;
+  }
+  RouteArgs a{};
+  a.x_in = x;
+  a.add_in = add;
+  a.x_out = x_out;
+  a.zero_out = moe_out;
+  a.norm_w = norm_w;
+  a.eps = 1e-6f;
+  a.normalize = normalize;
+  a.router_w = L->router_w;
+  a.router_b = L->router_b;
+  a.T = T;
+  a.D = L->D;
+  a.E = L->E;
+  a.top_k = L->top_k;
+  a.I = L->I;
+  a.act = L->act;
+  a.assoc_rule = ASSOC_MOE;
+  a.bias_term = 1;
+  a.experts = L->d_experts;
+  a.xq8 = L->xq8;
+  a.logits = L->logits;
+  a.counter = L->counter;
+  a.plan = L->plan;
+  a.slots = L->slots;
+  a.rows = L->rows;
+  a.wts = L->wts;
+  a.row_slot = L->row_slot;
+  a.sel_idx = L->sel_idx;
+  a.sel_w = L->sel_w;
+  cudaError_t e = launch_layer_route(a, s);
+  if (e == cudaSuccess)
+    e = launch_moe_gateup(L->plan, std::min(L->max_slots, T * L->top_k), L->gate_fmt, L->D, L->I, L->xq8, L->hidden,
+                          L->hq8, L->counters, status_ptr(), s);
+  if (e == cudaSuccess) e = launch_moe_down(L->plan, L->D, L->I, L->hq8, L->hidden, moe_out, status_ptr(), s);
+  count_launches(3);
+  if (e != cudaSuccess) {
+    set_host_error(100 + (int)e, "%s: %s", what, cudaGetErrorString(e));
+    return false;
+  }
+  return true;
+}
+
+}  // namespace tg
+
+using namespace tg;
+
+extern "C" {
+
+// Expert-parallel shard: this GPU holds experts e with e % n_shards == shard
+// (the router is replicated); a step computes only the local experts' part.
+void* tg_layer_create_shard(int n_experts, const uint8_t* const* gate_ptrs, const uint8_t* const* up_ptrs,
+                            const void* const* down_ptrs, int gate_fmt, const int* down_fmts,
+                            const float* const* gate_bias, const float* const* up_bias, const float* const* down_bias,
+                            int act, int embed_dim, int inter_dim, const float* router_w, const float* router_b,
+                            int top_k, int max_tokens, int shard, int n_shards) {
+  std::lock_guard<std::recursive_mutex> lk(ctx_mutex());
+  const char* what = "tg_layer_create";
+  if (n_shards < 1 || shard < 0 || shard >= n_shards) {
+    set_host_error(3, "%s: shard %d of %d", what, shard, n_shards);
+    return nullptr;
+  }
+  if (n_experts < 1 || top_k < 1 || top_k > 8 || top_k > n_experts || max_tokens < 1 || !router_w) {
+    set_host_error(3, "%s: bad arguments (n_experts %d, top_k %d in 1..8, max_tokens %d, router %p)", what, n_experts,
+                   top_k, max_tokens, (const void*)router_w);
+    return nullptr;
+  }
+  if (!(gate_fmt == FMT_Q4K || gate_fmt == FMT_Q6K || gate_fmt == FMT_MXFP4 || gate_fmt == FMT_Q80)) {
+    set_host_error(4, "%s: gate format %d is not supported", what, gate_fmt);
+    return nullptr;
+  }
+  if (gate_bias && !up_bias) {
+    set_host_error(4, "%s: gate_bias given without up_bias", what);
+    return nullptr;
+  }
+  if (!ensure_init()) return nullptr;
+  Layer* L = new Layer;
+  L->E = n_experts;
+  L->D = embed_dim;
+  L->I = inter_dim;
+  L->gate_fmt = gate_fmt;
+  L->act = act == ACT_GPTOSS ? ACT_GPTOSS : ACT_SILU;
+  L->top_k = top_k;
+  L->max_tokens = max_tokens;
+  L->experts.resize(n_experts);
+  for (int e = 0; e < n_experts; e++) {
+    ExpertDesc& X = L->experts[e];
+    memset(&X, 0, sizeof X);
+    if (e % n_shards != shard) continue;   // held by another GPU
+    if (!lookup_matrix(gate_ptrs[e], gate_fmt, inter_dim, embed_dim, &X.gate) ||
+        !lookup_matrix(up_ptrs[e], gate_fmt, inter_dim, embed_dim, &X.up) ||
+        !lookup_matrix(down_ptrs[e], down_fmts[e], embed_dim, inter_dim, &X.down)) {
+      free_layer(L);
+      return nullptr;
+    }
+    if (gate_bias) {
+      X.gb = lookup_vector(gate_bias[e], inter_dim);
+      X.ub = lookup_vector(up_bias[e], inter_dim);
+    }
+    if (down_bias) X.db = lookup_vector(down_bias[e], embed_dim);
+  }
+  const size_t rw = sizeof(float) * (size_t)n_experts * embed_dim;
+  if (!dmalloc(L, (void**)&L->d_experts, sizeof(ExpertDesc) * n_experts) ||
+      !dmalloc(L, (void**)&L->router_w, rw) || (router_b && !dmalloc(L, (void**)&L->router_b, sizeof(float) * n_experts)) ||
+      !alloc_scratch(L)) {
+    free_layer(L);
+    return nullptr;
+  }
+  cudaMemcpy(L->d_experts, L->experts.data(), sizeof(ExpertDesc) * n_experts, cudaMemcpyHostToDevice);
+  cudaMemcpy(L->router_w, router_w, rw, cudaMemcpyHostToDevice);
+  if (router_b) cudaMemcpy(L->router_b, router_b, sizeof(float) * n_experts, cudaMemcpyHostToDevice);
+  if (cudaGetLastError() != cudaSuccess) {
+    set_host_error(100, "%s: upload failed", what);
+    free_layer(L);
+    return nullptr;
+  }
+  return L;
+}
+
+void* tg_layer_create(int n_experts, const uint8_t* const* gate_ptrs, const uint8_t* const* up_ptrs,
+                      const void* const* down_ptrs, int gate_fmt, const int* down_fmts, const float* const* gate_bias,
+                      const float* const* up_bias, const float* const* down_bias, int act, int embed_dim,
+                      int inter_dim, const float* router_w, const float* router_b, int top_k, int max_tokens) {
+  return tg_layer_create_shard(n_experts, gate_ptrs, up_ptrs, down_ptrs, gate_fmt, down_fmts, gate_bias, up_bias,
+                               down_bias, act, embed_dim, inter_dim, router_w, router_b, top_k, max_tokens, 0, 1);
+}
+
+// A second resident copy of a layer: every expert weight byte and the router
+// are copied to fresh HBM (used to measure with working sets beyond L2).
+void* tg_layer_clone(void* handle) {
+  std::lock_guard<std::recursive_mutex> lk(ctx_mutex());
+  Layer* src = (Layer*)handle;
+  if (!src) return nullptr;
+  Layer* L = new Layer;
+  L->E = src->E;
+  L->D = src->D;
+  L->I = src->I;
+  L->gate_fmt = src->gate_fmt;
+  L->act = src->act;
+  L->top_k = src->top_k;
+  L->max_tokens = src->max_tokens;
+  L->experts = src->experts;
+  auto copy_w = [&](WDesc& w) -> bool {
+    if (!w.main) return true;   // expert held by another GPU
+    const uint8_t* srcs[3] = {w.main, w.aux1, w.aux2};
+    const size_t nblk = w.fmt == FMT_Q6K ? (size_t)w.rows * (w.cols / QK) : (size_t)w.rows * (w.cols / 32);
+    size_t sizes[3] = {0, 0, 0};
+    switch (w.fmt) {
+      case FMT_Q4K: sizes[0] = (size_t)w.rows * host_row_bytes(FMT_Q4K, w.cols); break;
+      case FMT_Q6K: sizes[0] = nblk * 192; sizes[1] = nblk * 16; sizes[2] = nblk * 2; break;
+      case FMT_MXFP4: sizes[0] = nblk * 16; sizes[1] = nblk; break;
+      case FMT_Q80: sizes[0] = nblk * 32; sizes[2] = nblk * 2; break;
+      default: sizes[0] = (size_t)w.rows * w.cols * 2; break;
+    }
+    const uint8_t** dst[3] = {&w.main, &w.aux1, &w.aux2};
+    for (int i = 0; i < 3; i++) {
+      if (!sizes[i]) continue;
+      void* p = nullptr;
+      if (!dmalloc(L, &p, sizes[i] + 64)) return false;
+      if (cudaMemcpy(p, srcs[i], sizes[i], cudaMemcpyDeviceToDevice) != cudaSuccess) return false;
+      *dst[i] = (const uint8_t*)p;
+    }
+    return true;
+  };
+  for (auto& X : L->experts)
+    if (!copy_w(X.gate) || !copy_w(X.up) || !copy_w(X.down)) {
+      free_layer(L);
+      return nullptr;
+    }
+  const size_t rw = sizeof(float) * (size_t)L->E * L->D;
+  if (!dmalloc(L, (void**)&L->d_experts, sizeof(ExpertDesc) * L->E) || !dmalloc(L, (void**)&L->router_w, rw) ||
+      (src->router_b && !dmalloc(L, (void**)&L->router_b, sizeof(float) * L->E)) || !alloc_scratch(L)) {
+    free_layer(L);
+    return nullptr;
+  }
+  cudaMemcpy(L->d_experts, L->experts.data(), sizeof(ExpertDesc) * L->E, cudaMemcpyHostToDevice);
+  cudaMemcpy(L->router_w, src->router_w, rw, cudaMemcpyDeviceToDevice);
+  if (src->router_b) cudaMemcpy(L->router_b, src->router_b, sizeof(float) * L->E, cudaMemcpyDeviceToDevice);
+  return L;
+}
+
+void tg_layer_destroy(void* handle) {
+  std::lock_guard<std::recursive_mutex> lk(ctx_mutex());
+  if (!handle) return;
+  cudaStreamSynchronize(stream());
+  free_layer((Layer*)handle);
+}
+
+// Bytes of expert weights of one expert of the layer (gate + up + down, HBM layout).
+size_t tg_layer_expert_bytes(void* handle, int e) {
+  Layer* L = (Layer*)handle;
+  if (!L || e < 0 || e >= L->E) return 0;
+  const ExpertDesc& X = L->experts[e];
+  if (!X.gate.main) return 0;
+  return (size_t)X.gate.rows * host_row_bytes(X.gate.fmt, X.gate.cols) +
+         (size_t)X.up.rows * host_row_bytes(X.up.fmt, X.up.cols) +
+         (size_t)X.down.rows * host_row_bytes(X.down.fmt, X.down.cols);
+}
+
+// Device-resident step, enqueued on the library stream (no synchronisation):
+// x' = x + add (add may be NULL), N = normalize ? rmsnorm(x') * norm_w : x',
+// moe_out = sum over the selected experts (cleared first), x_out = x' (may be NULL).
+int tg_layer_forward_dev(void* handle, const float* x, const float* add, float* x_out, float* moe_out, int T,
+                         int normalize, const float* norm_w) {
+  std::lock_guard<std::recursive_mutex> lk(ctx_mutex());
+  if (!handle || !ensure_init()) return -1;
+  return layer_enqueue((Layer*)handle, x, add, x_out, moe_out, T, normalize, norm_w, stream(),
+                       "tg_layer_forward_dev")
+             ? 0
+             : -1;
+}
+
+// Host buffers, synchronous: out[T][D] += experts(rmsnorm(x)) (normalize=1)
+// or experts(x) (normalize=0).
+int tg_layer_forward(void* handle, const float* x_host, float* out_host, int T, int normalize) {
+  std::lock_guard<std::recursive_mutex> lk(ctx_mutex());
+  const char* what = "tg_layer_forward";
+  Layer* L = (Layer*)handle;
+  if (!L || !ensure_init()) return -1;
+  if (T < 1 || T > L->max_tokens) {
+    set_host_error(3, "%s: %d rows exceed max_tokens %d", what, T, L->max_tokens);
+    return -1;
+  }
+  const size_t n = sizeof(float) * (size_t)T * L->D;
+  float* hx = (float*)pinned_up(n);
+  float* ho = (float*)pinned_down(n);
+  if (!hx || !ho) return -1;
+  cudaStream_t s = stream();
+  memcpy(hx, x_host, n);
+  float* moe = L->moe_out;
+  if (cudaMemcpyAsync(L->xbuf, hx, n, cudaMemcpyHostToDevice, s) != cudaSuccess) return -1;
+  if (!layer_enqueue(L, L->xbuf, nullptr, nullptr, moe, T, normalize, nullptr, s, what)) return -1;
+  if (cudaMemcpyAsync(ho, moe, n, cudaMemcpyDeviceToHost, s) != cudaSuccess) return -1;
+  if (!finish(what)) return -1;
+  for (size_t i = 0; i < (size_t)T * L->D; i++) out_host[i] += ho[i];
+  return 0;
+}
+
+// The routing of the last step of a layer: idx/w [T][top_k] (host).
+int tg_layer_last_routing(void* handle, int T, int* idx, float* w) {
+  std::lock_guard<std::recursive_mutex> lk(ctx_mutex());
+  Layer* L = (Layer*)handle;
+  if (!L || T < 1 || T > L->max_tokens) return -1;
+  cudaStreamSynchronize(stream());
+  cudaMemcpy(idx, L->sel_idx, sizeof(int) * (size_t)T * L->top_k, cudaMemcpyDeviceToHost);
+  cudaMemcpy(w, L->sel_w, sizeof(float) * (size_t)T * L->top_k, cudaMemcpyDeviceToHost);
+  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
+// A residual stack on the device: for each layer, x += experts(rmsnorm(x) *
+// norm_w[l]) (norm_w may be NULL: weight 1).  x [T][D] is updated in place;
+// enqueued on the library stream.
+int tg_stack_forward_dev(void* const* layers, int n_layers, float* x, int T, const float* const* norm_w) {
+  std::lock_guard<std::recursive_mutex> lk(ctx_mutex());
+  const char* what = "tg_stack_forward_dev";
+  if (n_layers < 1 || !layers || !ensure_init()) return -1;
+  Layer* L0 = (Layer*)layers[0];
+  float* bufs[2] = {x, L0->xbuf};   // residual ping-pong
+  float* moe[2] = {L0->moe_out, L0->moe_out + (size_t)L0->max_tokens * L0->D};
+  cudaStream_t s = stream();
+  int cur = 0;
+  for (int l = 0; l < n_layers; l++) {
+    Layer* L = (Layer*)layers[l];
+    if (L->D != L0->D || T > L0->max_tokens) {
+      set_host_error(3, "%s: layer %d does not match layer 0", what, l);
+      return -1;
+    }
+    const float* add = l ? moe[(l - 1) & 1] : nullptr;
+    float* x_out = l ? bufs[cur ^ 1] : nullptr;
+    if (!layer_enqueue(L, bufs[cur], add, x_out, moe[l & 1], T, 1, norm_w ? norm_w[l] : nullptr, s, what))
+      return -1;
+    if (l) cur ^= 1;
+  }
+  // x = x_last' + moe_last, written back into the caller's buffer.
+  launch_add(bufs[cur], moe[(n_layers - 1) & 1], x, (size_t)T * L0->D, s);
+  count_launches(1);
+  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
+// ---- CUDA graphs over the library stream --------------------------------
+
+int tg_cuda_graph_begin(void) {
+  std::lock_guard<std::recursive_mutex> lk(ctx_mutex());
+  if (!ensure_init()) return -1;
+  return cudaStreamBeginCapture(stream(), cudaStreamCaptureModeThreadLocal) == cudaSuccess ? 0 : -1;
+}
+
+void* tg_cuda_graph_end(void) {
+  std::lock_guard<std::recursive_mutex> lk(ctx_mutex());
+  cudaGraph_t graph = nullptr;
+  if (cudaStreamEndCapture(stream(), &graph) != cudaSuccess || !graph) {
+    set_host_error(102, "tg_cuda_graph_end: capture failed (%s)", cudaGetErrorString(cudaGetLastError()));
+    return nullptr;
+  }
+  cudaGraphExec_t exec = nullptr;
+  cudaError_t e = cudaGraphInstantiate(&exec, graph, 0);
+  cudaGraphDestroy(graph);
+  if (e != cudaSuccess) {
+    set_host_error(102, "tg_cuda_graph_end: instantiate failed (%s)", cudaGetErrorString(e));
+    return nullptr;
+  }
+  return exec;
+}
+
+int tg_cuda_graph_launch(void* exec) {
+  std::lock_guard<std::recursive_mutex> lk(ctx_mutex());
+  return cudaGraphLaunch((cudaGraphExec_t)exec, stream()) == cudaSuccess ? 0 : -1;
+}
+
+void tg_cuda_graph_destroy(void* exec) {
+  if (exec) cudaGraphExecDestroy((cudaGraphExec_t)exec);
+}
+
+void* tg_cuda_stream(void) {
+  std::lock_guard<std::recursive_mutex> lk(ctx_mutex());
+  if (!ensure_init()) return nullptr;
+  return (void*)stream();
+}
+
+int tg_cuda_synchronize(void) {
+  std::lock_guard<std::recursive_mutex> lk(ctx_mutex());
+  if (!ensure_init()) return -1;
+  return finish("tg_cuda_synchronize") ? 0 : -1;
+}
+
+}  // extern "C"

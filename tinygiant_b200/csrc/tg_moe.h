@@ -1,0 +1,44 @@
+// tg_moe.h — launchers of the MoE expert kernels (tg_moe.cu) and of the
+// fused routing kernel (tg_route.cu).
+#pragma once
+#include <cuda_runtime.h>
+
+#include "tg_plan.cuh"
+
+namespace tg {
+
+cudaError_t launch_moe_gateup(const PlanHdr* ph, int max_slots, int gate_fmt, int D, int I, const Q8Dev* xq8,
+                              float* hidden, Q8Dev* hq8, int* counters, DevStatus* st, cudaStream_t s);
+cudaError_t launch_moe_down(const PlanHdr* ph, int D, int I, const Q8Dev* hq8, const float* hidden, float* out,
+                            DevStatus* st, cudaStream_t s);
+// Ints of zero-initialised counter space moe_gateup needs for max_slots slots.
+size_t moe_counter_ints(int max_slots, int I);
+
+struct RouteArgs {
+  const float* x_in;      // [T][D] residual stream before this layer
+  const float* add_in;    // [T][D] previous MoE output to add first, or null
+  float* x_out;           // [T][D] x_in + add_in (written by CTA 0), or null
+  float* zero_out;        // [T][D] buffer to clear for this layer's MoE output, or null
+  const float* norm_w;    // [D] RMSNorm weight, or null for 1
+  float eps;
+  int normalize;          // 1: N = rmsnorm(x'); 0: N = x'
+  const float* router_w;  // [E][D] fp32
+  const float* router_b;  // [E] or null
+  int T, D, E, top_k, I, act, assoc_rule, bias_term;
+  const ExpertDesc* experts;  // [E]
+  Q8Dev* xq8;             // [T][ceil(D/256)]
+  float* logits;          // [T][E]
+  int* counter;           // one int, zero between launches
+  PlanHdr* plan;
+  SlotDesc* slots;        // [min(E, T*top_k)]
+  int* rows;              // [T*top_k]
+  float* wts;             // [T*top_k]
+  int* row_slot;          // [T*top_k]
+  int* sel_idx;           // [T][top_k]
+  float* sel_w;           // [T][top_k]
+};
+
+size_t route_smem_bytes(int D, int E);
+cudaError_t launch_layer_route(const RouteArgs& a, cudaStream_t s);
+
+}  // namespace tg

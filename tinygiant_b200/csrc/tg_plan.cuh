@@ -1,10 +1,13 @@
 // tg_plan.cuh — the device-side description of one MoE call.
 //
-// A call (tg_moe_forward_rows_v2 and the entries built on it) selects
-// n_slots experts, in the caller's order.  Slot s uses rows[row_off ..
-// row_off + n_rows) of the k input rows with weights wts[...]; this is the
-// reference's per-expert gather of active rows (csrc/libtinygiant.c:1411-1423),
-// laid out flat so every kernel indexes it without host help.
+// A call (tg_moe_forward_rows_v2 and the entries built on it, or one layer
+// step routed on the GPU) selects n_slots experts, in order.  Slot s uses
+// rows[row_off .. row_off + n_rows) of the k input rows with weights
+// wts[...]; this is the reference's per-expert gather of active rows
+// (csrc/libtinygiant.c:1411-1423), laid out flat.  The header lives in device
+// memory so a plan built on the GPU (by the router kernel) and one staged
+// from the host drive the same kernels; grids are sized by host-side upper
+// bounds and surplus CTAs exit.
 #pragma once
 #include "tg_common.cuh"
 
@@ -20,10 +23,15 @@ struct SlotDesc {
   int pad[2];
 };
 
-struct MoePlan {
-  const SlotDesc* slots;  // [n_slots]
-  const int* rows;        // [total_rows] input row of each active (slot, j)
-  const float* wts;       // [total_rows] combine weight of each active (slot, j)
+// One expert of a resident layer (the GPU router selects among these).
+struct ExpertDesc {
+  WDesc gate, up, down;
+  const float* gb;
+  const float* ub;
+  const float* db;
+};
+
+struct PlanHdr {
   int n_slots;
   int total_rows;
   int k;                  // input rows of the call
@@ -32,6 +40,10 @@ struct MoePlan {
   int act;                // Act
   int assoc_rule;         // AssocRule
   int bias_term;          // 1: part = w * (v + (db ? db[r] : 0.f)); 0: part = w * v
+  const SlotDesc* slots;  // [n_slots]
+  const int* rows;        // [total_rows] input row of each active (slot, j)
+  const float* wts;       // [total_rows] combine weight of each active (slot, j)
+  const int* row_slot;    // [total_rows] slot of each active (slot, j)
 };
 
 // Whether active row j (0-based within its slot of n rows) is computed with

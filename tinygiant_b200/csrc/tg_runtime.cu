@@ -24,6 +24,7 @@
 
 #include "../../include/tinygiant.h"
 #include "tg_kernels.h"
+#include "tg_moe.h"
 #include "tg_runtime.h"
 
 namespace tg {
@@ -106,7 +107,7 @@ struct Ctx {
   bool user_stream_set = false;
   DevStatus* d_status = nullptr;
   DevStatus* h_status = nullptr;  // pinned
-  DevBuf d_stage, d_xq8, d_hidden, d_hq8, d_tmp;
+  DevBuf d_stage, d_xq8, d_hidden, d_hq8, d_tmp, d_counters;
   PinBuf h_up, h_down;
   int threads = 1;
 };
@@ -114,6 +115,21 @@ struct Ctx {
 static Ctx g;
 
 cudaStream_t stream() { return g.user_stream_set ? g.user_stream : g.own_stream; }
+
+std::recursive_mutex& ctx_mutex() { return g.mu; }
+DevStatus* status_ptr() { return g.d_status; }
+void count_launches(int n) { g_launches += n; }
+void* pinned_up(size_t n) { return g.h_up.reserve(n) ? g.h_up.p : nullptr; }
+void* pinned_down(size_t n) { return g.h_down.reserve(n) ? g.h_down.p : nullptr; }
+
+// The gate/up kernel's per-(slot, 256-block) arrival counters must start at
+// zero; they reset themselves, and are cleared again after a device error.
+bool reserve_counters(size_t n_ints) {
+  const size_t old = g.d_counters.n;
+  if (!g.d_counters.reserve(sizeof(int) * n_ints)) return false;
+  if (g.d_counters.n != old) return cuda_ok(cudaMemset(g.d_counters.p, 0, g.d_counters.n), "cudaMemset(counters)");
+  return true;
+}
 
 bool ensure_init() {
   if (g.inited) return true;
@@ -158,6 +174,7 @@ bool finish(const char* what) {
   if (g.h_status->code != 0) {
     DevStatus st = *g.h_status;
     cudaMemsetAsync(g.d_status, 0, sizeof(DevStatus), s);
+    if (g.d_counters.p) cudaMemsetAsync(g.d_counters.p, 0, g.d_counters.n, s);
     cudaStreamSynchronize(s);
     set_host_error(200 + st.code, "%s: device error %d at site %d (%d, %d)", what, st.code, st.where, st.a, st.b);
     return false;
@@ -372,6 +389,7 @@ bool run_moe(std::vector<HostSlot>& slots, int gate_fmt, int act, int rule, int 
   const int gbpr = (D + QK - 1) / QK, dbpr = (I + QK - 1) / QK;
 
   Stage st;
+  size_t o_hdr = st.take(sizeof(PlanHdr));
   size_t o_slots = st.take(sizeof(SlotDesc) * n);
   size_t o_rows = st.take(sizeof(int) * total);
   size_t o_wts = st.take(sizeof(float) * total);
@@ -381,7 +399,7 @@ bool run_moe(std::vector<HostSlot>& slots, int gate_fmt, int act, int rule, int 
   size_t bytes = st.off;
   if (!g.h_up.reserve(bytes) || !g.d_stage.reserve(bytes) || !g.h_down.reserve(sizeof(float) * (size_t)k * D) ||
       !g.d_xq8.reserve(sizeof(Q8Dev) * (size_t)k * gbpr) || !g.d_hidden.reserve(sizeof(float) * (size_t)total * I) ||
-      !g.d_hq8.reserve(sizeof(Q8Dev) * (size_t)total * dbpr))
+      !g.d_hq8.reserve(sizeof(Q8Dev) * (size_t)total * dbpr) || !reserve_counters(moe_counter_ints(n, I)))
     return false;
   uint8_t* hb = (uint8_t*)g.h_up.p;
   uint8_t* db = (uint8_t*)g.d_stage.p;
@@ -409,23 +427,25 @@ bool run_moe(std::vector<HostSlot>& slots, int gate_fmt, int act, int rule, int 
       off++;
     }
   }
+  PlanHdr* hh = (PlanHdr*)(hb + o_hdr);
+  hh->n_slots = n;
+  hh->total_rows = total;
+  hh->k = k;
+  hh->embed_dim = D;
+  hh->inter_dim = I;
+  hh->act = act;
+  hh->assoc_rule = rule;
+  hh->bias_term = bias_term;
+  hh->slots = (const SlotDesc*)(db + o_slots);
+  hh->rows = (const int*)(db + o_rows);
+  hh->wts = (const float*)(db + o_wts);
+  hh->row_slot = (const int*)(db + o_rslot);
   memcpy(hb + o_in, inputs, sizeof(float) * (size_t)k * D);
   memcpy(hb + o_out, output, sizeof(float) * (size_t)k * D);
 
   cudaStream_t s = stream();
   if (!cuda_ok(cudaMemcpyAsync(db, hb, bytes, cudaMemcpyHostToDevice, s), what)) return false;
-  MoePlan plan{};
-  plan.slots = (const SlotDesc*)(db + o_slots);
-  plan.rows = (const int*)(db + o_rows);
-  plan.wts = (const float*)(db + o_wts);
-  plan.n_slots = n;
-  plan.total_rows = total;
-  plan.k = k;
-  plan.embed_dim = D;
-  plan.inter_dim = I;
-  plan.act = act;
-  plan.assoc_rule = rule;
-  plan.bias_term = bias_term;
+  const PlanHdr* dph = (const PlanHdr*)(db + o_hdr);
   const float* d_in = (const float*)(db + o_in);
   float* d_out = (float*)(db + o_out);
   Q8Dev* xq8 = (Q8Dev*)g.d_xq8.p;
@@ -433,11 +453,11 @@ bool run_moe(std::vector<HostSlot>& slots, int gate_fmt, int act, int rule, int 
   Q8Dev* hq8 = (Q8Dev*)g.d_hq8.p;
 
   launch_quantize_rows(d_in, k, D, D, xq8, s);
-  if (!cuda_ok(launch_moe_gateup(plan, gate_fmt, xq8, gbpr, hidden, g.d_status, s), what)) return false;
-  launch_quantize_rows(hidden, total, I, I, hq8, s);
-  if (!cuda_ok(launch_moe_down(plan, (const int*)(db + o_rslot), hq8, dbpr, hidden, d_out, g.d_status, s), what))
+  if (!cuda_ok(launch_moe_gateup(dph, n, gate_fmt, D, I, xq8, hidden, hq8, (int*)g.d_counters.p, g.d_status, s),
+               what) ||
+      !cuda_ok(launch_moe_down(dph, D, I, hq8, hidden, d_out, g.d_status, s), what))
     return false;
-  g_launches += 4;
+  g_launches += 3;
   if (!cuda_ok(cudaMemcpyAsync(g.h_down.p, d_out, sizeof(float) * (size_t)k * D, cudaMemcpyDeviceToHost, s), what))
     return false;
   if (!finish(what)) return false;

@@ -2,6 +2,8 @@
 #pragma once
 #include <cuda_runtime.h>
 
+#include <mutex>
+
 #include "tg_common.cuh"
 
 namespace tg {
@@ -13,5 +15,10 @@ bool finish(const char* what);
 size_t host_row_bytes(int fmt, int ncols);
 bool lookup_matrix(const void* h, int fmt, int rows, int cols, WDesc* out);
 const float* lookup_vector(const float* h, int n);
+std::recursive_mutex& ctx_mutex();
+DevStatus* status_ptr();
+void count_launches(int n);
+void* pinned_up(size_t n);
+void* pinned_down(size_t n);
 
 }  // namespace tg

@@ -1,0 +1,71 @@
+"""Python handle for a resident MoE layer routed on the GPU.
+
+Wraps tg_layer_* of libtinygiant.so: all experts of a synth.MoeLayer (or any
+expert byte arrays) go to HBM once; a step runs rmsnorm -> router -> top-k
+-> experts entirely on the device.
+"""
+import ctypes
+
+import numpy as np
+
+from . import check, load
+
+
+class ResidentLayer:
+    def __init__(self, layer, max_tokens=1, lib=None, handle=None, shard=0, n_shards=1):
+        self.lib = lib or load()
+        self.layer = layer
+        self.max_tokens = max_tokens
+        self.D, self.I, self.E, self.k = layer.embed_dim, layer.inter_dim, layer.n_experts, layer.top_k
+        if handle is not None:
+            self.h = handle
+            return
+        P = ctypes.c_void_p
+        self._g = (P * self.E)(*[a.ctypes.data for a in layer.gates])
+        self._u = (P * self.E)(*[a.ctypes.data for a in layer.ups])
+        self._d = (P * self.E)(*[a.ctypes.data for a in layer.downs])
+        self._f = (ctypes.c_int * self.E)(*layer.down_fmts)
+        self._rw = np.ascontiguousarray(layer.router_w, dtype=np.float32)
+        self._rb = None if layer.router_b is None else np.ascontiguousarray(layer.router_b, dtype=np.float32)
+        self.shard, self.n_shards = shard, n_shards
+        self.h = self.lib.tg_layer_create_shard(self.E, ctypes.addressof(self._g), ctypes.addressof(self._u),
+                                                ctypes.addressof(self._d), layer.gate_fmt, ctypes.addressof(self._f),
+                                                None, None, None, layer.act, self.D, self.I, self._rw.ctypes.data,
+                                                None if self._rb is None else self._rb.ctypes.data, self.k,
+                                                max_tokens, shard, n_shards)
+        if not self.h:
+            check(self.lib)
+            raise RuntimeError("tg_layer_create failed")
+
+    def clone(self):
+        h = self.lib.tg_layer_clone(self.h)
+        if not h:
+            check(self.lib)
+        r = ResidentLayer(self.layer, self.max_tokens, self.lib, handle=h)
+        r.shard, r.n_shards = self.shard, self.n_shards
+        return r
+
+    def expert_bytes(self, e):
+        return self.lib.tg_layer_expert_bytes(self.h, e)
+
+    def forward(self, x, out=None, normalize=True):
+        """Host arrays: out [T, D] += experts(rmsnorm(x))."""
+        x = np.ascontiguousarray(np.atleast_2d(x), dtype=np.float32)
+        if out is None:
+            out = np.zeros_like(x)
+        rc = self.lib.tg_layer_forward(self.h, x.ctypes.data, out.ctypes.data, x.shape[0], int(normalize))
+        check(self.lib)
+        if rc != 0:
+            raise RuntimeError("tg_layer_forward failed")
+        return out
+
+    def last_routing(self, T):
+        idx = np.zeros((T, self.k), np.int32)
+        w = np.zeros((T, self.k), np.float32)
+        self.lib.tg_layer_last_routing(self.h, T, idx.ctypes.data, w.ctypes.data)
+        return idx, w
+
+    def close(self):
+        if self.h:
+            self.lib.tg_layer_destroy(self.h)
+            self.h = None
