@@ -18,7 +18,7 @@
 namespace tg {
 
 struct Layer {
-  int E = 0, D = 0, I = 0, gate_fmt = 0, act = 0, top_k = 0, max_tokens = 0;
+  int E = 0, D = 0, I = 0, gate_fmt = 0, down_fmt = 0, act = 0, top_k = 0, max_tokens = 0;
   int max_slots = 0, max_rows = 0;
   std::vector<ExpertDesc> experts;  // host copy of the device table
   std::vector<void*> owned;         // device allocations to free
@@ -71,11 +71,13 @@ static bool alloc_scratch(Layer* L) {
          dmalloc(L, (void**)&L->hidden, sizeof(float) * (size_t)L->max_rows * I) &&
          dmalloc(L, (void**)&L->hq8, sizeof(Q8Dev) * (size_t)L->max_rows * dbpr) &&
          dmalloc(L, (void**)&L->counters, sizeof(int) * moe_counter_ints(L->max_slots, I)) &&
+         (register_counters(L->counters, sizeof(int) * moe_counter_ints(L->max_slots, I)), true) &&
          dmalloc(L, (void**)&L->moe_out, sizeof(float) * 2 * (size_t)T * D) &&
          dmalloc(L, (void**)&L->xbuf, sizeof(float) * (size_t)T * D);
 }
 
 static void free_layer(Layer* L) {
+  if (L->counters) unregister_counters(L->counters);
   for (void* p : L->owned) cudaFree(p);
   delete L;
 }
@@ -117,11 +119,15 @@ static bool layer_enqueue(Layer* L, const float* x, const float* add, float* x_o
   a.row_slot = L->row_slot;
   a.sel_idx = L->sel_idx;
   a.sel_w = L->sel_w;
+  a.st = status_ptr();
   cudaError_t e = launch_layer_route(a, s);
   if (e == cudaSuccess)
     e = launch_moe_gateup(L->plan, std::min(L->max_slots, T * L->top_k), L->gate_fmt, L->D, L->I, L->xq8, L->hidden,
                           L->hq8, L->counters, status_ptr(), s);
-  if (e == cudaSuccess) e = launch_moe_down(L->plan, L->D, L->I, L->hq8, L->hidden, moe_out, status_ptr(), s);
+  if (e == cudaSuccess)
+    e = launch_moe_down(L->plan, std::min(L->max_slots, T * L->top_k), T * L->top_k, L->down_fmt, L->D, L->I, T, L->hq8,
+                        L->hidden,
+                        moe_out, nullptr, status_ptr(), s);
   count_launches(3);
   if (e != cudaSuccess) {
     set_host_error(100 + (int)e, "%s: %s", what, cudaGetErrorString(e));
@@ -162,12 +168,19 @@ void* tg_layer_create_shard(int n_experts, const uint8_t* const* gate_ptrs, cons
     set_host_error(4, "%s: gate_bias given without up_bias", what);
     return nullptr;
   }
+  for (int e = 1; e < n_experts; e++)
+    if (down_fmts[e] != down_fmts[0]) {
+      set_host_error(4, "%s: experts of a resident layer share one down format (expert %d: %d, expert 0: %d)", what,
+                     e, down_fmts[e], down_fmts[0]);
+      return nullptr;
+    }
   if (!ensure_init()) return nullptr;
   Layer* L = new Layer;
   L->E = n_experts;
   L->D = embed_dim;
   L->I = inter_dim;
   L->gate_fmt = gate_fmt;
+  L->down_fmt = down_fmts[0];
   L->act = act == ACT_GPTOSS ? ACT_GPTOSS : ACT_SILU;
   L->top_k = top_k;
   L->max_tokens = max_tokens;
@@ -225,6 +238,7 @@ void* tg_layer_clone(void* handle) {
   L->D = src->D;
   L->I = src->I;
   L->gate_fmt = src->gate_fmt;
+  L->down_fmt = src->down_fmt;
   L->act = src->act;
   L->top_k = src->top_k;
   L->max_tokens = src->max_tokens;

@@ -9,8 +9,14 @@ namespace tg {
 
 cudaError_t launch_moe_gateup(const PlanHdr* ph, int max_slots, int gate_fmt, int D, int I, const Q8Dev* xq8,
                               float* hidden, Q8Dev* hq8, int* counters, DevStatus* st, cudaStream_t s);
-cudaError_t launch_moe_down(const PlanHdr* ph, int D, int I, const Q8Dev* hq8, const float* hidden, float* out,
-                            DevStatus* st, cudaStream_t s);
+// Down phase for a plan whose experts all use down format down_fmt_all, or,
+// with parts_out ([total_rows][D]), the slots of that format only, storing
+// their parts for launch_combine_parts.  T: the call's input rows;
+// max_slots / max_rows: upper bounds of the plan's slots and active rows.
+cudaError_t launch_moe_down(const PlanHdr* ph, int max_slots, int max_rows, int down_fmt_all, int D, int I, int T,
+                            const Q8Dev* hq8, const float* hidden, float* out, float* parts_out, DevStatus* st,
+                            cudaStream_t s);
+cudaError_t launch_combine_parts(const PlanHdr* ph, int D, int T, const float* parts, float* out, cudaStream_t s);
 // Ints of zero-initialised counter space moe_gateup needs for max_slots slots.
 size_t moe_counter_ints(int max_slots, int I);
 
@@ -36,9 +42,10 @@ struct RouteArgs {
   int* row_slot;          // [T*top_k]
   int* sel_idx;           // [T][top_k]
   float* sel_w;           // [T][top_k]
+  DevStatus* st;          // device error record
 };
 
-size_t route_smem_bytes(int D, int E);
+size_t route_smem_bytes(int D, int E, int T, int K);
 cudaError_t launch_layer_route(const RouteArgs& a, cudaStream_t s);
 
 }  // namespace tg

@@ -1,0 +1,71 @@
+// tg_ptx.cuh — inline-PTX helpers for sm_100a: bulk async copies (TMA,
+// non-tensor, no multicast) into shared memory with mbarrier completion,
+// bounded mbarrier waits, and programmatic dependent launch control.
+//
+// Rules kept here: every cp.async.bulk starts and ends on 16-byte
+// boundaries (callers round tile sizes up; weight allocations are padded);
+// no copy uses .multicast::cluster; every wait has an iteration limit after
+// which it reports failure instead of spinning forever.
+#pragma once
+#include <cstdint>
+
+#include "tg_common.cuh"
+
+namespace tg {
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+// Makes mbarrier initialisation visible to the async (TMA) proxy.
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+
+// Global -> shared bulk copy completing on `bar`; dst, src and bytes must be
+// multiples of 16.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Waits for phase `parity` of `bar` to complete; gives up after ~2^31 clock
+// cycles (about a second) and returns false.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (!mbar_try_wait(bar, parity))
+    if (clock64() - t0 > (1ll << 31)) return false;
+  return true;
+}
+
+// Programmatic dependent launch: wait for the preceding kernel in the stream
+// to complete (no-op when this kernel was launched without the attribute),
+// and allow the next kernel to be scheduled early.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+__host__ __device__ __forceinline__ uint32_t round16(size_t n) { return (uint32_t)((n + 15) & ~(size_t)15); }
+
+}  // namespace tg

@@ -8,20 +8,22 @@
 //   union of selected experts ascending by id, active rows in token
 //   order with their weights (a zero weight is inactive)             engine.py:297-318,
 //                                                                    libtinygiant.c:1411-1423
-// and the Q8 blocks of N (libtinygiant.c:1408-1410).  CTAs split the experts
-// (one warp per expert); the last CTA to finish selects and builds the plan
-// that the expert kernels read, so no host round trip is needed.
+// and the Q8 blocks of N (libtinygiant.c:1408-1410).  One CTA per expert
+// computes that expert's logits (its 8 KB router row is read once); the last
+// CTA to finish selects the experts and writes the plan the expert kernels
+// read, so the step needs no host round trip.
 //
 // Float order: the norm and the logit dots reduce in a fixed order (warp
-// trees), which differs from numpy's; routing agrees with the reference
-// except where two logits tie to within rounding.
+// trees), not numpy's; routing agrees with the reference except where two
+// logits tie to within rounding.
 #include "tg_moe.h"
+#include "tg_ptx.cuh"
 #include "tg_q8.cuh"
 
 namespace tg {
 
-constexpr int RT_WARPS = 8;   // experts per CTA
-constexpr int RT_TC = 8;      // token rows per smem chunk
+constexpr int RT_TC = 8;      // token rows per shared-memory chunk
+constexpr int RT_THREADS = 256;
 
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
@@ -29,67 +31,173 @@ __device__ __forceinline__ float warp_sum(float v) {
   return v;
 }
 
-__global__ void __launch_bounds__(256) layer_route_kernel(RouteArgs a) {
-  extern __shared__ float sm[];
-  __shared__ Q8Scratch qsh;
-  __shared__ float red[RT_WARPS];
+// Warp-level quantize_q8 of one 256-value block (tg_q8.cuh semantics): lane l
+// holds values 8l..8l+7 (valid below n).
+__device__ __forceinline__ void quantize_block_warp(const float* src, int n, Q8Dev* o) {
+  const int lane = threadIdx.x & 31;
+  float v[8];
+  float a = 0.f;
+#pragma unroll
+  for (int j = 0; j < 8; j++) {
+    const int i = lane * 8 + j;
+    v[j] = i < n ? src[i] : 0.f;
+    if (i < n) a = max_nan(a, fabsf(v[j]));
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) a = max_nan(a, __shfl_xor_sync(0xffffffffu, a, off));
+  const float inv = a > 0.f ? __fdiv_rn(127.f, a) : 0.f;
+  int q[8], s = 0;
+#pragma unroll
+  for (int j = 0; j < 8; j++) {
+    const int i = lane * 8 + j;
+    q[j] = 0;
+    if (i < n) {
+      const float sv = __fmul_rn(v[j], inv);
+      q[j] = (sv != sv) ? 0 : __float2int_rn(sv);
+    }
+    s += q[j];
+  }
+  uint32_t w0 = 0, w1 = 0;
+#pragma unroll
+  for (int j = 0; j < 4; j++) {
+    w0 |= ((uint32_t)q[j] & 0xFFu) << (8 * j);
+    w1 |= ((uint32_t)q[4 + j] & 0xFFu) << (8 * j);
+  }
+  reinterpret_cast<uint2*>(o->qs)[lane] = make_uint2(w0, w1);
+  // bsums: 4 lanes per 32-value sub-block
+  int bs = s;
+  bs += __shfl_xor_sync(0xffffffffu, bs, 1);
+  bs += __shfl_xor_sync(0xffffffffu, bs, 2);
+  if ((lane & 3) == 0) o->bsums[lane >> 2] = bs;
+  int tot = s;
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) tot += __shfl_xor_sync(0xffffffffu, tot, off);
+  if (lane == 0) {
+    o->scale = __fdiv_rn(a, 127.f);
+    o->sum = tot;
+  }
+}
+
+__global__ void __launch_bounds__(RT_THREADS) layer_route_kernel(RouteArgs a) {
+  extern __shared__ __align__(16) float sm[];
+  __shared__ float red[RT_THREADS / 32][RT_TC];
+  __shared__ float rr_s[RT_TC];
   __shared__ int last_flag;
+  __shared__ uint64_t bar;
   const int T = a.T, D = a.D, E = a.E, t = threadIdx.x, lane = t & 31, w = t >> 5;
+  const int nw = RT_THREADS / 32;
   const int gbpr = (D + QK - 1) / QK;
-  float* xs = sm;   // [RT_TC][D]
-  const int e = blockIdx.x * RT_WARPS + w;
+  const int e = blockIdx.x;                 // this CTA's expert
+  float* xs = sm;                           // [RT_TC][D]
+  float* wrow = sm + RT_TC * D;             // [D] this expert's router row
+  // Router weights do not depend on the preceding kernel: start the copy of
+  // this expert's row before waiting for it.
+  const float* wsrc = a.router_w + (size_t)e * D;
+  const bool bulk = ((uintptr_t)wsrc & 15) == 0 && (D * 4) % 16 == 0;
+  if (t == 0 && bulk) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+    mbar_arrive_expect_tx(&bar, (uint32_t)D * 4);
+    bulk_g2s(wrow, wsrc, (uint32_t)D * 4, &bar);
+  }
+  pdl_wait();
+  pdl_trigger();
+  const float* wr = bulk ? wrow : wsrc;
+  bool have_w = !bulk;
   for (int t0 = 0; t0 < T; t0 += RT_TC) {
     const int nt = min(RT_TC, T - t0);
-    for (int i = t; i < nt * D; i += blockDim.x) {
-      const size_t gi = (size_t)t0 * D + i;
-      float v = a.x_in[gi];
-      if (a.add_in) v = fadd(v, a.add_in[gi]);
-      xs[i] = v;
-      if (blockIdx.x == 0 && a.x_out) a.x_out[gi] = v;
+    if ((D & 3) == 0) {
+      // float4 loads, all issued before any use
+      const float4* xi = reinterpret_cast<const float4*>(a.x_in + (size_t)t0 * D);
+      const float4* ai = a.add_in ? reinterpret_cast<const float4*>(a.add_in + (size_t)t0 * D) : nullptr;
+      float4* xo = a.x_out && e == 0 ? reinterpret_cast<float4*>(a.x_out + (size_t)t0 * D) : nullptr;
+      for (int i = t; i < nt * D / 4; i += RT_THREADS) {
+        float4 v = xi[i];
+        if (ai) {
+          const float4 d = ai[i];
+          v = make_float4(fadd(v.x, d.x), fadd(v.y, d.y), fadd(v.z, d.z), fadd(v.w, d.w));
+        }
+        reinterpret_cast<float4*>(xs)[i] = v;
+        if (xo) xo[i] = v;
+      }
+    } else {
+      for (int i = t; i < nt * D; i += RT_THREADS) {
+        const size_t gi = (size_t)t0 * D + i;
+        float v = a.x_in[gi];
+        if (a.add_in) v = fadd(v, a.add_in[gi]);
+        xs[i] = v;
+        if (e == 0 && a.x_out) a.x_out[gi] = v;
+      }
     }
     __syncthreads();
     if (a.normalize) {
-      for (int tt = 0; tt < nt; tt++) {
-        float ss = 0.f;
-        for (int i = t; i < D; i += blockDim.x) ss = __fmaf_rn(xs[tt * D + i], xs[tt * D + i], ss);
-        ss = warp_sum(ss);
-        if (lane == 0) red[w] = ss;
-        __syncthreads();
-        float tot = 0.f;
+      float ss[RT_TC];
 #pragma unroll
-        for (int j = 0; j < RT_WARPS; j++) tot = fadd(tot, red[j]);
-        const float rr = __fsqrt_rn(fadd(__fdiv_rn(tot, (float)D), a.eps));
-        for (int i = t; i < D; i += blockDim.x) {
-          float v = __fdiv_rn(xs[tt * D + i], rr);
-          if (a.norm_w) v = fmul(v, a.norm_w[i]);
-          xs[tt * D + i] = v;
+      for (int tt = 0; tt < RT_TC; tt++) ss[tt] = 0.f;
+#pragma unroll
+      for (int tt = 0; tt < RT_TC; tt++)
+        if (tt < nt)
+          for (int i = t; i < D; i += RT_THREADS) ss[tt] = __fmaf_rn(xs[tt * D + i], xs[tt * D + i], ss[tt]);
+#pragma unroll
+      for (int tt = 0; tt < RT_TC; tt++)
+        if (tt < nt) {
+          const float v = warp_sum(ss[tt]);
+          if (lane == 0) red[w][tt] = v;
         }
-        __syncthreads();
+      __syncthreads();
+      if (t < nt) {
+        float tot = 0.f;
+        for (int j = 0; j < nw; j++) tot = fadd(tot, red[j][t]);
+        rr_s[t] = __fsqrt_rn(fadd(__fdiv_rn(tot, (float)D), a.eps));
       }
-    }
-    // Q8 blocks of the normalized rows (CTA 0).
-    if (blockIdx.x == 0) {
-      for (int tt = 0; tt < nt; tt++)
-        for (int b = 0; b < gbpr; b++) {
-          const int n = min(QK, D - b * QK);
-          const bool valid = t < n;
-          quantize_block_cta(valid ? xs[tt * D + b * QK + t] : 0.f, valid, a.xq8 + (size_t)(t0 + tt) * gbpr + b, qsh);
-        }
-    }
-    // Logits: one warp per expert.
-    if (e < E) {
-      const float* wr = a.router_w + (size_t)e * D;
-      for (int tt = 0; tt < nt; tt++) {
-        float acc = 0.f;
-        for (int i = lane; i < D; i += 32) acc = __fmaf_rn(__ldg(wr + i), xs[tt * D + i], acc);
-        acc = warp_sum(acc);
-        if (lane == 0) a.logits[(size_t)(t0 + tt) * E + e] = a.router_b ? fadd(acc, a.router_b[e]) : acc;
+      __syncthreads();
+      for (int i = t; i < nt * D; i += RT_THREADS) {
+        const int tt = i / D;
+        float v = __fdiv_rn(xs[i], rr_s[tt]);
+        if (a.norm_w) v = fmul(v, a.norm_w[i - tt * D]);
+        xs[i] = v;
       }
+      __syncthreads();
+    }
+    // Q8 blocks of the (normalized) rows: CTA 0, one warp per block.
+    if (e == 0)
+      for (int q = w; q < nt * gbpr; q += nw) {
+        const int tt = q / gbpr, b = q - tt * gbpr;
+        quantize_block_warp(xs + tt * D + b * QK, min(QK, D - b * QK), a.xq8 + (size_t)(t0 + tt) * gbpr + b);
+      }
+    // This expert's logits for the chunk.
+    if (!have_w) {
+      if (!mbar_wait(&bar, 0)) {
+        if (t == 0) set_error(a.st, ERR_WAIT_TIMEOUT, 20, e, 0);
+        return;
+      }
+      have_w = true;
+    }
+    float part[RT_TC];
+#pragma unroll
+    for (int tt = 0; tt < RT_TC; tt++) part[tt] = 0.f;
+    for (int i = t; i < D; i += RT_THREADS) {
+      const float wv = wr[i];
+#pragma unroll
+      for (int tt = 0; tt < RT_TC; tt++)
+        if (tt < nt) part[tt] = __fmaf_rn(wv, xs[tt * D + i], part[tt]);
+    }
+#pragma unroll
+    for (int tt = 0; tt < RT_TC; tt++)
+      if (tt < nt) {
+        const float v = warp_sum(part[tt]);
+        if (lane == 0) red[w][tt] = v;
+      }
+    __syncthreads();
+    if (t < nt) {
+      float acc = 0.f;
+      for (int j = 0; j < nw; j++) acc = fadd(acc, red[j][t]);
+      a.logits[(size_t)(t0 + t) * E + e] = a.router_b ? fadd(acc, a.router_b[e]) : acc;
     }
     __syncthreads();
   }
-  if (blockIdx.x == 0 && a.zero_out)
-    for (size_t i = t; i < (size_t)T * D; i += blockDim.x) a.zero_out[i] = 0.f;
+  if (e == 0 && a.zero_out)
+    for (size_t i = t; i < (size_t)T * D; i += RT_THREADS) a.zero_out[i] = 0.f;
 
   // The last CTA to finish selects experts and builds the plan.
   if (t == 0) {
@@ -104,25 +212,32 @@ __global__ void __launch_bounds__(256) layer_route_kernel(RouteArgs a) {
 
   const int K = a.top_k;
   int* cnt = reinterpret_cast<int*>(sm);   // [E]
-  int* off = cnt + E;                      // [E]
+  int* off = cnt + E;                      // [E] row offset of each expert
   int* slot_of = off + E;                  // [E]
-  for (int i = t; i < E; i += blockDim.x) cnt[i] = 0;
+  int* wsum = slot_of + E;                 // [2][nw] scan scratch
+  int* sidx = wsum + 2 * nw;               // [T][K] selected experts
+  float* sw = reinterpret_cast<float*>(sidx + T * K);   // [T][K] their weights
+  for (int i = t; i < E; i += RT_THREADS) cnt[i] = 0;
   __syncthreads();
-  // Selection: one warp per token.
-  for (int tok = w; tok < T; tok += RT_WARPS) {
+  // Selection: one warp per token; lane l holds logits l, l+32, ... (E <= 256).
+  for (int tok = w; tok < T; tok += nw) {
     const float* lg = a.logits + (size_t)tok * E;
-    float best_v[8];
-    int best_i[8];
-    float m0 = 0.f, sum = 0.f;
-    for (int j = 0; j < K; j++) {
+    float v[8];
+#pragma unroll
+    for (int q = 0; q < 8; q++) v[q] = lane + 32 * q < E ? __ldcg(lg + lane + 32 * q) : -INFINITY;
+    unsigned taken = 0;
+    float bvs[8], ex[8];
+    int bis[8];
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+      if (j >= K) break;
       float bv = -INFINITY;
       int bi = 0x7fffffff;
-      for (int i = lane; i < E; i += 32) {
-        bool taken = false;
-        for (int q = 0; q < j; q++) taken |= (best_i[q] == i);
-        const float v = __ldcg(lg + i);
-        if (!taken && (v > bv || (v == bv && i < bi))) {
-          bv = v;
+#pragma unroll
+      for (int q = 0; q < 8; q++) {
+        const int i = lane + 32 * q;
+        if (i < E && !(taken >> q & 1u) && (v[q] > bv || (v[q] == bv && i < bi))) {
+          bv = v[q];
           bi = i;
         }
       }
@@ -136,75 +251,95 @@ __global__ void __launch_bounds__(256) layer_route_kernel(RouteArgs a) {
         }
       }
       if (bi >= E) {
-        // no candidate compared greater (NaN logits): take the lowest
-        // untaken index with weight 0, so every index stays in range
-        bv = -INFINITY;
-        bi = 0;
-        for (bool hit = true; hit && bi < E;) {
-          hit = false;
-          for (int q = 0; q < j; q++) hit |= (best_i[q] == bi);
-          if (hit) bi++;
+        // nothing compared greater (NaN logits): the lowest untaken index, weight 0
+        bi = E;
+        for (int q = 0; q < 8; q++) {
+          const int i = lane + 32 * q;
+          if (i < E && !(taken >> q & 1u) && i < bi) bi = i;
         }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) bi = min(bi, __shfl_xor_sync(0xffffffffu, bi, o));
+        bv = -INFINITY;
       }
-      best_v[j] = bv;
-      best_i[j] = bi;
+      if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
+      bvs[j] = bv;
+      bis[j] = bi;
     }
-    m0 = best_v[0];
-    float ex[8];
-    for (int j = 0; j < K; j++) {
-      ex[j] = expf(fsub(best_v[j], m0));
-      sum = fadd(sum, ex[j]);
-    }
-    if (lane == 0) {
-      for (int j = 0; j < K; j++) {
-        const float wt = __fdiv_rn(ex[j], sum);
-        a.sel_idx[(size_t)tok * K + j] = best_i[j];
-        a.sel_w[(size_t)tok * K + j] = wt;
-        // experts held by another GPU (no local weights) are skipped here;
-        // their contribution arrives through the cross-GPU sum
-        if (wt != 0.f && a.experts[best_i[j]].gate.main) atomicAdd(&cnt[best_i[j]], 1);
+    float sum = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; j++)
+      if (j < K) {
+        ex[j] = expf(fsub(bvs[j], bvs[0]));
+        sum = fadd(sum, ex[j]);
       }
+    if (lane < K) {
+      // lane j publishes selection j
+      float wt = 0.f;
+      int bi = 0;
+#pragma unroll
+      for (int j = 0; j < 8; j++)
+        if (j == lane) {
+          wt = __fdiv_rn(ex[j], sum);
+          bi = bis[j];
+        }
+      sidx[tok * K + lane] = bi;
+      sw[tok * K + lane] = wt;
+      a.sel_idx[(size_t)tok * K + lane] = bi;
+      a.sel_w[(size_t)tok * K + lane] = wt;
+      // experts held by another GPU (no local weights) are skipped; their
+      // contribution arrives through the cross-GPU sum
+      if (wt != 0.f && a.experts[bi].gate.main) atomicAdd(&cnt[bi], 1);
     }
   }
   __syncthreads();
-  if (t == 0) {
-    int ns = 0, o = 0;
-    for (int i = 0; i < E; i++) {
-      off[i] = o;
-      slot_of[i] = cnt[i] ? ns : -1;
-      if (cnt[i]) ns++;
-      o += cnt[i];
+  // Exclusive scans of row counts and of non-empty experts (E <= 256).
+  {
+    const int c = t < E ? cnt[t] : 0, nz = c > 0;
+    int sc = c, sz = nz;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int a1 = __shfl_up_sync(0xffffffffu, sc, o), a2 = __shfl_up_sync(0xffffffffu, sz, o);
+      if (lane >= o) {
+        sc += a1;
+        sz += a2;
+      }
     }
-    PlanHdr* h = a.plan;
-    h->n_slots = ns;
-    h->total_rows = o;
-    h->k = T;
-    h->embed_dim = D;
-    h->inter_dim = a.I;
-    h->act = a.act;
-    h->assoc_rule = a.assoc_rule;
-    h->bias_term = a.bias_term;
-    h->slots = a.slots;
-    h->rows = a.rows;
-    h->wts = a.wts;
-    h->row_slot = a.row_slot;
+    if (lane == 31) {
+      wsum[w] = sc;
+      wsum[nw + w] = sz;
+    }
+    __syncthreads();
+    int bc = 0, bz = 0;
+    for (int j = 0; j < w; j++) {
+      bc += wsum[j];
+      bz += wsum[nw + j];
+    }
+    if (t < E) {
+      off[t] = bc + sc - c;
+      slot_of[t] = nz ? bz + sz - 1 : -1;
+    }
+    if (t == RT_THREADS - 1) {
+      PlanHdr* h = a.plan;
+      h->n_slots = bz + sz;
+      h->total_rows = bc + sc;
+      h->k = T;
+      h->embed_dim = D;
+      h->inter_dim = a.I;
+      h->act = a.act;
+      h->assoc_rule = a.assoc_rule;
+      h->bias_term = a.bias_term;
+      h->slots = a.slots;
+      h->rows = a.rows;
+      h->wts = a.wts;
+      h->row_slot = a.row_slot;
+    }
   }
   __syncthreads();
-  for (int ex_i = t; ex_i < E; ex_i += blockDim.x) {
+  for (int ex_i = t; ex_i < E; ex_i += RT_THREADS) {
     const int c = cnt[ex_i];
     if (!c) continue;
     int o = off[ex_i];
     const int sl = slot_of[ex_i];
-    for (int tok = 0; tok < T; tok++)
-      for (int j = 0; j < K; j++) {
-        const float wt = a.sel_w[(size_t)tok * K + j];
-        if (a.sel_idx[(size_t)tok * K + j] == ex_i && wt != 0.f) {  // cnt > 0 implies the expert is local
-          a.rows[o] = tok;
-          a.wts[o] = wt;
-          a.row_slot[o] = sl;
-          o++;
-        }
-      }
     const ExpertDesc& X = a.experts[ex_i];
     SlotDesc d;
     d.gate = X.gate;
@@ -214,25 +349,45 @@ __global__ void __launch_bounds__(256) layer_route_kernel(RouteArgs a) {
     d.ub = X.ub;
     d.db = X.db;
     d.n_rows = c;
-    d.row_off = off[ex_i];
+    d.row_off = o;
     d.pad[0] = ex_i;
     d.pad[1] = 0;
+    for (int q = 0; q < T * K; q++)
+      if (sidx[q] == ex_i && sw[q] != 0.f) {
+        a.rows[o] = q / K;
+        a.wts[o] = sw[q];
+        a.row_slot[o] = sl;
+        o++;
+      }
     a.slots[sl] = d;
   }
 }
 
-size_t route_smem_bytes(int D, int E) {
-  const size_t xs = sizeof(float) * (size_t)RT_TC * D, sel = sizeof(int) * 3 * (size_t)E;
+size_t route_smem_bytes(int D, int E, int T, int K) {
+  const size_t xs = sizeof(float) * (size_t)(RT_TC + 1) * D;
+  const size_t sel = sizeof(int) * (3 * (size_t)E + 2 * (RT_THREADS / 32) + 2 * (size_t)T * K);
   return xs > sel ? xs : sel;
 }
 
 cudaError_t launch_layer_route(const RouteArgs& a, cudaStream_t s) {
-  if (a.top_k < 1 || a.top_k > 8 || a.top_k > a.E) return cudaErrorInvalidValue;
-  const size_t smem = route_smem_bytes(a.D, a.E);
+  if (a.top_k < 1 || a.top_k > 8 || a.top_k > a.E || a.E > RT_THREADS) return cudaErrorInvalidValue;
+  const size_t smem = route_smem_bytes(a.D, a.E, a.T, a.top_k);
+  if (smem > 227 * 1024) return cudaErrorInvalidValue;
   cudaError_t e = ensure_smem(reinterpret_cast<const void*>(layer_route_kernel), smem);
   if (e != cudaSuccess) return e;
-  layer_route_kernel<<<(a.E + RT_WARPS - 1) / RT_WARPS, 256, smem, s>>>(a);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(a.E);
+  cfg.blockDim = dim3(RT_THREADS);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  RouteArgs args = a;
+  void* kargs[] = {(void*)&args};
+  return cudaLaunchKernelExC(&cfg, reinterpret_cast<const void*>(layer_route_kernel), kargs);
 }
 
 }  // namespace tg

@@ -107,7 +107,7 @@ struct Ctx {
   bool user_stream_set = false;
   DevStatus* d_status = nullptr;
   DevStatus* h_status = nullptr;  // pinned
-  DevBuf d_stage, d_xq8, d_hidden, d_hq8, d_tmp, d_counters;
+  DevBuf d_stage, d_xq8, d_hidden, d_hq8, d_tmp, d_counters, d_parts;
   PinBuf h_up, h_down;
   int threads = 1;
 };
@@ -117,6 +117,18 @@ static Ctx g;
 cudaStream_t stream() { return g.user_stream_set ? g.user_stream : g.own_stream; }
 
 std::recursive_mutex& ctx_mutex() { return g.mu; }
+
+// Arrival counters owned by resident layers, cleared with the library's own
+// after a device-side error.
+static std::vector<std::pair<void*, size_t>> g_counter_bufs;
+void register_counters(void* p, size_t n) { g_counter_bufs.push_back({p, n}); }
+void unregister_counters(void* p) {
+  for (size_t i = 0; i < g_counter_bufs.size(); i++)
+    if (g_counter_bufs[i].first == p) {
+      g_counter_bufs.erase(g_counter_bufs.begin() + i);
+      return;
+    }
+}
 DevStatus* status_ptr() { return g.d_status; }
 void count_launches(int n) { g_launches += n; }
 void* pinned_up(size_t n) { return g.h_up.reserve(n) ? g.h_up.p : nullptr; }
@@ -175,6 +187,7 @@ bool finish(const char* what) {
     DevStatus st = *g.h_status;
     cudaMemsetAsync(g.d_status, 0, sizeof(DevStatus), s);
     if (g.d_counters.p) cudaMemsetAsync(g.d_counters.p, 0, g.d_counters.n, s);
+    for (auto& c : g_counter_bufs) cudaMemsetAsync(c.first, 0, c.second, s);
     cudaStreamSynchronize(s);
     set_host_error(200 + st.code, "%s: device error %d at site %d (%d, %d)", what, st.code, st.where, st.a, st.b);
     return false;
@@ -452,12 +465,25 @@ bool run_moe(std::vector<HostSlot>& slots, int gate_fmt, int act, int rule, int 
   float* hidden = (float*)g.d_hidden.p;
   Q8Dev* hq8 = (Q8Dev*)g.d_hq8.p;
 
+  // down formats of the call: one pass if uniform, else one pass per format
+  // writing parts, then the ordered combine
+  std::vector<int> dfmts;
+  for (HostSlot* hsl : act_slots)
+    if (std::find(dfmts.begin(), dfmts.end(), hsl->down.fmt) == dfmts.end()) dfmts.push_back(hsl->down.fmt);
+  float* parts = nullptr;
+  if (dfmts.size() > 1) {
+    if (!g.d_parts.reserve(sizeof(float) * (size_t)total * D)) return false;
+    parts = (float*)g.d_parts.p;
+  }
   launch_quantize_rows(d_in, k, D, D, xq8, s);
   if (!cuda_ok(launch_moe_gateup(dph, n, gate_fmt, D, I, xq8, hidden, hq8, (int*)g.d_counters.p, g.d_status, s),
-               what) ||
-      !cuda_ok(launch_moe_down(dph, D, I, hq8, hidden, d_out, g.d_status, s), what))
+               what))
     return false;
-  g_launches += 3;
+  for (int f : dfmts)
+    if (!cuda_ok(launch_moe_down(dph, n, total, f, D, I, k, hq8, hidden, d_out, parts, g.d_status, s), what))
+      return false;
+  if (parts && !cuda_ok(launch_combine_parts(dph, D, k, parts, d_out, s), what)) return false;
+  g_launches += 2 + (int)dfmts.size() + (parts ? 1 : 0);
   if (!cuda_ok(cudaMemcpyAsync(g.h_down.p, d_out, sizeof(float) * (size_t)k * D, cudaMemcpyDeviceToHost, s), what))
     return false;
   if (!finish(what)) return false;

@@ -20,5 +20,7 @@ DevStatus* status_ptr();
 void count_launches(int n);
 void* pinned_up(size_t n);
 void* pinned_down(size_t n);
+void register_counters(void* p, size_t n);
+void unregister_counters(void* p);
 
 }  // namespace tg
