@@ -7,7 +7,7 @@
  * on the product path.  It is pinned against the reference itself: the
  * reference's csrc/libtinygiant.c compiled unmodified through
  * oracle/neon_shim/arm_neon.h into oracle/_ref/libtinygiant_ref.so
- * (tests/test_oracle_vs_ref.py), and against gguf-py's independent block
+ * (tests/test_oracle_golden.py), and against gguf-py's independent block
  * decoders (tests/golden/).
  *
  * Every function restates the reference algorithm in scalar C with the same

@@ -3,8 +3,8 @@
 // Block formats are TinyGiant's (csrc/libtinygiant.c:22-24, 159-166, 511-514,
 // 574, 594): Q4_K 144 B / 256 values, Q6_K 210 B / 256, MXFP4 17 B / 32,
 // Q8_0 34 B / 32, F16 2 B / value.  In HBM every quantized matrix is stored
-// repacked so each per-block payload starts on a 16-byte boundary (see
-// tg_layout.cuh); the values are unchanged.
+// repacked so each per-block payload starts on a 16-byte boundary (WDesc
+// below); the values are unchanged.
 #pragma once
 #include <cstdint>
 #include <cuda_runtime.h>
