@@ -229,6 +229,25 @@ int tg_cuda_debug_row_isums(int fmt, const void *mat, int nrows, int ncols, cons
 void tg_pack_q4k(const float *w, int rows, int cols, uint8_t *out);
 void tg_pack_q6k(const float *w, int rows, int cols, uint8_t *out);
 
+/* ---- Allocation-free matvec -------------------------------------------- *
+ * No counterpart in the reference: an extension for callers that cannot
+ * allocate device memory.  out[r] = row r of a Q4_K matrix . input, the
+ * arithmetic of tg_matmul_q4k (bit-identical to it), with every pointer
+ * caller-owned device memory on the current device: q4_matrix (16-byte
+ * aligned, nrows x ncols/256 blocks of 144 bytes, the reference layout),
+ * input[ncols], output[nrows].  Enqueued on `stream` (a cudaStream_t; NULL is
+ * the default stream) and asynchronous: the caller synchronises.
+ * Allocates nothing: the Q8 copy of the input lives in a fixed 80 KiB
+ * __device__ array that each GPU loading the library holds until exit, so
+ * ncols is limited to 65536 (larger sizes are rejected with error 3).
+ * Calls that overlap on one device (several streams or host threads in
+ * flight at once) race on that scratch: order them on one stream.  The first
+ * call on each device looks up the scratch address; make it outside any
+ * stream capture.  Returns 0 when enqueued, else the error code that
+ * tg_cuda_last_error reports. */
+int tg_cuda_matmul_q4k_noalloc(const uint8_t *q4_matrix, const float *input, float *output, int nrows, int ncols,
+                               void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -76,6 +76,7 @@ EXT = {
     "tg_cuda_synchronize": ([], CI),
     "tg_pack_q4k": ([VP, CI, CI, VP], None),
     "tg_pack_q6k": ([VP, CI, CI, VP], None),
+    "tg_cuda_matmul_q4k_noalloc": ([VP, VP, VP, CI, CI, VP], CI),
 }
 
 
