@@ -190,6 +190,14 @@ size_t tg_layer_expert_bytes(void *layer, int expert);
  * x_out = x' (may be NULL).  Asynchronous on the library stream. */
 int tg_layer_forward_dev(void *layer, const float *x, const float *add, float *x_out, float *moe_out, int T,
                          int normalize, const float *norm_w);
+/* 1 (default): a step runs as one persistent kernel when the batch is
+ * decode-sized (T <= 8) and the formats have one; 0: three kernels (router,
+ * gate/up, down).  Same results either way.  Returns the previous setting. */
+int tg_layer_set_fused(void *layer, int on);
+/* Diagnostics: fused steps launched after this call write per-CTA phase
+ * timestamps (16 uint64 per CTA: SM clocks, and the global timer in slots
+ * 12/13) into dev_buf; NULL stops it.  Returns the step's grid size. */
+int tg_cuda_step_trace(void *dev_buf);
 /* Host buffers, synchronous: out[T][D] += experts(normalize ? rmsnorm(x) : x). */
 int tg_layer_forward(void *layer, const float *x_host, float *out_host, int T, int normalize);
 /* Selected experts and weights [T][top_k] of the layer's last step. */

@@ -52,6 +52,37 @@ def test_layer_matches_reference_pipeline(gpu, oracle, qwen16, T):
     assert rel_err(got, want) <= TOL
 
 
+@pytest.mark.parametrize("T", [1, 3, 8])
+def test_fused_step_matches_three_kernel_path(gpu, qwen16, T):
+    """The single-kernel step and the three-kernel step route and compute alike."""
+    L, R = qwen16
+    x = np.random.default_rng(300 + T).standard_normal((T, 2048)).astype(np.float32)
+    outs, routes = [], []
+    for fused in (True, False):
+        R.set_fused(fused)
+        outs.append(R.forward(x, normalize=True))
+        routes.append(R.last_routing(T))
+    R.set_fused(True)
+    N = synth.rms_norm(x)
+    for idx, w in routes:
+        routing_agrees(L, N, idx, w)
+    if np.array_equal(routes[0][0], routes[1][0]):
+        assert rel_err(outs[0], outs[1]) <= TOL
+
+
+def test_fused_step_more_experts_than_sms(gpu, oracle):
+    """200 experts: some CTAs hold two router rows."""
+    L = synth.qwen_layer(seed=7, n_experts=200, D=512, I=256)
+    R = ResidentLayer(L, max_tokens=4, lib=gpu)
+    N = synth.rms_norm(np.random.default_rng(8).standard_normal((4, 512)).astype(np.float32))
+    got = R.forward(N, normalize=False)
+    idx, w = R.last_routing(4)
+    routing_agrees(L, N, idx, w)
+    want = M.moe_layer_forward(oracle, L, N)
+    assert rel_err(got, want) <= TOL
+    R.close()
+
+
 def test_layer_rmsnorm_in_kernel(gpu, oracle, qwen16):
     L, R = qwen16
     x = np.random.default_rng(9).standard_normal((2, 2048)).astype(np.float32) * 3

@@ -3,8 +3,8 @@
 // Block formats are TinyGiant's (csrc/libtinygiant.c:22-24, 159-166, 511-514,
 // 574, 594): Q4_K 144 B / 256 values, Q6_K 210 B / 256, MXFP4 17 B / 32,
 // Q8_0 34 B / 32, F16 2 B / value.  In HBM every quantized matrix is stored
-// repacked so each per-block payload starts on a 16-byte boundary (WDesc
-// below); the values are unchanged.
+// re-laid out so each row is one 16-byte-aligned window (WDesc below); the
+// values are unchanged.
 #pragma once
 #include <cstdint>
 #include <cuda_runtime.h>
@@ -41,12 +41,17 @@ struct __align__(16) Q8Dev {
 };
 static_assert(sizeof(Q8Dev) == 320, "Q8Dev layout");
 
-// A weight matrix resident in HBM in the repacked layout.
-//   Q4_K : main = raw 144-byte blocks, rows x bpr
-//   Q6_K : main = 192 B/block (ql[128] | qh[64]); aux1 = int8 scales 16 B/block; aux2 = fp16 d 2 B/block
-//   MXFP4: main = 16 B/block codes; aux1 = e8m0 1 B/block
-//   Q8_0 : main = 32 B/block int8; aux2 = fp16 d 2 B/block
-//   F16  : main = raw fp16 rows
+// A weight matrix resident in HBM.  Rows are stored one after the other,
+// rs bytes apart, each row holding all of its own data (one contiguous
+// window per row, so a row moves in one bulk copy):
+//   Q4_K : the raw 144-byte blocks                          rs = 144 bpr
+//   Q6_K : ql|qh 192 B/block, then int8 scales 16 B/block, then fp16 d
+//          2 B/block, zero-padded to 16 bytes                rs = round16(210 bpr)
+//   MXFP4: codes 16 B/block, then e8m0 1 B/block, padded     rs = round16(17 nsub)
+//   Q8_0 : int8 32 B/block, then fp16 d 2 B/block, padded    rs = round16(34 nsub)
+//   F16  : raw fp16 values                                   rs = 2 cols
+// main, aux1 and aux2 point at row 0's blocks, scales (Q6_K int8 scales,
+// MXFP4 e8m0) and fp16 d values (Q6_K, Q8_0); row r's are rs * r further on.
 struct WDesc {
   const uint8_t* main;
   const uint8_t* aux1;
@@ -54,8 +59,24 @@ struct WDesc {
   int fmt;
   int rows;
   int cols;
-  int pad;
+  int rs;
 };
+
+// Row stride and the offsets of aux1 / aux2 inside a row (-1: none).
+struct RowLayout {
+  int rs, a1, a2;
+};
+
+__host__ __device__ __forceinline__ RowLayout row_layout(int fmt, int cols) {
+  const int bpr = cols / QK, nsub = cols / 32;
+  switch (fmt) {
+    case FMT_Q4K: return {bpr * Q4K_BYTES, -1, -1};
+    case FMT_Q6K: return {(bpr * Q6K_BYTES + 15) & ~15, bpr * 192, bpr * 208};
+    case FMT_MXFP4: return {(nsub * MXFP4_BYTES + 15) & ~15, nsub * 16, -1};
+    case FMT_Q80: return {(nsub * Q80_BYTES + 15) & ~15, -1, nsub * 32};
+    default: return {cols * 2, -1, -1};
+  }
+}
 
 // ---------------------------------------------------------------------
 // Exact scalar decoders.

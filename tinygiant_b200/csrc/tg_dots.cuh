@@ -215,31 +215,28 @@ __device__ __forceinline__ bool row_terms(const WDesc& W, int r, int p, const Q8
   Q8Ref xr;
   switch (W.fmt) {
     case FMT_Q4K: {
-      int bpr = W.cols / QK;
       for (int t = 0; t < n; t++) xr.blk[t] = xrow[t] + p;
-      q4k_terms(W.main + ((size_t)r * bpr + p) * Q4K_BYTES, xr, n, x4, out);
+      q4k_terms(W.main + (size_t)r * W.rs + (size_t)p * Q4K_BYTES, xr, n, x4, out);
       return true;
     }
     case FMT_Q6K: {
-      int bpr = W.cols / QK;
-      size_t bi = (size_t)r * bpr + p;
+      const size_t ro = (size_t)r * W.rs;
       for (int t = 0; t < n; t++) xr.blk[t] = xrow[t] + p;
-      q6k_terms(W.main + bi * 192, W.aux1 + bi * 16, W.aux2 + bi * 2, xr, n, out);
+      q6k_terms(W.main + ro + (size_t)p * 192, W.aux1 + ro + (size_t)p * 16, W.aux2 + ro + (size_t)p * 2, xr, n, out);
       return true;
     }
     case FMT_MXFP4: {
-      int nsub = W.cols / 32;
-      size_t bi = (size_t)r * nsub + p;
+      const size_t ro = (size_t)r * W.rs;
       for (int t = 0; t < n; t++) xr.blk[t] = xrow[t] + (p >> 3);
-      mxfp4_terms(W.main + bi * 16, __ldg(W.aux1 + bi), p, xr, n, out);
+      mxfp4_terms(W.main + ro + (size_t)p * 16, __ldg(W.aux1 + ro + p), p, xr, n, out);
       return true;
     }
     case FMT_Q80: {
-      int nsub = W.cols / 32;
-      size_t bi = (size_t)r * nsub + p;
+      const size_t ro = (size_t)r * W.rs;
       for (int t = 0; t < n; t++) xr.blk[t] = xrow[t] + (p >> 3);
-      uint32_t db = (uint32_t)__ldg(W.aux2 + 2 * bi) | ((uint32_t)__ldg(W.aux2 + 2 * bi + 1) << 8);
-      q80_terms(W.main + bi * 32, db, p, xr, n, out);
+      const uint8_t* dp = W.aux2 + ro + 2 * (size_t)p;
+      uint32_t db = (uint32_t)__ldg(dp) | ((uint32_t)__ldg(dp + 1) << 8);
+      q80_terms(W.main + ro + (size_t)p * 32, db, p, xr, n, out);
       return true;
     }
     default:

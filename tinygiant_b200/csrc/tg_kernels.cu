@@ -44,7 +44,7 @@ __global__ void __launch_bounds__(256) matvec_kernel(WDesc W, const Q8Dev* __res
   if (W.fmt == FMT_F16) {
     for (int rho = threadIdx.x; rho < nr; rho += blockDim.x) {
       const int r = r0 + rho;
-      float v = dot_f16_row(reinterpret_cast<const uint16_t*>(W.main) + (size_t)r * W.cols, x, W.cols);
+      float v = dot_f16_row(reinterpret_cast<const uint16_t*>(W.main + (size_t)r * W.rs), x, W.cols);
       out[r] = bias_term ? fadd(v, bias ? bias[r] : 0.f) : v;
     }
     return;
@@ -128,27 +128,38 @@ __global__ void add_kernel(const float* __restrict__ a, const float* __restrict_
   if (i < n) out[i] = fadd(a[i], b[i]);
 }
 
-// Raw reference blocks -> HBM layout (tg_common.cuh WDesc).
-__global__ void repack_kernel(const uint8_t* __restrict__ raw, int fmt, long nblocks, uint8_t* __restrict__ mainp,
-                              uint8_t* __restrict__ aux1, uint8_t* __restrict__ aux2) {
+// Raw blocks (rows x nb of the reference's layout) -> the row layout of
+// WDesc; one thread per block, the row's first block also zeroes its padding.
+__global__ void repack_kernel(const uint8_t* __restrict__ raw, int fmt, int rows, int cols, uint8_t* __restrict__ dst) {
+  const RowLayout L = row_layout(fmt, cols);
+  const int nb = (fmt == FMT_Q6K) ? cols / QK : cols / 32;
   const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= nblocks) return;
+  if (i >= (long)rows * nb) return;
+  const long row = i / nb;
+  const int b = (int)(i - row * nb);
+  uint8_t* d = dst + row * L.rs;
+  int used = 0;
   if (fmt == FMT_Q6K) {
-    const uint8_t* b = raw + i * Q6K_BYTES;
-    for (int j = 0; j < 192; j++) mainp[i * 192 + j] = b[j];
-    for (int j = 0; j < 16; j++) aux1[i * 16 + j] = b[192 + j];
-    aux2[i * 2] = b[208];
-    aux2[i * 2 + 1] = b[209];
+    const uint8_t* s = raw + i * Q6K_BYTES;
+    for (int j = 0; j < 192; j++) d[b * 192 + j] = s[j];
+    for (int j = 0; j < 16; j++) d[L.a1 + b * 16 + j] = s[192 + j];
+    d[L.a2 + b * 2] = s[208];
+    d[L.a2 + b * 2 + 1] = s[209];
+    used = nb * Q6K_BYTES;
   } else if (fmt == FMT_MXFP4) {
-    const uint8_t* b = raw + i * MXFP4_BYTES;
-    aux1[i] = b[0];
-    for (int j = 0; j < 16; j++) mainp[i * 16 + j] = b[1 + j];
+    const uint8_t* s = raw + i * MXFP4_BYTES;
+    d[L.a1 + b] = s[0];
+    for (int j = 0; j < 16; j++) d[b * 16 + j] = s[1 + j];
+    used = nb * MXFP4_BYTES;
   } else if (fmt == FMT_Q80) {
-    const uint8_t* b = raw + i * Q80_BYTES;
-    aux2[i * 2] = b[0];
-    aux2[i * 2 + 1] = b[1];
-    for (int j = 0; j < 32; j++) mainp[i * 32 + j] = b[2 + j];
+    const uint8_t* s = raw + i * Q80_BYTES;
+    d[L.a2 + b * 2] = s[0];
+    d[L.a2 + b * 2 + 1] = s[1];
+    for (int j = 0; j < 32; j++) d[b * 32 + j] = s[2 + j];
+    used = nb * Q80_BYTES;
   }
+  if (b == 0)
+    for (int j = used; j < L.rs; j++) d[j] = 0;
 }
 
 // Test hook: the exact int32 sub-block sums of every row of W against one
@@ -161,22 +172,22 @@ __global__ void debug_isums_kernel(WDesc W, const Q8Dev* __restrict__ xq, int32_
   const int r = (int)(i / units), p = (int)(i % units);
   if (W.fmt == FMT_Q4K) {
     uint32_t w[36];
-    load_words(W.main + ((size_t)r * units + p) * Q4K_BYTES, w, 9);
+    load_words(W.main + (size_t)r * W.rs + (size_t)p * Q4K_BYTES, w, 9);
     int is[8];
     q4k_isums(w, reinterpret_cast<const int*>(xq[p].qs), is);
     for (int j = 0; j < 8; j++) out[i * 8 + j] = is[j];
   } else if (W.fmt == FMT_Q6K) {
     uint32_t w[48];
-    load_words(W.main + ((size_t)r * units + p) * 192, w, 12);
+    load_words(W.main + (size_t)r * W.rs + (size_t)p * 192, w, 12);
     int is[16];
     q6k_isums(w, reinterpret_cast<const int*>(xq[p].qs), is);
     for (int j = 0; j < 16; j++) out[i * 16 + j] = is[j];
   } else if (W.fmt == FMT_MXFP4) {
-    uint4 cv = ldg16(W.main + ((size_t)r * units + p) * 16);
+    uint4 cv = ldg16(W.main + (size_t)r * W.rs + (size_t)p * 16);
     uint32_t cw[4] = {cv.x, cv.y, cv.z, cv.w};
     out[i] = mxfp4_isum(cw, reinterpret_cast<const int*>(xq[p >> 3].qs) + (p & 7) * 8);
   } else if (W.fmt == FMT_Q80) {
-    const uint8_t* q = W.main + ((size_t)r * units + p) * 32;
+    const uint8_t* q = W.main + (size_t)r * W.rs + (size_t)p * 32;
     uint4 a = ldg16(q), b = ldg16(q + 16);
     int qw[8] = {(int)a.x, (int)a.y, (int)a.z, (int)a.w, (int)b.x, (int)b.y, (int)b.z, (int)b.w};
     out[i] = q80_isum(qw, reinterpret_cast<const int*>(xq[p >> 3].qs) + (p & 7) * 8);
@@ -231,10 +242,10 @@ void launch_debug_isums(const WDesc& W, const Q8Dev* xq, int32_t* out, cudaStrea
   debug_isums_kernel<<<(unsigned)((n + 127) / 128), 128, 0, s>>>(W, xq, out);
 }
 
-void launch_repack(const uint8_t* raw, int fmt, long nblocks, uint8_t* mainp, uint8_t* aux1, uint8_t* aux2,
-                   cudaStream_t s) {
+void launch_repack(const uint8_t* raw, int fmt, int rows, int cols, uint8_t* dst, cudaStream_t s) {
+  const long nblocks = (long)rows * ((fmt == FMT_Q6K) ? cols / QK : cols / 32);
   if (nblocks <= 0) return;
-  repack_kernel<<<(unsigned)((nblocks + 255) / 256), 256, 0, s>>>(raw, fmt, nblocks, mainp, aux1, aux2);
+  repack_kernel<<<(unsigned)((nblocks + 255) / 256), 256, 0, s>>>(raw, fmt, rows, cols, dst);
 }
 
 }  // namespace tg

@@ -39,6 +39,8 @@ struct Layer {
   float* hidden = nullptr;
   Q8Dev* hq8 = nullptr;
   int* counters = nullptr;
+  unsigned long long* step_sync = nullptr;   // grid-barrier arrival count of the fused step kernel
+  bool fused = true;               // use the fused step kernel when the shape allows
   float* moe_out = nullptr;  // [2][max_tokens][D] for stacks and the host entry
   float* xbuf = nullptr;     // [max_tokens][D]
 };
@@ -72,12 +74,15 @@ static bool alloc_scratch(Layer* L) {
          dmalloc(L, (void**)&L->hq8, sizeof(Q8Dev) * (size_t)L->max_rows * dbpr) &&
          dmalloc(L, (void**)&L->counters, sizeof(int) * moe_counter_ints(L->max_slots, I)) &&
          (register_counters(L->counters, sizeof(int) * moe_counter_ints(L->max_slots, I)), true) &&
+         dmalloc(L, (void**)&L->step_sync, sizeof(unsigned long long)) &&
+         (register_counters(L->step_sync, sizeof(unsigned long long)), true) &&
          dmalloc(L, (void**)&L->moe_out, sizeof(float) * 2 * (size_t)T * D) &&
          dmalloc(L, (void**)&L->xbuf, sizeof(float) * (size_t)T * D);
 }
 
 static void free_layer(Layer* L) {
   if (L->counters) unregister_counters(L->counters);
+  if (L->step_sync) unregister_counters(L->step_sync);
   for (void* p : L->owned) cudaFree(p);
   delete L;
 }
@@ -89,6 +94,43 @@ static bool layer_enqueue(Layer* L, const float* x, const float* add, float* x_o
   if (T < 1 || T > L->max_tokens) {
     set_host_error(3, "%s: %d rows exceed the layer's max_tokens %d", what, T, L->max_tokens);
     return false;
+  }
+  StepLaunch sl{};
+  sl.x_in = x;
+  sl.add_in = add;
+  sl.x_out = x_out;
+  sl.norm_w = norm_w;
+  sl.eps = 1e-6f;
+  sl.normalize = normalize;
+  sl.router_w = L->router_w;
+  sl.router_b = L->router_b;
+  sl.T = T;
+  sl.D = L->D;
+  sl.E = L->E;
+  sl.top_k = L->top_k;
+  sl.I = L->I;
+  sl.act = L->act;
+  sl.assoc_rule = ASSOC_MOE;
+  sl.bias_term = 1;
+  sl.gate_fmt = L->gate_fmt;
+  sl.down_fmt = L->down_fmt;
+  sl.experts = L->d_experts;
+  sl.xq8 = L->xq8;
+  sl.logits = L->logits;
+  sl.hidden = L->hidden;
+  sl.out = moe_out;
+  sl.sel_idx = L->sel_idx;
+  sl.sel_w = L->sel_w;
+  sl.sync = L->step_sync;
+  sl.st = status_ptr();
+  if (L->fused && step_eligible(sl)) {
+    const cudaError_t e = launch_layer_step(sl, s);
+    count_launches(1);
+    if (e != cudaSuccess) {
+      set_host_error(100 + (int)e, "%s: %s", what, cudaGetErrorString(e));
+      return false;
+    }
+    return true;
   }
   RouteArgs a{};
   a.x_in = x;
@@ -242,27 +284,18 @@ void* tg_layer_clone(void* handle) {
   L->act = src->act;
   L->top_k = src->top_k;
   L->max_tokens = src->max_tokens;
+  L->fused = src->fused;
   L->experts = src->experts;
   auto copy_w = [&](WDesc& w) -> bool {
     if (!w.main) return true;   // expert held by another GPU
-    const uint8_t* srcs[3] = {w.main, w.aux1, w.aux2};
-    const size_t nblk = w.fmt == FMT_Q6K ? (size_t)w.rows * (w.cols / QK) : (size_t)w.rows * (w.cols / 32);
-    size_t sizes[3] = {0, 0, 0};
-    switch (w.fmt) {
-      case FMT_Q4K: sizes[0] = (size_t)w.rows * host_row_bytes(FMT_Q4K, w.cols); break;
-      case FMT_Q6K: sizes[0] = nblk * 192; sizes[1] = nblk * 16; sizes[2] = nblk * 2; break;
-      case FMT_MXFP4: sizes[0] = nblk * 16; sizes[1] = nblk; break;
-      case FMT_Q80: sizes[0] = nblk * 32; sizes[2] = nblk * 2; break;
-      default: sizes[0] = (size_t)w.rows * w.cols * 2; break;
-    }
-    const uint8_t** dst[3] = {&w.main, &w.aux1, &w.aux2};
-    for (int i = 0; i < 3; i++) {
-      if (!sizes[i]) continue;
-      void* p = nullptr;
-      if (!dmalloc(L, &p, sizes[i] + 64)) return false;
-      if (cudaMemcpy(p, srcs[i], sizes[i], cudaMemcpyDeviceToDevice) != cudaSuccess) return false;
-      *dst[i] = (const uint8_t*)p;
-    }
+    const size_t bytes = (size_t)w.rows * w.rs;
+    void* p = nullptr;
+    if (!dmalloc(L, &p, bytes + 64)) return false;
+    if (cudaMemcpy(p, w.main, bytes, cudaMemcpyDeviceToDevice) != cudaSuccess) return false;
+    const uint8_t* m = (const uint8_t*)p;
+    if (w.aux1) w.aux1 = m + (w.aux1 - w.main);
+    if (w.aux2) w.aux2 = m + (w.aux2 - w.main);
+    w.main = m;
     return true;
   };
   for (auto& X : L->experts)
@@ -303,6 +336,27 @@ size_t tg_layer_expert_bytes(void* handle, int e) {
 // Device-resident step, enqueued on the library stream (no synchronisation):
 // x' = x + add (add may be NULL), N = normalize ? rmsnorm(x') * norm_w : x',
 // moe_out = sum over the selected experts (cleared first), x_out = x' (may be NULL).
+// Diagnostics: fused steps launched after this call record per-CTA phase
+// timestamps into dev_buf ([grid][16] uint64, device memory); NULL stops it.
+// Returns the grid size a fused step uses.
+int tg_cuda_step_trace(void* dev_buf) {
+  set_step_trace(dev_buf);
+  int dev = 0, sms = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  return sms;
+}
+
+// Selects the fused single-kernel step (on = 1, the default) or the
+// three-kernel step (on = 0) for this layer.  Returns the previous setting.
+int tg_layer_set_fused(void* handle, int on) {
+  Layer* L = static_cast<Layer*>(handle);
+  if (!L) return -1;
+  const int prev = L->fused ? 1 : 0;
+  L->fused = on != 0;
+  return prev;
+}
+
 int tg_layer_forward_dev(void* handle, const float* x, const float* add, float* x_out, float* moe_out, int T,
                          int normalize, const float* norm_w) {
   std::lock_guard<std::recursive_mutex> lk(ctx_mutex());

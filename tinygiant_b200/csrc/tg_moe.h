@@ -13,11 +13,13 @@ cudaError_t launch_moe_gateup(const PlanHdr* ph, int max_slots, int gate_fmt, in
 // with parts_out ([total_rows][D]), the slots of that format only, storing
 // their parts for launch_combine_parts.  T: the call's input rows;
 // max_slots / max_rows: upper bounds of the plan's slots and active rows.
+// hq8 ([max_rows][ceil(I/256)]) receives the Q8 blocks of hidden when
+// max_rows is too large for the down kernel to quantize them itself.
 cudaError_t launch_moe_down(const PlanHdr* ph, int max_slots, int max_rows, int down_fmt_all, int D, int I, int T,
-                            const Q8Dev* hq8, const float* hidden, float* out, float* parts_out, DevStatus* st,
+                            Q8Dev* hq8, const float* hidden, float* out, float* parts_out, DevStatus* st,
                             cudaStream_t s);
 cudaError_t launch_combine_parts(const PlanHdr* ph, int D, int T, const float* parts, float* out, cudaStream_t s);
-// Ints of zero-initialised counter space moe_gateup needs for max_slots slots.
+// Ints of zero-initialised counter space the expert kernels need.
 size_t moe_counter_ints(int max_slots, int I);
 
 struct RouteArgs {
@@ -46,6 +48,35 @@ struct RouteArgs {
 };
 
 size_t route_smem_bytes(int D, int E, int T, int K);
+
+// One layer step (routing + experts) as a single persistent kernel, for
+// decode-sized batches (tg_step.cu).  `out` is overwritten with the MoE
+// output.
+struct StepLaunch {
+  const float* x_in;
+  const float* add_in;
+  float* x_out;
+  const float* norm_w;
+  float eps;
+  int normalize;
+  const float* router_w;
+  const float* router_b;
+  int T, D, E, top_k, I, act, assoc_rule, bias_term, gate_fmt, down_fmt;
+  const ExpertDesc* experts;
+  Q8Dev* xq8;         // [T][ceil(D/256)]
+  float* logits;      // [T][E]
+  float* hidden;      // [T*top_k][I]
+  float* out;         // [T][D]
+  int* sel_idx;       // [T][top_k]
+  float* sel_w;       // [T][top_k]
+  unsigned long long* sync;   // grid-barrier arrival count, zero at creation
+  DevStatus* st;
+};
+bool step_eligible(const StepLaunch& l);
+cudaError_t launch_layer_step(const StepLaunch& l, cudaStream_t s);
+// Diagnostics: later step launches write [grid][16] phase timestamps to p
+// (device memory; null turns it off).
+void set_step_trace(void* p);
 cudaError_t launch_layer_route(const RouteArgs& a, cudaStream_t s);
 
 }  // namespace tg

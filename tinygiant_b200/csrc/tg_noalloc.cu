@@ -86,7 +86,7 @@ extern "C" int tg_cuda_matmul_q4k_noalloc(const uint8_t* q4_matrix, const float*
   Q8Dev* xq8 = noalloc_scratch(dev);
   if (!xq8) return 100;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  WDesc w{q4_matrix, nullptr, nullptr, FMT_Q4K, nrows, ncols, 0};
+  WDesc w{q4_matrix, nullptr, nullptr, FMT_Q4K, nrows, ncols, (ncols / QK) * Q4K_BYTES};
   launch_quantize_rows(input, 1, ncols, ncols, xq8, s);
   e = cudaGetLastError();
   if (e == cudaSuccess) e = launch_matvec(w, xq8, input, nullptr, 0, output, nullptr, s);

@@ -31,53 +31,6 @@ __device__ __forceinline__ float warp_sum(float v) {
   return v;
 }
 
-// Warp-level quantize_q8 of one 256-value block (tg_q8.cuh semantics): lane l
-// holds values 8l..8l+7 (valid below n).
-__device__ __forceinline__ void quantize_block_warp(const float* src, int n, Q8Dev* o) {
-  const int lane = threadIdx.x & 31;
-  float v[8];
-  float a = 0.f;
-#pragma unroll
-  for (int j = 0; j < 8; j++) {
-    const int i = lane * 8 + j;
-    v[j] = i < n ? src[i] : 0.f;
-    if (i < n) a = max_nan(a, fabsf(v[j]));
-  }
-#pragma unroll
-  for (int off = 16; off > 0; off >>= 1) a = max_nan(a, __shfl_xor_sync(0xffffffffu, a, off));
-  const float inv = a > 0.f ? __fdiv_rn(127.f, a) : 0.f;
-  int q[8], s = 0;
-#pragma unroll
-  for (int j = 0; j < 8; j++) {
-    const int i = lane * 8 + j;
-    q[j] = 0;
-    if (i < n) {
-      const float sv = __fmul_rn(v[j], inv);
-      q[j] = (sv != sv) ? 0 : __float2int_rn(sv);
-    }
-    s += q[j];
-  }
-  uint32_t w0 = 0, w1 = 0;
-#pragma unroll
-  for (int j = 0; j < 4; j++) {
-    w0 |= ((uint32_t)q[j] & 0xFFu) << (8 * j);
-    w1 |= ((uint32_t)q[4 + j] & 0xFFu) << (8 * j);
-  }
-  reinterpret_cast<uint2*>(o->qs)[lane] = make_uint2(w0, w1);
-  // bsums: 4 lanes per 32-value sub-block
-  int bs = s;
-  bs += __shfl_xor_sync(0xffffffffu, bs, 1);
-  bs += __shfl_xor_sync(0xffffffffu, bs, 2);
-  if ((lane & 3) == 0) o->bsums[lane >> 2] = bs;
-  int tot = s;
-#pragma unroll
-  for (int off = 16; off > 0; off >>= 1) tot += __shfl_xor_sync(0xffffffffu, tot, off);
-  if (lane == 0) {
-    o->scale = __fdiv_rn(a, 127.f);
-    o->sum = tot;
-  }
-}
-
 __global__ void __launch_bounds__(RT_THREADS) layer_route_kernel(RouteArgs a) {
   extern __shared__ __align__(16) float sm[];
   __shared__ float red[RT_THREADS / 32][RT_TC];

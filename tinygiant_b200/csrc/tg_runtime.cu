@@ -287,14 +287,12 @@ static bool in_registered_range(uintptr_t p, size_t n) {
 // Copies raw host bytes to HBM in the layout of WDesc w (already allocated).
 static bool upload_into(const uint8_t* h, size_t raw, const WDesc& w) {
   cudaStream_t s = stream();
-  const long nblk = w.fmt == FMT_Q6K ? (long)w.rows * (w.cols / QK)
-                  : (w.fmt == FMT_MXFP4 || w.fmt == FMT_Q80) ? (long)w.rows * (w.cols / 32) : 0;
-  if (nblk == 0) {
+  if (!(w.fmt == FMT_Q6K || w.fmt == FMT_MXFP4 || w.fmt == FMT_Q80)) {
     if (!cuda_ok(cudaMemcpyAsync((void*)w.main, h, raw, cudaMemcpyHostToDevice, s), "upload weights")) return false;
   } else {
     if (!g.d_tmp.reserve(raw)) return false;
     if (!cuda_ok(cudaMemcpyAsync(g.d_tmp.p, h, raw, cudaMemcpyHostToDevice, s), "upload weights")) return false;
-    launch_repack((const uint8_t*)g.d_tmp.p, w.fmt, nblk, (uint8_t*)w.main, (uint8_t*)w.aux1, (uint8_t*)w.aux2, s);
+    launch_repack((const uint8_t*)g.d_tmp.p, w.fmt, w.rows, w.cols, (uint8_t*)w.main, s);
     g_launches++;
   }
   return cuda_ok(cudaStreamSynchronize(s), "upload weights");
@@ -324,29 +322,19 @@ bool lookup_matrix(const void* hp, int fmt, int rows, int cols, WDesc* out) {
   e.w.fmt = fmt;
   e.w.rows = rows;
   e.w.cols = cols;
-  if (fmt == FMT_Q6K) {
-    size_t nb = (size_t)rows * (cols / QK);
-    uint8_t* m = g_slab.alloc(nb * 192);
-    uint8_t* a1 = g_slab.alloc(nb * 16);
-    uint8_t* a2 = g_slab.alloc(nb * 2);
-    if (!m || !a1 || !a2) return false;
-    e.w.main = m; e.w.aux1 = a1; e.w.aux2 = a2;
-  } else if (fmt == FMT_MXFP4) {
-    size_t nb = (size_t)rows * (cols / 32);
-    uint8_t* m = g_slab.alloc(nb * 16);
-    uint8_t* a1 = g_slab.alloc(nb);
-    if (!m || !a1) return false;
-    e.w.main = m; e.w.aux1 = a1;
-  } else if (fmt == FMT_Q80) {
-    size_t nb = (size_t)rows * (cols / 32);
-    uint8_t* m = g_slab.alloc(nb * 32);
-    uint8_t* a2 = g_slab.alloc(nb * 2);
-    if (!m || !a2) return false;
-    e.w.main = m; e.w.aux2 = a2;
+  if (fmt == FMT_Q4K || fmt == FMT_Q6K || fmt == FMT_MXFP4 || fmt == FMT_Q80 || fmt == FMT_F16) {
+    const RowLayout L = row_layout(fmt, cols);
+    uint8_t* m = g_slab.alloc((size_t)rows * L.rs);
+    if (!m) return false;
+    e.w.main = m;
+    e.w.aux1 = L.a1 >= 0 ? m + L.a1 : nullptr;
+    e.w.aux2 = L.a2 >= 0 ? m + L.a2 : nullptr;
+    e.w.rs = L.rs;
   } else {
     uint8_t* m = g_slab.alloc(raw);
     if (!m) return false;
     e.w.main = m;
+    e.w.rs = fmt == -1 ? cols * 4 : 4;
   }
   take_sample(h, raw, e.sample);
   if (!upload_into(h, raw, e.w)) return false;

@@ -1,0 +1,891 @@
+// tg_step.cu — one MoE layer step for decode-sized batches (T <= 8) as a
+// single persistent kernel.
+//
+// The step is the engine's MoE block (tinygiant/engine.py:281-342) followed by
+// tg_moe_forward_rows_v2 (csrc/libtinygiant.c:1386-1437):
+//   R  x' = x + add; N = x' / sqrt(mean(x'^2) + eps) * w; logits = W_r N (+ b);
+//      Q8 blocks of N                                  (router.py:29-33, 169-208)
+//   S  top-k by descending logit, softmax over the selected, union of the
+//      selected experts ascending by id, active rows in token order
+//                                                      (router.py:35-42, engine.py:297-318)
+//   A  gate.x, up.x (+ biases), activation -> hidden   (moe_phase_a, 1279-1327)
+//   B  Q8 of hidden, down.hidden, part = w * (v + b), combine in expert order
+//                                                      (moe_phase_b 1329-1384, 1428-1434)
+// One CTA per SM.  R runs on one warp per expert; a grid barrier makes the
+// logits and N's Q8 blocks visible; every CTA then repeats S on its own (it
+// is tiny) instead of waiting for one CTA to publish it.  A and B stream
+// their weight rows through a per-warp ring of shared-memory stages filled
+// by bulk asynchronous copies (cp.async.bulk, no multicast): the ring runs
+// straight from a warp's gate/up items into its down items, so the down
+// weights are in flight while phase A computes; a second grid barrier only
+// orders hidden before phase B reads it.
+//
+// Grid barriers are a self-resetting arrival count plus a generation word;
+// every wait (barrier, mbarrier) gives up after about a second and records
+// an error instead of hanging.  The grid never exceeds the CTAs the GPU holds
+// at once, so all CTAs reach each barrier.
+#include <algorithm>
+
+#include "tg_moe.h"
+#include "tg_q8.cuh"
+#include "tg_warpdot.cuh"
+
+namespace tg {
+
+constexpr int SW = 16;             // warps per CTA
+constexpr int ST_MAX_NST = 8;      // ring stages per warp
+constexpr int STEP_T_MAX = 8;
+constexpr int STEP_K_MAX = 8;
+constexpr int STEP_R_MAX = STEP_T_MAX * STEP_K_MAX;   // active rows
+constexpr int STEP_E_MAX = 256;
+
+struct StepShared {
+  float lg[STEP_T_MAX * STEP_E_MAX];
+  int sel_e[STEP_T_MAX][STEP_K_MAX];
+  float sel_v[STEP_T_MAX][STEP_K_MAX];
+  float sel_w[STEP_T_MAX][STEP_K_MAX];
+  int cnt[STEP_E_MAX];
+  int slot_of[STEP_E_MAX];
+  int off[STEP_E_MAX];
+  int wsum[2][SW];
+  int n_slots, total, ok;
+  int slot_e[STEP_R_MAX], slot_n[STEP_R_MAX], slot_off[STEP_R_MAX];
+  int row_t[STEP_R_MAX];
+  float row_w[STEP_R_MAX];
+  uint64_t rbar[SW];
+  uint64_t bars[SW][ST_MAX_NST];
+};
+
+__device__ __forceinline__ unsigned long long ld_acquire64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Grid-wide barrier over gridDim.x co-resident CTAs on a 64-bit arrival
+// count that only grows (zero at creation, a multiple of the grid between
+// launches): arrival k of a barrier returns it to at least the next multiple
+// of the grid.  Returns false after a timeout.
+__device__ bool grid_sync(unsigned long long* cnt, int& ok_sh) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    unsigned long long prev;
+    asm volatile("atom.add.release.gpu.u64 %0, [%1], 1;" : "=l"(prev) : "l"(cnt) : "memory");
+    const unsigned long long target = (prev / gridDim.x + 1) * gridDim.x;
+    bool ok = true;
+    const long long t0 = clock64();
+    while (ld_acquire64(cnt) < target) {
+      if (clock64() - t0 > (1ll << 31)) {
+        ok = false;
+        break;
+      }
+      __nanosleep(32);
+    }
+    __threadfence();
+    ok_sh = ok;
+  }
+  __syncthreads();
+  return ok_sh != 0;
+}
+
+// Whether (vj, j) ranks above (vi, i): larger logit first, NaN below every
+// number, ties to the lower index.
+__device__ __forceinline__ bool ranks_above(float vj, int j, float vi, int i) {
+  const bool jn = vj != vj, in = vi != vi;
+  if (jn) return in && j < i;
+  return in || vj > vi || (vj == vi && j < i);
+}
+
+struct StepArgs {
+  const float* x_in;      // [T][D]
+  const float* add_in;    // [T][D] or null
+  float* x_out;           // [T][D] x_in + add_in, or null
+  const float* norm_w;    // [D] or null
+  float eps;
+  int normalize;
+  const float* router_w;  // [E][D]
+  const float* router_b;  // [E] or null
+  int T, D, E, top_k, I, act, assoc_rule, bias_term;
+  const ExpertDesc* experts;
+  Q8Dev* xq8;             // [T][gbpr]
+  float* logits;          // [T][E]
+  float* hidden;          // [T*top_k][I]
+  float* out;             // [T][D], overwritten with the step's MoE output
+  int* sel_idx;           // [T][top_k]
+  float* sel_w;           // [T][top_k]
+  unsigned long long* sync;   // arrival count of the grid barriers
+  uint32_t stage_bytes;   // ring stage size
+  int nst;                // ring stages per warp
+  int xcap;               // active rows whose Q8 hidden blocks fit each CTA's shared memory
+  int rwc;                // router rows staged per CTA
+  int pa;                 // row pairs per phase-A item
+  int sb;                 // slots per phase-B item
+  DevStatus* st;
+  unsigned long long* trace;   // [gridDim.x][16] phase timestamps, or null
+};
+
+// Phase timestamps for the diagnostics hook tg_cuda_step_trace: slot i of
+// this CTA's 16 gets clock64(), slots 12/13 the global timer at start / end.
+__device__ __forceinline__ unsigned long long gtimer() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+#define TG_MARK(i)                                                                         \
+  do {                                                                                     \
+    if (a.trace && (threadIdx.x & 31) == 0)                                                \
+      a.trace[blockIdx.x * 16 + (i)] = (unsigned long long)clock64();                       \
+  } while (0)
+
+// A warp's position in its stream of items: phase 0 = gate/up item a (slot
+// a / I, row a % I); phase 1 = output row r, slots s .. s + SB - 1.
+struct SCur {
+  int ph;
+  long a, r;
+  int s;
+};
+
+__device__ __forceinline__ bool scur_next(SCur& c, long gw, long NW, long nA, int D, int n_slots, int SB) {
+  if (c.ph == 0) {
+    c.a += NW;
+    if (c.a < nA) return true;
+    c.ph = 1;
+    c.r = gw;
+    c.s = 0;
+    return n_slots > 0 && c.r < D;
+  }
+  c.s += SB;
+  if (c.s < n_slots) return true;
+  c.s = 0;
+  c.r += NW;
+  return c.r < D;
+}
+
+template <int GF, int DF>
+__global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
+  extern __shared__ __align__(128) uint8_t dsm[];
+  __shared__ StepShared sh;
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, tid = threadIdx.x;
+  const int T = a.T, D = a.D, E = a.E, K = a.top_k, I = a.I;
+  const int G = gridDim.x;
+  const long gw = (long)blockIdx.x * SW + wid, NW = (long)G * SW;
+  const int gbpr = (D + QK - 1) / QK, dbpr = (I + QK - 1) / QK;
+  uint8_t* ring = dsm + (size_t)wid * a.nst * a.stage_bytes;
+  float* rrow = reinterpret_cast<float*>(dsm + (size_t)SW * a.nst * a.stage_bytes);   // [rwc][D]
+  XQ* xa = reinterpret_cast<XQ*>(reinterpret_cast<uint8_t*>(rrow) + round16((size_t)a.rwc * D * 4));   // [T][gbpr]
+  XQ* xs = xa + (size_t)T * gbpr;   // [xcap][dbpr]
+  ExpertDesc* etab = reinterpret_cast<ExpertDesc*>(xs + (size_t)a.xcap * dbpr);   // [E]
+  uint64_t* bar = sh.bars[wid];
+  if (a.trace && tid == 0) a.trace[blockIdx.x * 16 + 12] = gtimer();
+  if (wid == 0) TG_MARK(0);
+
+  // ---- R: router rows do not depend on the preceding kernel: stage them now.
+  const int e_r = blockIdx.x + wid * G;   // this warp's expert, if wid < rwc
+  const bool router_warp = wid < a.rwc && e_r < E;
+  const float* wsrc = a.router_w + (size_t)(router_warp ? e_r : 0) * D;
+  const bool wbulk = router_warp && ((uintptr_t)wsrc & 15) == 0 && (D & 3) == 0;
+  if (lane == 0) {
+    for (int i = 0; i < a.nst; i++) mbar_init(&bar[i], 1);
+    if (wbulk) mbar_init(&sh.rbar[wid], 1);
+    fence_mbar_init();
+    if (wbulk) {
+      mbar_arrive_expect_tx(&sh.rbar[wid], (uint32_t)D * 4);
+      bulk_g2s(rrow + (size_t)wid * D, wsrc, (uint32_t)D * 4, &sh.rbar[wid]);
+    }
+  }
+  // the layer's expert table does not change between steps either
+  for (int i = tid; i < E * (int)(sizeof(ExpertDesc) / 8); i += SW * 32)
+    reinterpret_cast<unsigned long long*>(etab)[i] = __ldg(reinterpret_cast<const unsigned long long*>(a.experts) + i);
+  __syncwarp();
+  pdl_wait();   // x (and add) are written by the preceding kernel
+  if (wid == 0) TG_MARK(1);
+
+  // Router warps (wid < rwc): expert e_r's logits for every token.  Quantizer
+  // warps (wid >= rwc): Q8 block qb of N (token qb / gbpr).  Both read their
+  // token rows once, in 16-byte loads issued RCH per lane at a time.
+  const int qb = wid >= a.rwc ? (int)blockIdx.x + (wid - a.rwc) * G : -1;
+  const bool quant_warp = qb >= 0 && qb < T * gbpr;
+  if (router_warp || quant_warp) {
+    constexpr int RCH = 8;
+    const int nc = (D + 127) / 128;   // 16-byte chunks per lane
+    const float* wr = wbulk ? rrow + (size_t)wid * D : wsrc;
+    if (router_warp && wbulk && !mbar_wait(&sh.rbar[wid], 0) && lane == 0)
+      set_error(a.st, ERR_WAIT_TIMEOUT, 30, e_r, 0);
+    const int t_lo = router_warp ? 0 : qb / gbpr, t_hi = router_warp ? T : qb / gbpr + 1;
+    const int bq = quant_warp ? qb - (qb / gbpr) * gbpr : -1;
+    for (int t = t_lo; t < t_hi; t++) {
+      const float* xt = a.x_in + (size_t)t * D;
+      const float* at = a.add_in ? a.add_in + (size_t)t * D : nullptr;
+      float ss = 0.f, dot = 0.f;
+      float4 hlo = make_float4(0.f, 0.f, 0.f, 0.f), hhi = hlo;
+      for (int c0 = 0; c0 < nc; c0 += RCH) {
+        float4 xv[RCH];
+#pragma unroll
+        for (int c = 0; c < RCH; c++) {
+          const int i = 128 * (c0 + c) + 4 * lane;
+          xv[c] = c0 + c < nc && i < D ? __ldcg(reinterpret_cast<const float4*>(xt + i)) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        if (at)
+#pragma unroll
+          for (int c = 0; c < RCH; c++) {
+            const int i = 128 * (c0 + c) + 4 * lane;
+            if (c0 + c < nc && i < D) {
+              const float4 d = __ldcg(reinterpret_cast<const float4*>(at + i));
+              xv[c] = make_float4(fadd(xv[c].x, d.x), fadd(xv[c].y, d.y), fadd(xv[c].z, d.z), fadd(xv[c].w, d.w));
+            }
+          }
+#pragma unroll
+        for (int c = 0; c < RCH; c++) {
+          const int i = 128 * (c0 + c) + 4 * lane;
+          if (c0 + c < nc && i < D) {
+            float4 v = xv[c];
+            if (e_r == 0 && router_warp && a.x_out) *reinterpret_cast<float4*>(a.x_out + (size_t)t * D + i) = v;
+            ss = __fmaf_rn(v.x, v.x, ss);
+            ss = __fmaf_rn(v.y, v.y, ss);
+            ss = __fmaf_rn(v.z, v.z, ss);
+            ss = __fmaf_rn(v.w, v.w, ss);
+            if (c0 + c == 2 * bq) hlo = v;
+            if (c0 + c == 2 * bq + 1) hhi = v;
+            if (router_warp) {
+              if (a.normalize && a.norm_w) {
+                const float4 nw = __ldg(reinterpret_cast<const float4*>(a.norm_w + i));
+                v = make_float4(fmul(v.x, nw.x), fmul(v.y, nw.y), fmul(v.z, nw.z), fmul(v.w, nw.w));
+              }
+              const float4 w = *reinterpret_cast<const float4*>(wr + i);
+              dot = __fmaf_rn(w.x, v.x, dot);
+              dot = __fmaf_rn(w.y, v.y, dot);
+              dot = __fmaf_rn(w.z, v.z, dot);
+              dot = __fmaf_rn(w.w, v.w, dot);
+            }
+          }
+        }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        ss = fadd(ss, __shfl_xor_sync(FULL, ss, o));
+        dot = fadd(dot, __shfl_xor_sync(FULL, dot, o));
+      }
+      const float rr = a.normalize ? __fsqrt_rn(fadd(__fdiv_rn(ss, (float)D), a.eps)) : 1.f;
+      if (router_warp) {
+        if (a.normalize) dot = __fdiv_rn(dot, rr);
+        if (lane == 0) a.logits[(size_t)t * E + e_r] = a.router_b ? fadd(dot, a.router_b[e_r]) : dot;
+      }
+      if (quant_warp) {
+        const int b0 = bq * QK, n = min(QK, D - b0);
+        float* hv[2] = {&hlo.x, &hhi.x};
+#pragma unroll
+        for (int h = 0; h < 2; h++)
+#pragma unroll
+          for (int jj = 0; jj < 4; jj++) {
+            const int i = 128 * h + 4 * lane + jj;
+            float x = 0.f;
+            if (i < n) {
+              x = hv[h][jj];
+              if (a.normalize) {
+                x = __fdiv_rn(x, rr);
+                if (a.norm_w) x = fmul(x, a.norm_w[b0 + i]);
+              }
+            }
+            hv[h][jj] = x;
+          }
+        quantize_block_warp_f4(hlo, hhi, n, a.xq8 + qb);
+      }
+    }
+  }
+
+  if (wid == 0) TG_MARK(2);
+  // ---- barrier 1: logits and xq8 visible everywhere
+  if (!grid_sync(a.sync, sh.ok)) {
+    if (tid == 0) set_error(a.st, ERR_WAIT_TIMEOUT, 31, blockIdx.x, 0);
+    return;
+  }
+
+  if (wid == 0) TG_MARK(3);
+  // ---- S: selection and plan, in every CTA
+  bool nan_here = false;
+  // N's Q8 blocks (written by other CTAs before barrier 1) into shared
+  // memory, in the same round trip as the logits
+  for (int i = tid; i < T * gbpr * (int)(sizeof(Q8Dev) / 16); i += SW * 32) {
+    const int q = i / (int)(sizeof(Q8Dev) / 16), w = i - q * (int)(sizeof(Q8Dev) / 16);
+    reinterpret_cast<uint4*>(xa + q)[w] = __ldcg(reinterpret_cast<const uint4*>(a.xq8) + i);
+  }
+  for (int i = tid; i < T * E; i += SW * 32) {
+    const float v = __ldcg(a.logits + i);
+    sh.lg[i] = v;
+    nan_here |= v != v;
+  }
+  for (int i = tid; i < E; i += SW * 32) sh.cnt[i] = 0;
+  const bool any_nan = __syncthreads_or(nan_here) != 0;
+  if (wid == 0) TG_MARK(9);
+  {
+    // rank of each (token, expert) among its token's logits; P lanes share
+    // one element's comparisons
+    int P = 1;
+    while (P < 32 && 2 * P * T * E <= SW * 32) P *= 2;
+    for (int base = 0; base < T * E * P; base += SW * 32) {
+      const int idx = base + tid, el = idx / P, part = idx - el * P;
+      const bool valid = el < T * E;
+      int rank = 0, t = 0, e = 0;
+      float v = 0.f;
+      if (valid) {
+        t = el / E;
+        e = el - t * E;
+        v = sh.lg[el];
+        const float* row = sh.lg + t * E;
+        if (!any_nan)
+          for (int jj = part; jj < E; jj += P) {
+            const float vj = row[jj];
+            rank += (vj > v) | ((vj == v) & (jj < e));
+          }
+        else
+          for (int jj = part; jj < E; jj += P) rank += ranks_above(row[jj], jj, v, e);
+      }
+      for (int o = 1; o < P; o <<= 1) rank += __shfl_xor_sync(FULL, rank, o);
+      if (valid && part == 0 && rank < K) {
+        sh.sel_e[t][rank] = e;
+        sh.sel_v[t][rank] = v != v ? -INFINITY : v;
+      }
+    }
+  }
+  __syncthreads();
+  if (wid == 0) TG_MARK(14);
+  if (tid < T) {
+    float ex[STEP_K_MAX], sum = 0.f;
+#pragma unroll
+    for (int j = 0; j < STEP_K_MAX; j++)
+      if (j < K) {
+        ex[j] = expf(fsub(sh.sel_v[tid][j], sh.sel_v[tid][0]));
+        sum = fadd(sum, ex[j]);
+      }
+#pragma unroll
+    for (int j = 0; j < STEP_K_MAX; j++)
+      if (j < K) {
+        const float w = __fdiv_rn(ex[j], sum);
+        sh.sel_w[tid][j] = w;
+        if (blockIdx.x == 0) {
+          a.sel_idx[tid * K + j] = sh.sel_e[tid][j];
+          a.sel_w[tid * K + j] = w;
+        }
+      }
+  }
+  __syncthreads();
+  // sums of each 16 values of N's staged blocks (Q6_K's bias correction)
+  for (int i = tid; i < T * gbpr * 16; i += SW * 32) {
+    const int q = i >> 4, g = i & 15;
+    const int4 w = *reinterpret_cast<const int4*>(xa[q].qs + 16 * g);
+    xa[q].xs16[g] = dp4a(w.x, 0x01010101, dp4a(w.y, 0x01010101, dp4a(w.z, 0x01010101, dp4a(w.w, 0x01010101, 0))));
+  }
+  // experts held by another GPU (no local weights) are skipped; their
+  // contribution arrives through the cross-GPU sum
+  for (int i = tid; i < T * K; i += SW * 32) {
+    const int t = i / K, j = i - t * K;
+    const int e = sh.sel_e[t][j];
+    if (sh.sel_w[t][j] != 0.f && etab[e].gate.main) atomicAdd(&sh.cnt[e], 1);
+  }
+  __syncthreads();
+  {   // exclusive scans of row counts and of non-empty experts over e < E <= 256
+    const int c = tid < E ? sh.cnt[tid] : 0, nz = c > 0;
+    int sc = c, sz = nz;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int a1 = __shfl_up_sync(FULL, sc, o), a2 = __shfl_up_sync(FULL, sz, o);
+      if (lane >= o) {
+        sc += a1;
+        sz += a2;
+      }
+    }
+    if (lane == 31) {
+      sh.wsum[0][wid] = sc;
+      sh.wsum[1][wid] = sz;
+    }
+    __syncthreads();
+    int bc = 0, bz = 0;
+    for (int j = 0; j < wid; j++) {
+      bc += sh.wsum[0][j];
+      bz += sh.wsum[1][j];
+    }
+    if (tid < E) {
+      sh.off[tid] = bc + sc - c;
+      sh.slot_of[tid] = nz ? bz + sz - 1 : -1;
+    }
+    if (tid == SW * 32 - 1) {
+      sh.n_slots = bz + sz;
+      sh.total = bc + sc;
+    }
+  }
+  __syncthreads();
+  for (int e = tid; e < E; e += SW * 32) {
+    const int s = sh.slot_of[e];
+    if (s < 0) continue;
+    int o = sh.off[e];
+    sh.slot_e[s] = e;
+    sh.slot_n[s] = sh.cnt[e];
+    sh.slot_off[s] = o;
+    for (int t = 0; t < T; t++)
+      for (int j = 0; j < K; j++)
+        if (sh.sel_e[t][j] == e && sh.sel_w[t][j] != 0.f) {
+          sh.row_t[o] = t;
+          sh.row_w[o] = sh.sel_w[t][j];
+          o++;
+        }
+  }
+  __syncthreads();
+
+  if (wid == 0) TG_MARK(4);
+  // ---- A and B: the per-warp ring
+  // Phase A items are (slot, block of pa consecutive rows of gate and of up);
+  // phase B items are (output row, group of sb consecutive slots).  With a
+  // 256-block format, phase A lanes are (row, gate|up, block) and phase B
+  // lanes (slot, block): each lane folds one block's term in the reference's
+  // order and the row's lanes fold the terms in block order.  Other formats
+  // spread each row over the whole warp (warp_dot1).
+  const int n_slots = sh.n_slots, total = sh.total;
+  const int grs = row_layout(GF, D).rs, drs = row_layout(DF, I).rs;
+  constexpr bool GBLK = GF == FMT_Q4K || GF == FMT_Q6K;
+  constexpr bool DBLK = DF == FMT_Q4K || DF == FMT_Q6K;
+  const int pa = a.pa, SB = a.sb;
+  const uint32_t ghalf = rows_stage_bytes(grs, pa), dr = rows_stage_bytes(drs, 1);
+  const int nrb = (I + pa - 1) / pa;   // row blocks per slot
+  const long nA = (long)n_slots * nrb;
+  const int k = T, rule = a.assoc_rule, act = a.act;
+  const int gbb = GF == FMT_Q4K ? Q4K_BYTES : 192, dbb = DF == FMT_Q4K ? Q4K_BYTES : 192;   // main bytes per block
+
+  auto issue = [&](const SCur& c, int stg) {   // lane 0
+    uint8_t* dst = ring + (size_t)stg * a.stage_bytes;
+    if (c.ph == 0) {
+      const int s = (int)(c.a / nrb), r0 = (int)(c.a - (long)s * nrb) * pa, nr = min(pa, I - r0);
+      const WDesc& Gw = etab[sh.slot_e[s]].gate;
+      const WDesc& Uw = etab[sh.slot_e[s]].up;
+      mbar_arrive_expect_tx(&bar[stg], row_tx(Gw, r0, nr) + row_tx(Uw, r0, nr));
+      stage_row(Gw, r0, dst, &bar[stg], nr);
+      stage_row(Uw, r0, dst + ghalf, &bar[stg], nr);
+    } else {
+      const int s1 = min(n_slots, c.s + SB);
+      uint32_t tx = 0;
+      for (int s = c.s; s < s1; s++) tx += row_tx(etab[sh.slot_e[s]].down, (int)c.r);
+      mbar_arrive_expect_tx(&bar[stg], tx);
+      for (int s = c.s; s < s1; s++) stage_row(etab[sh.slot_e[s]].down, (int)c.r, dst + (s - c.s) * dr, &bar[stg]);
+    }
+  };
+  SCur ic{0, gw - NW, 0, 0};
+  int issued = 0;
+  bool more = true;
+  for (int i = 0; i < a.nst && more; i++) {
+    more = scur_next(ic, gw, NW, nA, D, n_slots, SB);
+    if (more) {
+      if (lane == 0) issue(ic, i);
+      issued++;
+    }
+  }
+  bool dead = false;
+  int j = 0;   // items consumed
+  // Stops the warp: no further copies are issued, and those in flight
+  // (items from .. issued-1) are waited for, each wait bounded.
+  auto stop = [&](int from) {
+    if (dead) return;
+    dead = true;
+    for (int i = from; i < issued; i++) mbar_wait(&bar[i % a.nst], (uint32_t)(i / a.nst) & 1u);
+  };
+  unsigned long long tw[6] = {0, 0, 0, 0, 0, 0};   // trace: wait / compute / issue cycles, phases A and B
+  int tph = 0;
+  long long tc = 0;
+  auto wait_stage = [&](int stg, int item) -> bool {
+    if (dead) return false;
+    if (a.trace) tc = clock64();
+    const bool okw = mbar_wait(&bar[stg], (uint32_t)(item / a.nst) & 1u);
+    if (a.trace) {
+      const long long t1 = clock64();
+      tw[3 * tph] += t1 - tc;
+      tc = t1;
+    }
+    if (!okw) {
+      if (lane == 0) set_error(a.st, ERR_WAIT_TIMEOUT, 32, blockIdx.x, wid);
+      stop(item + 1);
+      return false;
+    }
+    return true;
+  };
+  auto refill = [&](int stg) {
+    __syncwarp();
+    long long t0 = 0;
+    if (a.trace) {
+      t0 = clock64();
+      tw[3 * tph + 1] += t0 - tc;
+    }
+    if (dead || !more) return;
+    more = scur_next(ic, gw, NW, nA, D, n_slots, SB);
+    if (more) {
+      if (lane == 0) issue(ic, stg);
+      issued++;
+    }
+    if (a.trace) tw[3 * tph + 2] += clock64() - t0;
+  };
+
+  // phase A: items gw, gw + NW, ... < nA
+  const int gbpr2 = GBLK ? gbpr : 1;                 // lanes per row
+  const int a_pr = lane / (2 * gbpr2), a_m = (lane / gbpr2) & 1, a_b = lane - (lane / gbpr2) * gbpr2;
+  for (long it = gw; it < nA; it += NW, j++) {
+    const int stg = j % a.nst;
+    if (!wait_stage(stg, j)) continue;
+    const int s = (int)(it / nrb), r0 = (int)(it - (long)s * nrb) * pa, nr = min(pa, I - r0);
+    const ExpertDesc& X = etab[sh.slot_e[s]];
+    const uint8_t* dst = ring + (size_t)stg * a.stage_bytes;
+    const int n = sh.slot_n[s], off = sh.slot_off[s];
+    if constexpr (GBLK) {
+      const bool on = a_pr < nr;
+      const RowPtrs rp = row_ptrs(a_m ? X.up : X.gate, r0, dst + (a_m ? ghalf : 0));
+      const uint8_t* mb = rp.m + (size_t)a_pr * grs + (size_t)a_b * gbb;
+      const uint8_t* s1b = rp.a1 ? rp.a1 + (size_t)a_pr * grs + a_b * 16 : nullptr;
+      const uint8_t* s2b = rp.a2 ? rp.a2 + (size_t)a_pr * grs + a_b * 2 : nullptr;
+      const int r = r0 + a_pr;
+#pragma unroll 1
+      for (int jj = 0; jj < n; jj++) {
+        const bool x4 = use_x4(rule, jj & ~3, n, k);
+        float term = 0.f;
+        if (on) {
+          const XQ& xb = xa[(size_t)sh.row_t[off + jj] * gbpr + a_b];
+          if constexpr (GF == FMT_Q4K) term = q4k_block_term(mb, xb, x4);
+          else term = q6k_block_term(mb, s1b, s2b, xb);
+        }
+        const float tot = fold_row(term, lane - a_b, gbpr2);
+        const float up = shfl(tot, min(lane + gbpr2, 31));
+        if (on && a_m == 0 && a_b == 0) {
+          float gt = tot, ut = up;
+          if (X.gb) {
+            gt = fadd(gt, X.gb[r]);
+            ut = fadd(ut, X.ub[r]);
+          }
+          a.hidden[(size_t)(off + jj) * I + r] = act_fn(act, gt, ut);
+        }
+      }
+    } else {
+      const RowPtrs pg = row_ptrs(X.gate, r0, dst), pu = row_ptrs(X.up, r0, dst + ghalf);
+#pragma unroll 1
+      for (int g0 = 0; g0 < n; g0 += 4) {
+        const int ng = min(4, n - g0);
+        const bool x4 = use_x4(rule, g0, n, k);
+        float gt = 0.f, ut = 0.f;
+#pragma unroll 1
+        for (int q = 0; q < 2 * ng; q++) {
+          const int t = q >> 1;
+          const float v = warp_dot1<GF>((q & 1) ? pu : pg, D, xa + (size_t)sh.row_t[off + g0 + t] * gbpr, x4);
+          const float vb = shfl(v, 0);
+          if (lane == t) {
+            if (q & 1) ut = vb;
+            else gt = vb;
+          }
+        }
+        if (lane < ng) {
+          if (X.gb) {
+            gt = fadd(gt, X.gb[r0]);
+            ut = fadd(ut, X.ub[r0]);
+          }
+          a.hidden[(size_t)(off + g0 + lane) * I + r0] = act_fn(act, gt, ut);
+        }
+      }
+    }
+    refill(stg);
+  }
+
+  if (wid == 0) TG_MARK(5);
+  if (wid == SW - 1) TG_MARK(10);
+  tph = 1;
+  // ---- barrier 2: hidden complete
+  const bool ok2 = grid_sync(a.sync, sh.ok);
+  if (ok2) pdl_trigger();
+  else if (tid == 0) set_error(a.st, ERR_WAIT_TIMEOUT, 33, blockIdx.x, 0);
+  if (wid == 0) TG_MARK(6);
+  bool ok3 = ok2;
+  if (ok2) {
+    if (total > a.xcap) {
+      if (tid == 0) set_error(a.st, ERR_BAD_PLAN, 35, total, a.xcap);
+      ok3 = false;
+    } else {
+      // every CTA quantizes the (few) hidden rows into its shared memory,
+      // loading two blocks per warp before quantizing either
+      const int nq = total * dbpr;
+      for (int q0 = wid; q0 < nq; q0 += 2 * SW) {
+        float v[2][8];
+        int nn[2];
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+          const int q = q0 + h * SW;
+          const int row = q / dbpr, b = q - row * dbpr;
+          nn[h] = q < nq ? min(QK, I - b * QK) : 0;
+#pragma unroll
+          for (int jj = 0; jj < 8; jj++) {
+            const int i = lane * 8 + jj;
+            v[h][jj] = i < nn[h] ? __ldcg(a.hidden + (size_t)row * I + (size_t)b * QK + i) : 0.f;
+          }
+        }
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+          const int q = q0 + h * SW;
+          if (q < nq) {
+            quantize_block_warp_vals(v[h], nn[h], reinterpret_cast<Q8Dev*>(xs + q));
+            __syncwarp();
+            if (lane < 16) {   // sums of each 16 values
+              const int4 w = *reinterpret_cast<const int4*>(xs[q].qs + 16 * lane);
+              xs[q].xs16[lane] = dp4a(w.x, 0x01010101, dp4a(w.y, 0x01010101, dp4a(w.z, 0x01010101, dp4a(w.w, 0x01010101, 0))));
+            }
+          }
+        }
+      }
+    }
+  }
+  if (wid == 0) TG_MARK(15);
+  __syncthreads();
+  if (!ok3) stop(j);
+  if (wid == 0) TG_MARK(7);
+
+  // phase B: rows r = gw, gw + NW, ... < D; slots in groups of SB
+  const int dbpr2 = DBLK ? dbpr : 1;
+  const int b_sl = lane / dbpr2, b_b = lane - b_sl * dbpr2;
+  if (n_slots > 0)
+    for (long r = gw; r < D; r += NW) {
+      float acc[STEP_T_MAX];
+#pragma unroll
+      for (int t = 0; t < STEP_T_MAX; t++) acc[t] = 0.f;
+      for (int s0 = 0; s0 < n_slots; s0 += SB, j++) {
+        const int stg = j % a.nst;
+        if (!wait_stage(stg, j)) continue;
+        const uint8_t* dst = ring + (size_t)stg * a.stage_bytes;
+        const int s1 = min(n_slots, s0 + SB);
+        if constexpr (DBLK) {
+          const int s = s0 + b_sl;
+          const bool on = s < s1 && b_sl < SB;
+          const int sc = on ? s : s0;
+          const ExpertDesc& X = etab[sh.slot_e[sc]];
+          const int n = on ? sh.slot_n[sc] : 0, off = sh.slot_off[sc];
+          const RowPtrs rp = row_ptrs(X.down, (int)r, dst + (sc - s0) * dr);
+          const uint8_t* mb = rp.m + (size_t)b_b * dbb;
+          const uint8_t* s1b = rp.a1 ? rp.a1 + b_b * 16 : nullptr;
+          const uint8_t* s2b = rp.a2 ? rp.a2 + b_b * 2 : nullptr;
+          int nmax = n;
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) nmax = max(nmax, __shfl_xor_sync(FULL, nmax, o));
+          float parts[STEP_T_MAX];
+#pragma unroll
+          for (int t = 0; t < STEP_T_MAX; t++) parts[t] = 0.f;
+#pragma unroll 1
+          for (int jj = 0; jj < nmax; jj++) {
+            float term = 0.f;
+            if (jj < n) {
+              const XQ& xb = xs[(size_t)(off + jj) * dbpr + b_b];
+              if constexpr (DF == FMT_Q4K) term = q4k_block_term(mb, xb, use_x4(rule, jj & ~3, n, k));
+              else term = q6k_block_term(mb, s1b, s2b, xb);
+            }
+            const float tot = fold_row(term, lane - b_b, dbpr2);
+            if (jj < n && b_b == 0) {
+              const float w = sh.row_w[off + jj];
+              const float part = a.bias_term ? fmul(w, fadd(tot, X.db ? X.db[r] : 0.f)) : fmul(w, tot);
+#pragma unroll
+              for (int t = 0; t < STEP_T_MAX; t++)
+                if (t == jj) parts[t] = part;
+            }
+          }
+          // combine into the running output in slot order
+          for (int q = s0; q < s1; q++) {
+            const int nq = sh.slot_n[q], oq = sh.slot_off[q], lead = (q - s0) * dbpr2;
+#pragma unroll
+            for (int jj = 0; jj < STEP_T_MAX; jj++)
+              if (jj < nq) {
+                const float pv = shfl(parts[jj], lead);
+                if (lane == 0) {
+                  const int tt = sh.row_t[oq + jj];
+#pragma unroll
+                  for (int t = 0; t < STEP_T_MAX; t++)
+                    if (t == tt) acc[t] = fadd(acc[t], pv);
+                }
+              }
+          }
+        } else {
+          for (int s = s0; s < s1; s++) {
+            const ExpertDesc& X = etab[sh.slot_e[s]];
+            const RowPtrs rp = row_ptrs(X.down, (int)r, dst + (s - s0) * dr);
+            const int n = sh.slot_n[s], off = sh.slot_off[s];
+#pragma unroll 1
+            for (int g0 = 0; g0 < n; g0 += 4) {
+              const int ng = min(4, n - g0);
+              const bool x4 = use_x4(rule, g0, n, k);
+#pragma unroll 1
+              for (int t = 0; t < ng; t++) {
+                const int sr = off + g0 + t;
+                const float v = warp_dot1<DF>(rp, I, xs + (size_t)sr * dbpr, x4);
+                if (lane == 0) {
+                  const float w = sh.row_w[sr];
+                  const float part = a.bias_term ? fmul(w, fadd(v, X.db ? X.db[r] : 0.f)) : fmul(w, v);
+                  const int tt = sh.row_t[sr];
+#pragma unroll
+                  for (int q = 0; q < STEP_T_MAX; q++)
+                    if (q == tt) acc[q] = fadd(acc[q], part);
+                }
+              }
+            }
+          }
+        }
+        refill(stg);
+      }
+      if (lane == 0 && !dead)
+#pragma unroll
+        for (int t = 0; t < STEP_T_MAX; t++)
+          if (t < T) a.out[(size_t)t * D + r] = acc[t];
+    }
+  else if (!dead)
+    for (long r = gw; r < D; r += NW)
+      if (lane < T) a.out[(size_t)lane * D + r] = 0.f;
+
+  if (wid == 0) TG_MARK(8);
+  if (wid == SW - 1) TG_MARK(11);
+  if (a.trace && tid == 0) a.trace[blockIdx.x * 16 + 13] = gtimer();
+  if (a.trace && lane == 0)
+    for (int q = 0; q < 6; q++) a.trace[(size_t)gridDim.x * 16 + ((size_t)blockIdx.x * SW + wid) * 8 + q] = tw[q];
+  // bounded waits for any copies still in flight before the CTA exits
+  if (!dead)
+    for (int i = j; i < issued; i++) mbar_wait(&bar[i % a.nst], (uint32_t)(i / a.nst) & 1u);
+}
+
+// ---------------------------------------------------------------------
+// Launcher.
+
+// Shared-memory shape of one launch, or false when the step does not fit.
+struct StepShape {
+  uint32_t stage;
+  int nst, rwc, xcap, pa, sb;
+  size_t smem;
+};
+
+static int step_sms() {
+  static int sms = 0;
+  if (!sms) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (sms < 1) sms = 1;
+  }
+  return sms;
+}
+
+static bool step_shape(const StepLaunch& l, StepShape& sh) {
+  const bool gf = l.gate_fmt == FMT_Q4K || l.gate_fmt == FMT_Q6K || l.gate_fmt == FMT_MXFP4 || l.gate_fmt == FMT_Q80;
+  const bool df = l.down_fmt == FMT_Q4K || l.down_fmt == FMT_Q6K || l.down_fmt == FMT_MXFP4 || l.down_fmt == FMT_Q80;
+  if (!gf || !df || l.T < 1 || l.T > STEP_T_MAX || l.E < 1 || l.E > STEP_E_MAX || l.top_k < 1 ||
+      l.top_k > STEP_K_MAX || l.top_k > l.E || (l.D & 3))
+    return false;
+  // rows are read and written as float4
+  const void* ptrs[] = {l.x_in, l.add_in, l.x_out, l.norm_w, l.router_w, l.out};
+  for (const void* q : ptrs)
+    if (reinterpret_cast<uintptr_t>(q) & 15) return false;
+  // 256-block formats put a row's blocks on consecutive lanes: at most 16
+  // blocks per gate / up row (a row pair fills the warp), 32 per down row
+  const bool gblk = l.gate_fmt == FMT_Q4K || l.gate_fmt == FMT_Q6K;
+  const bool dblk = l.down_fmt == FMT_Q4K || l.down_fmt == FMT_Q6K;
+  const int bg = l.D / QK, bd = l.I / QK;
+  if ((gblk && (bg < 1 || bg > 16)) || (dblk && (bd < 1 || bd > 32))) return false;
+  const int G = step_sms();
+  sh.pa = gblk ? std::max(1, 16 / bg) : 1;
+  const uint32_t dr = rows_stage_bytes(row_layout(l.down_fmt, l.I).rs, 1);
+  sh.stage = std::max(2 * rows_stage_bytes(row_layout(l.gate_fmt, l.D).rs, sh.pa), dr);
+  const int sbmax = dblk ? 32 / bd : 1 << 20;
+  sh.sb = std::max(1, std::min<int>(sbmax, (int)(sh.stage / dr)));
+  sh.rwc = (l.E + G - 1) / G;
+  if (sh.rwc > SW) return false;
+  const int gbpr = (l.D + QK - 1) / QK, dbpr = (l.I + QK - 1) / QK;
+  sh.xcap = l.T * l.top_k;
+  const size_t fixed = round16((size_t)sh.rwc * l.D * 4) + (size_t)l.T * gbpr * sizeof(XQ) +
+                       (size_t)sh.xcap * dbpr * sizeof(XQ) + (size_t)l.E * sizeof(ExpertDesc);
+  const size_t budget = 220 * 1024 - sizeof(StepShared);
+  if (fixed + (size_t)SW * 2 * sh.stage > budget) return false;
+  sh.nst = (int)std::min<size_t>(ST_MAX_NST, (budget - fixed) / ((size_t)SW * sh.stage));
+  sh.smem = (size_t)SW * sh.nst * sh.stage + fixed;
+  return true;
+}
+
+template <int GF, int DF>
+static cudaError_t step_launch(StepArgs a, const StepShape& sh, cudaStream_t s) {
+  a.stage_bytes = sh.stage;
+  a.nst = sh.nst;
+  a.rwc = sh.rwc;
+  a.xcap = sh.xcap;
+  a.pa = sh.pa;
+  a.sb = sh.sb;
+  const void* fn = reinterpret_cast<const void*>(layer_step_kernel<GF, DF>);
+  cudaError_t e = ensure_smem(fn, sh.smem);
+  if (e != cudaSuccess) return e;
+  int per = 0;
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, fn, SW * 32, sh.smem);
+  if (e != cudaSuccess) return e;
+  if (per < 1) return cudaErrorInvalidConfiguration;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(step_sms());
+  cfg.blockDim = dim3(SW * 32);
+  cfg.dynamicSmemBytes = sh.smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  void* args[] = {(void*)&a};
+  return cudaLaunchKernelExC(&cfg, fn, args);
+}
+
+// Gate / down format pairs with a fused step kernel.
+#define TG_STEP_PAIRS(X)       \
+  X(FMT_Q4K, FMT_Q6K)          \
+  X(FMT_Q4K, FMT_Q4K)          \
+  X(FMT_MXFP4, FMT_MXFP4)      \
+  X(FMT_Q6K, FMT_Q6K)          \
+  X(FMT_Q80, FMT_Q80)
+
+bool step_eligible(const StepLaunch& l) {
+  StepShape sh;
+  if (!step_shape(l, sh)) return false;
+#define TG_STEP_HAS(GFV, DFV) \
+  if (l.gate_fmt == GFV && l.down_fmt == DFV) return true;
+  TG_STEP_PAIRS(TG_STEP_HAS)
+#undef TG_STEP_HAS
+  return false;
+}
+
+static unsigned long long* g_step_trace = nullptr;
+void set_step_trace(void* p) { g_step_trace = static_cast<unsigned long long*>(p); }
+
+cudaError_t launch_layer_step(const StepLaunch& l, cudaStream_t s) {
+  StepShape sh;
+  if (!step_shape(l, sh)) return cudaErrorInvalidValue;
+  StepArgs a{};
+  a.x_in = l.x_in;
+  a.add_in = l.add_in;
+  a.x_out = l.x_out;
+  a.norm_w = l.norm_w;
+  a.eps = l.eps;
+  a.normalize = l.normalize;
+  a.router_w = l.router_w;
+  a.router_b = l.router_b;
+  a.T = l.T;
+  a.D = l.D;
+  a.E = l.E;
+  a.top_k = l.top_k;
+  a.I = l.I;
+  a.act = l.act;
+  a.assoc_rule = l.assoc_rule;
+  a.bias_term = l.bias_term;
+  a.experts = l.experts;
+  a.xq8 = l.xq8;
+  a.logits = l.logits;
+  a.hidden = l.hidden;
+  a.out = l.out;
+  a.sel_idx = l.sel_idx;
+  a.sel_w = l.sel_w;
+  a.sync = l.sync;
+  a.st = l.st;
+  a.trace = g_step_trace;
+#define TG_STEP_CASE(GFV, DFV) \
+  if (l.gate_fmt == GFV && l.down_fmt == DFV) return step_launch<GFV, DFV>(a, sh, s);
+  TG_STEP_PAIRS(TG_STEP_CASE)
+#undef TG_STEP_CASE
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace tg

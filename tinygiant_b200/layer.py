@@ -45,6 +45,10 @@ class ResidentLayer:
         r.shard, r.n_shards = self.shard, self.n_shards
         return r
 
+    def set_fused(self, on=True):
+        """Fused single-kernel steps (default) or the three-kernel path."""
+        return bool(self.lib.tg_layer_set_fused(self.h, int(bool(on))))
+
     def expert_bytes(self, e):
         return self.lib.tg_layer_expert_bytes(self.h, e)
 
