@@ -70,6 +70,29 @@ def test_fused_step_matches_three_kernel_path(gpu, qwen16, T):
         assert rel_err(outs[0], outs[1]) <= TOL
 
 
+@pytest.mark.parametrize("T", [1, 5])
+def test_fused_step_bit_exact_vs_reference_abi(gpu, qwen16, T):
+    """Given the step's own routing, its output equals the reference-ABI call
+    (tg_moe_forward_rows_v2) on the same rows bit for bit: the dots, the
+    activation and the ordered combine are the same arithmetic."""
+    L, R = qwen16
+    N = synth.rms_norm(np.random.default_rng(400 + T).standard_normal((T, 2048)).astype(np.float32))
+    got = R.forward(N, normalize=False)
+    idx, w = R.last_routing(T)
+    sel = sorted({int(idx[t, j]) for t in range(T) for j in range(L.top_k) if w[t, j] != 0})
+    row_w = np.zeros((len(sel), T), np.float32)
+    for t in range(T):
+        for j in range(L.top_k):
+            if w[t, j] != 0:
+                row_w[sel.index(int(idx[t, j])), t] = w[t, j]
+    want = np.zeros_like(N)
+    M.moe_forward_rows_v2(gpu, [L.gates[e] for e in sel], [L.ups[e] for e in sel], [L.downs[e] for e in sel],
+                          L.gate_fmt, [L.down_fmts[e] for e in sel], None, None, None, L.act, row_w, N, want,
+                          L.embed_dim, L.inter_dim)
+    tg.check(gpu)
+    np.testing.assert_array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
 def test_fused_step_more_experts_than_sms(gpu, oracle):
     """200 experts: some CTAs hold two router rows."""
     L = synth.qwen_layer(seed=7, n_experts=200, D=512, I=256)

@@ -64,7 +64,8 @@ __device__ __forceinline__ void quantize_block_cta(float v, bool valid, Q8Dev* o
 // The same quantizer run by one warp on values it holds: lane l holds v[j] =
 // value 8l + j of the block (positions at or past n must be passed as 0 and
 // are stored as 0).  No CTA barrier.
-__device__ __forceinline__ void quantize_block_warp_vals(const float* v, int n, Q8Dev* o) {
+template <typename O>
+__device__ __forceinline__ void quantize_block_warp_vals(const float* v, int n, O* o) {
   const int lane = threadIdx.x & 31;
   float a = 0.f;
 #pragma unroll

@@ -53,6 +53,9 @@ struct StepShared {
   int row_t[STEP_R_MAX];
   float row_w[STEP_R_MAX];
   uint64_t rbar[SW];
+  uint64_t xbar;
+  float accw[SW][STEP_T_MAX];
+  unsigned long long tw[SW][6];
   uint64_t bars[SW][ST_MAX_NST];
 };
 
@@ -96,6 +99,30 @@ __device__ __forceinline__ bool ranks_above(float vj, int j, float vi, int i) {
   return in || vj > vi || (vj == vi && j < i);
 }
 
+// The weight pointers of one expert (its matrices' row layouts follow from
+// the layer's formats and shape).
+struct StepExpert {
+  const uint8_t* g;
+  const uint8_t* u;
+  const uint8_t* d;
+  const float* gb;
+  const float* ub;
+  const float* db;
+};
+
+__device__ __forceinline__ WDesc wdesc(const uint8_t* m, int fmt, int rows, int cols) {
+  const RowLayout L = row_layout(fmt, cols);
+  WDesc w;
+  w.main = m;
+  w.aux1 = m && L.a1 >= 0 ? m + L.a1 : nullptr;
+  w.aux2 = m && L.a2 >= 0 ? m + L.a2 : nullptr;
+  w.fmt = fmt;
+  w.rows = rows;
+  w.cols = cols;
+  w.rs = L.rs;
+  return w;
+}
+
 struct StepArgs {
   const float* x_in;      // [T][D]
   const float* add_in;    // [T][D] or null
@@ -105,7 +132,7 @@ struct StepArgs {
   int normalize;
   const float* router_w;  // [E][D]
   const float* router_b;  // [E] or null
-  int T, D, E, top_k, I, act, assoc_rule, bias_term;
+  int T, D, E, top_k, I, act, assoc_rule, bias_term, gate_fmt, down_fmt;
   const ExpertDesc* experts;
   Q8Dev* xq8;             // [T][gbpr]
   float* logits;          // [T][E]
@@ -120,6 +147,7 @@ struct StepArgs {
   int rwc;                // router rows staged per CTA
   int pa;                 // row pairs per phase-A item
   int sb;                 // slots per phase-B item
+  int sl;                 // phase-B lanes per block (slot lanes), a power of two
   DevStatus* st;
   unsigned long long* trace;   // [gridDim.x][16] phase timestamps, or null
 };
@@ -168,13 +196,15 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, tid = threadIdx.x;
   const int T = a.T, D = a.D, E = a.E, K = a.top_k, I = a.I;
   const int G = gridDim.x;
-  const long gw = (long)blockIdx.x * SW + wid, NW = (long)G * SW;
+  // work items go to warps CTA-interleaved, so every SM gets an even share
+  const long gw = (long)wid * G + blockIdx.x, NW = (long)G * SW;
   const int gbpr = (D + QK - 1) / QK, dbpr = (I + QK - 1) / QK;
   uint8_t* ring = dsm + (size_t)wid * a.nst * a.stage_bytes;
   float* rrow = reinterpret_cast<float*>(dsm + (size_t)SW * a.nst * a.stage_bytes);   // [rwc][D]
   XQ* xa = reinterpret_cast<XQ*>(reinterpret_cast<uint8_t*>(rrow) + round16((size_t)a.rwc * D * 4));   // [T][gbpr]
   XQ* xs = xa + (size_t)T * gbpr;   // [xcap][dbpr]
-  ExpertDesc* etab = reinterpret_cast<ExpertDesc*>(xs + (size_t)a.xcap * dbpr);   // [E]
+  ExpertDesc* sx = reinterpret_cast<ExpertDesc*>(xs + (size_t)a.xcap * dbpr);       // [xcap] the slots' experts
+  StepExpert* etab = reinterpret_cast<StepExpert*>(sx + a.xcap);                     // [E] weight pointers
   uint64_t* bar = sh.bars[wid];
   if (a.trace && tid == 0) a.trace[blockIdx.x * 16 + 12] = gtimer();
   if (wid == 0) TG_MARK(0);
@@ -193,19 +223,47 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
       bulk_g2s(rrow + (size_t)wid * D, wsrc, (uint32_t)D * 4, &sh.rbar[wid]);
     }
   }
-  // the layer's expert table does not change between steps either
-  for (int i = tid; i < E * (int)(sizeof(ExpertDesc) / 8); i += SW * 32)
-    reinterpret_cast<unsigned long long*>(etab)[i] = __ldg(reinterpret_cast<const unsigned long long*>(a.experts) + i);
-  __syncwarp();
+  // the layer's expert table does not change between steps either: its
+  // loads are issued now and stored to shared memory after the router work
+  constexpr int EV = 3;   // table words per thread (E * 6 <= EV * 512)
+  const void* ev[EV];
+#pragma unroll
+  for (int q = 0; q < EV; q++) {
+    const int i = tid + q * SW * 32, e = i / 6, f = i - e * 6;
+    ev[q] = nullptr;
+    if (e < E) {
+      const ExpertDesc& X = a.experts[e];
+      ev[q] = f == 0 ? (const void*)X.gate.main : f == 1 ? (const void*)X.up.main : f == 2 ? (const void*)X.down.main
+            : f == 3 ? (const void*)X.gb : f == 4 ? (const void*)X.ub : (const void*)X.db;
+    }
+  }
+  // x (and add) rows: staged into the ring's space, which phase A only uses
+  // after barrier 1, with one bulk copy each
+  const int qb = wid >= a.rwc ? (int)blockIdx.x + (wid - a.rwc) * G : -1;
+  const bool quant_warp = qb >= 0 && qb < T * gbpr;
+  const bool cta_reads_x = (int)blockIdx.x < E || (int)blockIdx.x < T * gbpr;
+  const uint32_t xbytes = (uint32_t)T * D * 4;
+  const bool xstaged = (size_t)xbytes * (a.add_in ? 2 : 1) <= (size_t)SW * a.nst * a.stage_bytes;
+  const float* xsm = reinterpret_cast<const float*>(dsm);
+  const float* asm_ = a.add_in ? xsm + (size_t)T * D : nullptr;
+  if (tid == 0) {
+    mbar_init(&sh.xbar, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
   pdl_wait();   // x (and add) are written by the preceding kernel
+  if (tid == 0 && xstaged && cta_reads_x) {
+    mbar_arrive_expect_tx(&sh.xbar, xbytes * (a.add_in ? 2 : 1));
+    bulk_g2s(dsm, a.x_in, xbytes, &sh.xbar);
+    if (a.add_in) bulk_g2s(dsm + xbytes, a.add_in, xbytes, &sh.xbar);
+  }
   if (wid == 0) TG_MARK(1);
 
   // Router warps (wid < rwc): expert e_r's logits for every token.  Quantizer
   // warps (wid >= rwc): Q8 block qb of N (token qb / gbpr).  Both read their
-  // token rows once, in 16-byte loads issued RCH per lane at a time.
-  const int qb = wid >= a.rwc ? (int)blockIdx.x + (wid - a.rwc) * G : -1;
-  const bool quant_warp = qb >= 0 && qb < T * gbpr;
+  // token rows once, from the staged copy (or global memory), 16 bytes a lane.
   if (router_warp || quant_warp) {
+    if (xstaged && !mbar_wait(&sh.xbar, 0) && lane == 0) set_error(a.st, ERR_WAIT_TIMEOUT, 36, blockIdx.x, wid);
     constexpr int RCH = 8;
     const int nc = (D + 127) / 128;   // 16-byte chunks per lane
     const float* wr = wbulk ? rrow + (size_t)wid * D : wsrc;
@@ -223,14 +281,18 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
 #pragma unroll
         for (int c = 0; c < RCH; c++) {
           const int i = 128 * (c0 + c) + 4 * lane;
-          xv[c] = c0 + c < nc && i < D ? __ldcg(reinterpret_cast<const float4*>(xt + i)) : make_float4(0.f, 0.f, 0.f, 0.f);
+          xv[c] = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (c0 + c < nc && i < D)
+            xv[c] = xstaged ? *reinterpret_cast<const float4*>(xsm + (size_t)t * D + i)
+                            : __ldcg(reinterpret_cast<const float4*>(xt + i));
         }
         if (at)
 #pragma unroll
           for (int c = 0; c < RCH; c++) {
             const int i = 128 * (c0 + c) + 4 * lane;
             if (c0 + c < nc && i < D) {
-              const float4 d = __ldcg(reinterpret_cast<const float4*>(at + i));
+              const float4 d = xstaged ? *reinterpret_cast<const float4*>(asm_ + (size_t)t * D + i)
+                                       : __ldcg(reinterpret_cast<const float4*>(at + i));
               xv[c] = make_float4(fadd(xv[c].x, d.x), fadd(xv[c].y, d.y), fadd(xv[c].z, d.z), fadd(xv[c].w, d.w));
             }
           }
@@ -293,6 +355,11 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
     }
   }
 
+#pragma unroll
+  for (int q = 0; q < EV; q++) {
+    const int i = tid + q * SW * 32, e = i / 6, f = i - e * 6;
+    if (e < E) reinterpret_cast<const void**>(etab + e)[f] = ev[q];
+  }
   if (wid == 0) TG_MARK(2);
   // ---- barrier 1: logits and xq8 visible everywhere
   if (!grid_sync(a.sync, sh.ok)) {
@@ -305,9 +372,27 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
   bool nan_here = false;
   // N's Q8 blocks (written by other CTAs before barrier 1) into shared
   // memory, in the same round trip as the logits
-  for (int i = tid; i < T * gbpr * (int)(sizeof(Q8Dev) / 16); i += SW * 32) {
-    const int q = i / (int)(sizeof(Q8Dev) / 16), w = i - q * (int)(sizeof(Q8Dev) / 16);
-    reinterpret_cast<uint4*>(xa + q)[w] = __ldcg(reinterpret_cast<const uint4*>(a.xq8) + i);
+  for (int i = tid; i < T * gbpr * 19; i += SW * 32) {   // qs in 16 pieces, scale / sum, bsums in 2
+    const int q = i / 19, w = i - q * 19;
+    const uint4* src = reinterpret_cast<const uint4*>(a.xq8 + q);
+    if (w < 16) {
+      reinterpret_cast<uint4*>(xa[q].qs)[w] = __ldcg(src + w);
+    } else if (w == 16) {
+      const uint4 v = __ldcg(src + 16);   // scale, sum, bsums[0..1]
+      xa[q].scale = __uint_as_float(v.x);
+      xa[q].sum = (int)v.y;
+      xa[q].bsums[0] = (int)v.z;
+      xa[q].bsums[1] = (int)v.w;
+    } else {
+      const uint4 v = __ldcg(src + w);    // bsums[2..5] or bsums[6..7] and padding
+      const int b0 = 2 + 4 * (w - 17);
+      xa[q].bsums[b0] = (int)v.x;
+      xa[q].bsums[b0 + 1] = (int)v.y;
+      if (w == 17) {
+        xa[q].bsums[4] = (int)v.z;
+        xa[q].bsums[5] = (int)v.w;
+      }
+    }
   }
   for (int i = tid; i < T * E; i += SW * 32) {
     const float v = __ldcg(a.logits + i);
@@ -333,6 +418,7 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
         v = sh.lg[el];
         const float* row = sh.lg + t * E;
         if (!any_nan)
+#pragma unroll 8
           for (int jj = part; jj < E; jj += P) {
             const float vj = row[jj];
             rank += (vj > v) | ((vj == v) & (jj < e));
@@ -349,38 +435,38 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
   }
   __syncthreads();
   if (wid == 0) TG_MARK(14);
-  if (tid < T) {
-    float ex[STEP_K_MAX], sum = 0.f;
-#pragma unroll
-    for (int j = 0; j < STEP_K_MAX; j++)
-      if (j < K) {
-        ex[j] = expf(fsub(sh.sel_v[tid][j], sh.sel_v[tid][0]));
-        sum = fadd(sum, ex[j]);
+  if (wid < T) {   // warp t: lane j < K takes selection j; the sum runs in j order
+    const int t = wid;
+    const float ex = lane < K ? expf(fsub(sh.sel_v[t][lane], sh.sel_v[t][0])) : 0.f;
+    float sum = 0.f;
+    for (int j = 0; j < K; j++) sum = fadd(sum, shfl(ex, j));
+    if (lane < K) {
+      const float w = __fdiv_rn(ex, sum);
+      sh.sel_w[t][lane] = w;
+      if (blockIdx.x == 0) {
+        a.sel_idx[t * K + lane] = sh.sel_e[t][lane];
+        a.sel_w[t * K + lane] = w;
       }
-#pragma unroll
-    for (int j = 0; j < STEP_K_MAX; j++)
-      if (j < K) {
-        const float w = __fdiv_rn(ex[j], sum);
-        sh.sel_w[tid][j] = w;
-        if (blockIdx.x == 0) {
-          a.sel_idx[tid * K + j] = sh.sel_e[tid][j];
-          a.sel_w[tid * K + j] = w;
-        }
-      }
+    }
   }
   __syncthreads();
   // sums of each 16 values of N's staged blocks (Q6_K's bias correction)
-  for (int i = tid; i < T * gbpr * 16; i += SW * 32) {
-    const int q = i >> 4, g = i & 15;
-    const int4 w = *reinterpret_cast<const int4*>(xa[q].qs + 16 * g);
-    xa[q].xs16[g] = dp4a(w.x, 0x01010101, dp4a(w.y, 0x01010101, dp4a(w.z, 0x01010101, dp4a(w.w, 0x01010101, 0))));
+  // and the 32-value sums as fp32
+  for (int i = tid; i < T * gbpr * 24; i += SW * 32) {
+    const int q = i / 24, g = i - q * 24;
+    if (g < 16) {
+      const int4 w = *reinterpret_cast<const int4*>(xa[q].qs + 16 * g);
+      xa[q].xs16[xs16_slot(g)] = dp4a(w.x, 0x01010101, dp4a(w.y, 0x01010101, dp4a(w.z, 0x01010101, dp4a(w.w, 0x01010101, 0))));
+    } else {
+      xa[q].bsf[g - 16] = (float)xa[q].bsums[g - 16];
+    }
   }
   // experts held by another GPU (no local weights) are skipped; their
   // contribution arrives through the cross-GPU sum
   for (int i = tid; i < T * K; i += SW * 32) {
     const int t = i / K, j = i - t * K;
     const int e = sh.sel_e[t][j];
-    if (sh.sel_w[t][j] != 0.f && etab[e].gate.main) atomicAdd(&sh.cnt[e], 1);
+    if (sh.sel_w[t][j] != 0.f && etab[e].g) atomicAdd(&sh.cnt[e], 1);
   }
   __syncthreads();
   {   // exclusive scans of row counts and of non-empty experts over e < E <= 256
@@ -428,6 +514,15 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
           sh.row_w[o] = sh.sel_w[t][j];
           o++;
         }
+    const StepExpert& q = etab[e];
+    ExpertDesc X;
+    X.gate = wdesc(q.g, a.gate_fmt, I, D);
+    X.up = wdesc(q.u, a.gate_fmt, I, D);
+    X.down = wdesc(q.d, a.down_fmt, D, I);
+    X.gb = q.gb;
+    X.ub = q.ub;
+    X.db = q.db;
+    sx[s] = X;
   }
   __syncthreads();
 
@@ -454,17 +549,17 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
     uint8_t* dst = ring + (size_t)stg * a.stage_bytes;
     if (c.ph == 0) {
       const int s = (int)(c.a / nrb), r0 = (int)(c.a - (long)s * nrb) * pa, nr = min(pa, I - r0);
-      const WDesc& Gw = etab[sh.slot_e[s]].gate;
-      const WDesc& Uw = etab[sh.slot_e[s]].up;
+      const WDesc& Gw = sx[s].gate;
+      const WDesc& Uw = sx[s].up;
       mbar_arrive_expect_tx(&bar[stg], row_tx(Gw, r0, nr) + row_tx(Uw, r0, nr));
       stage_row(Gw, r0, dst, &bar[stg], nr);
       stage_row(Uw, r0, dst + ghalf, &bar[stg], nr);
     } else {
       const int s1 = min(n_slots, c.s + SB);
       uint32_t tx = 0;
-      for (int s = c.s; s < s1; s++) tx += row_tx(etab[sh.slot_e[s]].down, (int)c.r);
+      for (int s = c.s; s < s1; s++) tx += row_tx(sx[s].down, (int)c.r);
       mbar_arrive_expect_tx(&bar[stg], tx);
-      for (int s = c.s; s < s1; s++) stage_row(etab[sh.slot_e[s]].down, (int)c.r, dst + (s - c.s) * dr, &bar[stg]);
+      for (int s = c.s; s < s1; s++) stage_row(sx[s].down, (int)c.r, dst + (s - c.s) * dr, &bar[stg]);
     }
   };
   SCur ic{0, gw - NW, 0, 0};
@@ -486,7 +581,9 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
     dead = true;
     for (int i = from; i < issued; i++) mbar_wait(&bar[i % a.nst], (uint32_t)(i / a.nst) & 1u);
   };
-  unsigned long long tw[6] = {0, 0, 0, 0, 0, 0};   // trace: wait / compute / issue cycles, phases A and B
+  unsigned long long* tw = sh.tw[wid];   // trace: wait / compute / issue cycles, phases A and B
+  if (lane == 0)
+    for (int q = 0; q < 6; q++) tw[q] = 0;
   int tph = 0;
   long long tc = 0;
   auto wait_stage = [&](int stg, int item) -> bool {
@@ -495,7 +592,7 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
     const bool okw = mbar_wait(&bar[stg], (uint32_t)(item / a.nst) & 1u);
     if (a.trace) {
       const long long t1 = clock64();
-      tw[3 * tph] += t1 - tc;
+      if (lane == 0) tw[3 * tph] += t1 - tc;
       tc = t1;
     }
     if (!okw) {
@@ -510,7 +607,7 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
     long long t0 = 0;
     if (a.trace) {
       t0 = clock64();
-      tw[3 * tph + 1] += t0 - tc;
+      if (lane == 0) tw[3 * tph + 1] += t0 - tc;
     }
     if (dead || !more) return;
     more = scur_next(ic, gw, NW, nA, D, n_slots, SB);
@@ -518,7 +615,7 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
       if (lane == 0) issue(ic, stg);
       issued++;
     }
-    if (a.trace) tw[3 * tph + 2] += clock64() - t0;
+    if (a.trace && lane == 0) tw[3 * tph + 2] += clock64() - t0;
   };
 
   // phase A: items gw, gw + NW, ... < nA
@@ -528,7 +625,7 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
     const int stg = j % a.nst;
     if (!wait_stage(stg, j)) continue;
     const int s = (int)(it / nrb), r0 = (int)(it - (long)s * nrb) * pa, nr = min(pa, I - r0);
-    const ExpertDesc& X = etab[sh.slot_e[s]];
+    const ExpertDesc& X = sx[s];
     const uint8_t* dst = ring + (size_t)stg * a.stage_bytes;
     const int n = sh.slot_n[s], off = sh.slot_off[s];
     if constexpr (GBLK) {
@@ -622,11 +719,13 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
         for (int h = 0; h < 2; h++) {
           const int q = q0 + h * SW;
           if (q < nq) {
-            quantize_block_warp_vals(v[h], nn[h], reinterpret_cast<Q8Dev*>(xs + q));
+            quantize_block_warp_vals(v[h], nn[h], xs + q);
             __syncwarp();
             if (lane < 16) {   // sums of each 16 values
               const int4 w = *reinterpret_cast<const int4*>(xs[q].qs + 16 * lane);
-              xs[q].xs16[lane] = dp4a(w.x, 0x01010101, dp4a(w.y, 0x01010101, dp4a(w.z, 0x01010101, dp4a(w.w, 0x01010101, 0))));
+              xs[q].xs16[xs16_slot(lane)] = dp4a(w.x, 0x01010101, dp4a(w.y, 0x01010101, dp4a(w.z, 0x01010101, dp4a(w.w, 0x01010101, 0))));
+            } else if (lane < 24) {
+              xs[q].bsf[lane - 16] = (float)xs[q].bsums[lane - 16];
             }
           }
         }
@@ -639,13 +738,15 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
   if (wid == 0) TG_MARK(7);
 
   // phase B: rows r = gw, gw + NW, ... < D; slots in groups of SB
-  const int dbpr2 = DBLK ? dbpr : 1;
-  const int b_sl = lane / dbpr2, b_b = lane - b_sl * dbpr2;
+  // phase-B lanes: lane = block * SL + slot, so the 8 lanes of a quarter warp
+  // read 8 different slots' rows (distinct banks)
+  const int dbpr2 = DBLK ? dbpr : 1, SL = a.sl;
+  const int b_b = lane / SL, b_sl = lane - b_b * SL;
+  float* accw = sh.accw[wid];   // running output of the warp's row, per token
   if (n_slots > 0)
     for (long r = gw; r < D; r += NW) {
-      float acc[STEP_T_MAX];
-#pragma unroll
-      for (int t = 0; t < STEP_T_MAX; t++) acc[t] = 0.f;
+      if (lane < T) accw[lane] = 0.f;
+      __syncwarp();
       for (int s0 = 0; s0 < n_slots; s0 += SB, j++) {
         const int stg = j % a.nst;
         if (!wait_stage(stg, j)) continue;
@@ -653,55 +754,46 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
         const int s1 = min(n_slots, s0 + SB);
         if constexpr (DBLK) {
           const int s = s0 + b_sl;
-          const bool on = s < s1 && b_sl < SB;
-          const int sc = on ? s : s0;
-          const ExpertDesc& X = etab[sh.slot_e[sc]];
-          const int n = on ? sh.slot_n[sc] : 0, off = sh.slot_off[sc];
+          const bool in = s < s1, on = in && b_b < dbpr2;
+          const int sc = in ? s : s0;
+          const ExpertDesc& X = sx[sc];
+          const int n = in ? sh.slot_n[sc] : 0, off = sh.slot_off[sc];
           const RowPtrs rp = row_ptrs(X.down, (int)r, dst + (sc - s0) * dr);
           const uint8_t* mb = rp.m + (size_t)b_b * dbb;
           const uint8_t* s1b = rp.a1 ? rp.a1 + b_b * 16 : nullptr;
           const uint8_t* s2b = rp.a2 ? rp.a2 + b_b * 2 : nullptr;
-          int nmax = n;
-#pragma unroll
-          for (int o = 16; o > 0; o >>= 1) nmax = max(nmax, __shfl_xor_sync(FULL, nmax, o));
-          float parts[STEP_T_MAX];
-#pragma unroll
-          for (int t = 0; t < STEP_T_MAX; t++) parts[t] = 0.f;
 #pragma unroll 1
-          for (int jj = 0; jj < nmax; jj++) {
+          for (int t = 0; t < T; t++) {
+            // this slot's active row for token t (a slot's rows are in token order)
+            int jr = -1;
+            for (int jj = 0; jj < n; jj++)
+              if (sh.row_t[off + jj] == t) jr = jj;
             float term = 0.f;
-            if (jj < n) {
-              const XQ& xb = xs[(size_t)(off + jj) * dbpr + b_b];
-              if constexpr (DF == FMT_Q4K) term = q4k_block_term(mb, xb, use_x4(rule, jj & ~3, n, k));
+            if (on && jr >= 0) {
+              const XQ& xb = xs[(size_t)(off + jr) * dbpr + b_b];
+              if constexpr (DF == FMT_Q4K) term = q4k_block_term(mb, xb, use_x4(rule, jr & ~3, n, k));
               else term = q6k_block_term(mb, s1b, s2b, xb);
             }
-            const float tot = fold_row(term, lane - b_b, dbpr2);
-            if (jj < n && b_b == 0) {
-              const float w = sh.row_w[off + jj];
-              const float part = a.bias_term ? fmul(w, fadd(tot, X.db ? X.db[r] : 0.f)) : fmul(w, tot);
-#pragma unroll
-              for (int t = 0; t < STEP_T_MAX; t++)
-                if (t == jj) parts[t] = part;
+            const float tot = fold_row(term, b_sl, dbpr2, SL);
+            float part = 0.f;
+            if (in && jr >= 0 && b_b == 0) {
+              const float w = sh.row_w[off + jr];
+              part = a.bias_term ? fmul(w, fadd(tot, X.db ? X.db[r] : 0.f)) : fmul(w, tot);
             }
-          }
-          // combine into the running output in slot order
-          for (int q = s0; q < s1; q++) {
-            const int nq = sh.slot_n[q], oq = sh.slot_off[q], lead = (q - s0) * dbpr2;
-#pragma unroll
-            for (int jj = 0; jj < STEP_T_MAX; jj++)
-              if (jj < nq) {
-                const float pv = shfl(parts[jj], lead);
-                if (lane == 0) {
-                  const int tt = sh.row_t[oq + jj];
-#pragma unroll
-                  for (int t = 0; t < STEP_T_MAX; t++)
-                    if (t == tt) acc[t] = fadd(acc[t], pv);
-                }
-              }
+            const int has = in && jr >= 0;
+            // the parts of the group's slots, added in slot order
+            float acc = accw[t];
+            for (int q = 0; q < s1 - s0; q++) {
+              const float pv = shfl(part, q);
+              if (__shfl_sync(FULL, has, q)) acc = fadd(acc, pv);
+            }
+            __syncwarp();
+            if (lane == 0) accw[t] = acc;
+            __syncwarp();
           }
         } else {
           for (int s = s0; s < s1; s++) {
-            const ExpertDesc& X = etab[sh.slot_e[s]];
+            const ExpertDesc& X = sx[s];
             const RowPtrs rp = row_ptrs(X.down, (int)r, dst + (s - s0) * dr);
             const int n = sh.slot_n[s], off = sh.slot_off[s];
 #pragma unroll 1
@@ -716,20 +808,17 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
                   const float w = sh.row_w[sr];
                   const float part = a.bias_term ? fmul(w, fadd(v, X.db ? X.db[r] : 0.f)) : fmul(w, v);
                   const int tt = sh.row_t[sr];
-#pragma unroll
-                  for (int q = 0; q < STEP_T_MAX; q++)
-                    if (q == tt) acc[q] = fadd(acc[q], part);
+                  accw[tt] = fadd(accw[tt], part);
                 }
               }
             }
           }
+          __syncwarp();
         }
         refill(stg);
       }
-      if (lane == 0 && !dead)
-#pragma unroll
-        for (int t = 0; t < STEP_T_MAX; t++)
-          if (t < T) a.out[(size_t)t * D + r] = acc[t];
+      if (lane < T && !dead) a.out[(size_t)lane * D + r] = accw[lane];
+      __syncwarp();
     }
   else if (!dead)
     for (long r = gw; r < D; r += NW)
@@ -751,7 +840,7 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
 // Shared-memory shape of one launch, or false when the step does not fit.
 struct StepShape {
   uint32_t stage;
-  int nst, rwc, xcap, pa, sb;
+  int nst, rwc, xcap, pa, sb, sl;
   size_t smem;
 };
 
@@ -784,17 +873,28 @@ static bool step_shape(const StepLaunch& l, StepShape& sh) {
   if ((gblk && (bg < 1 || bg > 16)) || (dblk && (bd < 1 || bd > 32))) return false;
   const int G = step_sms();
   sh.pa = gblk ? std::max(1, 16 / bg) : 1;
-  const uint32_t dr = rows_stage_bytes(row_layout(l.down_fmt, l.I).rs, 1);
-  sh.stage = std::max(2 * rows_stage_bytes(row_layout(l.gate_fmt, l.D).rs, sh.pa), dr);
-  const int sbmax = dblk ? 32 / bd : 1 << 20;
-  sh.sb = std::max(1, std::min<int>(sbmax, (int)(sh.stage / dr)));
   sh.rwc = (l.E + G - 1) / G;
   if (sh.rwc > SW) return false;
   const int gbpr = (l.D + QK - 1) / QK, dbpr = (l.I + QK - 1) / QK;
   sh.xcap = l.T * l.top_k;
   const size_t fixed = round16((size_t)sh.rwc * l.D * 4) + (size_t)l.T * gbpr * sizeof(XQ) +
-                       (size_t)sh.xcap * dbpr * sizeof(XQ) + (size_t)l.E * sizeof(ExpertDesc);
+                       (size_t)sh.xcap * dbpr * sizeof(XQ) + (size_t)sh.xcap * sizeof(ExpertDesc) +
+                       (size_t)l.E * sizeof(StepExpert);
   const size_t budget = 220 * 1024 - sizeof(StepShared);
+  const uint32_t dr = rows_stage_bytes(row_layout(l.down_fmt, l.I).rs, 1);
+  const uint32_t sa = 2 * rows_stage_bytes(row_layout(l.gate_fmt, l.D).rs, sh.pa);
+  // phase-B slots per item: every slot of the step if the stage allows
+  sh.sl = 1;
+  if (dblk)
+    while (2 * sh.sl * bd <= 32) sh.sl *= 2;
+  const int max_slots = std::min(l.E, l.T * l.top_k);
+  int sb = dblk ? std::min(sh.sl, max_slots) : std::max(1, (int)(sa / dr));
+  for (;;) {
+    sh.stage = std::max(sa, (uint32_t)sb * dr);
+    if (fixed + (size_t)SW * 2 * sh.stage <= budget || sb == 1) break;
+    sb = std::max(1, sb / 2);
+  }
+  sh.sb = sb;
   if (fixed + (size_t)SW * 2 * sh.stage > budget) return false;
   sh.nst = (int)std::min<size_t>(ST_MAX_NST, (budget - fixed) / ((size_t)SW * sh.stage));
   sh.smem = (size_t)SW * sh.nst * sh.stage + fixed;
@@ -809,6 +909,7 @@ static cudaError_t step_launch(StepArgs a, const StepShape& sh, cudaStream_t s) 
   a.xcap = sh.xcap;
   a.pa = sh.pa;
   a.sb = sh.sb;
+  a.sl = sh.sl;
   const void* fn = reinterpret_cast<const void*>(layer_step_kernel<GF, DF>);
   cudaError_t e = ensure_smem(fn, sh.smem);
   if (e != cudaSuccess) return e;
@@ -871,6 +972,8 @@ cudaError_t launch_layer_step(const StepLaunch& l, cudaStream_t s) {
   a.act = l.act;
   a.assoc_rule = l.assoc_rule;
   a.bias_term = l.bias_term;
+  a.gate_fmt = l.gate_fmt;
+  a.down_fmt = l.down_fmt;
   a.experts = l.experts;
   a.xq8 = l.xq8;
   a.logits = l.logits;

@@ -350,22 +350,42 @@ __device__ __forceinline__ void warp_dot(const RowPtrs& rp, int cols, const Q8De
 // folded over their blocks by the caller (block order, one lane).
 
 // Q8 input block as staged in shared memory: the Q8Dev fields, the int32
-// sums of each 16 values (Q6_K's bias correction) and padding to a 400-byte
-// stride, which puts the blocks read by 8 consecutive lanes on distinct banks.
+// sums of each 16 values (Q6_K's bias correction, in the order the Q6_K
+// block term reads them), the 32-value sums as
+// fp32 (Q4_K's min terms), every field 16-byte
+// aligned so it is read with 16-byte loads, and a 400-byte stride, which puts
+// the blocks read by 8 consecutive lanes on distinct banks.
 struct __align__(16) XQ {
-  int8_t qs[QK];
-  float scale;
-  int32_t sum;
-  int32_t bsums[8];
-  int32_t xs16[16];
-  int32_t pad[10];
+  int8_t qs[QK];        // 0
+  float scale;          // 256
+  int32_t sum;          // 260
+  int32_t pad0[2];
+  int32_t bsums[8];     // 272
+  int32_t xs16[16];     // 304: sum of 16-value group g = 8h + 2k + lq at 4 (2h + lq) + k
+  float bsf[8];         // 368: bsums as fp32 (exact: |bsum| <= 4064)
 };
 static_assert(sizeof(XQ) == 400, "XQ layout");
+
+// Slot of the sum of 16-value group g (values 16g .. 16g + 15) in XQ.xs16.
+__host__ __device__ __forceinline__ int xs16_slot(int g) { return 4 * (2 * (g >> 3) + (g & 1)) + ((g & 7) >> 1); }
+
+// Exact int -> fp32 for |v| < 2^22 on the integer and fp32 pipes: the bits of
+// 1.5 * 2^23 + v, minus 1.5 * 2^23.
+__device__ __forceinline__ float i2f_small(int v) { return __fsub_rn(__int_as_float(0x4B400000 + v), 12582912.0f); }
+
+// dp4a with unsigned bytes in a and signed bytes in b.
+__device__ __forceinline__ int dp4a_us(uint32_t a, int b, int c) {
+  int d;
+  asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
 
 // Q4_K block term (dot_q4k_q8 223-272 for x1, dot_q4k_q8_x4 276-337 for x4).
 __device__ __forceinline__ float q4k_block_term(const uint8_t* blk, const XQ& xb, bool x4) {
   const uint4 h = ld16(blk);
   const float d = f16_fast(h.x & 0xFFFFu), dmin = f16_fast(h.x >> 16);
+  const float4 bf0 = *reinterpret_cast<const float4*>(xb.bsf), bf1 = *reinterpret_cast<const float4*>(xb.bsf + 4);
+  const float bsv[8] = {bf0.x, bf0.y, bf0.z, bf0.w, bf1.x, bf1.y, bf1.z, bf1.w};
   float bs = 0.f;
 #pragma unroll
   for (int g = 0; g < 4; g++) {
@@ -375,75 +395,107 @@ __device__ __forceinline__ float q4k_block_term(const uint8_t* blk, const XQ& xb
     const uint32_t qw[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
     const uint32_t xl[8] = {xa.x, xa.y, xa.z, xa.w, xe.x, xe.y, xe.z, xe.w};
     const uint32_t xh[8] = {xc.x, xc.y, xc.z, xc.w, xd.x, xd.y, xd.z, xd.w};
-    int ilo = 0, ihi = 0;
+    int ilo = 0, ihi16 = 0;
 #pragma unroll
     for (int j = 0; j < 8; j++) {
-      ilo = dp4a((int)(qw[j] & 0x0F0F0F0Fu), (int)xl[j], ilo);
-      ihi = dp4a((int)((qw[j] >> 4) & 0x0F0F0F0Fu), (int)xh[j], ihi);
+      ilo = dp4a_us(qw[j] & 0x0F0F0F0Fu, (int)xl[j], ilo);
+      ihi16 = dp4a_us(qw[j] & 0xF0F0F0F0u, (int)xh[j], ihi16);   // 16 * (high nibbles . x)
     }
+    const int ihi = ihi16 >> 4;
     int sl, ml, sh, mh;
     q4k_pair_scales(g, h.y, h.z, h.w, sl, ml, sh, mh);
     const float dsl = fmul(d, (float)sl), dml = fmul(dmin, (float)ml);
     const float dsh = fmul(d, (float)sh), dmh = fmul(dmin, (float)mh);
-    const float blo = (float)xb.bsums[2 * g], bhi = (float)xb.bsums[2 * g + 1];
+    const float flo = i2f_small(ilo), fhi = i2f_small(ihi);
+    const float blo = bsv[2 * g], bhi = bsv[2 * g + 1];
     if (x4) {
-      bs = fadd(bs, fsub(fadd(fsub(fmul(dsl, (float)ilo), fmul(dml, blo)), fmul(dsh, (float)ihi)), fmul(dmh, bhi)));
+      bs = fadd(bs, fsub(fadd(fsub(fmul(dsl, flo), fmul(dml, blo)), fmul(dsh, fhi)), fmul(dmh, bhi)));
     } else {
-      bs = fadd(bs, fsub(fmul(dsl, (float)ilo), fmul(dml, blo)));
-      bs = fadd(bs, fsub(fmul(dsh, (float)ihi), fmul(dmh, bhi)));
+      bs = fadd(bs, fsub(fmul(dsl, flo), fmul(dml, blo)));
+      bs = fadd(bs, fsub(fmul(dsh, fhi), fmul(dmh, bhi)));
     }
   }
   return fmul(xb.scale, bs);
 }
 
+// The product sc * isum16 of (half h, l-half lq, quarter k) of a Q6_K block.
+__device__ __forceinline__ int q6k_prod(const uint32_t* qa, const uint32_t* qb, const uint32_t* qh, const XQ& xb,
+                                        const uint32_t* sw, int xsum, int h, int lq, int k) {
+  const uint4 xv = ld16(xb.qs + 128 * h + 32 * k + 16 * lq);
+  const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w};
+  int raw = 0;
+#pragma unroll
+  for (int q = 0; q < 4; q++) {
+    uint32_t v;
+    if (k == 0) v = (qa[q] & 0x0F0F0F0Fu) | ((qh[q] & 0x03030303u) << 4);
+    else if (k == 1) v = (qb[q] & 0x0F0F0F0Fu) | ((qh[q] & 0x0C0C0C0Cu) << 2);
+    else if (k == 2) v = ((qa[q] >> 4) & 0x0F0F0F0Fu) | (qh[q] & 0x30303030u);
+    else v = ((qb[q] >> 4) & 0x0F0F0F0Fu) | ((qh[q] >> 2) & 0x30303030u);
+    raw = dp4a_us(v, (int)xw[q], raw);
+  }
+  // (q - 32) . x = q . x - 32 * sum(x) over the 16 values
+  const int si = 8 * h + lq + 2 * k;
+  return sbyte(sw[si >> 2], si & 3) * (raw - 32 * xsum);
+}
+
+// The reference's fp32 fold of a Q6_K block's 16 products, in order (the
+// rare blocks whose partial sums may not be exact integers in fp32).
+static __device__ __noinline__ float q6k_fold_slow(const uint8_t* mb, const uint32_t* sw, const XQ& xb) {
+  float bs = 0.f;
+  for (int hl = 0; hl < 4; hl++) {
+    const int h = hl >> 1, lq = hl & 1;
+    const uint4 va = ld16(mb + 64 * h + 16 * lq), vb = ld16(mb + 64 * h + 32 + 16 * lq);
+    const uint4 vh = ld16(mb + 128 + 32 * h + 16 * lq);
+    const uint4 xs = ld16(xb.xs16 + 4 * hl);
+    const uint32_t qa[4] = {va.x, va.y, va.z, va.w}, qb[4] = {vb.x, vb.y, vb.z, vb.w};
+    const uint32_t qh[4] = {vh.x, vh.y, vh.z, vh.w};
+    const int xsv[4] = {(int)xs.x, (int)xs.y, (int)xs.z, (int)xs.w};
+#pragma unroll
+    for (int k = 0; k < 4; k++) bs = fadd(bs, (float)q6k_prod(qa, qb, qh, xb, sw, xsv[k], h, lq, k));
+  }
+  return bs;
+}
+
 // Q6_K block term (dot_q6k_q8 403-443): block_sum += sc * isum16 over
-// (half, l = 0 / 16, quarter), then (d * sx) * block_sum.  Each product of
-// two integers below 2^24 is exact in fp32, as in the reference.
+// (half, l = 0 / 16, quarter), then (d * sx) * block_sum.  Every product is
+// an integer below 2^24 in magnitude (exact in fp32), so while the sum of
+// their magnitudes stays below 2^24 every partial sum of the reference's
+// fp32 fold is an exact integer and the fold equals the int32 sum; larger
+// blocks replay the fold in order.
 __device__ __forceinline__ float q6k_block_term(const uint8_t* mb, const uint8_t* scb, const uint8_t* db,
                                                 const XQ& xb) {
   const uint4 sv = ld16(scb);
   const uint32_t sw[4] = {sv.x, sv.y, sv.z, sv.w};
-  const float d = f16_fast((uint32_t)db[0] | ((uint32_t)db[1] << 8));
-  float bs = 0.f;
+  int S = 0, A = 0;
 #pragma unroll
   for (int h = 0; h < 2; h++)
 #pragma unroll
     for (int lq = 0; lq < 2; lq++) {
       const uint4 va = ld16(mb + 64 * h + 16 * lq), vb = ld16(mb + 64 * h + 32 + 16 * lq);
       const uint4 vh = ld16(mb + 128 + 32 * h + 16 * lq);
+      const uint4 xs = ld16(xb.xs16 + 4 * (2 * h + lq));
       const uint32_t qa[4] = {va.x, va.y, va.z, va.w}, qb[4] = {vb.x, vb.y, vb.z, vb.w};
       const uint32_t qh[4] = {vh.x, vh.y, vh.z, vh.w};
+      const int xsv[4] = {(int)xs.x, (int)xs.y, (int)xs.z, (int)xs.w};
 #pragma unroll
       for (int k = 0; k < 4; k++) {
-        const uint4 xv = ld16(xb.qs + 128 * h + 32 * k + 16 * lq);
-        const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w};
-        int raw = 0;
-#pragma unroll
-        for (int q = 0; q < 4; q++) {
-          uint32_t v;
-          if (k == 0) v = (qa[q] & 0x0F0F0F0Fu) | ((qh[q] & 0x03030303u) << 4);
-          else if (k == 1) v = (qb[q] & 0x0F0F0F0Fu) | ((qh[q] & 0x0C0C0C0Cu) << 2);
-          else if (k == 2) v = ((qa[q] >> 4) & 0x0F0F0F0Fu) | (qh[q] & 0x30303030u);
-          else v = ((qb[q] >> 4) & 0x0F0F0F0Fu) | ((qh[q] >> 2) & 0x30303030u);
-          raw = dp4a((int)v, (int)xw[q], raw);
-        }
-        // (q - 32) . x = q . x - 32 * sum(x) over the 16 values
-        const int is = raw - 32 * xb.xs16[8 * h + 2 * k + lq];
-        const int si = 8 * h + lq + 2 * k;
-        const float sc = (float)(int8_t)((sw[si >> 2] >> (8 * (si & 3))) & 0xFFu);
-        bs = fadd(bs, fmul(sc, (float)is));
+        const int p = q6k_prod(qa, qb, qh, xb, sw, xsv[k], h, lq, k);
+        S += p;
+        A += abs(p);
       }
     }
+  const float bs = A < (1 << 24) ? (float)S : q6k_fold_slow(mb, sw, xb);
+  const float d = f16_fast((uint32_t)db[0] | ((uint32_t)db[1] << 8));
   return fmul(fmul(d, xb.scale), bs);
 }
 
-// Row fold over lanes: lanes lead .. lead + n - 1 hold the block terms of
-// one row in block order; every lane returns the left fold of its row,
-// starting from 0.  n must be the same on every lane.
-__device__ __forceinline__ float fold_row(float term, int lead, int n) {
+// Row fold over lanes: lanes lead, lead + stride, ... (n of them) hold the
+// block terms of one row in block order; every lane returns the left fold of
+// its row, starting from 0.  n and stride must be the same on every lane.
+__device__ __forceinline__ float fold_row(float term, int lead, int n, int stride = 1) {
   float tot = 0.f;
 #pragma unroll 4
-  for (int i = 0; i < n; i++) tot = fadd(tot, shfl(term, lead + i));
+  for (int i = 0; i < n; i++) tot = fadd(tot, shfl(term, (lead + i * stride) & 31));
   return tot;
 }
 
