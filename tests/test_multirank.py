@@ -1,0 +1,131 @@
+"""Expert-parallel layers across ranks: experts e with e % world == rank on
+each rank, the parts summed by one all-reduce (the multi-GPU plan of the
+layer path).  The decomposition is checked on CPU ranks over gloo with the
+oracle standing in for the GPU kernels; on a box with two GPUs the same is
+run through the library over NCCL."""
+import os
+import socket
+
+import numpy as np
+import pytest
+
+TOL = 1e-5
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _layer():
+    from tinygiant_b200 import synth
+    return synth.qwen_layer(seed=11, n_experts=8, D=512, I=256, top_k=3)
+
+
+def _rows():
+    from tinygiant_b200 import synth
+    return synth.rms_norm(np.random.default_rng(12).standard_normal((3, 512)).astype(np.float32))
+
+
+def _shard_part(lib, layer, N, rank, world):
+    """This rank's experts' share of the layer output (oracle or library)."""
+    from tinygiant_b200 import moe as M
+    from tinygiant_b200 import synth
+    experts, row_w, _, _ = synth.route(layer, N)
+    keep = [i for i, e in enumerate(experts) if int(e) % world == rank]
+    out = np.zeros_like(N)
+    if keep:
+        sel = [int(experts[i]) for i in keep]
+        M.moe_forward_rows_v2(lib, [layer.gates[e] for e in sel], [layer.ups[e] for e in sel],
+                              [layer.downs[e] for e in sel], layer.gate_fmt, [layer.down_fmts[e] for e in sel],
+                              None, None, None, layer.act, np.ascontiguousarray(row_w[keep]), N, out,
+                              layer.embed_dim, layer.inter_dim)
+    return out
+
+
+def _gloo_rank(rank, world, port, q):
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+    from oracle import oracle as O
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=60))
+    try:
+        lib = O.load_oracle()
+        L, N = _layer(), _rows()
+        part = torch.from_numpy(_shard_part(lib, L, N, rank, world))
+        dist.all_reduce(part)
+        if rank == 0:
+            whole = _shard_part(lib, L, N, 0, 1)
+            q.put(float(np.max(np.abs(part.numpy() - whole)) / np.max(np.abs(whole))))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_expert_shards_sum_to_whole_gloo():
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_gloo_rank, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    assert q.get(timeout=5) <= TOL
+
+
+def _nccl_rank(rank, world, port, q):
+    import ctypes
+
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+    import tinygiant_b200 as tg
+    from tinygiant_b200.layer import ResidentLayer
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        lib = tg.load()
+        lib.tg_cuda_set_device(rank)
+        L, N = _layer(), _rows()
+        shard = ResidentLayer(L, max_tokens=N.shape[0], lib=lib, shard=rank, n_shards=world)
+        x = torch.from_numpy(N).cuda()
+        out = torch.zeros_like(x)
+        stream = torch.cuda.current_stream()
+        lib.tg_cuda_set_stream(ctypes.c_void_p(stream.cuda_stream))
+        assert lib.tg_layer_forward_dev(shard.h, ctypes.c_void_p(x.data_ptr()), None, None,
+                                        ctypes.c_void_p(out.data_ptr()), N.shape[0], 0, None) == 0
+        dist.all_reduce(out)
+        torch.cuda.synchronize()
+        tg.check(lib)
+        if rank == 0:
+            whole = ResidentLayer(L, max_tokens=N.shape[0], lib=lib).forward(N, normalize=False)
+            got = out.cpu().numpy()
+            q.put(float(np.max(np.abs(got - whole)) / np.max(np.abs(whole))))
+        lib.tg_cuda_set_stream(None)
+        shard.close()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.gpu
+def test_expert_shards_nccl_two_gpus():
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_nccl_rank, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=180)
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    assert q.get(timeout=5) <= TOL

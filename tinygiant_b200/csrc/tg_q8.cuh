@@ -106,6 +106,68 @@ __device__ __forceinline__ void quantize_block_warp_vals(const float* v, int n, 
   }
 }
 
+// NB blocks at once, interleaved so their warp reductions overlap: lane l
+// holds v[b][j] = value 8l + j of block b (positions at or past n[b] passed
+// as 0); blocks with n[b] == 0 are not written.
+template <int NB, typename O>
+__device__ __forceinline__ void quantize_blocks_warp_vals(const float (*v)[8], const int* n, O* const* o) {
+  const int lane = threadIdx.x & 31;
+  float a[NB];
+#pragma unroll
+  for (int b = 0; b < NB; b++) {
+    a[b] = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; j++)
+      if (lane * 8 + j < n[b]) a[b] = max_nan(a[b], fabsf(v[b][j]));
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1)
+#pragma unroll
+    for (int b = 0; b < NB; b++) a[b] = max_nan(a[b], __shfl_xor_sync(0xffffffffu, a[b], off));
+  int s[NB], tot[NB], bs[NB];
+#pragma unroll
+  for (int b = 0; b < NB; b++) {
+    const float inv = a[b] > 0.f ? __fdiv_rn(127.f, a[b]) : 0.f;
+    int q[8];
+    s[b] = 0;
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+      q[j] = 0;
+      if (lane * 8 + j < n[b]) {
+        const float sv = __fmul_rn(v[b][j], inv);
+        q[j] = (sv != sv) ? 0 : __float2int_rn(sv);
+      }
+      s[b] += q[j];
+    }
+    uint32_t w0 = 0, w1 = 0;
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      w0 |= ((uint32_t)q[j] & 0xFFu) << (8 * j);
+      w1 |= ((uint32_t)q[4 + j] & 0xFFu) << (8 * j);
+    }
+    if (n[b] > 0) reinterpret_cast<uint2*>(o[b]->qs)[lane] = make_uint2(w0, w1);
+    bs[b] = s[b];
+    tot[b] = s[b];
+  }
+#pragma unroll
+  for (int b = 0; b < NB; b++) bs[b] += __shfl_xor_sync(0xffffffffu, bs[b], 1);
+#pragma unroll
+  for (int b = 0; b < NB; b++) bs[b] += __shfl_xor_sync(0xffffffffu, bs[b], 2);
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1)
+#pragma unroll
+    for (int b = 0; b < NB; b++) tot[b] += __shfl_xor_sync(0xffffffffu, tot[b], off);
+#pragma unroll
+  for (int b = 0; b < NB; b++) {
+    if (n[b] == 0) continue;
+    if ((lane & 3) == 0) o[b]->bsums[lane >> 2] = bs[b];
+    if (lane == 0) {
+      o[b]->scale = __fdiv_rn(a[b], 127.f);
+      o[b]->sum = tot[b];
+    }
+  }
+}
+
 // The same quantizer on a block held as two halves in 16-byte lane order:
 // lane l holds values 4l..4l+3 (lo) and 128+4l..128+4l+3 (hi); positions at
 // or past n are passed as 0.

@@ -435,21 +435,6 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
   }
   __syncthreads();
   if (wid == 0) TG_MARK(14);
-  if (wid < T) {   // warp t: lane j < K takes selection j; the sum runs in j order
-    const int t = wid;
-    const float ex = lane < K ? expf(fsub(sh.sel_v[t][lane], sh.sel_v[t][0])) : 0.f;
-    float sum = 0.f;
-    for (int j = 0; j < K; j++) sum = fadd(sum, shfl(ex, j));
-    if (lane < K) {
-      const float w = __fdiv_rn(ex, sum);
-      sh.sel_w[t][lane] = w;
-      if (blockIdx.x == 0) {
-        a.sel_idx[t * K + lane] = sh.sel_e[t][lane];
-        a.sel_w[t * K + lane] = w;
-      }
-    }
-  }
-  __syncthreads();
   // sums of each 16 values of N's staged blocks (Q6_K's bias correction)
   // and the 32-value sums as fp32
   for (int i = tid; i < T * gbpr * 24; i += SW * 32) {
@@ -461,70 +446,129 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
       xa[q].bsf[g - 16] = (float)xa[q].bsums[g - 16];
     }
   }
-  // experts held by another GPU (no local weights) are skipped; their
-  // contribution arrives through the cross-GPU sum
-  for (int i = tid; i < T * K; i += SW * 32) {
-    const int t = i / K, j = i - t * K;
-    const int e = sh.sel_e[t][j];
-    if (sh.sel_w[t][j] != 0.f && etab[e].g) atomicAdd(&sh.cnt[e], 1);
-  }
-  __syncthreads();
-  {   // exclusive scans of row counts and of non-empty experts over e < E <= 256
-    const int c = tid < E ? sh.cnt[tid] : 0, nz = c > 0;
-    int sc = c, sz = nz;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int a1 = __shfl_up_sync(FULL, sc, o), a2 = __shfl_up_sync(FULL, sz, o);
-      if (lane >= o) {
-        sc += a1;
-        sz += a2;
+  if (T == 1) {
+    // one token: its selected experts (nonzero weight, local) ascending by id
+    // are the slots, one active row each; warp 0 builds the plan
+    if (wid == 0) {
+      const float ex = lane < K ? expf(fsub(sh.sel_v[0][lane], sh.sel_v[0][0])) : 0.f;
+      float sum = 0.f;
+      for (int jj = 0; jj < K; jj++) sum = fadd(sum, shfl(ex, jj));
+      const int e = lane < K ? sh.sel_e[0][lane] : 0x7fffffff;
+      const float w = lane < K ? __fdiv_rn(ex, sum) : 0.f;
+      if (lane < K && blockIdx.x == 0) {
+        a.sel_idx[lane] = e;
+        a.sel_w[lane] = w;
+      }
+      const bool valid = lane < K && w != 0.f && etab[lane < K ? e : 0].g != nullptr;
+      const unsigned vm = __ballot_sync(FULL, valid);
+      int rank = 0;
+      for (int i = 0; i < K; i++) {
+        const int ei = __shfl_sync(FULL, e, i);
+        rank += ((vm >> i) & 1u) && ei < e;
+      }
+      if (valid) {
+        sh.slot_e[rank] = e;
+        sh.slot_n[rank] = 1;
+        sh.slot_off[rank] = rank;
+        sh.row_t[rank] = 0;
+        sh.row_w[rank] = w;
+        const StepExpert& q = etab[e];
+        ExpertDesc X;
+        X.gate = wdesc(q.g, a.gate_fmt, I, D);
+        X.up = wdesc(q.u, a.gate_fmt, I, D);
+        X.down = wdesc(q.d, a.down_fmt, D, I);
+        X.gb = q.gb;
+        X.ub = q.ub;
+        X.db = q.db;
+        sx[rank] = X;
+      }
+      if (lane == 0) {
+        sh.n_slots = __popc(vm);
+        sh.total = __popc(vm);
       }
     }
-    if (lane == 31) {
-      sh.wsum[0][wid] = sc;
-      sh.wsum[1][wid] = sz;
+    __syncthreads();
+  } else {
+    if (wid < T) {   // warp t: lane j < K takes selection j; the sum runs in j order
+      const int t = wid;
+      const float ex = lane < K ? expf(fsub(sh.sel_v[t][lane], sh.sel_v[t][0])) : 0.f;
+      float sum = 0.f;
+      for (int j = 0; j < K; j++) sum = fadd(sum, shfl(ex, j));
+      if (lane < K) {
+        const float w = __fdiv_rn(ex, sum);
+        sh.sel_w[t][lane] = w;
+        if (blockIdx.x == 0) {
+          a.sel_idx[t * K + lane] = sh.sel_e[t][lane];
+          a.sel_w[t * K + lane] = w;
+        }
+      }
     }
     __syncthreads();
-    int bc = 0, bz = 0;
-    for (int j = 0; j < wid; j++) {
-      bc += sh.wsum[0][j];
-      bz += sh.wsum[1][j];
+    // experts held by another GPU (no local weights) are skipped; their
+    // contribution arrives through the cross-GPU sum
+    for (int i = tid; i < T * K; i += SW * 32) {
+      const int t = i / K, j = i - t * K;
+      const int e = sh.sel_e[t][j];
+      if (sh.sel_w[t][j] != 0.f && etab[e].g) atomicAdd(&sh.cnt[e], 1);
     }
-    if (tid < E) {
-      sh.off[tid] = bc + sc - c;
-      sh.slot_of[tid] = nz ? bz + sz - 1 : -1;
-    }
-    if (tid == SW * 32 - 1) {
-      sh.n_slots = bz + sz;
-      sh.total = bc + sc;
-    }
-  }
-  __syncthreads();
-  for (int e = tid; e < E; e += SW * 32) {
-    const int s = sh.slot_of[e];
-    if (s < 0) continue;
-    int o = sh.off[e];
-    sh.slot_e[s] = e;
-    sh.slot_n[s] = sh.cnt[e];
-    sh.slot_off[s] = o;
-    for (int t = 0; t < T; t++)
-      for (int j = 0; j < K; j++)
-        if (sh.sel_e[t][j] == e && sh.sel_w[t][j] != 0.f) {
-          sh.row_t[o] = t;
-          sh.row_w[o] = sh.sel_w[t][j];
-          o++;
+    __syncthreads();
+    {   // exclusive scans of row counts and of non-empty experts over e < E <= 256
+      const int c = tid < E ? sh.cnt[tid] : 0, nz = c > 0;
+      int sc = c, sz = nz;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int a1 = __shfl_up_sync(FULL, sc, o), a2 = __shfl_up_sync(FULL, sz, o);
+        if (lane >= o) {
+          sc += a1;
+          sz += a2;
         }
-    const StepExpert& q = etab[e];
-    ExpertDesc X;
-    X.gate = wdesc(q.g, a.gate_fmt, I, D);
-    X.up = wdesc(q.u, a.gate_fmt, I, D);
-    X.down = wdesc(q.d, a.down_fmt, D, I);
-    X.gb = q.gb;
-    X.ub = q.ub;
-    X.db = q.db;
-    sx[s] = X;
+      }
+      if (lane == 31) {
+        sh.wsum[0][wid] = sc;
+        sh.wsum[1][wid] = sz;
+      }
+      __syncthreads();
+      int bc = 0, bz = 0;
+      for (int j = 0; j < wid; j++) {
+        bc += sh.wsum[0][j];
+        bz += sh.wsum[1][j];
+      }
+      if (tid < E) {
+        sh.off[tid] = bc + sc - c;
+        sh.slot_of[tid] = nz ? bz + sz - 1 : -1;
+      }
+      if (tid == SW * 32 - 1) {
+        sh.n_slots = bz + sz;
+        sh.total = bc + sc;
+      }
+    }
+    __syncthreads();
+    for (int e = tid; e < E; e += SW * 32) {
+      const int s = sh.slot_of[e];
+      if (s < 0) continue;
+      int o = sh.off[e];
+      sh.slot_e[s] = e;
+      sh.slot_n[s] = sh.cnt[e];
+      sh.slot_off[s] = o;
+      for (int t = 0; t < T; t++)
+        for (int j = 0; j < K; j++)
+          if (sh.sel_e[t][j] == e && sh.sel_w[t][j] != 0.f) {
+            sh.row_t[o] = t;
+            sh.row_w[o] = sh.sel_w[t][j];
+            o++;
+          }
+      const StepExpert& q = etab[e];
+      ExpertDesc X;
+      X.gate = wdesc(q.g, a.gate_fmt, I, D);
+      X.up = wdesc(q.u, a.gate_fmt, I, D);
+      X.down = wdesc(q.d, a.down_fmt, D, I);
+      X.gb = q.gb;
+      X.ub = q.ub;
+      X.db = q.db;
+      sx[s] = X;
+    }
+    __syncthreads();
   }
-  __syncthreads();
 
   if (wid == 0) TG_MARK(4);
   // ---- A and B: the per-warp ring
@@ -715,12 +759,13 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
             v[h][jj] = i < nn[h] ? __ldcg(a.hidden + (size_t)row * I + (size_t)b * QK + i) : 0.f;
           }
         }
+        XQ* outs[2] = {xs + q0, xs + min(q0 + SW, nq - 1)};
+        quantize_blocks_warp_vals<2>(v, nn, outs);
+        __syncwarp();
 #pragma unroll
         for (int h = 0; h < 2; h++) {
           const int q = q0 + h * SW;
           if (q < nq) {
-            quantize_block_warp_vals(v[h], nn[h], xs + q);
-            __syncwarp();
             if (lane < 16) {   // sums of each 16 values
               const int4 w = *reinterpret_cast<const int4*>(xs[q].qs + 16 * lane);
               xs[q].xs16[xs16_slot(lane)] = dp4a(w.x, 0x01010101, dp4a(w.y, 0x01010101, dp4a(w.z, 0x01010101, dp4a(w.w, 0x01010101, 0))));
