@@ -18,7 +18,9 @@ traffic) earlier and are not L2-resident.
 e2e: the same step through the C-ABI entry tg_layer_forward with host
 buffers (x in, MoE output back), host<->device copies inside the timed region.
 
-Multi-GPU (torchrun): experts sharded by id (e % N == rank), router
+Multi-GPU (torchrun), --parallel dp (default): every GPU holds the layer
+and serves its own tokens; no collective on the data path, per-GPU work is
+fixed ("weak").  --parallel ep: experts sharded by id (e % N == rank), router
 replicated, one NCCL all-reduce of the [T, D] output per step; total work is
 fixed ("strong").
 
@@ -46,6 +48,10 @@ sys.path.insert(0, str(ROOT))
 METRIC = "MoE-layer decode tok/s; fused quant-matvec HBM GB/s vs ~8 TB/s B200 peak"
 UNIT = "tok/s"
 R_COPIES = 16
+DTYPES = {"c2": "int8xQ4_K/Q6_K (int32 accumulate), fp32 combine",
+          "c3": "int8xQ4_K/Q6_K (int32 accumulate), fp32 combine",
+          "c4": "int8xMXFP4 (int32 accumulate), fp32 combine",
+          "c5": "int8xQ4_K/Q6_K (int32 accumulate), fp32 combine"}
 
 
 def parse():
@@ -58,6 +64,7 @@ def parse():
     ap.add_argument("--tokens", type=int, default=None)
     ap.add_argument("--copies", type=int, default=R_COPIES)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--parallel", default="dp", choices=["dp", "ep"])
     return ap.parse_args()
 
 
@@ -92,7 +99,7 @@ def step_inputs(n, T, D, seed=4):
 
 def algorithmic_bytes(L, xs):
     """Per step: each distinct selected expert's weight bytes once + the fp32
-    router + x in and out (SURVEY 8d); routing by the reference router."""
+    router + x in and out; routing by the reference router."""
     from tinygiant_b200 import synth
     eb = L.expert_bytes(0)
     out = []
@@ -230,7 +237,7 @@ def run_reference(a):
     value = a.steps * T / el
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": a.gpus, "steps": a.steps,
             "warmup": a.warmup, "ms_per_step": el / a.steps * 1e3, "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "int8xQ4_K/Q6_K (int32 accumulate), fp32 combine", "data": "synthetic",
+            "vs_baseline": None, "dtype": DTYPES.get(cfg, DTYPES["c2"]), "data": "synthetic",
             "config": workload_desc(cfg, T, 1, L),
             "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": kind,
                              "sample": f"{a.steps} steps x {T} token(s); numpy router + "
@@ -268,19 +275,21 @@ def run_ours(a):
     L = make_layer(cfg)
     D = L.embed_dim
     R = max(1, a.copies)
-    base = ResidentLayer(L, max_tokens=T, lib=lib, shard=rank, n_shards=world)
+    ep = world > 1 and a.parallel == "ep"
+    base = ResidentLayer(L, max_tokens=T, lib=lib, shard=rank if ep else 0, n_shards=world if ep else 1)
     layers = [base] + [base.clone() for _ in range(R - 1)]
     tg.check(lib)
 
     S = a.warmup + a.steps
-    xs_host = step_inputs(S, T, D)
+    # data-parallel ranks serve different tokens; expert-parallel ranks the same ones
+    xs_host = step_inputs(S, T, D, seed=4 if ep or world == 1 else 4 + 1000 * rank)
     xs = torch.from_numpy(xs_host).to(f"cuda:{local}")
     out = torch.zeros((T, D), dtype=torch.float32, device=f"cuda:{local}")
 
     def step(i):
         lay = layers[i % R]
         lib.tg_layer_forward_dev(lay.h, xs[i].data_ptr(), None, None, out.data_ptr(), T, 1, None)
-        if world > 1:
+        if ep:
             dist.all_reduce(out)
 
     # warm-up (also exercises every copy once)
@@ -330,11 +339,12 @@ def run_ours(a):
     tg.check(lib)
 
     ms_step = ms / a.steps
-    value = a.steps * T / (ms / 1e3)
+    ranks_tokens = 1 if ep else world   # data-parallel ranks each process their own tokens
+    value = ranks_tokens * a.steps * T / (ms / 1e3)
     line = None
     if rank == 0:
         nbytes = algorithmic_bytes(L, xs_host[a.warmup:])
-        achieved = nbytes.sum() / (ms / 1e3) / 1e9
+        achieved = ranks_tokens * nbytes.sum() / (ms / 1e3) / 1e9
         peak, peak_src = measured_peak()
         peak *= world            # whole-job bytes against every GPU's HBM
         tr = traffic_from_profiles()
@@ -343,14 +353,17 @@ def run_ours(a):
                 "kernel": "fused MoE layer step (router + gate/up + down kernels), per step",
                 "algorithmic_bytes_per_step": float(nbytes.mean()), "peak_source": peak_src}
         line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": a.steps,
-                "warmup": a.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong",
-                "vs_baseline": None, "dtype": "int8xQ4_K/Q6_K (int32 accumulate), fp32 combine",
+                "warmup": a.warmup, "ms_per_step": ms_step, "higher_is_better": True,
+                "scaling": "strong" if ep or world == 1 else "weak",
+                "vs_baseline": None, "dtype": DTYPES.get(cfg, DTYPES["c2"]),
                 "data": "synthetic (seeded weights and inputs)",
-                "config": {**workload_desc(cfg, T, R, L), "parallelism": f"ep{world}"},
+                "config": {**workload_desc(cfg, T, R, L), "parallelism": f"ep{world}" if ep else f"dp{world}"},
                 "gbps": achieved, "clocks": clk, "roofline": roof, "gpu_launches": int(launches)}
 
-    # e2e through the C ABI with host buffers (rank 0 of a single-GPU run;
-    # with N > 1 every rank runs it and the slowest counts)
+    # e2e: one GPU through the C-ABI entry tg_layer_forward with host buffers
+    # (synchronous, x in / MoE output out every step); several GPUs through
+    # tg_layer_forward_dev with each step's x copied from pinned host memory
+    # and its output read back, plus the all-reduce for ep; max over ranks.
     e2e = None
     if world == 1:
         xh = [np.ascontiguousarray(x) for x in xs_host]
@@ -364,6 +377,35 @@ def run_ours(a):
         tg.check(lib)
         e2e = {"value": a.steps * T / el, "unit": UNIT, "h2d_bytes_per_step": int(xh[0].nbytes),
                "d2h_bytes_per_step": int(outh.nbytes), "api": "tg_layer_forward (C ABI, host buffers)",
+               "ms_per_step": el / a.steps * 1e3}
+    else:
+        xpin = torch.from_numpy(xs_host).pin_memory()
+        opin = torch.zeros((T, D), dtype=torch.float32).pin_memory()
+        xd = torch.empty((T, D), dtype=torch.float32, device=f"cuda:{local}")
+
+        def e2e_step(i):
+            with torch.cuda.stream(stream):
+                xd.copy_(xpin[i], non_blocking=True)
+                lib.tg_layer_forward_dev(layers[i % R].h, xd.data_ptr(), None, None, out.data_ptr(), T, 1, None)
+                if ep:
+                    dist.all_reduce(out)
+                opin.copy_(out, non_blocking=True)
+            stream.synchronize()
+
+        for i in range(min(a.warmup, S)):
+            e2e_step(i)
+        dist.barrier()
+        t0 = time.perf_counter()
+        for i in range(a.warmup, S):
+            e2e_step(i)
+        el = time.perf_counter() - t0
+        t = torch.tensor([el], device=f"cuda:{local}")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        el = float(t.item())
+        tg.check(lib)
+        e2e = {"value": ranks_tokens * a.steps * T / el, "unit": UNIT, "h2d_bytes_per_step": int(xs_host[0].nbytes),
+               "d2h_bytes_per_step": int(opin.numel() * 4),
+               "api": "tg_layer_forward_dev per rank, pinned host copies" + (" + NCCL all-reduce" if ep else ""),
                "ms_per_step": el / a.steps * 1e3}
     if rank == 0:
         line["e2e"] = e2e

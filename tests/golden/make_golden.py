@@ -1,6 +1,6 @@
 """Writes the golden fixtures in tests/golden/ from the REFERENCE itself.
 
-    python tests/golden/make_golden.py          (needs /root/reference)
+    python tests/golden/make_golden.py          (needs the reference checkout: TG_REFERENCE_DIR)
 
 Sources, all run in this container:
   * oracle/_ref/libtinygiant_ref_hooks.so — the reference's
