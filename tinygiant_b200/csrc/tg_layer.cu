@@ -23,6 +23,7 @@ struct Layer {
   std::vector<ExpertDesc> experts;  // host copy of the device table
   std::vector<void*> owned;         // device allocations to free
   ExpertDesc* d_experts = nullptr;
+  StepExpert* d_step = nullptr;     // [E] weight pointers for the fused step kernel
   float* router_w = nullptr;
   float* router_b = nullptr;
   // scratch
@@ -39,7 +40,7 @@ struct Layer {
   float* hidden = nullptr;
   Q8Dev* hq8 = nullptr;
   int* counters = nullptr;
-  unsigned long long* step_sync = nullptr;   // grid-barrier arrival count of the fused step kernel
+  unsigned long long* step_sync = nullptr;   // the fused step kernel's exchange block (step_sync_words)
   bool fused = true;               // use the fused step kernel when the shape allows
   float* moe_out = nullptr;  // [2][max_tokens][D] for stacks and the host entry
   float* xbuf = nullptr;     // [max_tokens][D]
@@ -74,10 +75,25 @@ static bool alloc_scratch(Layer* L) {
          dmalloc(L, (void**)&L->hq8, sizeof(Q8Dev) * (size_t)L->max_rows * dbpr) &&
          dmalloc(L, (void**)&L->counters, sizeof(int) * moe_counter_ints(L->max_slots, I)) &&
          (register_counters(L->counters, sizeof(int) * moe_counter_ints(L->max_slots, I)), true) &&
-         dmalloc(L, (void**)&L->step_sync, sizeof(unsigned long long)) &&
-         (register_counters(L->step_sync, sizeof(unsigned long long)), true) &&
+         dmalloc(L, (void**)&L->step_sync, sizeof(unsigned long long) * step_sync_words(T, E, L->top_k, I)) &&
+         (register_counters(L->step_sync, sizeof(unsigned long long) * step_sync_words(T, E, L->top_k, I)), true) &&
          dmalloc(L, (void**)&L->moe_out, sizeof(float) * 2 * (size_t)T * D) &&
          dmalloc(L, (void**)&L->xbuf, sizeof(float) * (size_t)T * D);
+}
+
+// Device copies of the expert table and of the step kernel's pointer table.
+static bool upload_tables(Layer* L) {
+  std::vector<StepExpert> st(L->E);
+  for (int e = 0; e < L->E; e++) {
+    const ExpertDesc& X = L->experts[e];
+    st[e] = StepExpert{X.gate.main, X.up.main, X.down.main, X.gb, X.ub, X.db};
+  }
+  if (!dmalloc(L, (void**)&L->d_experts, sizeof(ExpertDesc) * L->E) ||
+      !dmalloc(L, (void**)&L->d_step, sizeof(StepExpert) * L->E))
+    return false;
+  return cudaMemcpy(L->d_experts, L->experts.data(), sizeof(ExpertDesc) * L->E, cudaMemcpyHostToDevice) ==
+             cudaSuccess &&
+         cudaMemcpy(L->d_step, st.data(), sizeof(StepExpert) * L->E, cudaMemcpyHostToDevice) == cudaSuccess;
 }
 
 static void free_layer(Layer* L) {
@@ -114,10 +130,8 @@ static bool layer_enqueue(Layer* L, const float* x, const float* add, float* x_o
   sl.bias_term = 1;
   sl.gate_fmt = L->gate_fmt;
   sl.down_fmt = L->down_fmt;
-  sl.experts = L->d_experts;
-  sl.xq8 = L->xq8;
+  sl.etab = L->d_step;
   sl.logits = L->logits;
-  sl.hidden = L->hidden;
   sl.out = moe_out;
   sl.sel_idx = L->sel_idx;
   sl.sel_w = L->sel_w;
@@ -244,13 +258,11 @@ void* tg_layer_create_shard(int n_experts, const uint8_t* const* gate_ptrs, cons
     if (down_bias) X.db = lookup_vector(down_bias[e], embed_dim);
   }
   const size_t rw = sizeof(float) * (size_t)n_experts * embed_dim;
-  if (!dmalloc(L, (void**)&L->d_experts, sizeof(ExpertDesc) * n_experts) ||
-      !dmalloc(L, (void**)&L->router_w, rw) || (router_b && !dmalloc(L, (void**)&L->router_b, sizeof(float) * n_experts)) ||
-      !alloc_scratch(L)) {
+  if (!upload_tables(L) || !dmalloc(L, (void**)&L->router_w, rw) ||
+      (router_b && !dmalloc(L, (void**)&L->router_b, sizeof(float) * n_experts)) || !alloc_scratch(L)) {
     free_layer(L);
     return nullptr;
   }
-  cudaMemcpy(L->d_experts, L->experts.data(), sizeof(ExpertDesc) * n_experts, cudaMemcpyHostToDevice);
   cudaMemcpy(L->router_w, router_w, rw, cudaMemcpyHostToDevice);
   if (router_b) cudaMemcpy(L->router_b, router_b, sizeof(float) * n_experts, cudaMemcpyHostToDevice);
   if (cudaGetLastError() != cudaSuccess) {
@@ -304,12 +316,11 @@ void* tg_layer_clone(void* handle) {
       return nullptr;
     }
   const size_t rw = sizeof(float) * (size_t)L->E * L->D;
-  if (!dmalloc(L, (void**)&L->d_experts, sizeof(ExpertDesc) * L->E) || !dmalloc(L, (void**)&L->router_w, rw) ||
+  if (!upload_tables(L) || !dmalloc(L, (void**)&L->router_w, rw) ||
       (src->router_b && !dmalloc(L, (void**)&L->router_b, sizeof(float) * L->E)) || !alloc_scratch(L)) {
     free_layer(L);
     return nullptr;
   }
-  cudaMemcpy(L->d_experts, L->experts.data(), sizeof(ExpertDesc) * L->E, cudaMemcpyHostToDevice);
   cudaMemcpy(L->router_w, src->router_w, rw, cudaMemcpyDeviceToDevice);
   if (src->router_b) cudaMemcpy(L->router_b, src->router_b, sizeof(float) * L->E, cudaMemcpyDeviceToDevice);
   return L;

@@ -49,6 +49,25 @@ struct RouteArgs {
 
 size_t route_smem_bytes(int D, int E, int T, int K);
 
+// One expert's weight pointers for the fused step kernel; the row layouts
+// follow from the layer's formats and shape.  A null gate marks an expert
+// held by another GPU.
+struct StepExpert {
+  const uint8_t* g;
+  const uint8_t* u;
+  const uint8_t* d;
+  const float* gb;
+  const float* ub;
+  const float* db;
+};
+static_assert(sizeof(StepExpert) == 48, "StepExpert is copied in 16-byte units");
+
+// Words of the fused step's exchange block for a layer of E experts, top_k,
+// intermediate I and up to T rows per step: the launch counter, the tagged
+// logits [T][E] and the tagged hidden activations [T*top_k][ceil(I/256)][256].
+// All zero at creation (and after an error reset).
+size_t step_sync_words(int T, int E, int top_k, int I);
+
 // One layer step (routing + experts) as a single persistent kernel, for
 // decode-sized batches (tg_step.cu).  `out` is overwritten with the MoE
 // output.
@@ -62,14 +81,12 @@ struct StepLaunch {
   const float* router_w;
   const float* router_b;
   int T, D, E, top_k, I, act, assoc_rule, bias_term, gate_fmt, down_fmt;
-  const ExpertDesc* experts;
-  Q8Dev* xq8;         // [T][ceil(D/256)]
-  float* logits;      // [T][E]
-  float* hidden;      // [T*top_k][I]
-  float* out;         // [T][D]
-  int* sel_idx;       // [T][top_k]
-  float* sel_w;       // [T][top_k]
-  unsigned long long* sync;   // grid-barrier arrival count, zero at creation
+  const StepExpert* etab;     // [E]
+  float* logits;              // [T][E]
+  float* out;                 // [T][D]
+  int* sel_idx;               // [T][top_k]
+  float* sel_w;               // [T][top_k]
+  unsigned long long* sync;   // the exchange block (step_sync_words), 256-byte aligned
   DevStatus* st;
 };
 bool step_eligible(const StepLaunch& l);

@@ -171,7 +171,8 @@ __device__ __forceinline__ void quantize_blocks_warp_vals(const float (*v)[8], c
 // The same quantizer on a block held as two halves in 16-byte lane order:
 // lane l holds values 4l..4l+3 (lo) and 128+4l..128+4l+3 (hi); positions at
 // or past n are passed as 0.
-__device__ __forceinline__ void quantize_block_warp_f4(const float4& lo, const float4& hi, int n, Q8Dev* o) {
+template <typename O>
+__device__ __forceinline__ void quantize_block_warp_f4(const float4& lo, const float4& hi, int n, O* o) {
   const int lane = threadIdx.x & 31;
   const float v[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
   float a = 0.f;

@@ -11,19 +11,26 @@
 //   A  gate.x, up.x (+ biases), activation -> hidden   (moe_phase_a, 1279-1327)
 //   B  Q8 of hidden, down.hidden, part = w * (v + b), combine in expert order
 //                                                      (moe_phase_b 1329-1384, 1428-1434)
-// One CTA per SM.  R runs on one warp per expert; a grid barrier makes the
-// logits and N's Q8 blocks visible; every CTA then repeats S on its own (it
-// is tiny) instead of waiting for one CTA to publish it.  A and B stream
-// their weight rows through a per-warp ring of shared-memory stages filled
-// by bulk asynchronous copies (cp.async.bulk, no multicast): the ring runs
-// straight from a warp's gate/up items into its down items, so the down
-// weights are in flight while phase A computes; a second grid barrier only
-// orders hidden before phase B reads it.
+// One CTA per SM.  R runs one warp per expert (its router row); every CTA
+// quantizes N itself and repeats S on its own (both are tiny) instead of
+// waiting for one CTA to publish them.  A and B stream their weight rows
+// through a per-warp ring of shared-memory stages filled by bulk
+// asynchronous copies (cp.async.bulk, no multicast): the ring runs straight
+// from a warp's gate/up items into its down items, so the down weights are
+// in flight while phase A computes.
 //
-// Grid barriers are a self-resetting arrival count plus a generation word;
-// every wait (barrier, mbarrier) gives up after about a second and records
-// an error instead of hanging.  The grid never exceeds the CTAs the GPU holds
-// at once, so all CTAs reach each barrier.
+// There is no grid-wide barrier.  The two values CTAs exchange — router
+// logits and hidden activations — are written as 64-bit words holding the
+// launch's epoch in the high half and the fp32 value in the low half; one
+// aligned 64-bit store is seen whole, so a consumer that reads a word tagged
+// with this launch's epoch has its value, and consumers poll the words
+// themselves (one L2 round trip per poll, no separate flag).  The epoch is the
+// launch count: each CTA adds one to a 64-bit counter as it starts (before
+// it lets the next kernel launch), so the G CTAs of launch n read counts
+// n*G .. n*G + G - 1.  Words a launch does not rewrite are never read by it.
+// Every wait (poll, mbarrier) gives up after about a second and records an
+// error instead of hanging; the grid never exceeds the CTAs the GPU holds at
+// once, so every producer runs.
 #include <algorithm>
 
 #include "tg_moe.h"
@@ -38,6 +45,7 @@ constexpr int STEP_T_MAX = 8;
 constexpr int STEP_K_MAX = 8;
 constexpr int STEP_R_MAX = STEP_T_MAX * STEP_K_MAX;   // active rows
 constexpr int STEP_E_MAX = 256;
+constexpr int STEP_POLLS = 1 << 23;   // polls of another CTA's words before giving up (~1 s with the sleeps)
 
 struct StepShared {
   float lg[STEP_T_MAX * STEP_E_MAX];
@@ -48,47 +56,45 @@ struct StepShared {
   int slot_of[STEP_E_MAX];
   int off[STEP_E_MAX];
   int wsum[2][SW];
-  int n_slots, total, ok;
+  int n_slots, total;
+  uint32_t epoch;
   int slot_e[STEP_R_MAX], slot_n[STEP_R_MAX], slot_off[STEP_R_MAX];
   int row_t[STEP_R_MAX];
   float row_w[STEP_R_MAX];
   uint64_t rbar[SW];
-  uint64_t xbar;
+  uint64_t xbar, ebar;
   float accw[SW][STEP_T_MAX];
   unsigned long long tw[SW][6];
   uint64_t bars[SW][ST_MAX_NST];
 };
 
-__device__ __forceinline__ unsigned long long ld_acquire64(const unsigned long long* p) {
-  unsigned long long v;
-  asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-  return v;
-}
+// ---------------------------------------------------------------------
+// Epoch-tagged words.
 
-// Grid-wide barrier over gridDim.x co-resident CTAs on a 64-bit arrival
-// count that only grows (zero at creation, a multiple of the grid between
-// launches): arrival k of a barrier returns it to at least the next multiple
-// of the grid.  Returns false after a timeout.
-__device__ bool grid_sync(unsigned long long* cnt, int& ok_sh) {
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    unsigned long long prev;
-    asm volatile("atom.add.release.gpu.u64 %0, [%1], 1;" : "=l"(prev) : "l"(cnt) : "memory");
-    const unsigned long long target = (prev / gridDim.x + 1) * gridDim.x;
-    bool ok = true;
-    const long long t0 = clock64();
-    while (ld_acquire64(cnt) < target) {
-      if (clock64() - t0 > (1ll << 31)) {
-        ok = false;
-        break;
-      }
-      __nanosleep(32);
-    }
-    __threadfence();
-    ok_sh = ok;
-  }
-  __syncthreads();
-  return ok_sh != 0;
+__device__ __forceinline__ void st_tagged(unsigned long long* p, uint32_t ep, float v) {
+  const unsigned long long w = ((unsigned long long)ep << 32) | __float_as_uint(v);
+  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_tagged(const unsigned long long* p) {
+  unsigned long long w;
+  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+  return w;
+}
+__device__ __forceinline__ ulonglong2 ld_tagged2(const unsigned long long* p) {
+  ulonglong2 w;
+  asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(w.x), "=l"(w.y) : "l"(p) : "memory");
+  return w;
+}
+__device__ __forceinline__ bool tag_is(unsigned long long w, uint32_t ep) { return (uint32_t)(w >> 32) == ep; }
+__device__ __forceinline__ float tag_val(unsigned long long w) { return __uint_as_float((uint32_t)w); }
+
+// Word of hidden value r (0 .. I-1) of active row o: each 256-value block is
+// stored so that lane l's values 8l .. 8l+7 are four 16-byte pairs at
+// 64-word strides (value p = 8l + j at word 64 (j / 2) + 2l + j % 2), which
+// makes each of a warp's four pair loads one contiguous 512-byte line set.
+__device__ __forceinline__ size_t hid_word(int o, int r, int dbpr) {
+  const int b = r >> 8, p = r & 255;
+  return ((size_t)o * dbpr + b) * 256 + ((p & 7) >> 1) * 64 + 2 * (p >> 3) + (p & 1);
 }
 
 // Whether (vj, j) ranks above (vi, i): larger logit first, NaN below every
@@ -99,24 +105,16 @@ __device__ __forceinline__ bool ranks_above(float vj, int j, float vi, int i) {
   return in || vj > vi || (vj == vi && j < i);
 }
 
-// The weight pointers of one expert (its matrices' row layouts follow from
-// the layer's formats and shape).
-struct StepExpert {
-  const uint8_t* g;
-  const uint8_t* u;
-  const uint8_t* d;
-  const float* gb;
-  const float* ub;
-  const float* db;
-};
-
-__device__ __forceinline__ WDesc wdesc(const uint8_t* m, int fmt, int rows, int cols) {
-  const RowLayout L = row_layout(fmt, cols);
+// Matrix descriptor of format F with `rows` rows of `cols` values at m (row
+// layout of tg_common.cuh).
+template <int F>
+__device__ __forceinline__ WDesc wdesc(const uint8_t* m, int rows, int cols) {
+  const RowLayout L = row_layout(F, cols);
   WDesc w;
   w.main = m;
-  w.aux1 = m && L.a1 >= 0 ? m + L.a1 : nullptr;
-  w.aux2 = m && L.a2 >= 0 ? m + L.a2 : nullptr;
-  w.fmt = fmt;
+  w.aux1 = L.a1 >= 0 ? m + L.a1 : nullptr;
+  w.aux2 = L.a2 >= 0 ? m + L.a2 : nullptr;
+  w.fmt = F;
   w.rows = rows;
   w.cols = cols;
   w.rs = L.rs;
@@ -132,15 +130,15 @@ struct StepArgs {
   int normalize;
   const float* router_w;  // [E][D]
   const float* router_b;  // [E] or null
-  int T, D, E, top_k, I, act, assoc_rule, bias_term, gate_fmt, down_fmt;
-  const ExpertDesc* experts;
-  Q8Dev* xq8;             // [T][gbpr]
+  int T, D, E, top_k, I, act, assoc_rule, bias_term;
+  const StepExpert* etab; // [E]
   float* logits;          // [T][E]
-  float* hidden;          // [T*top_k][I]
   float* out;             // [T][D], overwritten with the step's MoE output
   int* sel_idx;           // [T][top_k]
   float* sel_w;           // [T][top_k]
-  unsigned long long* sync;   // arrival count of the grid barriers
+  unsigned long long* sync;   // launch counter
+  unsigned long long* lgt;    // [T][E] tagged logits
+  unsigned long long* hidt;   // [T*top_k][dbpr][256] tagged hidden
   uint32_t stage_bytes;   // ring stage size
   int nst;                // ring stages per warp
   int xcap;               // active rows whose Q8 hidden blocks fit each CTA's shared memory
@@ -189,6 +187,30 @@ __device__ __forceinline__ bool scur_next(SCur& c, long gw, long NW, long nA, in
   return c.r < D;
 }
 
+// Lane 0 of a warp: the bulk copies of item c into stage dst (completing on
+// bar).  Phase 0: rows r0 .. r0 + nr - 1 of the slot's gate (at dst) and up
+// (at dst + ghalf); phase 1: row c.r of the down matrices of slots c.s ..
+// c.s + SB - 1, dr bytes apart.  Not inlined: the ring calls it from three
+// places.
+template <int GF, int DF>
+static __device__ __noinline__ void step_issue(const StepExpert* sx, SCur c, uint8_t* dst, uint64_t* bar, int nrb,
+                                               int pa, int I, int D, uint32_t ghalf, uint32_t dr, int n_slots,
+                                               int SB) {
+  if (c.ph == 0) {
+    const int s = (int)(c.a / nrb), r0 = (int)(c.a - (long)s * nrb) * pa, nr = min(pa, I - r0);
+    const WDesc Gw = wdesc<GF>(sx[s].g, I, D), Uw = wdesc<GF>(sx[s].u, I, D);
+    mbar_arrive_expect_tx(bar, row_tx(Gw, r0, nr) + row_tx(Uw, r0, nr));
+    stage_row(Gw, r0, dst, bar, nr);
+    stage_row(Uw, r0, dst + ghalf, bar, nr);
+  } else {
+    const int s1 = min(n_slots, c.s + SB);
+    uint32_t tx = 0;
+    for (int s = c.s; s < s1; s++) tx += row_tx(wdesc<DF>(sx[s].d, D, I), (int)c.r);
+    mbar_arrive_expect_tx(bar, tx);
+    for (int s = c.s; s < s1; s++) stage_row(wdesc<DF>(sx[s].d, D, I), (int)c.r, dst + (s - c.s) * dr, bar);
+  }
+}
+
 template <int GF, int DF>
 __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
   extern __shared__ __align__(128) uint8_t dsm[];
@@ -203,122 +225,106 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
   float* rrow = reinterpret_cast<float*>(dsm + (size_t)SW * a.nst * a.stage_bytes);   // [rwc][D]
   XQ* xa = reinterpret_cast<XQ*>(reinterpret_cast<uint8_t*>(rrow) + round16((size_t)a.rwc * D * 4));   // [T][gbpr]
   XQ* xs = xa + (size_t)T * gbpr;   // [xcap][dbpr]
-  ExpertDesc* sx = reinterpret_cast<ExpertDesc*>(xs + (size_t)a.xcap * dbpr);       // [xcap] the slots' experts
-  StepExpert* etab = reinterpret_cast<StepExpert*>(sx + a.xcap);                     // [E] weight pointers
+  StepExpert* sx = reinterpret_cast<StepExpert*>(xs + (size_t)a.xcap * dbpr);   // [xcap] the slots' experts
+  StepExpert* etab = sx + a.xcap;                                                 // [E]
   uint64_t* bar = sh.bars[wid];
   if (a.trace && tid == 0) a.trace[blockIdx.x * 16 + 12] = gtimer();
   if (wid == 0) TG_MARK(0);
 
-  // ---- R: router rows do not depend on the preceding kernel: stage them now.
+  // ---- Before the preceding kernel completes: the epoch, this warp's router
+  // row and the expert table (none of them written by a preceding kernel).
   const int e_r = blockIdx.x + wid * G;   // this warp's expert, if wid < rwc
   const bool router_warp = wid < a.rwc && e_r < E;
   const float* wsrc = a.router_w + (size_t)(router_warp ? e_r : 0) * D;
-  const bool wbulk = router_warp && ((uintptr_t)wsrc & 15) == 0 && (D & 3) == 0;
+  const bool wbulk = router_warp && ((uintptr_t)wsrc & 15) == 0;
   if (lane == 0) {
     for (int i = 0; i < a.nst; i++) mbar_init(&bar[i], 1);
-    if (wbulk) mbar_init(&sh.rbar[wid], 1);
+    mbar_init(&sh.rbar[wid], 1);
+    if (wid == 0) {
+      mbar_init(&sh.xbar, 1);
+      mbar_init(&sh.ebar, 1);
+    }
     fence_mbar_init();
     if (wbulk) {
       mbar_arrive_expect_tx(&sh.rbar[wid], (uint32_t)D * 4);
       bulk_g2s(rrow + (size_t)wid * D, wsrc, (uint32_t)D * 4, &sh.rbar[wid]);
     }
-  }
-  // the layer's expert table does not change between steps either: its
-  // loads are issued now and stored to shared memory after the router work
-  constexpr int EV = 3;   // table words per thread (E * 6 <= EV * 512)
-  const void* ev[EV];
-#pragma unroll
-  for (int q = 0; q < EV; q++) {
-    const int i = tid + q * SW * 32, e = i / 6, f = i - e * 6;
-    ev[q] = nullptr;
-    if (e < E) {
-      const ExpertDesc& X = a.experts[e];
-      ev[q] = f == 0 ? (const void*)X.gate.main : f == 1 ? (const void*)X.up.main : f == 2 ? (const void*)X.down.main
-            : f == 3 ? (const void*)X.gb : f == 4 ? (const void*)X.ub : (const void*)X.db;
+    if (wid == 0) {
+      mbar_arrive_expect_tx(&sh.ebar, (uint32_t)E * sizeof(StepExpert));
+      bulk_g2s(etab, a.etab, (uint32_t)E * sizeof(StepExpert), &sh.ebar);
+      unsigned long long prev;
+      asm volatile("atom.add.relaxed.gpu.u64 %0, [%1], 1;" : "=l"(prev) : "l"(a.sync) : "memory");
+      sh.epoch = (uint32_t)(prev / (unsigned long long)G) + 1u;
     }
   }
-  // x (and add) rows: staged into the ring's space, which phase A only uses
-  // after barrier 1, with one bulk copy each
-  const int qb = wid >= a.rwc ? (int)blockIdx.x + (wid - a.rwc) * G : -1;
-  const bool quant_warp = qb >= 0 && qb < T * gbpr;
-  const bool cta_reads_x = (int)blockIdx.x < E || (int)blockIdx.x < T * gbpr;
+  __syncthreads();
+  pdl_trigger();   // this CTA holds its epoch count: the next launch may take its own
+  const uint32_t ep = sh.epoch;
+  pdl_wait();      // x (and add) are written by the preceding kernel
   const uint32_t xbytes = (uint32_t)T * D * 4;
   const bool xstaged = (size_t)xbytes * (a.add_in ? 2 : 1) <= (size_t)SW * a.nst * a.stage_bytes;
   const float* xsm = reinterpret_cast<const float*>(dsm);
   const float* asm_ = a.add_in ? xsm + (size_t)T * D : nullptr;
-  if (tid == 0) {
-    mbar_init(&sh.xbar, 1);
-    fence_mbar_init();
-  }
-  __syncthreads();
-  pdl_wait();   // x (and add) are written by the preceding kernel
-  if (tid == 0 && xstaged && cta_reads_x) {
+  if (tid == 0 && xstaged) {
     mbar_arrive_expect_tx(&sh.xbar, xbytes * (a.add_in ? 2 : 1));
     bulk_g2s(dsm, a.x_in, xbytes, &sh.xbar);
     if (a.add_in) bulk_g2s(dsm + xbytes, a.add_in, xbytes, &sh.xbar);
   }
   if (wid == 0) TG_MARK(1);
 
-  // Router warps (wid < rwc): expert e_r's logits for every token.  Quantizer
-  // warps (wid >= rwc): Q8 block qb of N (token qb / gbpr).  Both read their
-  // token rows once, from the staged copy (or global memory), 16 bytes a lane.
-  if (router_warp || quant_warp) {
-    if (xstaged && !mbar_wait(&sh.xbar, 0) && lane == 0) set_error(a.st, ERR_WAIT_TIMEOUT, 36, blockIdx.x, wid);
-    constexpr int RCH = 8;
-    const int nc = (D + 127) / 128;   // 16-byte chunks per lane
+  // ---- R.  Router warps (wid < rwc): expert e_r's logit for every token.
+  // The other warps: Q8 blocks of N, q = wid - rwc, + (SW - rwc), ...
+  // (token q / gbpr).  Each reads its token row once, 16 bytes a lane.
+  bool dead = false;   // this warp stopped on an error
+  {
+    const int nqw = SW - a.rwc, qw = wid - a.rwc;
+    const int nwork = router_warp ? T : qw >= 0 ? (T * gbpr - qw + nqw - 1) / nqw : 0;
+    if (nwork > 0 && xstaged && !mbar_wait(&sh.xbar, 0)) {
+      if (lane == 0) set_error(a.st, ERR_WAIT_TIMEOUT, 36, blockIdx.x, wid);
+      dead = true;
+    }
+    if (router_warp && wbulk && !mbar_wait(&sh.rbar[wid], 0)) {
+      if (lane == 0) set_error(a.st, ERR_WAIT_TIMEOUT, 30, e_r, 0);
+      dead = true;
+    }
     const float* wr = wbulk ? rrow + (size_t)wid * D : wsrc;
-    if (router_warp && wbulk && !mbar_wait(&sh.rbar[wid], 0) && lane == 0)
-      set_error(a.st, ERR_WAIT_TIMEOUT, 30, e_r, 0);
-    const int t_lo = router_warp ? 0 : qb / gbpr, t_hi = router_warp ? T : qb / gbpr + 1;
-    const int bq = quant_warp ? qb - (qb / gbpr) * gbpr : -1;
-    for (int t = t_lo; t < t_hi; t++) {
-      const float* xt = a.x_in + (size_t)t * D;
-      const float* at = a.add_in ? a.add_in + (size_t)t * D : nullptr;
+    const int nc = (D + 127) / 128;   // 16-byte chunks per lane
+#pragma unroll 1
+    for (int k = 0; k < (dead ? 0 : nwork); k++) {
+      const int q = router_warp ? -1 : qw + k * nqw;
+      const int t = router_warp ? k : q / gbpr;
+      const int bq = router_warp ? -1 : q - t * gbpr;
       float ss = 0.f, dot = 0.f;
       float4 hlo = make_float4(0.f, 0.f, 0.f, 0.f), hhi = hlo;
-      for (int c0 = 0; c0 < nc; c0 += RCH) {
-        float4 xv[RCH];
-#pragma unroll
-        for (int c = 0; c < RCH; c++) {
-          const int i = 128 * (c0 + c) + 4 * lane;
-          xv[c] = make_float4(0.f, 0.f, 0.f, 0.f);
-          if (c0 + c < nc && i < D)
-            xv[c] = xstaged ? *reinterpret_cast<const float4*>(xsm + (size_t)t * D + i)
-                            : __ldcg(reinterpret_cast<const float4*>(xt + i));
-        }
-        if (at)
-#pragma unroll
-          for (int c = 0; c < RCH; c++) {
-            const int i = 128 * (c0 + c) + 4 * lane;
-            if (c0 + c < nc && i < D) {
-              const float4 d = xstaged ? *reinterpret_cast<const float4*>(asm_ + (size_t)t * D + i)
-                                       : __ldcg(reinterpret_cast<const float4*>(at + i));
-              xv[c] = make_float4(fadd(xv[c].x, d.x), fadd(xv[c].y, d.y), fadd(xv[c].z, d.z), fadd(xv[c].w, d.w));
-            }
+#pragma unroll 2
+      for (int c = 0; c < nc; c++) {
+        const int i = 128 * c + 4 * lane;
+        if (i < D) {
+          const size_t o = (size_t)t * D + i;
+          float4 v = xstaged ? *reinterpret_cast<const float4*>(xsm + o)
+                             : __ldcg(reinterpret_cast<const float4*>(a.x_in + o));
+          if (a.add_in) {
+            const float4 d = xstaged ? *reinterpret_cast<const float4*>(asm_ + o)
+                                     : __ldcg(reinterpret_cast<const float4*>(a.add_in + o));
+            v = make_float4(fadd(v.x, d.x), fadd(v.y, d.y), fadd(v.z, d.z), fadd(v.w, d.w));
           }
-#pragma unroll
-        for (int c = 0; c < RCH; c++) {
-          const int i = 128 * (c0 + c) + 4 * lane;
-          if (c0 + c < nc && i < D) {
-            float4 v = xv[c];
-            if (e_r == 0 && router_warp && a.x_out) *reinterpret_cast<float4*>(a.x_out + (size_t)t * D + i) = v;
-            ss = __fmaf_rn(v.x, v.x, ss);
-            ss = __fmaf_rn(v.y, v.y, ss);
-            ss = __fmaf_rn(v.z, v.z, ss);
-            ss = __fmaf_rn(v.w, v.w, ss);
-            if (c0 + c == 2 * bq) hlo = v;
-            if (c0 + c == 2 * bq + 1) hhi = v;
-            if (router_warp) {
-              if (a.normalize && a.norm_w) {
-                const float4 nw = __ldg(reinterpret_cast<const float4*>(a.norm_w + i));
-                v = make_float4(fmul(v.x, nw.x), fmul(v.y, nw.y), fmul(v.z, nw.z), fmul(v.w, nw.w));
-              }
-              const float4 w = *reinterpret_cast<const float4*>(wr + i);
-              dot = __fmaf_rn(w.x, v.x, dot);
-              dot = __fmaf_rn(w.y, v.y, dot);
-              dot = __fmaf_rn(w.z, v.z, dot);
-              dot = __fmaf_rn(w.w, v.w, dot);
+          if (e_r == 0 && router_warp && a.x_out) *reinterpret_cast<float4*>(a.x_out + o) = v;
+          ss = __fmaf_rn(v.x, v.x, ss);
+          ss = __fmaf_rn(v.y, v.y, ss);
+          ss = __fmaf_rn(v.z, v.z, ss);
+          ss = __fmaf_rn(v.w, v.w, ss);
+          if (c == 2 * bq) hlo = v;
+          if (c == 2 * bq + 1) hhi = v;
+          if (router_warp) {
+            if (a.normalize && a.norm_w) {
+              const float4 nw = __ldg(reinterpret_cast<const float4*>(a.norm_w + i));
+              v = make_float4(fmul(v.x, nw.x), fmul(v.y, nw.y), fmul(v.z, nw.z), fmul(v.w, nw.w));
             }
+            const float4 w = *reinterpret_cast<const float4*>(wr + i);
+            dot = __fmaf_rn(w.x, v.x, dot);
+            dot = __fmaf_rn(w.y, v.y, dot);
+            dot = __fmaf_rn(w.z, v.z, dot);
+            dot = __fmaf_rn(w.w, v.w, dot);
           }
         }
       }
@@ -330,9 +336,12 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
       const float rr = a.normalize ? __fsqrt_rn(fadd(__fdiv_rn(ss, (float)D), a.eps)) : 1.f;
       if (router_warp) {
         if (a.normalize) dot = __fdiv_rn(dot, rr);
-        if (lane == 0) a.logits[(size_t)t * E + e_r] = a.router_b ? fadd(dot, a.router_b[e_r]) : dot;
-      }
-      if (quant_warp) {
+        const float lg = a.router_b ? fadd(dot, a.router_b[e_r]) : dot;
+        if (lane == 0) {
+          a.logits[(size_t)t * E + e_r] = lg;
+          st_tagged(a.lgt + (size_t)t * E + e_r, ep, lg);
+        }
+      } else {
         const int b0 = bq * QK, n = min(QK, D - b0);
         float* hv[2] = {&hlo.x, &hhi.x};
 #pragma unroll
@@ -350,54 +359,44 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
             }
             hv[h][jj] = x;
           }
-        quantize_block_warp_f4(hlo, hhi, n, a.xq8 + qb);
+        XQ& xb = xa[q];
+        quantize_block_warp_f4(hlo, hhi, n, &xb);
+        __syncwarp();
+        if (lane < 16) {   // sums of each 16 values (Q6_K's bias correction)
+          const int4 w = *reinterpret_cast<const int4*>(xb.qs + 16 * lane);
+          xb.xs16[xs16_slot(lane)] =
+              dp4a(w.x, 0x01010101, dp4a(w.y, 0x01010101, dp4a(w.z, 0x01010101, dp4a(w.w, 0x01010101, 0))));
+        } else if (lane < 24) {
+          xb.bsf[lane - 16] = (float)xb.bsums[lane - 16];
+        }
       }
     }
-  }
-
-#pragma unroll
-  for (int q = 0; q < EV; q++) {
-    const int i = tid + q * SW * 32, e = i / 6, f = i - e * 6;
-    if (e < E) reinterpret_cast<const void**>(etab + e)[f] = ev[q];
   }
   if (wid == 0) TG_MARK(2);
-  // ---- barrier 1: logits and xq8 visible everywhere
-  if (!grid_sync(a.sync, sh.ok)) {
-    if (tid == 0) set_error(a.st, ERR_WAIT_TIMEOUT, 31, blockIdx.x, 0);
-    return;
-  }
+  if (tid == 0 && !mbar_wait(&sh.ebar, 0)) set_error(a.st, ERR_WAIT_TIMEOUT, 37, blockIdx.x, 0);
+  if (__syncthreads_or(dead)) return;   // nothing in flight: the copies above were all waited for
 
-  if (wid == 0) TG_MARK(3);
-  // ---- S: selection and plan, in every CTA
+  // ---- S: every CTA polls the logits (tagged with this epoch), then ranks
+  // and plans on its own.
   bool nan_here = false;
-  // N's Q8 blocks (written by other CTAs before barrier 1) into shared
-  // memory, in the same round trip as the logits
-  for (int i = tid; i < T * gbpr * 19; i += SW * 32) {   // qs in 16 pieces, scale / sum, bsums in 2
-    const int q = i / 19, w = i - q * 19;
-    const uint4* src = reinterpret_cast<const uint4*>(a.xq8 + q);
-    if (w < 16) {
-      reinterpret_cast<uint4*>(xa[q].qs)[w] = __ldcg(src + w);
-    } else if (w == 16) {
-      const uint4 v = __ldcg(src + 16);   // scale, sum, bsums[0..1]
-      xa[q].scale = __uint_as_float(v.x);
-      xa[q].sum = (int)v.y;
-      xa[q].bsums[0] = (int)v.z;
-      xa[q].bsums[1] = (int)v.w;
-    } else {
-      const uint4 v = __ldcg(src + w);    // bsums[2..5] or bsums[6..7] and padding
-      const int b0 = 2 + 4 * (w - 17);
-      xa[q].bsums[b0] = (int)v.x;
-      xa[q].bsums[b0 + 1] = (int)v.y;
-      if (w == 17) {
-        xa[q].bsums[4] = (int)v.z;
-        xa[q].bsums[5] = (int)v.w;
+  for (int it = 0;; it++) {
+    bool miss = false;
+    for (int i = tid; i < T * E; i += SW * 32) {
+      const unsigned long long w = ld_tagged(a.lgt + i);
+      if (!tag_is(w, ep)) {
+        miss = true;
+      } else {
+        const float v = tag_val(w);
+        sh.lg[i] = v;
+        nan_here |= v != v;
       }
     }
-  }
-  for (int i = tid; i < T * E; i += SW * 32) {
-    const float v = __ldcg(a.logits + i);
-    sh.lg[i] = v;
-    nan_here |= v != v;
+    if (!__syncthreads_or(miss)) break;
+    if (it >= STEP_POLLS) {
+      if (tid == 0) set_error(a.st, ERR_WAIT_TIMEOUT, 31, blockIdx.x, 0);
+      return;
+    }
+    __nanosleep(64);
   }
   for (int i = tid; i < E; i += SW * 32) sh.cnt[i] = 0;
   const bool any_nan = __syncthreads_or(nan_here) != 0;
@@ -418,7 +417,7 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
         v = sh.lg[el];
         const float* row = sh.lg + t * E;
         if (!any_nan)
-#pragma unroll 8
+#pragma unroll 4
           for (int jj = part; jj < E; jj += P) {
             const float vj = row[jj];
             rank += (vj > v) | ((vj == v) & (jj < e));
@@ -435,17 +434,6 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
   }
   __syncthreads();
   if (wid == 0) TG_MARK(14);
-  // sums of each 16 values of N's staged blocks (Q6_K's bias correction)
-  // and the 32-value sums as fp32
-  for (int i = tid; i < T * gbpr * 24; i += SW * 32) {
-    const int q = i / 24, g = i - q * 24;
-    if (g < 16) {
-      const int4 w = *reinterpret_cast<const int4*>(xa[q].qs + 16 * g);
-      xa[q].xs16[xs16_slot(g)] = dp4a(w.x, 0x01010101, dp4a(w.y, 0x01010101, dp4a(w.z, 0x01010101, dp4a(w.w, 0x01010101, 0))));
-    } else {
-      xa[q].bsf[g - 16] = (float)xa[q].bsums[g - 16];
-    }
-  }
   if (T == 1) {
     // one token: its selected experts (nonzero weight, local) ascending by id
     // are the slots, one active row each; warp 0 builds the plan
@@ -472,15 +460,7 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
         sh.slot_off[rank] = rank;
         sh.row_t[rank] = 0;
         sh.row_w[rank] = w;
-        const StepExpert& q = etab[e];
-        ExpertDesc X;
-        X.gate = wdesc(q.g, a.gate_fmt, I, D);
-        X.up = wdesc(q.u, a.gate_fmt, I, D);
-        X.down = wdesc(q.d, a.down_fmt, D, I);
-        X.gb = q.gb;
-        X.ub = q.ub;
-        X.db = q.db;
-        sx[rank] = X;
+        sx[rank] = etab[e];
       }
       if (lane == 0) {
         sh.n_slots = __popc(vm);
@@ -557,15 +537,7 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
             sh.row_w[o] = sh.sel_w[t][j];
             o++;
           }
-      const StepExpert& q = etab[e];
-      ExpertDesc X;
-      X.gate = wdesc(q.g, a.gate_fmt, I, D);
-      X.up = wdesc(q.u, a.gate_fmt, I, D);
-      X.down = wdesc(q.d, a.down_fmt, D, I);
-      X.gb = q.gb;
-      X.ub = q.ub;
-      X.db = q.db;
-      sx[s] = X;
+      sx[s] = etab[e];
     }
     __syncthreads();
   }
@@ -590,21 +562,7 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
   const int gbb = GF == FMT_Q4K ? Q4K_BYTES : 192, dbb = DF == FMT_Q4K ? Q4K_BYTES : 192;   // main bytes per block
 
   auto issue = [&](const SCur& c, int stg) {   // lane 0
-    uint8_t* dst = ring + (size_t)stg * a.stage_bytes;
-    if (c.ph == 0) {
-      const int s = (int)(c.a / nrb), r0 = (int)(c.a - (long)s * nrb) * pa, nr = min(pa, I - r0);
-      const WDesc& Gw = sx[s].gate;
-      const WDesc& Uw = sx[s].up;
-      mbar_arrive_expect_tx(&bar[stg], row_tx(Gw, r0, nr) + row_tx(Uw, r0, nr));
-      stage_row(Gw, r0, dst, &bar[stg], nr);
-      stage_row(Uw, r0, dst + ghalf, &bar[stg], nr);
-    } else {
-      const int s1 = min(n_slots, c.s + SB);
-      uint32_t tx = 0;
-      for (int s = c.s; s < s1; s++) tx += row_tx(sx[s].down, (int)c.r);
-      mbar_arrive_expect_tx(&bar[stg], tx);
-      for (int s = c.s; s < s1; s++) stage_row(sx[s].down, (int)c.r, dst + (s - c.s) * dr, &bar[stg]);
-    }
+    step_issue<GF, DF>(sx, c, ring + (size_t)stg * a.stage_bytes, &bar[stg], nrb, pa, I, D, ghalf, dr, n_slots, SB);
   };
   SCur ic{0, gw - NW, 0, 0};
   int issued = 0;
@@ -616,7 +574,6 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
       issued++;
     }
   }
-  bool dead = false;
   int j = 0;   // items consumed
   // Stops the warp: no further copies are issued, and those in flight
   // (items from .. issued-1) are waited for, each wait bounded.
@@ -669,12 +626,13 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
     const int stg = j % a.nst;
     if (!wait_stage(stg, j)) continue;
     const int s = (int)(it / nrb), r0 = (int)(it - (long)s * nrb) * pa, nr = min(pa, I - r0);
-    const ExpertDesc& X = sx[s];
+    const StepExpert& X = sx[s];
+    const WDesc Gw = wdesc<GF>(X.g, I, D), Uw = wdesc<GF>(X.u, I, D);
     const uint8_t* dst = ring + (size_t)stg * a.stage_bytes;
     const int n = sh.slot_n[s], off = sh.slot_off[s];
     if constexpr (GBLK) {
       const bool on = a_pr < nr;
-      const RowPtrs rp = row_ptrs(a_m ? X.up : X.gate, r0, dst + (a_m ? ghalf : 0));
+      const RowPtrs rp = row_ptrs(a_m ? Uw : Gw, r0, dst + (a_m ? ghalf : 0));
       const uint8_t* mb = rp.m + (size_t)a_pr * grs + (size_t)a_b * gbb;
       const uint8_t* s1b = rp.a1 ? rp.a1 + (size_t)a_pr * grs + a_b * 16 : nullptr;
       const uint8_t* s2b = rp.a2 ? rp.a2 + (size_t)a_pr * grs + a_b * 2 : nullptr;
@@ -696,11 +654,11 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
             gt = fadd(gt, X.gb[r]);
             ut = fadd(ut, X.ub[r]);
           }
-          a.hidden[(size_t)(off + jj) * I + r] = act_fn(act, gt, ut);
+          st_tagged(a.hidt + hid_word(off + jj, r, dbpr), ep, act_fn(act, gt, ut));
         }
       }
     } else {
-      const RowPtrs pg = row_ptrs(X.gate, r0, dst), pu = row_ptrs(X.up, r0, dst + ghalf);
+      const RowPtrs pg = row_ptrs(Gw, r0, dst), pu = row_ptrs(Uw, r0, dst + ghalf);
 #pragma unroll 1
       for (int g0 = 0; g0 < n; g0 += 4) {
         const int ng = min(4, n - g0);
@@ -721,7 +679,7 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
             gt = fadd(gt, X.gb[r0]);
             ut = fadd(ut, X.ub[r0]);
           }
-          a.hidden[(size_t)(off + g0 + lane) * I + r0] = act_fn(act, gt, ut);
+          st_tagged(a.hidt + hid_word(off + g0 + lane, r0, dbpr), ep, act_fn(act, gt, ut));
         }
       }
     }
@@ -731,55 +689,72 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
   if (wid == 0) TG_MARK(5);
   if (wid == SW - 1) TG_MARK(10);
   tph = 1;
-  // ---- barrier 2: hidden complete
-  const bool ok2 = grid_sync(a.sync, sh.ok);
-  if (ok2) pdl_trigger();
-  else if (tid == 0) set_error(a.st, ERR_WAIT_TIMEOUT, 33, blockIdx.x, 0);
-  if (wid == 0) TG_MARK(6);
-  bool ok3 = ok2;
-  if (ok2) {
-    if (total > a.xcap) {
-      if (tid == 0) set_error(a.st, ERR_BAD_PLAN, 35, total, a.xcap);
-      ok3 = false;
-    } else {
-      // every CTA quantizes the (few) hidden rows into its shared memory,
-      // loading two blocks per warp before quantizing either
-      const int nq = total * dbpr;
-      for (int q0 = wid; q0 < nq; q0 += 2 * SW) {
-        float v[2][8];
-        int nn[2];
+  // ---- hidden: every CTA polls the active rows' hidden blocks (tagged with
+  // this epoch) and quantizes them into its shared memory, two blocks per
+  // warp at a time.
+  bool okh = !dead;
+  if (total > a.xcap) {
+    if (tid == 0) set_error(a.st, ERR_BAD_PLAN, 35, total, a.xcap);
+    okh = false;
+  }
+  const int nq = okh ? total * dbpr : 0;
+  for (int q0 = wid; q0 < nq; q0 += 2 * SW) {
+    float v[2][8];
+    int nn[2];
 #pragma unroll
-        for (int h = 0; h < 2; h++) {
-          const int q = q0 + h * SW;
-          const int row = q / dbpr, b = q - row * dbpr;
-          nn[h] = q < nq ? min(QK, I - b * QK) : 0;
+    for (int h = 0; h < 2; h++) {
+      const int q = q0 + h * SW;
+      nn[h] = q < nq ? min(QK, I - (q % dbpr) * QK) : 0;
+    }
+    for (int it = 0;; it++) {
+      bool ok = true;
 #pragma unroll
-          for (int jj = 0; jj < 8; jj++) {
-            const int i = lane * 8 + jj;
-            v[h][jj] = i < nn[h] ? __ldcg(a.hidden + (size_t)row * I + (size_t)b * QK + i) : 0.f;
-          }
-        }
-        XQ* outs[2] = {xs + q0, xs + min(q0 + SW, nq - 1)};
-        quantize_blocks_warp_vals<2>(v, nn, outs);
-        __syncwarp();
+      for (int h = 0; h < 2; h++) {
+        const unsigned long long* src = a.hidt + (size_t)(q0 + h * SW) * 256 + 2 * lane;
 #pragma unroll
-        for (int h = 0; h < 2; h++) {
-          const int q = q0 + h * SW;
-          if (q < nq) {
-            if (lane < 16) {   // sums of each 16 values
-              const int4 w = *reinterpret_cast<const int4*>(xs[q].qs + 16 * lane);
-              xs[q].xs16[xs16_slot(lane)] = dp4a(w.x, 0x01010101, dp4a(w.y, 0x01010101, dp4a(w.z, 0x01010101, dp4a(w.w, 0x01010101, 0))));
-            } else if (lane < 24) {
-              xs[q].bsf[lane - 16] = (float)xs[q].bsums[lane - 16];
+        for (int p = 0; p < 4; p++) {
+          const int i = 8 * lane + 2 * p;
+          v[h][2 * p] = v[h][2 * p + 1] = 0.f;
+          if (i < nn[h]) {
+            const ulonglong2 w = ld_tagged2(src + 64 * p);
+            ok &= tag_is(w.x, ep);
+            v[h][2 * p] = tag_val(w.x);
+            if (i + 1 < nn[h]) {
+              ok &= tag_is(w.y, ep);
+              v[h][2 * p + 1] = tag_val(w.y);
             }
           }
         }
       }
+      if (__all_sync(FULL, ok)) break;
+      if (it >= STEP_POLLS) {
+        if (lane == 0) set_error(a.st, ERR_WAIT_TIMEOUT, 33, blockIdx.x, wid);
+        okh = false;
+        break;
+      }
+      __nanosleep(64);
+    }
+    if (!okh) break;
+    if (wid == 0 && q0 == 0) TG_MARK(6);
+#pragma unroll 1
+    for (int h = 0; h < 2 && nn[h] > 0; h++) {
+      XQ& xb = xs[q0 + h * SW];
+      float vv[8];
+#pragma unroll
+      for (int jj = 0; jj < 8; jj++) vv[jj] = h ? v[1][jj] : v[0][jj];
+      quantize_block_warp_vals(vv, nn[h], &xb);
+      __syncwarp();
+      if (lane < 16) {   // sums of each 16 values
+        const int4 w = *reinterpret_cast<const int4*>(xb.qs + 16 * lane);
+        xb.xs16[xs16_slot(lane)] =
+            dp4a(w.x, 0x01010101, dp4a(w.y, 0x01010101, dp4a(w.z, 0x01010101, dp4a(w.w, 0x01010101, 0))));
+      } else if (lane < 24) {
+        xb.bsf[lane - 16] = (float)xb.bsums[lane - 16];
+      }
     }
   }
   if (wid == 0) TG_MARK(15);
-  __syncthreads();
-  if (!ok3) stop(j);
+  if (!__syncthreads_and(okh)) stop(j);
   if (wid == 0) TG_MARK(7);
 
   // phase B: rows r = gw, gw + NW, ... < D; slots in groups of SB
@@ -801,9 +776,9 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
           const int s = s0 + b_sl;
           const bool in = s < s1, on = in && b_b < dbpr2;
           const int sc = in ? s : s0;
-          const ExpertDesc& X = sx[sc];
+          const StepExpert& X = sx[sc];
           const int n = in ? sh.slot_n[sc] : 0, off = sh.slot_off[sc];
-          const RowPtrs rp = row_ptrs(X.down, (int)r, dst + (sc - s0) * dr);
+          const RowPtrs rp = row_ptrs(wdesc<DF>(X.d, D, I), (int)r, dst + (sc - s0) * dr);
           const uint8_t* mb = rp.m + (size_t)b_b * dbb;
           const uint8_t* s1b = rp.a1 ? rp.a1 + b_b * 16 : nullptr;
           const uint8_t* s2b = rp.a2 ? rp.a2 + b_b * 2 : nullptr;
@@ -838,8 +813,8 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
           }
         } else {
           for (int s = s0; s < s1; s++) {
-            const ExpertDesc& X = sx[s];
-            const RowPtrs rp = row_ptrs(X.down, (int)r, dst + (s - s0) * dr);
+            const StepExpert& X = sx[s];
+            const RowPtrs rp = row_ptrs(wdesc<DF>(X.d, D, I), (int)r, dst + (s - s0) * dr);
             const int n = sh.slot_n[s], off = sh.slot_off[s];
 #pragma unroll 1
             for (int g0 = 0; g0 < n; g0 += 4) {
@@ -882,6 +857,11 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
 // ---------------------------------------------------------------------
 // Launcher.
 
+size_t step_sync_words(int T, int E, int top_k, int I) {
+  const int t = std::min(T, STEP_T_MAX), dbpr = (I + QK - 1) / QK;
+  return 32 + (((size_t)t * E + 31) & ~(size_t)31) + (size_t)t * top_k * dbpr * 256;
+}
+
 // Shared-memory shape of one launch, or false when the step does not fit.
 struct StepShape {
   uint32_t stage;
@@ -906,10 +886,12 @@ static bool step_shape(const StepLaunch& l, StepShape& sh) {
   if (!gf || !df || l.T < 1 || l.T > STEP_T_MAX || l.E < 1 || l.E > STEP_E_MAX || l.top_k < 1 ||
       l.top_k > STEP_K_MAX || l.top_k > l.E || (l.D & 3))
     return false;
-  // rows are read and written as float4
-  const void* ptrs[] = {l.x_in, l.add_in, l.x_out, l.norm_w, l.router_w, l.out};
+  // rows are read and written as float4; the expert table and the exchange
+  // block are copied / addressed in 16-byte units
+  const void* ptrs[] = {l.x_in, l.add_in, l.x_out, l.norm_w, l.router_w, l.out, l.etab, l.sync};
   for (const void* q : ptrs)
     if (reinterpret_cast<uintptr_t>(q) & 15) return false;
+  if (!l.etab || !l.sync) return false;
   // 256-block formats put a row's blocks on consecutive lanes: at most 16
   // blocks per gate / up row (a row pair fills the warp), 32 per down row
   const bool gblk = l.gate_fmt == FMT_Q4K || l.gate_fmt == FMT_Q6K;
@@ -919,11 +901,11 @@ static bool step_shape(const StepLaunch& l, StepShape& sh) {
   const int G = step_sms();
   sh.pa = gblk ? std::max(1, 16 / bg) : 1;
   sh.rwc = (l.E + G - 1) / G;
-  if (sh.rwc > SW) return false;
+  if (sh.rwc >= SW) return false;   // at least one warp quantizes N
   const int gbpr = (l.D + QK - 1) / QK, dbpr = (l.I + QK - 1) / QK;
   sh.xcap = l.T * l.top_k;
   const size_t fixed = round16((size_t)sh.rwc * l.D * 4) + (size_t)l.T * gbpr * sizeof(XQ) +
-                       (size_t)sh.xcap * dbpr * sizeof(XQ) + (size_t)sh.xcap * sizeof(ExpertDesc) +
+                       (size_t)sh.xcap * dbpr * sizeof(XQ) + (size_t)sh.xcap * sizeof(StepExpert) +
                        (size_t)l.E * sizeof(StepExpert);
   const size_t budget = 220 * 1024 - sizeof(StepShared);
   const uint32_t dr = rows_stage_bytes(row_layout(l.down_fmt, l.I).rs, 1);
@@ -1017,16 +999,17 @@ cudaError_t launch_layer_step(const StepLaunch& l, cudaStream_t s) {
   a.act = l.act;
   a.assoc_rule = l.assoc_rule;
   a.bias_term = l.bias_term;
-  a.gate_fmt = l.gate_fmt;
-  a.down_fmt = l.down_fmt;
-  a.experts = l.experts;
-  a.xq8 = l.xq8;
+  a.etab = l.etab;
   a.logits = l.logits;
-  a.hidden = l.hidden;
   a.out = l.out;
   a.sel_idx = l.sel_idx;
   a.sel_w = l.sel_w;
   a.sync = l.sync;
+  // the tagged regions are placed for this launch's T (inside the block the
+  // layer sized for its largest T); words left there by earlier launches
+  // carry older epochs and are never taken
+  a.lgt = l.sync + 32;
+  a.hidt = a.lgt + (((size_t)std::min(l.T, STEP_T_MAX) * l.E + 31) & ~(size_t)31);
   a.st = l.st;
   a.trace = g_step_trace;
 #define TG_STEP_CASE(GFV, DFV) \

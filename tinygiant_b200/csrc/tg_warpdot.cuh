@@ -381,17 +381,19 @@ __device__ __forceinline__ int dp4a_us(uint32_t a, int b, int c) {
 }
 
 // Q4_K block term (dot_q4k_q8 223-272 for x1, dot_q4k_q8_x4 276-337 for x4).
+// The four 64-value groups run as a loop (not unrolled): the step kernel
+// executes each block term only a few times per launch, so its instruction
+// footprint costs more than the loop.
 __device__ __forceinline__ float q4k_block_term(const uint8_t* blk, const XQ& xb, bool x4) {
   const uint4 h = ld16(blk);
   const float d = f16_fast(h.x & 0xFFFFu), dmin = f16_fast(h.x >> 16);
-  const float4 bf0 = *reinterpret_cast<const float4*>(xb.bsf), bf1 = *reinterpret_cast<const float4*>(xb.bsf + 4);
-  const float bsv[8] = {bf0.x, bf0.y, bf0.z, bf0.w, bf1.x, bf1.y, bf1.z, bf1.w};
   float bs = 0.f;
-#pragma unroll
+#pragma unroll 1
   for (int g = 0; g < 4; g++) {
     const uint4 q0 = ld16(blk + 16 + 32 * g), q1 = ld16(blk + 32 + 32 * g);
     const uint4 xa = ld16(xb.qs + 64 * g), xe = ld16(xb.qs + 64 * g + 16);
     const uint4 xc = ld16(xb.qs + 64 * g + 32), xd = ld16(xb.qs + 64 * g + 48);
+    const float2 bf = *reinterpret_cast<const float2*>(xb.bsf + 2 * g);
     const uint32_t qw[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
     const uint32_t xl[8] = {xa.x, xa.y, xa.z, xa.w, xe.x, xe.y, xe.z, xe.w};
     const uint32_t xh[8] = {xc.x, xc.y, xc.z, xc.w, xd.x, xd.y, xd.z, xd.w};
@@ -407,12 +409,11 @@ __device__ __forceinline__ float q4k_block_term(const uint8_t* blk, const XQ& xb
     const float dsl = fmul(d, (float)sl), dml = fmul(dmin, (float)ml);
     const float dsh = fmul(d, (float)sh), dmh = fmul(dmin, (float)mh);
     const float flo = i2f_small(ilo), fhi = i2f_small(ihi);
-    const float blo = bsv[2 * g], bhi = bsv[2 * g + 1];
     if (x4) {
-      bs = fadd(bs, fsub(fadd(fsub(fmul(dsl, flo), fmul(dml, blo)), fmul(dsh, fhi)), fmul(dmh, bhi)));
+      bs = fadd(bs, fsub(fadd(fsub(fmul(dsl, flo), fmul(dml, bf.x)), fmul(dsh, fhi)), fmul(dmh, bf.y)));
     } else {
-      bs = fadd(bs, fsub(fmul(dsl, flo), fmul(dml, blo)));
-      bs = fadd(bs, fsub(fmul(dsh, fhi), fmul(dmh, bhi)));
+      bs = fadd(bs, fsub(fmul(dsl, flo), fmul(dml, bf.x)));
+      bs = fadd(bs, fsub(fmul(dsh, fhi), fmul(dmh, bf.y)));
     }
   }
   return fmul(xb.scale, bs);
@@ -461,29 +462,45 @@ static __device__ __noinline__ float q6k_fold_slow(const uint8_t* mb, const uint
 // an integer below 2^24 in magnitude (exact in fp32), so while the sum of
 // their magnitudes stays below 2^24 every partial sum of the reference's
 // fp32 fold is an exact integer and the fold equals the int32 sum; larger
-// blocks replay the fold in order.
+// blocks replay the fold in order.  The four (half, l-half) pairs run as a
+// loop (not unrolled), for a small instruction footprint.
 __device__ __forceinline__ float q6k_block_term(const uint8_t* mb, const uint8_t* scb, const uint8_t* db,
                                                 const XQ& xb) {
   const uint4 sv = ld16(scb);
-  const uint32_t sw[4] = {sv.x, sv.y, sv.z, sv.w};
   int S = 0, A = 0;
+#pragma unroll 1
+  for (int hl = 0; hl < 4; hl++) {
+    const int h = hl >> 1, lq = hl & 1;
+    const uint4 va = ld16(mb + 64 * h + 16 * lq), vb = ld16(mb + 64 * h + 32 + 16 * lq);
+    const uint4 vh = ld16(mb + 128 + 32 * h + 16 * lq);
+    const uint4 xs = ld16(xb.xs16 + 4 * hl);
+    const uint32_t qa[4] = {va.x, va.y, va.z, va.w}, qb[4] = {vb.x, vb.y, vb.z, vb.w};
+    const uint32_t qh[4] = {vh.x, vh.y, vh.z, vh.w};
+    const int xsv[4] = {(int)xs.x, (int)xs.y, (int)xs.z, (int)xs.w};
+    // scale 8h + lq + 2k: word 2h + k / 2, byte lq + 2 (k & 1)
+    const uint32_t w0 = h ? sv.z : sv.x, w1 = h ? sv.w : sv.y;
+    const int8_t* xq = xb.qs + 128 * h + 16 * lq;
 #pragma unroll
-  for (int h = 0; h < 2; h++)
+    for (int k = 0; k < 4; k++) {
+      const uint4 xv = ld16(xq + 32 * k);
+      const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w};
+      int raw = 0;
 #pragma unroll
-    for (int lq = 0; lq < 2; lq++) {
-      const uint4 va = ld16(mb + 64 * h + 16 * lq), vb = ld16(mb + 64 * h + 32 + 16 * lq);
-      const uint4 vh = ld16(mb + 128 + 32 * h + 16 * lq);
-      const uint4 xs = ld16(xb.xs16 + 4 * (2 * h + lq));
-      const uint32_t qa[4] = {va.x, va.y, va.z, va.w}, qb[4] = {vb.x, vb.y, vb.z, vb.w};
-      const uint32_t qh[4] = {vh.x, vh.y, vh.z, vh.w};
-      const int xsv[4] = {(int)xs.x, (int)xs.y, (int)xs.z, (int)xs.w};
-#pragma unroll
-      for (int k = 0; k < 4; k++) {
-        const int p = q6k_prod(qa, qb, qh, xb, sw, xsv[k], h, lq, k);
-        S += p;
-        A += abs(p);
+      for (int q = 0; q < 4; q++) {
+        uint32_t v;
+        if (k == 0) v = (qa[q] & 0x0F0F0F0Fu) | ((qh[q] & 0x03030303u) << 4);
+        else if (k == 1) v = (qb[q] & 0x0F0F0F0Fu) | ((qh[q] & 0x0C0C0C0Cu) << 2);
+        else if (k == 2) v = ((qa[q] >> 4) & 0x0F0F0F0Fu) | (qh[q] & 0x30303030u);
+        else v = ((qb[q] >> 4) & 0x0F0F0F0Fu) | ((qh[q] >> 2) & 0x30303030u);
+        raw = dp4a_us(v, (int)xw[q], raw);
       }
+      const int sc = sbyte(k < 2 ? w0 : w1, lq + 2 * (k & 1));
+      const int p = sc * (raw - 32 * xsv[k]);
+      S += p;
+      A += abs(p);
     }
+  }
+  const uint32_t sw[4] = {sv.x, sv.y, sv.z, sv.w};
   const float bs = A < (1 << 24) ? (float)S : q6k_fold_slow(mb, sw, xb);
   const float d = f16_fast((uint32_t)db[0] | ((uint32_t)db[1] << 8));
   return fmul(fmul(d, xb.scale), bs);

@@ -17,13 +17,13 @@ import numpy as np
 PHASES = [
     ("launch -> inputs ready", 0, 1),
     ("router dots + Q8 of N", 1, 2),
-    ("grid barrier 1", 2, 3),
-    ("logits + N staged", 3, 9),
+    ("logits poll", 2, 9),
     ("top-k ranks", 9, 14),
     ("weights + plan", 14, 4),
     ("phase A (warp 0)", 4, 5),
-    ("grid barrier 2", 5, 6),
+    ("hidden poll (warp 0)", 5, 6),
     ("Q8 of hidden (warp 0)", 6, 15),
+    ("CTA sync", 15, 7),
     ("phase B (warp 0)", 7, 8),
 ]
 WARP = ["A wait", "A compute", "A issue", "B wait", "B compute", "B issue"]
