@@ -195,8 +195,9 @@ int tg_layer_forward_dev(void *layer, const float *x, const float *add, float *x
  * gate/up, down).  Same results either way.  Returns the previous setting. */
 int tg_layer_set_fused(void *layer, int on);
 /* Diagnostics: fused steps launched after this call write per-CTA phase
- * timestamps (16 uint64 per CTA: SM clocks, and the global timer in slots
- * 12/13) into dev_buf; NULL stops it.  Returns the step's grid size. */
+ * timestamps into dev_buf (32 uint64 per CTA: SM clocks, the global timer in
+ * slots 12/13, the logits poll count in slot 19; then 8 uint64 per warp of
+ * ring and poll counters); NULL stops it.  Returns the step's grid size. */
 int tg_cuda_step_trace(void *dev_buf);
 /* Host buffers, synchronous: out[T][D] += experts(normalize ? rmsnorm(x) : x). */
 int tg_layer_forward(void *layer, const float *x_host, float *out_host, int T, int normalize);
@@ -229,6 +230,10 @@ int tg_cuda_device_count(void);
  * the count per row, or -1. */
 int tg_cuda_debug_quantize_q8(const float *x, int nrows, int ncols, void *out_blocks);
 int tg_cuda_debug_row_isums(int fmt, const void *mat, int nrows, int ncols, const void *xq_blocks, int32_t *out);
+/* Test hook: the fused step's double-assisted exact fp32 division against
+ * the IEEE division on n pseudo-random operand pairs; writes the number of
+ * results that differ (0 expected).  Returns 0, or -1 on error. */
+int tg_cuda_debug_div_check(long long n, unsigned seed, unsigned long long *mismatches);
 
 /* Q4_K / Q6_K packers (host, multi-threaded): rows x cols fp32 (cols a
  * multiple of 256) -> rows * tg_row_bytes(fmt, cols) bytes.  A per-sub-block

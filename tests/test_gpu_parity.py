@@ -305,3 +305,12 @@ def test_launches_are_counted(gpu):
     gpu.tg_matmul_q4k(mat.ctypes.data, x.ctypes.data, o.ctypes.data, 8, 256)
     ok(gpu)
     assert gpu.tg_cuda_launch_count() > before
+
+
+def test_step_division_is_exact(gpu):
+    """The fused step divides x by the RMS norm as x * RN_double(1 / d)
+    rounded to fp32; on 2^26 pseudo-random operand pairs (half of them near
+    1, the rest any bit pattern) that equals IEEE fp32 division bit for bit."""
+    bad = ctypes.c_ulonglong(123)
+    assert gpu.tg_cuda_debug_div_check(1 << 26, 12345, ctypes.byref(bad)) == 0, tg.last_error(gpu)
+    assert bad.value == 0

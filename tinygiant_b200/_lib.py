@@ -59,6 +59,7 @@ EXT = {
     "tg_cuda_device_count": ([], CI),
     "tg_cuda_debug_quantize_q8": ([VP, CI, CI, VP], CI),
     "tg_cuda_debug_row_isums": ([CI, VP, CI, CI, VP, VP], CI),
+    "tg_cuda_debug_div_check": ([ctypes.c_longlong, ctypes.c_uint, VP], CI),
     "tg_layer_create": ([CI, VP, VP, VP, CI, VP, VP, VP, VP, CI, CI, CI, VP, VP, CI, CI], VP),
     "tg_layer_create_shard": ([CI, VP, VP, VP, CI, VP, VP, VP, VP, CI, CI, CI, VP, VP, CI, CI, CI, CI], VP),
     "tg_layer_clone": ([VP], VP),

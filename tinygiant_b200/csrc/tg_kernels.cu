@@ -14,6 +14,7 @@
 #include "tg_kernels.h"
 #include "tg_plan.cuh"
 #include "tg_q8.cuh"
+#include "tg_warpdot.cuh"
 
 namespace tg {
 
@@ -246,6 +247,38 @@ void launch_repack(const uint8_t* raw, int fmt, int rows, int cols, uint8_t* dst
   const long nblocks = (long)rows * ((fmt == FMT_Q6K) ? cols / QK : cols / 32);
   if (nblocks <= 0) return;
   repack_kernel<<<(unsigned)((nblocks + 255) / 256), 256, 0, s>>>(raw, fmt, rows, cols, dst);
+}
+
+// Test hook: div_rn_d (the double-assisted exact division of the fused step)
+// against __fdiv_rn on n pseudo-random operand pairs; counts mismatches.
+// Half the dividends and divisors have exponents in 2^-30 .. 2^30, the rest
+// any bit pattern (divisors positive).
+__device__ __forceinline__ uint32_t mix32(uint32_t x) {
+  x ^= x >> 16;
+  x *= 0x7feb352du;
+  x ^= x >> 15;
+  x *= 0x846ca68bu;
+  x ^= x >> 16;
+  return x;
+}
+
+__global__ void debug_div_kernel(long long n, uint32_t seed, unsigned long long* bad) {
+  unsigned long long nb = 0;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    const uint32_t h1 = mix32((uint32_t)i * 2654435761u ^ seed), h2 = mix32(h1 ^ 0x9e3779b9u), h3 = mix32(h2 ^ seed);
+    uint32_t xb = h1, db = h2 & 0x7fffffffu;
+    if (h3 & 1u) db = (db & 0x007fffffu) | ((97u + (h3 >> 8) % 61u) << 23);
+    if (h3 & 2u) xb = (xb & 0x807fffffu) | ((97u + (h3 >> 16) % 61u) << 23);
+    const float x = __uint_as_float(xb), d = __uint_as_float(db);
+    if (!(d > 0.f)) continue;
+    const float got = div_rn_d(x, d, 1.0 / (double)d), want = __fdiv_rn(x, d);
+    if (__float_as_uint(got) != __float_as_uint(want) && !(got != got && want != want)) nb++;
+  }
+  if (nb) atomicAdd(bad, nb);
+}
+
+void launch_debug_div(long long n, uint32_t seed, unsigned long long* bad, cudaStream_t s) {
+  debug_div_kernel<<<148 * 4, 256, 0, s>>>(n, seed, bad);
 }
 
 }  // namespace tg

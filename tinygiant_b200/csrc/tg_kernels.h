@@ -15,6 +15,7 @@ void launch_add(const float* a, const float* b, float* out, size_t n, cudaStream
 void launch_rms_norm(const float* x, const float* w, float* out, int dim, float eps, cudaStream_t s);
 int debug_isums_per_row(int fmt, int cols);
 void launch_debug_isums(const WDesc& W, const Q8Dev* xq, int32_t* out, cudaStream_t s);
+void launch_debug_div(long long n, uint32_t seed, unsigned long long* bad, cudaStream_t s);
 // Raw reference blocks of a rows x cols matrix -> the WDesc row layout at dst.
 void launch_repack(const uint8_t* raw, int fmt, int rows, int cols, uint8_t* dst, cudaStream_t s);
 

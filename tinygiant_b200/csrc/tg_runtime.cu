@@ -895,6 +895,22 @@ int tg_cuda_debug_row_isums(int fmt, const void* mat, int nrows, int ncols, cons
   return per_row;
 }
 
+int tg_cuda_debug_div_check(long long n, unsigned seed, unsigned long long* mismatches) {
+  std::lock_guard<std::recursive_mutex> lk(g.mu);
+  const char* what = "tg_cuda_debug_div_check";
+  if (n < 0 || !mismatches || !ensure_init()) return -1;
+  if (!g.d_stage.reserve(256) || !g.h_down.reserve(256)) return -1;
+  cudaStream_t s = stream();
+  unsigned long long* d = (unsigned long long*)g.d_stage.p;
+  if (!cuda_ok(cudaMemsetAsync(d, 0, sizeof(*d), s), what)) return -1;
+  launch_debug_div(n, seed, d, s);
+  g_launches++;
+  if (!cuda_ok(cudaGetLastError(), what)) return -1;
+  if (!cuda_ok(cudaMemcpyAsync(g.h_down.p, d, sizeof(*d), cudaMemcpyDeviceToHost, s), what) || !finish(what)) return -1;
+  *mismatches = *(unsigned long long*)g.h_down.p;
+  return 0;
+}
+
 // Host page-cache hints on the caller's (host) memory, as the reference
 // issues them; they do not touch the GPU.
 static void page_range(const void* addr, size_t len, void** a, size_t* n) {

@@ -45,10 +45,12 @@ constexpr int STEP_T_MAX = 8;
 constexpr int STEP_K_MAX = 8;
 constexpr int STEP_R_MAX = STEP_T_MAX * STEP_K_MAX;   // active rows
 constexpr int STEP_E_MAX = 256;
+constexpr int STEP_GB_MAX = 16;    // 256-value blocks per token row (D <= 4096)
+constexpr int STEP_RW_MAX = 2;     // router rows per CTA
 constexpr int STEP_POLLS = 1 << 23;   // polls of another CTA's words before giving up (~1 s with the sleeps)
 
 struct StepShared {
-  float lg[STEP_T_MAX * STEP_E_MAX];
+  __align__(16) float lg[STEP_T_MAX * STEP_E_MAX];
   int sel_e[STEP_T_MAX][STEP_K_MAX];
   float sel_v[STEP_T_MAX][STEP_K_MAX];
   float sel_w[STEP_T_MAX][STEP_K_MAX];
@@ -61,10 +63,14 @@ struct StepShared {
   int slot_e[STEP_R_MAX], slot_n[STEP_R_MAX], slot_off[STEP_R_MAX];
   int row_t[STEP_R_MAX];
   float row_w[STEP_R_MAX];
+  float part_ss[STEP_T_MAX][STEP_GB_MAX];
+  float part_dot[STEP_RW_MAX][STEP_T_MAX][STEP_GB_MAX];
+  float rrt[STEP_T_MAX];
+  double yd[STEP_T_MAX];
   uint64_t rbar[SW];
   uint64_t xbar, ebar;
   float accw[SW][STEP_T_MAX];
-  unsigned long long tw[SW][6];
+  unsigned long long tw[SW][8];
   uint64_t bars[SW][ST_MAX_NST];
 };
 
@@ -151,7 +157,8 @@ struct StepArgs {
 };
 
 // Phase timestamps for the diagnostics hook tg_cuda_step_trace: slot i of
-// this CTA's 16 gets clock64(), slots 12/13 the global timer at start / end.
+// this CTA's 32 gets clock64(), slots 12/13 the global timer at start / end,
+// slot 19 the logits poll count; then 8 words per warp.
 __device__ __forceinline__ unsigned long long gtimer() {
   unsigned long long t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -160,7 +167,7 @@ __device__ __forceinline__ unsigned long long gtimer() {
 #define TG_MARK(i)                                                                         \
   do {                                                                                     \
     if (a.trace && (threadIdx.x & 31) == 0)                                                \
-      a.trace[blockIdx.x * 16 + (i)] = (unsigned long long)clock64();                       \
+      a.trace[blockIdx.x * 32 + (i)] = (unsigned long long)clock64();                       \
   } while (0)
 
 // A warp's position in its stream of items: phase 0 = gate/up item a (slot
@@ -228,15 +235,15 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
   StepExpert* sx = reinterpret_cast<StepExpert*>(xs + (size_t)a.xcap * dbpr);   // [xcap] the slots' experts
   StepExpert* etab = sx + a.xcap;                                                 // [E]
   uint64_t* bar = sh.bars[wid];
-  if (a.trace && tid == 0) a.trace[blockIdx.x * 16 + 12] = gtimer();
+  if (a.trace && tid == 0) a.trace[blockIdx.x * 32 + 12] = gtimer();
   if (wid == 0) TG_MARK(0);
 
   // ---- Before the preceding kernel completes: the epoch, this warp's router
   // row and the expert table (none of them written by a preceding kernel).
-  const int e_r = blockIdx.x + wid * G;   // this warp's expert, if wid < rwc
-  const bool router_warp = wid < a.rwc && e_r < E;
-  const float* wsrc = a.router_w + (size_t)(router_warp ? e_r : 0) * D;
-  const bool wbulk = router_warp && ((uintptr_t)wsrc & 15) == 0;
+  // router rows staged here: experts blockIdx.x + r G < E, r < rwc
+  const int nrw = min(a.rwc, (E - (int)blockIdx.x + G - 1) / G);
+  const bool wbulk = wid < nrw;
+  const float* wsrc = a.router_w + (size_t)(blockIdx.x + wid * G) * D;
   if (lane == 0) {
     for (int i = 0; i < a.nst; i++) mbar_init(&bar[i], 1);
     mbar_init(&sh.rbar[wid], 1);
@@ -272,109 +279,130 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
   }
   if (wid == 0) TG_MARK(1);
 
-  // ---- R.  Router warps (wid < rwc): expert e_r's logit for every token.
-  // The other warps: Q8 blocks of N, q = wid - rwc, + (SW - rwc), ...
-  // (token q / gbpr).  Each reads its token row once, 16 bytes a lane.
+  // ---- R, in three passes over the 256-value blocks q of the token rows
+  // (token q / gbpr, block q % gbpr), spread over all warps:
+  //  1  x' = x + add (written to x_out by CTA 0), each block's sum of squares
+  //     and, per router row staged here, its partial logit W_r[e] . (x' * w):
+  //     lane chains over the lane's 8 values, then warp trees;
+  //  2  per token ss = its blocks' sums in block order, rr = sqrt(ss / D +
+  //     eps); per (router row, token) the logit = (the blocks' partial dots
+  //     in block order) / rr (+ b), published tagged;
+  //  3  N = x' / rr * w, quantized into shared memory (XQ).
   bool dead = false;   // this warp stopped on an error
-  {
-    const int nqw = SW - a.rwc, qw = wid - a.rwc;
-    const int nwork = router_warp ? T : qw >= 0 ? (T * gbpr - qw + nqw - 1) / nqw : 0;
-    if (nwork > 0 && xstaged && !mbar_wait(&sh.xbar, 0)) {
-      if (lane == 0) set_error(a.st, ERR_WAIT_TIMEOUT, 36, blockIdx.x, wid);
+  const int nq = T * gbpr;
+  if (xstaged && !mbar_wait(&sh.xbar, 0)) {
+    if (lane == 0) set_error(a.st, ERR_WAIT_TIMEOUT, 36, blockIdx.x, wid);
+    dead = true;
+  }
+  for (int r = 0; r < nrw; r++)
+    if (!mbar_wait(&sh.rbar[r], 0)) {
+      if (lane == 0) set_error(a.st, ERR_WAIT_TIMEOUT, 30, blockIdx.x + r * G, 0);
       dead = true;
     }
-    if (router_warp && wbulk && !mbar_wait(&sh.rbar[wid], 0)) {
-      if (lane == 0) set_error(a.st, ERR_WAIT_TIMEOUT, 30, e_r, 0);
-      dead = true;
+  if (wid == 0) TG_MARK(3);
+  const bool nwt = a.normalize && a.norm_w;
+  // lane l's values 8l .. 8l + 7 of block q (0 past the row end)
+  auto load_block = [&](int q, float (&v)[8], bool store_x) {
+    const int t = q / gbpr, i0 = (q - t * gbpr) * QK + 8 * lane;
+    const size_t o = (size_t)t * D + i0;
+    float4 h[2];
+#pragma unroll
+    for (int k = 0; k < 2; k++) {
+      h[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (i0 + 4 * k < D) {
+        h[k] = xstaged ? *reinterpret_cast<const float4*>(xsm + o + 4 * k)
+                       : __ldcg(reinterpret_cast<const float4*>(a.x_in + o + 4 * k));
+        if (a.add_in) {
+          const float4 d = xstaged ? *reinterpret_cast<const float4*>(asm_ + o + 4 * k)
+                                   : __ldcg(reinterpret_cast<const float4*>(a.add_in + o + 4 * k));
+          h[k] = make_float4(fadd(h[k].x, d.x), fadd(h[k].y, d.y), fadd(h[k].z, d.z), fadd(h[k].w, d.w));
+        }
+        if (store_x) *reinterpret_cast<float4*>(a.x_out + o + 4 * k) = h[k];
+      }
     }
-    const float* wr = wbulk ? rrow + (size_t)wid * D : wsrc;
-    const int nc = (D + 127) / 128;   // 16-byte chunks per lane
+    v[0] = h[0].x; v[1] = h[0].y; v[2] = h[0].z; v[3] = h[0].w;
+    v[4] = h[1].x; v[5] = h[1].y; v[6] = h[1].z; v[7] = h[1].w;
+  };
+  auto load8 = [&](const float* p, int i0, float (&w)[8]) {   // 8 floats at p + i0 (0 past D)
+#pragma unroll
+    for (int k = 0; k < 2; k++) {
+      const float4 f = i0 + 4 * k < D ? *reinterpret_cast<const float4*>(p + i0 + 4 * k) : make_float4(0.f, 0.f, 0.f, 0.f);
+      w[4 * k] = f.x; w[4 * k + 1] = f.y; w[4 * k + 2] = f.z; w[4 * k + 3] = f.w;
+    }
+  };
 #pragma unroll 1
-    for (int k = 0; k < (dead ? 0 : nwork); k++) {
-      const int q = router_warp ? -1 : qw + k * nqw;
-      const int t = router_warp ? k : q / gbpr;
-      const int bq = router_warp ? -1 : q - t * gbpr;
-      float ss = 0.f, dot = 0.f;
-      float4 hlo = make_float4(0.f, 0.f, 0.f, 0.f), hhi = hlo;
-#pragma unroll 2
-      for (int c = 0; c < nc; c++) {
-        const int i = 128 * c + 4 * lane;
-        if (i < D) {
-          const size_t o = (size_t)t * D + i;
-          float4 v = xstaged ? *reinterpret_cast<const float4*>(xsm + o)
-                             : __ldcg(reinterpret_cast<const float4*>(a.x_in + o));
-          if (a.add_in) {
-            const float4 d = xstaged ? *reinterpret_cast<const float4*>(asm_ + o)
-                                     : __ldcg(reinterpret_cast<const float4*>(a.add_in + o));
-            v = make_float4(fadd(v.x, d.x), fadd(v.y, d.y), fadd(v.z, d.z), fadd(v.w, d.w));
-          }
-          if (e_r == 0 && router_warp && a.x_out) *reinterpret_cast<float4*>(a.x_out + o) = v;
-          ss = __fmaf_rn(v.x, v.x, ss);
-          ss = __fmaf_rn(v.y, v.y, ss);
-          ss = __fmaf_rn(v.z, v.z, ss);
-          ss = __fmaf_rn(v.w, v.w, ss);
-          if (c == 2 * bq) hlo = v;
-          if (c == 2 * bq + 1) hhi = v;
-          if (router_warp) {
-            if (a.normalize && a.norm_w) {
-              const float4 nw = __ldg(reinterpret_cast<const float4*>(a.norm_w + i));
-              v = make_float4(fmul(v.x, nw.x), fmul(v.y, nw.y), fmul(v.z, nw.z), fmul(v.w, nw.w));
-            }
-            const float4 w = *reinterpret_cast<const float4*>(wr + i);
-            dot = __fmaf_rn(w.x, v.x, dot);
-            dot = __fmaf_rn(w.y, v.y, dot);
-            dot = __fmaf_rn(w.z, v.z, dot);
-            dot = __fmaf_rn(w.w, v.w, dot);
-          }
-        }
-      }
+  for (int q = dead ? nq : wid; q < nq; q += SW) {
+    const int t = q / gbpr, b = q - t * gbpr, i0 = b * QK + 8 * lane;
+    float v[8];
+    load_block(q, v, blockIdx.x == 0 && a.x_out);
+    float ss = 0.f;
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        ss = fadd(ss, __shfl_xor_sync(FULL, ss, o));
-        dot = fadd(dot, __shfl_xor_sync(FULL, dot, o));
-      }
-      const float rr = a.normalize ? __fsqrt_rn(fadd(__fdiv_rn(ss, (float)D), a.eps)) : 1.f;
-      if (router_warp) {
-        if (a.normalize) dot = __fdiv_rn(dot, rr);
-        const float lg = a.router_b ? fadd(dot, a.router_b[e_r]) : dot;
-        if (lane == 0) {
-          a.logits[(size_t)t * E + e_r] = lg;
-          st_tagged(a.lgt + (size_t)t * E + e_r, ep, lg);
-        }
-      } else {
-        const int b0 = bq * QK, n = min(QK, D - b0);
-        float* hv[2] = {&hlo.x, &hhi.x};
+    for (int jj = 0; jj < 8; jj++) ss = __fmaf_rn(v[jj], v[jj], ss);
+    float nw[8];
+    if (nwt) load8(a.norm_w, i0, nw);
+#pragma unroll 1
+    for (int r = 0; r < nrw; r++) {
+      float w[8];
+      load8(rrow + (size_t)r * D, i0, w);
+      float dot = 0.f;
 #pragma unroll
-        for (int h = 0; h < 2; h++)
+      for (int jj = 0; jj < 8; jj++) dot = __fmaf_rn(w[jj], nwt ? fmul(v[jj], nw[jj]) : v[jj], dot);
 #pragma unroll
-          for (int jj = 0; jj < 4; jj++) {
-            const int i = 128 * h + 4 * lane + jj;
-            float x = 0.f;
-            if (i < n) {
-              x = hv[h][jj];
-              if (a.normalize) {
-                x = __fdiv_rn(x, rr);
-                if (a.norm_w) x = fmul(x, a.norm_w[b0 + i]);
-              }
-            }
-            hv[h][jj] = x;
-          }
-        XQ& xb = xa[q];
-        quantize_block_warp_f4(hlo, hhi, n, &xb);
-        __syncwarp();
-        if (lane < 16) {   // sums of each 16 values (Q6_K's bias correction)
-          const int4 w = *reinterpret_cast<const int4*>(xb.qs + 16 * lane);
-          xb.xs16[xs16_slot(lane)] =
-              dp4a(w.x, 0x01010101, dp4a(w.y, 0x01010101, dp4a(w.z, 0x01010101, dp4a(w.w, 0x01010101, 0))));
-        } else if (lane < 24) {
-          xb.bsf[lane - 16] = (float)xb.bsums[lane - 16];
-        }
-      }
+      for (int o = 16; o > 0; o >>= 1) dot = fadd(dot, __shfl_xor_sync(FULL, dot, o));
+      if (lane == 0) sh.part_dot[r][t][b] = dot;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss = fadd(ss, __shfl_xor_sync(FULL, ss, o));
+    if (lane == 0) sh.part_ss[t][b] = ss;
+  }
+  if (wid == 0) TG_MARK(16);
+  if (__syncthreads_or(dead)) {   // wait for the expert table copy, the last one in flight
+    if (tid == 0) mbar_wait(&sh.ebar, 0);
+    return;
+  }
+  for (int i = tid; i < T * (1 + nrw); i += SW * 32) {
+    const int t = i % T, r = i / T - 1;
+    float ss = 0.f;
+    for (int b = 0; b < gbpr; b++) ss = fadd(ss, sh.part_ss[t][b]);
+    const float rr = a.normalize ? __fsqrt_rn(fadd(__fdiv_rn(ss, (float)D), a.eps)) : 1.f;
+    if (r < 0) {
+      sh.rrt[t] = rr;
+      sh.yd[t] = 1.0 / (double)rr;
+    } else {
+      const int e = blockIdx.x + r * G;
+      float dot = 0.f;
+      for (int b = 0; b < gbpr; b++) dot = fadd(dot, sh.part_dot[r][t][b]);
+      if (a.normalize) dot = __fdiv_rn(dot, rr);
+      const float lg = a.router_b ? fadd(dot, a.router_b[e]) : dot;
+      a.logits[(size_t)t * E + e] = lg;
+      st_tagged(a.lgt + (size_t)t * E + e, ep, lg);
     }
   }
-  if (wid == 0) TG_MARK(2);
+  __syncthreads();
+  if (wid == 0) TG_MARK(17);
+#pragma unroll 1
+  for (int q = wid; q < nq; q += SW) {
+    const int t = q / gbpr, b = q - t * gbpr, i0 = b * QK + 8 * lane, n = min(QK, D - b * QK);
+    float v[8];
+    load_block(q, v, false);
+    if (a.normalize) {
+      const float rr = sh.rrt[t];
+      const double yd = sh.yd[t];
+      float nw[8];
+      if (a.norm_w) load8(a.norm_w, i0, nw);
+#pragma unroll
+      for (int jj = 0; jj < 8; jj++) {
+        float x = div_rn_d(v[jj], rr, yd);
+        if (a.norm_w) x = fmul(x, nw[jj]);
+        v[jj] = i0 + jj < D ? x : 0.f;
+      }
+    }
+    quantize_xq(v, n, xa + q);
+  }
+  if (wid == 0) TG_MARK(18);
   if (tid == 0 && !mbar_wait(&sh.ebar, 0)) set_error(a.st, ERR_WAIT_TIMEOUT, 37, blockIdx.x, 0);
   if (__syncthreads_or(dead)) return;   // nothing in flight: the copies above were all waited for
+  if (wid == 0) TG_MARK(2);
 
   // ---- S: every CTA polls the logits (tagged with this epoch), then ranks
   // and plans on its own.
@@ -391,7 +419,10 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
         nan_here |= v != v;
       }
     }
-    if (!__syncthreads_or(miss)) break;
+    if (!__syncthreads_or(miss)) {
+      if (a.trace && tid == 0) a.trace[blockIdx.x * 32 + 19] = it + 1;
+      break;
+    }
     if (it >= STEP_POLLS) {
       if (tid == 0) set_error(a.st, ERR_WAIT_TIMEOUT, 31, blockIdx.x, 0);
       return;
@@ -403,9 +434,10 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
   if (wid == 0) TG_MARK(9);
   {
     // rank of each (token, expert) among its token's logits; P lanes share
-    // one element's comparisons
+    // one element's comparisons, reading the row 4 logits at a time
     int P = 1;
     while (P < 32 && 2 * P * T * E <= SW * 32) P *= 2;
+    const bool v4 = (E & 3) == 0;
     for (int base = 0; base < T * E * P; base += SW * 32) {
       const int idx = base + tid, el = idx / P, part = idx - el * P;
       const bool valid = el < T * E;
@@ -416,14 +448,24 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
         e = el - t * E;
         v = sh.lg[el];
         const float* row = sh.lg + t * E;
-        if (!any_nan)
+        if (any_nan) {
+          for (int jj = part; jj < E; jj += P) rank += ranks_above(row[jj], jj, v, e);
+        } else if (v4) {
 #pragma unroll 4
+          for (int c = part; c < E / 4; c += P) {
+            const float4 q = reinterpret_cast<const float4*>(row)[c];
+            const int j0 = 4 * c;
+            rank += (q.x > v) | ((q.x == v) & (j0 < e));
+            rank += (q.y > v) | ((q.y == v) & (j0 + 1 < e));
+            rank += (q.z > v) | ((q.z == v) & (j0 + 2 < e));
+            rank += (q.w > v) | ((q.w == v) & (j0 + 3 < e));
+          }
+        } else {
           for (int jj = part; jj < E; jj += P) {
             const float vj = row[jj];
             rank += (vj > v) | ((vj == v) & (jj < e));
           }
-        else
-          for (int jj = part; jj < E; jj += P) rank += ranks_above(row[jj], jj, v, e);
+        }
       }
       for (int o = 1; o < P; o <<= 1) rank += __shfl_xor_sync(FULL, rank, o);
       if (valid && part == 0 && rank < K) {
@@ -584,7 +626,7 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
   };
   unsigned long long* tw = sh.tw[wid];   // trace: wait / compute / issue cycles, phases A and B
   if (lane == 0)
-    for (int q = 0; q < 6; q++) tw[q] = 0;
+    for (int q = 0; q < 8; q++) tw[q] = 0;
   int tph = 0;
   long long tc = 0;
   auto wait_stage = [&](int stg, int item) -> bool {
@@ -697,14 +739,15 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
     if (tid == 0) set_error(a.st, ERR_BAD_PLAN, 35, total, a.xcap);
     okh = false;
   }
-  const int nq = okh ? total * dbpr : 0;
-  for (int q0 = wid; q0 < nq; q0 += 2 * SW) {
+  const int nh = okh ? total * dbpr : 0;   // hidden blocks
+  const long long ta = a.trace ? clock64() : 0;
+  for (int q0 = wid; q0 < nh; q0 += 2 * SW) {
     float v[2][8];
     int nn[2];
 #pragma unroll
     for (int h = 0; h < 2; h++) {
       const int q = q0 + h * SW;
-      nn[h] = q < nq ? min(QK, I - (q % dbpr) * QK) : 0;
+      nn[h] = q < nh ? min(QK, I - (q % dbpr) * QK) : 0;
     }
     for (int it = 0;; it++) {
       bool ok = true;
@@ -726,7 +769,13 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
           }
         }
       }
-      if (__all_sync(FULL, ok)) break;
+      if (__all_sync(FULL, ok)) {
+        if (a.trace && lane == 0) {
+          tw[6] += it + 1;
+          if (q0 == wid) tw[7] = clock64() - ta;
+        }
+        break;
+      }
       if (it >= STEP_POLLS) {
         if (lane == 0) set_error(a.st, ERR_WAIT_TIMEOUT, 33, blockIdx.x, wid);
         okh = false;
@@ -742,15 +791,7 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
       float vv[8];
 #pragma unroll
       for (int jj = 0; jj < 8; jj++) vv[jj] = h ? v[1][jj] : v[0][jj];
-      quantize_block_warp_vals(vv, nn[h], &xb);
-      __syncwarp();
-      if (lane < 16) {   // sums of each 16 values
-        const int4 w = *reinterpret_cast<const int4*>(xb.qs + 16 * lane);
-        xb.xs16[xs16_slot(lane)] =
-            dp4a(w.x, 0x01010101, dp4a(w.y, 0x01010101, dp4a(w.z, 0x01010101, dp4a(w.w, 0x01010101, 0))));
-      } else if (lane < 24) {
-        xb.bsf[lane - 16] = (float)xb.bsums[lane - 16];
-      }
+      quantize_xq(vv, nn[h], &xb);
     }
   }
   if (wid == 0) TG_MARK(15);
@@ -846,9 +887,9 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
 
   if (wid == 0) TG_MARK(8);
   if (wid == SW - 1) TG_MARK(11);
-  if (a.trace && tid == 0) a.trace[blockIdx.x * 16 + 13] = gtimer();
+  if (a.trace && tid == 0) a.trace[blockIdx.x * 32 + 13] = gtimer();
   if (a.trace && lane == 0)
-    for (int q = 0; q < 6; q++) a.trace[(size_t)gridDim.x * 16 + ((size_t)blockIdx.x * SW + wid) * 8 + q] = tw[q];
+    for (int q = 0; q < 8; q++) a.trace[(size_t)gridDim.x * 32 + ((size_t)blockIdx.x * SW + wid) * 8 + q] = tw[q];
   // bounded waits for any copies still in flight before the CTA exits
   if (!dead)
     for (int i = j; i < issued; i++) mbar_wait(&bar[i % a.nst], (uint32_t)(i / a.nst) & 1u);
@@ -901,7 +942,7 @@ static bool step_shape(const StepLaunch& l, StepShape& sh) {
   const int G = step_sms();
   sh.pa = gblk ? std::max(1, 16 / bg) : 1;
   sh.rwc = (l.E + G - 1) / G;
-  if (sh.rwc >= SW) return false;   // at least one warp quantizes N
+  if (sh.rwc > STEP_RW_MAX || (l.D + QK - 1) / QK > STEP_GB_MAX) return false;
   const int gbpr = (l.D + QK - 1) / QK, dbpr = (l.I + QK - 1) / QK;
   sh.xcap = l.T * l.top_k;
   const size_t fixed = round16((size_t)sh.rwc * l.D * 4) + (size_t)l.T * gbpr * sizeof(XQ) +

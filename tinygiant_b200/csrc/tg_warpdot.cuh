@@ -369,6 +369,78 @@ static_assert(sizeof(XQ) == 400, "XQ layout");
 // Slot of the sum of 16-value group g (values 16g .. 16g + 15) in XQ.xs16.
 __host__ __device__ __forceinline__ int xs16_slot(int g) { return 4 * (2 * (g >> 3) + (g & 1)) + ((g & 7) >> 1); }
 
+// x / d correctly rounded to fp32, given yd = RN_double(1 / d).  The double
+// product x * yd is within 2^-52 (relative) of x / d.  A quotient of two
+// fp32 numbers that is not itself an fp32 number lies at least 2^-49
+// (relative) from every fp32 rounding midpoint m: x - d m is a nonzero
+// multiple of 2^min(e_x, e_d + e_m) (the exponents of the three numbers'
+// last significant bits), and x = d m is impossible for a 25-bit m.  So
+// rounding the product to fp32 rounds x / d.  Operands outside 2^-57 .. 2^58
+// (zeros, subnormals, infinities, NaNs included) take __fdiv_rn, which keeps
+// every quotient in the normal range.
+__device__ __forceinline__ float div_rn_d(float x, float d, double yd) {
+  const uint32_t ex = (__float_as_uint(x) >> 23) & 0xFFu, ed = (__float_as_uint(d) >> 23) & 0xFFu;
+  if (ex - 70u > 114u || ed - 70u > 114u) return __fdiv_rn(x, d);
+  return __double2float_rn((double)x * yd);
+}
+
+// max with NaN propagation (either operand NaN gives NaN).
+__device__ __forceinline__ float fmax_nan(float a, float b) {
+  float d;
+  asm("max.NaN.f32 %0, %1, %2;" : "=f"(d) : "f"(a), "f"(b));
+  return d;
+}
+
+// The quantizer of tg_q8.cuh (quantize_q8, csrc/libtinygiant.c:169-208) run
+// by one warp into the staged form XQ, its extra fields (sums of each 16
+// values, 32-value sums as fp32) formed from the same lane sums.  Lane l
+// holds v[j] = value 8l + j of the block; positions at or past n are stored
+// as 0.  The amax reduction is a tree (max is order-free); a NaN in the block
+// gives the canonical NaN scale, where the reference propagates the NaN it
+// met first — the block's dots are NaN either way.
+__device__ __forceinline__ void quantize_xq(const float (&v)[8], int n, XQ* o) {
+  const int lane = threadIdx.x & 31;
+  float m[8];
+#pragma unroll
+  for (int j = 0; j < 8; j++) m[j] = 8 * lane + j < n ? fabsf(v[j]) : 0.f;
+  float a = fmax_nan(fmax_nan(fmax_nan(m[0], m[1]), fmax_nan(m[2], m[3])),
+                     fmax_nan(fmax_nan(m[4], m[5]), fmax_nan(m[6], m[7])));
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) a = fmax_nan(a, __shfl_xor_sync(FULL, a, off));
+  const float inv = a > 0.f ? __fdiv_rn(127.f, a) : 0.f;
+  int q[8], s = 0;
+#pragma unroll
+  for (int j = 0; j < 8; j++) {
+    q[j] = 0;
+    if (8 * lane + j < n) {
+      const float sv = __fmul_rn(v[j], inv);
+      q[j] = (sv != sv) ? 0 : __float2int_rn(sv);
+    }
+    s += q[j];
+  }
+  uint32_t w0 = 0, w1 = 0;
+#pragma unroll
+  for (int j = 0; j < 4; j++) {
+    w0 |= ((uint32_t)q[j] & 0xFFu) << (8 * j);
+    w1 |= ((uint32_t)q[4 + j] & 0xFFu) << (8 * j);
+  }
+  *reinterpret_cast<uint2*>(o->qs + 8 * lane) = make_uint2(w0, w1);
+  const int s16 = s + __shfl_xor_sync(FULL, s, 1);        // values 16 (l / 2) .. + 15
+  const int s32 = s16 + __shfl_xor_sync(FULL, s16, 2);    // sub-block l / 4
+  int tot = s32 + __shfl_xor_sync(FULL, s32, 4);
+  tot += __shfl_xor_sync(FULL, tot, 8);
+  tot += __shfl_xor_sync(FULL, tot, 16);
+  if ((lane & 1) == 0) o->xs16[xs16_slot(lane >> 1)] = s16;
+  if ((lane & 3) == 0) {
+    o->bsums[lane >> 2] = s32;
+    o->bsf[lane >> 2] = (float)s32;
+  }
+  if (lane == 0) {
+    o->scale = div_rn_d(a, 127.f, 1.0 / 127.0);
+    o->sum = tot;
+  }
+}
+
 // Exact int -> fp32 for |v| < 2^22 on the integer and fp32 pipes: the bits of
 // 1.5 * 2^23 + v, minus 1.5 * 2^23.
 __device__ __forceinline__ float i2f_small(int v) { return __fsub_rn(__int_as_float(0x4B400000 + v), 12582912.0f); }

@@ -16,7 +16,11 @@ import numpy as np
 
 PHASES = [
     ("launch -> inputs ready", 0, 1),
-    ("router dots + Q8 of N", 1, 2),
+    ("R: x + router rows (w0)", 1, 3),
+    ("R1: sums, partial logits (w0)", 3, 16),
+    ("R2: rr, logits (CTA)", 16, 17),
+    ("R3: Q8 of N (w0)", 17, 18),
+    ("R: CTA sync", 18, 2),
     ("logits poll", 2, 9),
     ("top-k ranks", 9, 14),
     ("weights + plan", 14, 4),
@@ -27,15 +31,18 @@ PHASES = [
     ("phase B (warp 0)", 7, 8),
 ]
 WARP = ["A wait", "A compute", "A issue", "B wait", "B compute", "B issue"]
+SLOTS = 32   # trace words per CTA
 
 
 def trace(lib, step, n_steps=1):
-    """Runs `step()` n_steps times with tracing on; returns (phases, warps):
-    dicts name -> array of microseconds over CTAs / warps (last step)."""
+    """Runs `step()` n_steps times with tracing on; returns (phases, warps,
+    counts): dicts name -> array over CTAs / warps (last step); phases and
+    warps in microseconds (cycles are converted with the CTA's own
+    global-timer span), counts in polls."""
     import torch
 
     grid = lib.tg_cuda_step_trace(None)
-    buf = torch.zeros(grid * 16 + grid * 16 * 8, dtype=torch.int64, device="cuda")
+    buf = torch.zeros(grid * SLOTS + grid * 16 * 8, dtype=torch.int64, device="cuda")
     torch.cuda.synchronize()
     lib.tg_cuda_step_trace(ctypes.c_void_p(buf.data_ptr()))
     try:
@@ -45,15 +52,18 @@ def trace(lib, step, n_steps=1):
     finally:
         lib.tg_cuda_step_trace(None)
     v = buf.cpu().numpy().astype(np.int64)
-    t = v[: grid * 16].reshape(grid, 16)
+    t = v[: grid * SLOTS].reshape(grid, SLOTS)
     span_ns = (t[:, 13] - t[:, 12]).astype(np.float64)
     span_cyc = (t[:, 8] - t[:, 0]).astype(np.float64)
     cyc_per_us = np.median(span_cyc / np.maximum(span_ns, 1.0)) * 1000.0
     phases = {name: (t[:, b] - t[:, a]) / cyc_per_us for name, a, b in PHASES}
     phases["whole step (CTA)"] = span_ns / 1000.0
-    w = v[grid * 16:].reshape(grid * 16, 8)[:, :6] / cyc_per_us
+    wv = v[grid * SLOTS:].reshape(grid * 16, 8)
+    w = wv[:, :6] / cyc_per_us
     warps = {name: w[:, i] for i, name in enumerate(WARP)}
-    return phases, warps
+    warps["A end -> hidden ready"] = wv[:, 7] / cyc_per_us
+    counts = {"logits polls (CTA)": t[:, 19], "hidden polls (warp)": wv[:, 6]}
+    return phases, warps, counts
 
 
 def main():
@@ -90,12 +100,14 @@ def main():
                 step()
             torch.cuda.synchronize()
             for tag, n in (("one step after idle", 1), ("last of 8 back-to-back steps", 8)):
-                phases, warps = trace(lib, step, n)
+                phases, warps, counts = trace(lib, step, n)
                 print(f"== {tag}")
                 for name, d in phases.items():
-                    print(f"  {name:26s} median {np.median(d):7.2f} us   max {d.max():7.2f}")
+                    print(f"  {name:28s} median {np.median(d):7.2f} us   max {d.max():7.2f}")
                 for name, d in warps.items():
-                    print(f"  per-warp {name:12s} median {np.median(d):7.2f} us   max {d.max():7.2f}")
+                    print(f"  per-warp {name:21s} median {np.median(d):7.2f} us   max {d.max():7.2f}")
+                for name, d in counts.items():
+                    print(f"  {name:28s} median {np.median(d):7.1f}      max {d.max():7.0f}")
         tg.check(lib)
     finally:
         lib.tg_cuda_set_stream(None)
