@@ -42,6 +42,13 @@ struct Layer {
   int* counters = nullptr;
   unsigned long long* step_sync = nullptr;   // the fused step kernel's exchange block (step_sync_words)
   bool fused = true;               // use the fused step kernel when the shape allows
+  // tg_layer_forward's CUDA graph (copy in, step, copies out) for one
+  // (rows, normalize, host staging buffers, stream)
+  cudaGraphExec_t fwd_exec = nullptr;
+  int fwd_T = 0, fwd_norm = -1;
+  const void* fwd_hx = nullptr;
+  const void* fwd_ho = nullptr;
+  cudaStream_t fwd_s = nullptr;
   float* moe_out = nullptr;  // [2][max_tokens][D] for stacks and the host entry
   float* xbuf = nullptr;     // [max_tokens][D]
 };
@@ -97,6 +104,7 @@ static bool upload_tables(Layer* L) {
 }
 
 static void free_layer(Layer* L) {
+  if (L->fwd_exec) cudaGraphExecDestroy(L->fwd_exec);
   if (L->counters) unregister_counters(L->counters);
   if (L->step_sync) unregister_counters(L->step_sync);
   for (void* p : L->owned) cudaFree(p);
@@ -396,10 +404,50 @@ int tg_layer_forward(void* handle, const float* x_host, float* out_host, int T, 
   cudaStream_t s = stream();
   memcpy(hx, x_host, n);
   float* moe = L->moe_out;
-  if (cudaMemcpyAsync(L->xbuf, hx, n, cudaMemcpyHostToDevice, s) != cudaSuccess) return -1;
-  if (!layer_enqueue(L, L->xbuf, nullptr, nullptr, moe, T, normalize, nullptr, s, what)) return -1;
-  if (cudaMemcpyAsync(ho, moe, n, cudaMemcpyDeviceToHost, s) != cudaSuccess) return -1;
-  if (!finish(what)) return -1;
+  // The step's device work — the copy of x in, the step, the copies of its
+  // output and of the device status out — is one CUDA graph per (rows,
+  // normalize, staging buffers, stream), captured on first use and replayed.
+  const bool same = L->fwd_exec && L->fwd_T == T && L->fwd_norm == normalize && L->fwd_hx == hx &&
+                    L->fwd_ho == ho && L->fwd_s == s;
+  if (!same && s != nullptr && s != cudaStreamLegacy && s != cudaStreamPerThread) {
+    if (L->fwd_exec) cudaGraphExecDestroy(L->fwd_exec);
+    L->fwd_exec = nullptr;
+    cudaGraph_t graph = nullptr;
+    bool ok = cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal) == cudaSuccess;
+    if (ok) {
+      ok = cudaMemcpyAsync(L->xbuf, hx, n, cudaMemcpyHostToDevice, s) == cudaSuccess &&
+           layer_enqueue(L, L->xbuf, nullptr, nullptr, moe, T, normalize, nullptr, s, what) &&
+           cudaMemcpyAsync(ho, moe, n, cudaMemcpyDeviceToHost, s) == cudaSuccess && status_copy_async(s, what);
+      ok = cudaStreamEndCapture(s, &graph) == cudaSuccess && ok;
+    }
+    if (ok) ok = cudaGraphInstantiate(&L->fwd_exec, graph, 0) == cudaSuccess;
+    if (graph) cudaGraphDestroy(graph);
+    if (!ok) {
+      if (L->fwd_exec) cudaGraphExecDestroy(L->fwd_exec);
+      L->fwd_exec = nullptr;
+      cudaGetLastError();
+    } else {
+      L->fwd_T = T;
+      L->fwd_norm = normalize;
+      L->fwd_hx = hx;
+      L->fwd_ho = ho;
+      L->fwd_s = s;
+    }
+  }
+  if (L->fwd_exec && L->fwd_T == T && L->fwd_norm == normalize && L->fwd_hx == hx && L->fwd_ho == ho &&
+      L->fwd_s == s) {
+    if (cudaGraphLaunch(L->fwd_exec, s) != cudaSuccess) {
+      set_host_error(100, "%s: graph launch failed", what);
+      return -1;
+    }
+    count_launches(1);
+    if (!finish_copied(what)) return -1;
+  } else {
+    if (cudaMemcpyAsync(L->xbuf, hx, n, cudaMemcpyHostToDevice, s) != cudaSuccess) return -1;
+    if (!layer_enqueue(L, L->xbuf, nullptr, nullptr, moe, T, normalize, nullptr, s, what)) return -1;
+    if (cudaMemcpyAsync(ho, moe, n, cudaMemcpyDeviceToHost, s) != cudaSuccess) return -1;
+    if (!finish(what)) return -1;
+  }
   for (size_t i = 0; i < (size_t)T * L->D; i++) out_host[i] += ho[i];
   return 0;
 }

@@ -177,11 +177,16 @@ bool ensure_init() {
   return true;
 }
 
-// Synchronises the stream and turns a device-side error record into a host error.
-bool finish(const char* what) {
+// Enqueues the copy of the device status record to its pinned host copy.
+bool status_copy_async(cudaStream_t s, const char* what) {
+  return cuda_ok(cudaMemcpyAsync(g.h_status, g.d_status, sizeof(DevStatus), cudaMemcpyDeviceToHost, s), what);
+}
+
+// Synchronises the stream, whose work ends with status_copy_async, and turns
+// a device-side error record into a host error (resetting the record and
+// every arrival counter).
+bool finish_copied(const char* what) {
   cudaStream_t s = stream();
-  if (!cuda_ok(cudaMemcpyAsync(g.h_status, g.d_status, sizeof(DevStatus), cudaMemcpyDeviceToHost, s), what))
-    return false;
   if (!cuda_ok(cudaStreamSynchronize(s), what)) return false;
   if (g.h_status->code != 0) {
     DevStatus st = *g.h_status;
@@ -189,10 +194,16 @@ bool finish(const char* what) {
     if (g.d_counters.p) cudaMemsetAsync(g.d_counters.p, 0, g.d_counters.n, s);
     for (auto& c : g_counter_bufs) cudaMemsetAsync(c.first, 0, c.second, s);
     cudaStreamSynchronize(s);
+    g.h_status->code = 0;
     set_host_error(200 + st.code, "%s: device error %d at site %d (%d, %d)", what, st.code, st.where, st.a, st.b);
     return false;
   }
   return true;
+}
+
+// Synchronises the stream and turns a device-side error record into a host error.
+bool finish(const char* what) {
+  return status_copy_async(stream(), what) && finish_copied(what);
 }
 
 // ---------------------------------------------------------------------

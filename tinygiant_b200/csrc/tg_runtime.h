@@ -12,6 +12,8 @@ void set_host_error(int code, const char* fmt, ...);
 bool ensure_init();
 cudaStream_t stream();
 bool finish(const char* what);
+bool status_copy_async(cudaStream_t s, const char* what);
+bool finish_copied(const char* what);
 size_t host_row_bytes(int fmt, int ncols);
 bool lookup_matrix(const void* h, int fmt, int rows, int cols, WDesc* out);
 const float* lookup_vector(const float* h, int n);

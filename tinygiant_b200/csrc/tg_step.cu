@@ -50,7 +50,6 @@ constexpr int STEP_RW_MAX = 2;     // router rows per CTA
 constexpr int STEP_POLLS = 1 << 23;   // polls of another CTA's words before giving up (~1 s with the sleeps)
 
 struct StepShared {
-  __align__(16) float lg[STEP_T_MAX * STEP_E_MAX];
   int sel_e[STEP_T_MAX][STEP_K_MAX];
   float sel_v[STEP_T_MAX][STEP_K_MAX];
   float sel_w[STEP_T_MAX][STEP_K_MAX];
@@ -58,7 +57,7 @@ struct StepShared {
   int slot_of[STEP_E_MAX];
   int off[STEP_E_MAX];
   int wsum[2][SW];
-  int n_slots, total;
+  int n_slots, total, ok;
   uint32_t epoch;
   int slot_e[STEP_R_MAX], slot_n[STEP_R_MAX], slot_off[STEP_R_MAX];
   int row_t[STEP_R_MAX];
@@ -101,14 +100,6 @@ __device__ __forceinline__ float tag_val(unsigned long long w) { return __uint_a
 __device__ __forceinline__ size_t hid_word(int o, int r, int dbpr) {
   const int b = r >> 8, p = r & 255;
   return ((size_t)o * dbpr + b) * 256 + ((p & 7) >> 1) * 64 + 2 * (p >> 3) + (p & 1);
-}
-
-// Whether (vj, j) ranks above (vi, i): larger logit first, NaN below every
-// number, ties to the lower index.
-__device__ __forceinline__ bool ranks_above(float vj, int j, float vi, int i) {
-  const bool jn = vj != vj, in = vi != vi;
-  if (jn) return in && j < i;
-  return in || vj > vi || (vj == vi && j < i);
 }
 
 // Matrix descriptor of format F with `rows` rows of `cols` values at m (row
@@ -174,11 +165,11 @@ __device__ __forceinline__ unsigned long long gtimer() {
 // a / I, row a % I); phase 1 = output row r, slots s .. s + SB - 1.
 struct SCur {
   int ph;
-  long a, r;
+  int a, r;
   int s;
 };
 
-__device__ __forceinline__ bool scur_next(SCur& c, long gw, long NW, long nA, int D, int n_slots, int SB) {
+__device__ __forceinline__ bool scur_next(SCur& c, int gw, int NW, int nA, int D, int n_slots, int SB) {
   if (c.ph == 0) {
     c.a += NW;
     if (c.a < nA) return true;
@@ -204,7 +195,7 @@ static __device__ __noinline__ void step_issue(const StepExpert* sx, SCur c, uin
                                                int pa, int I, int D, uint32_t ghalf, uint32_t dr, int n_slots,
                                                int SB) {
   if (c.ph == 0) {
-    const int s = (int)(c.a / nrb), r0 = (int)(c.a - (long)s * nrb) * pa, nr = min(pa, I - r0);
+    const int s = c.a / nrb, r0 = (c.a - s * nrb) * pa, nr = min(pa, I - r0);
     const WDesc Gw = wdesc<GF>(sx[s].g, I, D), Uw = wdesc<GF>(sx[s].u, I, D);
     mbar_arrive_expect_tx(bar, row_tx(Gw, r0, nr) + row_tx(Uw, r0, nr));
     stage_row(Gw, r0, dst, bar, nr);
@@ -226,7 +217,7 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
   const int T = a.T, D = a.D, E = a.E, K = a.top_k, I = a.I;
   const int G = gridDim.x;
   // work items go to warps CTA-interleaved, so every SM gets an even share
-  const long gw = (long)wid * G + blockIdx.x, NW = (long)G * SW;
+  const int gw = wid * G + blockIdx.x, NW = G * SW;
   const int gbpr = (D + QK - 1) / QK, dbpr = (I + QK - 1) / QK;
   uint8_t* ring = dsm + (size_t)wid * a.nst * a.stage_bytes;
   float* rrow = reinterpret_cast<float*>(dsm + (size_t)SW * a.nst * a.stage_bytes);   // [rwc][D]
@@ -250,6 +241,7 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
     if (wid == 0) {
       mbar_init(&sh.xbar, 1);
       mbar_init(&sh.ebar, 1);
+      sh.ok = 1;
     }
     fence_mbar_init();
     if (wbulk) {
@@ -380,8 +372,134 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
   }
   __syncthreads();
   if (wid == 0) TG_MARK(17);
+  if (tid == 0 && !mbar_wait(&sh.ebar, 0)) {
+    set_error(a.st, ERR_WAIT_TIMEOUT, 37, blockIdx.x, 0);
+    sh.ok = 0;
+  }
+  if (wid == 0) TG_MARK(2);
+
+  // ---- S: warp t < T polls token t's logits (tagged with this epoch) into
+  // registers, takes its top K and their softmax weights (and, for one
+  // token, plans); meanwhile the other warps quantize N (R3), and the
+  // selecting warps join in when done.  Every CTA plans on its own.
+  bool sfail = false;
+  if (wid < T) {
+    const int t = wid;
+    constexpr int NV = STEP_E_MAX / 32;   // logits per lane: experts lane + 32 i
+    float v[NV];
+    uint32_t key[NV];
+    int id[NV];
+    for (int it = 0;; it++) {
+      bool ok = true;
+#pragma unroll
+      for (int i = 0; i < NV; i++) {
+        const int e = lane + 32 * i;
+        v[i] = 0.f;
+        if (e < E) {
+          const unsigned long long w = ld_tagged(a.lgt + (size_t)t * E + e);
+          ok &= tag_is(w, ep);
+          v[i] = tag_val(w);
+        }
+      }
+      if (__all_sync(FULL, ok)) {
+        if (a.trace && t == 0 && lane == 0) a.trace[blockIdx.x * 32 + 19] = it + 1;
+        break;
+      }
+      if (it >= STEP_POLLS) {
+        if (lane == 0) set_error(a.st, ERR_WAIT_TIMEOUT, 31, blockIdx.x, t);
+        sfail = true;
+        break;
+      }
+      __nanosleep(64);
+    }
+    if (t == 0) TG_MARK(9);
+    // order keys: larger logit larger key, -0 as +0, NaN (1) below every
+    // number, absent (0) below NaN; equal keys go to the lower expert id
+    // (router.py:35-38, NaN last)
+#pragma unroll
+    for (int i = 0; i < NV; i++) {
+      uint32_t u = __float_as_uint(v[i]);
+      if (u == 0x80000000u) u = 0u;
+      id[i] = lane + 32 * i;
+      key[i] = id[i] >= E ? 0u : v[i] != v[i] ? 1u : (u >> 31) ? ~u : (u | 0x80000000u);
+    }
+    // the lane's 8 in that order (19-comparator sorting network), then K
+    // rounds: the warp's largest head, the lowest id among equal heads, and
+    // the winner's lane steps to its next
+    auto cas = [&](int x, int y) {
+      const bool sw = key[y] > key[x] || (key[y] == key[x] && id[y] < id[x]);
+      const uint32_t kx = key[x], ky = key[y];
+      const float vx = v[x], vy = v[y];
+      const int ix = id[x], iy = id[y];
+      key[x] = sw ? ky : kx; key[y] = sw ? kx : ky;
+      v[x] = sw ? vy : vx; v[y] = sw ? vx : vy;
+      id[x] = sw ? iy : ix; id[y] = sw ? ix : iy;
+    };
+    cas(0, 2); cas(1, 3); cas(4, 6); cas(5, 7);
+    cas(0, 4); cas(1, 5); cas(2, 6); cas(3, 7);
+    cas(0, 1); cas(2, 3); cas(4, 5); cas(6, 7);
+    cas(2, 4); cas(3, 5);
+    cas(1, 4); cas(3, 6);
+    cas(1, 2); cas(3, 4); cas(5, 6);
+    for (int jj = 0; jj < (sfail ? 0 : K); jj++) {
+      const uint32_t M = __reduce_max_sync(FULL, key[0]);
+      const uint32_t I = __reduce_min_sync(FULL, key[0] == M ? (uint32_t)id[0] : 0xffffffffu);
+      if ((uint32_t)id[0] == I) {
+        sh.sel_e[t][jj] = (int)I;
+        sh.sel_v[t][jj] = v[0] != v[0] ? -INFINITY : v[0];
+#pragma unroll
+        for (int i = 0; i < NV - 1; i++) {
+          key[i] = key[i + 1];
+          v[i] = v[i + 1];
+          id[i] = id[i + 1];
+        }
+        key[NV - 1] = 0u;
+      }
+    }
+    __syncwarp();
+    // softmax over the selected (lane j < K takes selection j; the sum runs
+    // in j order)
+    const float ex = lane < K ? expf(fsub(sh.sel_v[t][lane], sh.sel_v[t][0])) : 0.f;
+    float sum = 0.f;
+    for (int jj = 0; jj < K; jj++) sum = fadd(sum, shfl(ex, jj));
+    const float w = lane < K ? __fdiv_rn(ex, sum) : 0.f;
+    if (lane < K) {
+      sh.sel_w[t][lane] = w;
+      if (blockIdx.x == 0) {
+        a.sel_idx[t * K + lane] = sh.sel_e[t][lane];
+        a.sel_w[t * K + lane] = w;
+      }
+    }
+    if (T == 1) {
+      // one token: its selected experts (nonzero weight, local) ascending by
+      // id are the slots, one active row each
+      const int e = lane < K ? sh.sel_e[0][lane] : 0x7fffffff;
+      const bool valid = lane < K && w != 0.f && etab[lane < K ? e : 0].g != nullptr;
+      const unsigned vm = __ballot_sync(FULL, valid);
+      int rank = 0;
+      for (int q = 0; q < K; q++) {
+        const int eq = __shfl_sync(FULL, e, q);
+        rank += ((vm >> q) & 1u) && eq < e;
+      }
+      if (valid) {
+        sh.slot_e[rank] = e;
+        sh.slot_n[rank] = 1;
+        sh.slot_off[rank] = rank;
+        sh.row_t[rank] = 0;
+        sh.row_w[rank] = w;
+        sx[rank] = etab[e];
+      }
+      if (lane == 0) {
+        sh.n_slots = __popc(vm);
+        sh.total = __popc(vm);
+      }
+    }
+    if (t == 0) TG_MARK(14);
+  }
+  if (wid == T) TG_MARK(20);
+  // R3, warps T.. first
 #pragma unroll 1
-  for (int q = wid; q < nq; q += SW) {
+  for (int q = (wid + SW - T) % SW; q < nq; q += SW) {
     const int t = q / gbpr, b = q - t * gbpr, i0 = b * QK + 8 * lane, n = min(QK, D - b * QK);
     float v[8];
     load_block(q, v, false);
@@ -399,133 +517,11 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
     }
     quantize_xq(v, n, xa + q);
   }
-  if (wid == 0) TG_MARK(18);
-  if (tid == 0 && !mbar_wait(&sh.ebar, 0)) set_error(a.st, ERR_WAIT_TIMEOUT, 37, blockIdx.x, 0);
-  if (__syncthreads_or(dead)) return;   // nothing in flight: the copies above were all waited for
-  if (wid == 0) TG_MARK(2);
-
-  // ---- S: every CTA polls the logits (tagged with this epoch), then ranks
-  // and plans on its own.
-  bool nan_here = false;
-  for (int it = 0;; it++) {
-    bool miss = false;
-    for (int i = tid; i < T * E; i += SW * 32) {
-      const unsigned long long w = ld_tagged(a.lgt + i);
-      if (!tag_is(w, ep)) {
-        miss = true;
-      } else {
-        const float v = tag_val(w);
-        sh.lg[i] = v;
-        nan_here |= v != v;
-      }
-    }
-    if (!__syncthreads_or(miss)) {
-      if (a.trace && tid == 0) a.trace[blockIdx.x * 32 + 19] = it + 1;
-      break;
-    }
-    if (it >= STEP_POLLS) {
-      if (tid == 0) set_error(a.st, ERR_WAIT_TIMEOUT, 31, blockIdx.x, 0);
-      return;
-    }
-    __nanosleep(64);
-  }
+  if (wid == T) TG_MARK(18);
   for (int i = tid; i < E; i += SW * 32) sh.cnt[i] = 0;
-  const bool any_nan = __syncthreads_or(nan_here) != 0;
-  if (wid == 0) TG_MARK(9);
-  {
-    // rank of each (token, expert) among its token's logits; P lanes share
-    // one element's comparisons, reading the row 4 logits at a time
-    int P = 1;
-    while (P < 32 && 2 * P * T * E <= SW * 32) P *= 2;
-    const bool v4 = (E & 3) == 0;
-    for (int base = 0; base < T * E * P; base += SW * 32) {
-      const int idx = base + tid, el = idx / P, part = idx - el * P;
-      const bool valid = el < T * E;
-      int rank = 0, t = 0, e = 0;
-      float v = 0.f;
-      if (valid) {
-        t = el / E;
-        e = el - t * E;
-        v = sh.lg[el];
-        const float* row = sh.lg + t * E;
-        if (any_nan) {
-          for (int jj = part; jj < E; jj += P) rank += ranks_above(row[jj], jj, v, e);
-        } else if (v4) {
-#pragma unroll 4
-          for (int c = part; c < E / 4; c += P) {
-            const float4 q = reinterpret_cast<const float4*>(row)[c];
-            const int j0 = 4 * c;
-            rank += (q.x > v) | ((q.x == v) & (j0 < e));
-            rank += (q.y > v) | ((q.y == v) & (j0 + 1 < e));
-            rank += (q.z > v) | ((q.z == v) & (j0 + 2 < e));
-            rank += (q.w > v) | ((q.w == v) & (j0 + 3 < e));
-          }
-        } else {
-          for (int jj = part; jj < E; jj += P) {
-            const float vj = row[jj];
-            rank += (vj > v) | ((vj == v) & (jj < e));
-          }
-        }
-      }
-      for (int o = 1; o < P; o <<= 1) rank += __shfl_xor_sync(FULL, rank, o);
-      if (valid && part == 0 && rank < K) {
-        sh.sel_e[t][rank] = e;
-        sh.sel_v[t][rank] = v != v ? -INFINITY : v;
-      }
-    }
-  }
-  __syncthreads();
-  if (wid == 0) TG_MARK(14);
-  if (T == 1) {
-    // one token: its selected experts (nonzero weight, local) ascending by id
-    // are the slots, one active row each; warp 0 builds the plan
-    if (wid == 0) {
-      const float ex = lane < K ? expf(fsub(sh.sel_v[0][lane], sh.sel_v[0][0])) : 0.f;
-      float sum = 0.f;
-      for (int jj = 0; jj < K; jj++) sum = fadd(sum, shfl(ex, jj));
-      const int e = lane < K ? sh.sel_e[0][lane] : 0x7fffffff;
-      const float w = lane < K ? __fdiv_rn(ex, sum) : 0.f;
-      if (lane < K && blockIdx.x == 0) {
-        a.sel_idx[lane] = e;
-        a.sel_w[lane] = w;
-      }
-      const bool valid = lane < K && w != 0.f && etab[lane < K ? e : 0].g != nullptr;
-      const unsigned vm = __ballot_sync(FULL, valid);
-      int rank = 0;
-      for (int i = 0; i < K; i++) {
-        const int ei = __shfl_sync(FULL, e, i);
-        rank += ((vm >> i) & 1u) && ei < e;
-      }
-      if (valid) {
-        sh.slot_e[rank] = e;
-        sh.slot_n[rank] = 1;
-        sh.slot_off[rank] = rank;
-        sh.row_t[rank] = 0;
-        sh.row_w[rank] = w;
-        sx[rank] = etab[e];
-      }
-      if (lane == 0) {
-        sh.n_slots = __popc(vm);
-        sh.total = __popc(vm);
-      }
-    }
-    __syncthreads();
-  } else {
-    if (wid < T) {   // warp t: lane j < K takes selection j; the sum runs in j order
-      const int t = wid;
-      const float ex = lane < K ? expf(fsub(sh.sel_v[t][lane], sh.sel_v[t][0])) : 0.f;
-      float sum = 0.f;
-      for (int j = 0; j < K; j++) sum = fadd(sum, shfl(ex, j));
-      if (lane < K) {
-        const float w = __fdiv_rn(ex, sum);
-        sh.sel_w[t][lane] = w;
-        if (blockIdx.x == 0) {
-          a.sel_idx[t * K + lane] = sh.sel_e[t][lane];
-          a.sel_w[t * K + lane] = w;
-        }
-      }
-    }
-    __syncthreads();
+  if (__syncthreads_or(sfail || !sh.ok)) return;
+  if (wid == 0) TG_MARK(21);
+  if (T > 1) {
     // experts held by another GPU (no local weights) are skipped; their
     // contribution arrives through the cross-GPU sum
     for (int i = tid; i < T * K; i += SW * 32) {
@@ -599,7 +595,7 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
   const int pa = a.pa, SB = a.sb;
   const uint32_t ghalf = rows_stage_bytes(grs, pa), dr = rows_stage_bytes(drs, 1);
   const int nrb = (I + pa - 1) / pa;   // row blocks per slot
-  const long nA = (long)n_slots * nrb;
+  const int nA = n_slots * nrb;
   const int k = T, rule = a.assoc_rule, act = a.act;
   const int gbb = GF == FMT_Q4K ? Q4K_BYTES : 192, dbb = DF == FMT_Q4K ? Q4K_BYTES : 192;   // main bytes per block
 
@@ -664,10 +660,10 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
   // phase A: items gw, gw + NW, ... < nA
   const int gbpr2 = GBLK ? gbpr : 1;                 // lanes per row
   const int a_pr = lane / (2 * gbpr2), a_m = (lane / gbpr2) & 1, a_b = lane - (lane / gbpr2) * gbpr2;
-  for (long it = gw; it < nA; it += NW, j++) {
+  for (int it = gw; it < nA; it += NW, j++) {
     const int stg = j % a.nst;
     if (!wait_stage(stg, j)) continue;
-    const int s = (int)(it / nrb), r0 = (int)(it - (long)s * nrb) * pa, nr = min(pa, I - r0);
+    const int s = it / nrb, r0 = (it - s * nrb) * pa, nr = min(pa, I - r0);
     const StepExpert& X = sx[s];
     const WDesc Gw = wdesc<GF>(X.g, I, D), Uw = wdesc<GF>(X.u, I, D);
     const uint8_t* dst = ring + (size_t)stg * a.stage_bytes;
@@ -805,7 +801,7 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
   const int b_b = lane / SL, b_sl = lane - b_b * SL;
   float* accw = sh.accw[wid];   // running output of the warp's row, per token
   if (n_slots > 0)
-    for (long r = gw; r < D; r += NW) {
+    for (int r = gw; r < D; r += NW) {
       if (lane < T) accw[lane] = 0.f;
       __syncwarp();
       for (int s0 = 0; s0 < n_slots; s0 += SB, j++) {
@@ -882,7 +878,7 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
       __syncwarp();
     }
   else if (!dead)
-    for (long r = gw; r < D; r += NW)
+    for (int r = gw; r < D; r += NW)
       if (lane < T) a.out[(size_t)lane * D + r] = 0.f;
 
   if (wid == 0) TG_MARK(8);
@@ -981,10 +977,14 @@ static cudaError_t step_launch(StepArgs a, const StepShape& sh, cudaStream_t s) 
   const void* fn = reinterpret_cast<const void*>(layer_step_kernel<GF, DF>);
   cudaError_t e = ensure_smem(fn, sh.smem);
   if (e != cudaSuccess) return e;
-  int per = 0;
-  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, fn, SW * 32, sh.smem);
-  if (e != cudaSuccess) return e;
-  if (per < 1) return cudaErrorInvalidConfiguration;
+  static size_t fits = 0;   // largest shared-memory size known to fit one CTA per SM
+  if (sh.smem > fits) {
+    int per = 0;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, fn, SW * 32, sh.smem);
+    if (e != cudaSuccess) return e;
+    if (per < 1) return cudaErrorInvalidConfiguration;
+    fits = sh.smem;
+  }
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(step_sms());
   cfg.blockDim = dim3(SW * 32);

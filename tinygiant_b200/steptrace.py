@@ -19,11 +19,11 @@ PHASES = [
     ("R: x + router rows (w0)", 1, 3),
     ("R1: sums, partial logits (w0)", 3, 16),
     ("R2: rr, logits (CTA)", 16, 17),
-    ("R3: Q8 of N (w0)", 17, 18),
-    ("R: CTA sync", 18, 2),
-    ("logits poll", 2, 9),
-    ("top-k ranks", 9, 14),
-    ("weights + plan", 14, 4),
+    ("logits poll (w0)", 2, 9),
+    ("top-k, softmax (+plan) (w0)", 9, 14),
+    ("R3: Q8 of N (first R3 warp)", 20, 18),
+    ("S / R3 CTA sync (w0)", 14, 21),
+    ("plan (T>1)", 21, 4),
     ("phase A (warp 0)", 4, 5),
     ("hidden poll (warp 0)", 5, 6),
     ("Q8 of hidden (warp 0)", 6, 15),
