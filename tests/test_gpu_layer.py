@@ -93,6 +93,35 @@ def test_fused_step_bit_exact_vs_reference_abi(gpu, qwen16, T):
     np.testing.assert_array_equal(got.view(np.uint32), want.view(np.uint32))
 
 
+@pytest.fixture(scope="module")
+def gptoss8(gpu):
+    L = synth.gptoss_layer(seed=3, n_experts=8)
+    return L, ResidentLayer(L, max_tokens=4, lib=gpu)
+
+
+@pytest.mark.parametrize("T", [1, 3])
+def test_fused_step_bit_exact_vs_reference_abi_mxfp4(gpu, gptoss8, T):
+    """The MXFP4 (gpt-oss) fused step, whose rows are split over half warps
+    with the sub-block fold chained through the lanes, equals the
+    reference-ABI call on the step's own routing bit for bit."""
+    L, R = gptoss8
+    N = synth.rms_norm(np.random.default_rng(500 + T).standard_normal((T, L.embed_dim)).astype(np.float32))
+    got = R.forward(N, normalize=False)
+    idx, w = R.last_routing(T)
+    sel = sorted({int(idx[t, j]) for t in range(T) for j in range(L.top_k) if w[t, j] != 0})
+    row_w = np.zeros((len(sel), T), np.float32)
+    for t in range(T):
+        for j in range(L.top_k):
+            if w[t, j] != 0:
+                row_w[sel.index(int(idx[t, j])), t] = w[t, j]
+    want = np.zeros_like(N)
+    M.moe_forward_rows_v2(gpu, [L.gates[e] for e in sel], [L.ups[e] for e in sel], [L.downs[e] for e in sel],
+                          L.gate_fmt, [L.down_fmts[e] for e in sel], None, None, None, L.act, row_w, N, want,
+                          L.embed_dim, L.inter_dim)
+    tg.check(gpu)
+    np.testing.assert_array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
 def test_fused_step_more_experts_than_sms(gpu, oracle):
     """200 experts: some CTAs hold two router rows."""
     L = synth.qwen_layer(seed=7, n_experts=200, D=512, I=256)

@@ -515,7 +515,7 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
         v[jj] = i0 + jj < D ? x : 0.f;
       }
     }
-    quantize_xq(v, n, xa + q);
+    quantize_xq<GF == FMT_MXFP4>(v, n, xa + q);
   }
   if (wid == T) TG_MARK(18);
   for (int i = tid; i < E; i += SW * 32) sh.cnt[i] = 0;
@@ -587,7 +587,7 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
   // 256-block format, phase A lanes are (row, gate|up, block) and phase B
   // lanes (slot, block): each lane folds one block's term in the reference's
   // order and the row's lanes fold the terms in block order.  Other formats
-  // spread each row over the whole warp (warp_dot1).
+  // split each row over half a warp (half_dot_sub32).
   const int n_slots = sh.n_slots, total = sh.total;
   const int grs = row_layout(GF, D).rs, drs = row_layout(DF, I).rs;
   constexpr bool GBLK = GF == FMT_Q4K || GF == FMT_Q6K;
@@ -696,28 +696,19 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
         }
       }
     } else {
-      const RowPtrs pg = row_ptrs(Gw, r0, dst), pu = row_ptrs(Uw, r0, dst + ghalf);
+      // one row: lanes 0-15 its gate row, lanes 16-31 its up row
+      const RowPtrs rp = row_ptrs(lane < 16 ? Gw : Uw, r0, dst + (lane < 16 ? 0 : ghalf));
 #pragma unroll 1
-      for (int g0 = 0; g0 < n; g0 += 4) {
-        const int ng = min(4, n - g0);
-        const bool x4 = use_x4(rule, g0, n, k);
-        float gt = 0.f, ut = 0.f;
-#pragma unroll 1
-        for (int q = 0; q < 2 * ng; q++) {
-          const int t = q >> 1;
-          const float v = warp_dot1<GF>((q & 1) ? pu : pg, D, xa + (size_t)sh.row_t[off + g0 + t] * gbpr, x4);
-          const float vb = shfl(v, 0);
-          if (lane == t) {
-            if (q & 1) ut = vb;
-            else gt = vb;
-          }
-        }
-        if (lane < ng) {
+      for (int jj = 0; jj < n; jj++) {
+        const float v = half_dot_sub32<GF>(rp, D / 32, xa + (size_t)sh.row_t[off + jj] * gbpr);
+        const float up = shfl(v, 16);
+        if (lane == 0) {
+          float gt = v, ut = up;
           if (X.gb) {
             gt = fadd(gt, X.gb[r0]);
             ut = fadd(ut, X.ub[r0]);
           }
-          st_tagged(a.hidt + hid_word(off + g0 + lane, r0, dbpr), ep, act_fn(act, gt, ut));
+          st_tagged(a.hidt + hid_word(off + jj, r0, dbpr), ep, act_fn(act, gt, ut));
         }
       }
     }
@@ -787,7 +778,7 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
       float vv[8];
 #pragma unroll
       for (int jj = 0; jj < 8; jj++) vv[jj] = h ? v[1][jj] : v[0][jj];
-      quantize_xq(vv, nn[h], &xb);
+      quantize_xq<DF == FMT_MXFP4>(vv, nn[h], &xb);
     }
   }
   if (wid == 0) TG_MARK(15);
@@ -849,24 +840,32 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
             __syncwarp();
           }
         } else {
-          for (int s = s0; s < s1; s++) {
-            const StepExpert& X = sx[s];
-            const RowPtrs rp = row_ptrs(wdesc<DF>(X.d, D, I), (int)r, dst + (s - s0) * dr);
-            const int n = sh.slot_n[s], off = sh.slot_off[s];
+          // two slots per pass: lanes 0-15 slot sp, lanes 16-31 slot sp + 1;
+          // their parts are added in slot order
 #pragma unroll 1
-            for (int g0 = 0; g0 < n; g0 += 4) {
-              const int ng = min(4, n - g0);
-              const bool x4 = use_x4(rule, g0, n, k);
+          for (int sp = s0; sp < s1; sp += 2) {
+            const int s = sp + (lane >> 4);
+            const bool in = s < s1;
+            const int sc = in ? s : sp;
+            const StepExpert& X = sx[sc];
+            const RowPtrs rp = row_ptrs(wdesc<DF>(X.d, D, I), r, dst + (sc - s0) * dr);
+            const int n = in ? sh.slot_n[sc] : 0, off = sh.slot_off[sc];
+            const float db = X.db ? X.db[r] : 0.f;
 #pragma unroll 1
-              for (int t = 0; t < ng; t++) {
-                const int sr = off + g0 + t;
-                const float v = warp_dot1<DF>(rp, I, xs + (size_t)sr * dbpr, x4);
-                if (lane == 0) {
-                  const float w = sh.row_w[sr];
-                  const float part = a.bias_term ? fmul(w, fadd(v, X.db ? X.db[r] : 0.f)) : fmul(w, v);
-                  const int tt = sh.row_t[sr];
-                  accw[tt] = fadd(accw[tt], part);
-                }
+            for (int t = 0; t < T; t++) {
+              int jr = -1;
+              for (int jj = 0; jj < n; jj++)
+                if (sh.row_t[off + jj] == t) jr = jj;
+              const float v = half_dot_sub32<DF>(rp, I / 32, xs + (size_t)(off + max(jr, 0)) * dbpr);
+              const float w = jr >= 0 ? sh.row_w[off + jr] : 0.f;
+              const float part = a.bias_term ? fmul(w, fadd(v, db)) : fmul(w, v);
+              const float p0 = shfl(part, 0), p1 = shfl(part, 16);
+              const int h0 = __shfl_sync(FULL, jr >= 0, 0), h1 = __shfl_sync(FULL, jr >= 0, 16);
+              if (lane == 0) {
+                float acc = accw[t];
+                if (h0) acc = fadd(acc, p0);
+                if (h1) acc = fadd(acc, p1);
+                accw[t] = acc;
               }
             }
           }
@@ -952,7 +951,7 @@ static bool step_shape(const StepLaunch& l, StepShape& sh) {
   if (dblk)
     while (2 * sh.sl * bd <= 32) sh.sl *= 2;
   const int max_slots = std::min(l.E, l.T * l.top_k);
-  int sb = dblk ? std::min(sh.sl, max_slots) : std::max(1, (int)(sa / dr));
+  int sb = dblk ? std::min(sh.sl, max_slots) : std::min(2, max_slots);   // 32-value formats: two slots per pass
   for (;;) {
     sh.stage = std::max(sa, (uint32_t)sb * dr);
     if (fixed + (size_t)SW * 2 * sh.stage <= budget || sb == 1) break;

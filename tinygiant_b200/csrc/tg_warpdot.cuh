@@ -398,6 +398,11 @@ __device__ __forceinline__ float fmax_nan(float a, float b) {
 // as 0.  The amax reduction is a tree (max is order-free); a NaN in the block
 // gives the canonical NaN scale, where the reference propagates the NaN it
 // met first — the block's dots are NaN either way.
+//
+// PERM stores each 32-value sub-block's qs in the MXFP4 order: word 2k + h
+// holds values (4k + 2h, 16 + 4k + 2h, 4k + 2h + 1, 17 + 4k + 2h), the
+// order in which mxfp4_isum reads a code word's nibbles.
+template <bool PERM = false>
 __device__ __forceinline__ void quantize_xq(const float (&v)[8], int n, XQ* o) {
   const int lane = threadIdx.x & 31;
   float m[8];
@@ -424,7 +429,22 @@ __device__ __forceinline__ void quantize_xq(const float (&v)[8], int n, XQ* o) {
     w0 |= ((uint32_t)q[j] & 0xFFu) << (8 * j);
     w1 |= ((uint32_t)q[4 + j] & 0xFFu) << (8 * j);
   }
-  *reinterpret_cast<uint2*>(o->qs + 8 * lane) = make_uint2(w0, w1);
+  if constexpr (PERM) {
+    // lane l holds sub-block l / 4's values 8 (l % 4) .. + 7; lanes with
+    // l % 4 < 2 take the values 16 further on from lane l + 2 and write
+    // 16 bytes of the sub-block each
+    const uint32_t p0 = __shfl_xor_sync(FULL, w0, 2), p1 = __shfl_xor_sync(FULL, w1, 2);
+    if ((lane & 2) == 0) {
+      uint4 nw;
+      nw.x = __byte_perm(w0, p0, 0x5140);
+      nw.y = __byte_perm(w0, p0, 0x7362);
+      nw.z = __byte_perm(w1, p1, 0x5140);
+      nw.w = __byte_perm(w1, p1, 0x7362);
+      *reinterpret_cast<uint4*>(o->qs + 32 * (lane >> 2) + 16 * (lane & 1)) = nw;
+    }
+  } else {
+    *reinterpret_cast<uint2*>(o->qs + 8 * lane) = make_uint2(w0, w1);
+  }
   const int s16 = s + __shfl_xor_sync(FULL, s, 1);        // values 16 (l / 2) .. + 15
   const int s32 = s16 + __shfl_xor_sync(FULL, s16, 2);    // sub-block l / 4
   int tot = s32 + __shfl_xor_sync(FULL, s32, 4);
@@ -576,6 +596,93 @@ __device__ __forceinline__ float q6k_block_term(const uint8_t* mb, const uint8_t
   const float bs = A < (1 << 24) ? (float)S : q6k_fold_slow(mb, sw, xb);
   const float d = f16_fast((uint32_t)db[0] | ((uint32_t)db[1] << 8));
   return fmul(fmul(d, xb.scale), bs);
+}
+
+// prmt with the PTX semantics of the selector's bit 3: the selected byte's
+// sign replicated.
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+  uint32_t d;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+  return d;
+}
+
+// Integer dot of one MXFP4 sub-block (16 code bytes: byte i holds value i in
+// its low nibble and value 16 + i in its high nibble) with x's 32 values in
+// the MXFP4 order of quantize_xq<true>.  A code word used as a prmt selector
+// indexes the doubled e2m1 magnitudes {0, 1, 2, 3, 4, 6, 8, 12} (csrc/
+// libtinygiant.c:514) by its nibbles' low 3 bits, while a set sign bit makes
+// prmt emit the (zero) sign of the entry: so the word itself gives the
+// positive codes' values and the word with its sign bits flipped the
+// negative codes' magnitudes, and the dot is dot(positives) - dot(negatives).
+__device__ __forceinline__ int mxfp4_isum(const uint4& cv, const int8_t* xq) {
+  constexpr uint32_t T0 = 0x03020100u, T1 = 0x0C080604u;
+  const uint4 xa = ld16(xq), xb = ld16(xq + 16);
+  const uint32_t xw[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
+  const uint32_t cw[4] = {cv.x, cv.y, cv.z, cv.w};
+  int p = 0, m = 0;
+#pragma unroll
+  for (int k = 0; k < 4; k++) {
+    const uint32_t c = cw[k], cn = c ^ 0x88888888u;
+    p = dp4a((int)prmt(T0, T1, c), (int)xw[2 * k], p);
+    m = dp4a((int)prmt(T0, T1, cn), (int)xw[2 * k], m);
+    p = dp4a((int)prmt(T0, T1, c >> 16), (int)xw[2 * k + 1], p);
+    m = dp4a((int)prmt(T0, T1, cn >> 16), (int)xw[2 * k + 1], m);
+  }
+  return p - m;
+}
+
+// Half-warp row dot of a 32-value-block format (MXFP4, Q8_0) against one
+// token's Q8 blocks x (XQ; for MXFP4 in the order of quantize_xq<true>): the
+// 16 lanes of half hb = lane & 16 share the row; lane h of the half forms the
+// terms of sub-blocks h C .. h C + C - 1 (C = ceil(nsub / 16) <= 8), and the
+// reference's left fold over sub-blocks (dot_mxfp4_q8 533-547, dot_q80_q8
+// 576-590) runs through the half's lanes in order, one shuffle per lane.
+// Terms past the row end are +0, whose addition leaves every partial sum of
+// these folds unchanged (no term and no partial sum is -0: the products of
+// positive scales with an integer sum round a zero to +0).  Both halves call
+// together; every lane of a half returns its row's dot.
+template <int FMT>
+__device__ __forceinline__ float half_dot_sub32(const RowPtrs& rp, int nsub, const XQ* x) {
+  const int lane = threadIdx.x & 31, h = lane & 15, hb = lane & 16;
+  const int C = (nsub + 15) >> 4;
+  float term[8];
+#pragma unroll
+  for (int c = 0; c < 8; c++) {
+    const int u = h * C + c;
+    term[c] = 0.f;
+    if (c < C && u < nsub) {
+      const XQ& xb = x[u >> 3];
+      const int8_t* xq = xb.qs + (u & 7) * 32;
+      if constexpr (FMT == FMT_MXFP4) {
+        const int isum = mxfp4_isum(ld16(rp.m + (size_t)u * 16), xq);
+        term[c] = fmul(fmul(xb.scale, e8m0_half(rp.a1[u])), i2f_small(isum));
+      } else {
+        const uint4 qa = ld16(rp.m + (size_t)u * 32), qb = ld16(rp.m + (size_t)u * 32 + 16);
+        const uint4 xa = ld16(xq), xc = ld16(xq + 16);
+        int acc = dp4a((int)qa.x, (int)xa.x, 0);
+        acc = dp4a((int)qa.y, (int)xa.y, acc);
+        acc = dp4a((int)qa.z, (int)xa.z, acc);
+        acc = dp4a((int)qa.w, (int)xa.w, acc);
+        acc = dp4a((int)qb.x, (int)xc.x, acc);
+        acc = dp4a((int)qb.y, (int)xc.y, acc);
+        acc = dp4a((int)qb.z, (int)xc.z, acc);
+        acc = dp4a((int)qb.w, (int)xc.w, acc);
+        const float sc = f16_fast((uint32_t)rp.a2[(size_t)u * 2] | ((uint32_t)rp.a2[(size_t)u * 2 + 1] << 8));
+        term[c] = fmul(fmul(xb.scale, sc), i2f_small(acc));
+      }
+    }
+  }
+  float tot = 0.f;
+#pragma unroll 1
+  for (int i = 0; i < 16; i++) {
+    const float prev = __shfl_sync(FULL, tot, hb | ((i + 15) & 15));
+    float r = i == 0 ? 0.f : prev;
+#pragma unroll
+    for (int c = 0; c < 8; c++)
+      if (c < C) r = fadd(r, term[c]);
+    if (h == i) tot = r;
+  }
+  return __shfl_sync(FULL, tot, hb | 15);
 }
 
 // Row fold over lanes: lanes lead, lead + stride, ... (n of them) hold the

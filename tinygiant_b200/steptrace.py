@@ -7,7 +7,7 @@ runs steps of a resident layer with tracing on and reports the median and
 maximum over CTAs / warps of each phase, in microseconds (cycles are
 converted with the CTA's own global-timer span).
 
-    python -m tinygiant_b200.steptrace [--experts 128] [--copies 4] [--tokens 1]
+    python -m tinygiant_b200.steptrace [--experts 128] [--copies 4] [--tokens 1] [--gptoss]
 """
 import argparse
 import ctypes
@@ -71,6 +71,7 @@ def main():
     ap.add_argument("--experts", type=int, default=128)
     ap.add_argument("--copies", type=int, default=4)
     ap.add_argument("--tokens", type=int, default=1)
+    ap.add_argument("--gptoss", action="store_true", help="the gpt-oss-shaped MXFP4 layer (C4) instead of Qwen3 (C2)")
     a = ap.parse_args()
     import torch
 
@@ -79,7 +80,7 @@ def main():
     from tinygiant_b200.layer import ResidentLayer
 
     lib = tg.load()
-    L = synth.qwen_layer(seed=1, n_experts=a.experts)
+    L = synth.gptoss_layer(seed=3, n_experts=a.experts) if a.gptoss else synth.qwen_layer(seed=1, n_experts=a.experts)
     base = ResidentLayer(L, max_tokens=a.tokens, lib=lib)
     lays = [base] + [base.clone() for _ in range(a.copies - 1)]
     stream = torch.cuda.Stream()
