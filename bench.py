@@ -65,6 +65,7 @@ def parse():
     ap.add_argument("--copies", type=int, default=R_COPIES)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--parallel", default="dp", choices=["dp", "ep"])
+    ap.add_argument("--layers", type=int, default=48, help="C5: layers in the stack")
     return ap.parse_args()
 
 
@@ -84,7 +85,7 @@ def workload_desc(cfg, T, R, L):
         "c2": "C2: one Qwen3-30B-A3B MoE layer (128 experts, Q4_K gate/up, Q6_K down, top-8, D=2048, I=768)",
         "c3": "C3: Qwen3-30B-A3B MoE layer with Zipf(1.1)-skewed router bias",
         "c4": "C4: gpt-oss-120b-shaped MXFP4 MoE layer (128 experts, top-4, D=I=2880)",
-        "c5": "C5: Qwen3-30B-A3B MoE-FFN stack layer",
+        "c5": "C5: 48-layer Qwen3-30B-A3B MoE-FFN stack (C2 experts per layer, per-layer routers, residual add)",
     }
     return {"workload": names[cfg], "tokens_per_step": T, "experts": L.n_experts, "top_k": L.top_k,
             "embed_dim": L.embed_dim, "inter_dim": L.inter_dim, "layer_copies": R,
@@ -107,6 +108,19 @@ def algorithmic_bytes(L, xs):
         experts, _, _, _ = synth.route(L, synth.rms_norm(x))
         out.append(len(experts) * eb + L.router_w.nbytes + 2 * x.nbytes)
     return np.array(out, dtype=np.float64)
+
+
+def stack_routers(n_layers, E, D, seed=4):
+    """C5's per-layer routers: fp32 N(0, 0.02) [E, D], layer l from seed (seed, l)."""
+    return [(np.random.default_rng([seed, 11, l]).standard_normal((E, D)) * 0.02).astype(np.float32)
+            for l in range(n_layers)]
+
+
+def stack_bytes(L, n_layers, T):
+    """C5 per step at T = 1: every layer reads its top_k selected experts once
+    (T = 1 selects top_k distinct experts), its router and x in / out."""
+    assert T == 1, "C5 is defined at batch 1"
+    return float(n_layers * (L.top_k * L.expert_bytes(0) + L.router_w.nbytes + 2 * T * L.embed_dim * 4))
 
 
 # ---- clocks ------------------------------------------------------------------
@@ -228,11 +242,30 @@ def run_reference(a):
     cores = os.cpu_count() or 1
     lib.tg_set_threads(cores)
     out = np.zeros_like(xs[0])
+    if cfg == "c5":
+        # the engine's layer loop: x += MoE_l(rmsnorm(x)) for each layer's router
+        import copy
+        stack = []
+        for rw in stack_routers(a.layers, L.n_experts, L.embed_dim):
+            Ll = copy.copy(L)
+            Ll.router_w = rw
+            stack.append(Ll)
+
+        def one(x):
+            x = x.copy()
+            for Ll in stack:
+                o = np.zeros_like(x)
+                moe.moe_layer_forward(lib, Ll, synth.rms_norm(x), o)
+                x += o
+            return x
+    else:
+        def one(x):
+            moe.moe_layer_forward(lib, L, synth.rms_norm(x), out)
     for i in range(a.warmup):
-        moe.moe_layer_forward(lib, L, synth.rms_norm(xs[i]), out)
+        one(xs[i])
     t0 = time.perf_counter()
     for i in range(a.steps):
-        moe.moe_layer_forward(lib, L, synth.rms_norm(xs[a.warmup + i]), out)
+        one(xs[a.warmup + i])
     el = time.perf_counter() - t0
     value = a.steps * T / el
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": a.gpus, "steps": a.steps,
@@ -420,10 +453,163 @@ def run_ours(a):
         dist.destroy_process_group()
 
 
+def run_stack(a):
+    """C5: a token through an n-layer stack (x += MoE(rmsnorm(x)) per layer) per step."""
+    import torch
+    import torch.distributed as dist
+
+    import tinygiant_b200 as tg
+    from tinygiant_b200 import synth
+    from tinygiant_b200.layer import ResidentLayer
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    a.gpus = world
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+    lib = tg.load()
+    lib.tg_cuda_set_device(local)
+    stream = torch.cuda.Stream()
+    lib.tg_cuda_set_stream(ctypes.c_void_p(stream.cuda_stream))
+    T, NL = 1, a.layers
+    ep = world > 1 and a.parallel == "ep"
+    L = synth.qwen_layer(seed=1)
+    D = L.embed_dim
+    base = ResidentLayer(L, max_tokens=T, lib=lib, shard=rank if ep else 0, n_shards=world if ep else 1)
+    layers = [base] + [base.clone() for _ in range(NL - 1)]
+    for lay, rw in zip(layers, stack_routers(NL, L.n_experts, D)):
+        lay.set_router(rw)
+    tg.check(lib)
+    handles = (ctypes.c_void_p * NL)(*[lay.h for lay in layers])
+    S = a.warmup + a.steps
+    xs_host = step_inputs(S, T, D, seed=4 if ep or world == 1 else 4 + 1000 * rank)
+    xs = torch.from_numpy(xs_host).to(f"cuda:{local}")
+    xb = [torch.zeros((T, D), dtype=torch.float32, device=f"cuda:{local}") for _ in range(4)]
+
+    def step(i):
+        if not ep:
+            xb[0].copy_(xs[i])
+            lib.tg_stack_forward_dev(handles, NL, xb[0].data_ptr(), T, None)
+            return
+        # expert parallel: each layer's MoE parts are summed before the next layer reads them
+        x, xn, m0, m1 = xb
+        x.copy_(xs[i])
+        for l, lay in enumerate(layers):
+            lib.tg_layer_forward_dev(lay.h, x.data_ptr(), m0.data_ptr() if l else None,
+                                     xn.data_ptr() if l else None, m1.data_ptr(), T, 1, None)
+            dist.all_reduce(m1)
+            if l:
+                x, xn = xn, x
+            m0, m1 = m1, m0
+        x.add_(m0)
+        if x.data_ptr() != xb[0].data_ptr():
+            xb[0].copy_(x)
+
+    with torch.cuda.stream(stream):
+        for i in range(a.warmup):
+            step(i)
+    torch.cuda.synchronize()
+    tg.check(lib)
+    g = torch.cuda.CUDAGraph()
+    launches0 = lib.tg_cuda_launch_count()
+    with torch.cuda.graph(g, stream=stream):
+        for i in range(a.warmup, S):
+            step(i)
+    launches = lib.tg_cuda_launch_count() - launches0
+    tg.check(lib)
+    g.replay()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    clocks.start()
+    t_soak = time.perf_counter()
+    with torch.cuda.stream(stream):
+        while time.perf_counter() - t_soak < 1.5:
+            g.replay()
+            torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        ev0.record(stream)
+        g.replay()
+        ev1.record(stream)
+    torch.cuda.synchronize()
+    ms = ev0.elapsed_time(ev1)
+    if world > 1:
+        t = torch.tensor([ms], device=f"cuda:{local}")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    clk = clocks.stop()
+    tg.check(lib)
+    ranks_tokens = 1 if ep else world
+    value = ranks_tokens * a.steps * T / (ms / 1e3)
+
+    # e2e: x from pinned host memory, the stack, x back, every step (one GPU,
+    # or every rank for data parallel; max over ranks)
+    xpin = torch.from_numpy(xs_host).pin_memory()
+    opin = torch.zeros((T, D), dtype=torch.float32).pin_memory()
+
+    def e2e_step(i):
+        with torch.cuda.stream(stream):
+            xs[i].copy_(xpin[i], non_blocking=True)
+            step(i)
+            opin.copy_(xb[0], non_blocking=True)
+        stream.synchronize()
+
+    for i in range(min(a.warmup, S)):
+        e2e_step(i)
+    if world > 1:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for i in range(a.warmup, S):
+        e2e_step(i)
+    el = time.perf_counter() - t0
+    if world > 1:
+        t = torch.tensor([el], device=f"cuda:{local}")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        el = float(t.item())
+    tg.check(lib)
+    if rank == 0:
+        nbytes = stack_bytes(L, NL, T)
+        achieved = ranks_tokens * a.steps * nbytes / (ms / 1e3) / 1e9
+        peak, peak_src = measured_peak()
+        peak *= world
+        roof = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                "traffic": None, "kernel": f"fused MoE layer step x {NL} layers per token",
+                "algorithmic_bytes_per_step": nbytes, "peak_source": peak_src}
+        desc = workload_desc("c5", T, 1, L)
+        desc.update({"layers": NL, "l2": f"inputs larger than L2: {NL} distinct layers resident "
+                                       f"({NL * L.n_experts * L.expert_bytes(0) / 1e9:.1f} GB of experts)",
+                     "step": "one token through the stack: per layer rmsnorm + router + top-k + experts + residual add"})
+        line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": a.steps,
+                "warmup": a.warmup, "ms_per_step": ms / a.steps, "higher_is_better": True,
+                "scaling": "strong" if ep or world == 1 else "weak", "vs_baseline": None,
+                "dtype": DTYPES["c5"], "data": "synthetic (seeded weights and inputs)",
+                "config": {**desc, "parallelism": f"ep{world}" if ep else f"dp{world}"},
+                "gbps": achieved, "clocks": clk, "roofline": roof, "gpu_launches": int(launches),
+                "e2e": {"value": ranks_tokens * a.steps * T / el, "unit": UNIT,
+                        "h2d_bytes_per_step": int(T * D * 4), "d2h_bytes_per_step": int(T * D * 4),
+                        "api": "tg_stack_forward_dev with pinned host copies" if not ep else
+                               "tg_layer_forward_dev per layer + NCCL all-reduce, pinned host copies",
+                        "ms_per_step": el / a.steps * 1e3}}
+        print(json.dumps(line), flush=True)
+    del g
+    for lay in layers:
+        lay.close()
+    if world > 1:
+        dist.destroy_process_group()
+
+
 def main():
     a = parse()
     if a.impl == "reference":
         run_reference(a)
+    elif a.config == "c5":
+        run_stack(a)
     else:
         run_ours(a)
 

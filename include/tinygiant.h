@@ -194,6 +194,10 @@ int tg_layer_forward_dev(void *layer, const float *x, const float *add, float *x
  * decode-sized (T <= 8) and the formats have one; 0: three kernels (router,
  * gate/up, down).  Same results either way.  Returns the previous setting. */
 int tg_layer_set_fused(void *layer, int on);
+/* Replaces a layer's fp32 router [E][D] (and bias [E], or NULL: a layer made
+ * with a bias gets zeros, one made without keeps none) from host arrays;
+ * stacks give each layer its own.  Returns 0, or -1 on error. */
+int tg_layer_set_router(void *layer, const float *router_w, const float *router_b);
 /* Diagnostics: fused steps launched after this call write per-CTA phase
  * timestamps into dev_buf (32 uint64 per CTA: SM clocks, the global timer in
  * slots 12/13, the logits poll count in slot 19; then 8 uint64 per warp of

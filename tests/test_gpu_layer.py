@@ -179,6 +179,40 @@ def test_layer_shards_sum_to_whole(gpu, qwen16):
         p.close()
 
 
+def test_stack_of_clones_with_own_routers(gpu, oracle):
+    """C5's construction: layers cloned from one set of experts, each given
+    its own router by tg_layer_set_router, run as a device stack."""
+    torch = pytest.importorskip("torch")
+    import copy
+    L = synth.qwen_layer(seed=4, n_experts=12)
+    base = ResidentLayer(L, max_tokens=1, lib=gpu)
+    res = [base, base.clone(), base.clone()]
+    layers = []
+    for l, r in enumerate(res):
+        Ll = copy.copy(L)
+        Ll.router_w = (np.random.default_rng([9, l]).standard_normal((12, 2048)) * 0.02).astype(np.float32)
+        r.set_router(Ll.router_w)
+        layers.append(Ll)
+    x0 = np.random.default_rng(5).standard_normal((1, 2048)).astype(np.float32)
+    want = x0.copy()
+    for Ll in layers:
+        want = want + M.moe_layer_forward(oracle, Ll, synth.rms_norm(want))
+    stream = torch.cuda.Stream()
+    gpu.tg_cuda_set_stream(ctypes.c_void_p(stream.cuda_stream))
+    try:
+        hs = (ctypes.c_void_p * 3)(*[r.h for r in res])
+        x = torch.from_numpy(x0.copy()).cuda()
+        with torch.cuda.stream(stream):
+            assert gpu.tg_stack_forward_dev(hs, 3, ctypes.c_void_p(x.data_ptr()), 1, None) == 0
+        torch.cuda.synchronize()
+        tg.check(gpu)
+        assert rel_err(x.cpu().numpy(), want) <= TOL
+    finally:
+        gpu.tg_cuda_set_stream(None)
+        for r in res:
+            r.close()
+
+
 def test_stack_forward_and_graph_replay(gpu, oracle):
     torch = pytest.importorskip("torch")
     layers = [synth.qwen_layer(seed=4, layer=l, n_experts=12) for l in range(3)]

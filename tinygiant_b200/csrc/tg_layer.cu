@@ -368,6 +368,33 @@ int tg_cuda_step_trace(void* dev_buf) {
 
 // Selects the fused single-kernel step (on = 1, the default) or the
 // three-kernel step (on = 0) for this layer.  Returns the previous setting.
+// Replaces a layer's router with host arrays router_w [E][D] and router_b
+// [E] (or NULL for none; a layer created without a bias keeps none).
+int tg_layer_set_router(void* handle, const float* router_w, const float* router_b) {
+  std::lock_guard<std::recursive_mutex> lk(ctx_mutex());
+  const char* what = "tg_layer_set_router";
+  Layer* L = static_cast<Layer*>(handle);
+  if (!L || !router_w) {
+    set_host_error(3, "%s: null layer or router", what);
+    return -1;
+  }
+  if (router_b && !L->router_b) {
+    set_host_error(3, "%s: the layer was created without a router bias", what);
+    return -1;
+  }
+  cudaStream_t s = stream();
+  bool ok = cudaStreamSynchronize(s) == cudaSuccess &&
+            cudaMemcpy(L->router_w, router_w, sizeof(float) * (size_t)L->E * L->D, cudaMemcpyHostToDevice) == cudaSuccess;
+  if (ok && L->router_b)
+    ok = router_b ? cudaMemcpy(L->router_b, router_b, sizeof(float) * L->E, cudaMemcpyHostToDevice) == cudaSuccess
+                  : cudaMemset(L->router_b, 0, sizeof(float) * L->E) == cudaSuccess;
+  if (!ok) {
+    set_host_error(100, "%s: upload failed", what);
+    return -1;
+  }
+  return 0;
+}
+
 int tg_layer_set_fused(void* handle, int on) {
   Layer* L = static_cast<Layer*>(handle);
   if (!L) return -1;

@@ -45,6 +45,16 @@ class ResidentLayer:
         r.shard, r.n_shards = self.shard, self.n_shards
         return r
 
+    def set_router(self, router_w, router_b=None):
+        """A new fp32 router [E, D] (and bias [E]) for this layer."""
+        self._rw2 = np.ascontiguousarray(router_w, dtype=np.float32)
+        self._rb2 = None if router_b is None else np.ascontiguousarray(router_b, dtype=np.float32)
+        rc = self.lib.tg_layer_set_router(self.h, self._rw2.ctypes.data,
+                                          None if self._rb2 is None else self._rb2.ctypes.data)
+        check(self.lib)
+        if rc != 0:
+            raise RuntimeError("tg_layer_set_router failed")
+
     def set_fused(self, on=True):
         """Fused single-kernel steps (default) or the three-kernel path."""
         return bool(self.lib.tg_layer_set_fused(self.h, int(bool(on))))
