@@ -194,6 +194,10 @@ int tg_layer_forward_dev(void *layer, const float *x, const float *add, float *x
  * decode-sized (T <= 8) and the formats have one; 0: three kernels (router,
  * gate/up, down).  Same results either way.  Returns the previous setting. */
 int tg_layer_set_fused(void *layer, int on);
+/* 1 (default): batched steps (T > 8) run the expert GEMMs on the tensor
+ * cores (tcgen05); 0: the matvec kernels.  Same results either way.  Returns
+ * the previous setting. */
+int tg_layer_set_tc(void *layer, int on);
 /* Replaces a layer's fp32 router [E][D] (and bias [E], or NULL: a layer made
  * with a bias gets zeros, one made without keeps none) from host arrays;
  * stacks give each layer its own.  Returns 0, or -1 on error. */

@@ -122,6 +122,52 @@ def test_fused_step_bit_exact_vs_reference_abi_mxfp4(gpu, gptoss8, T):
     np.testing.assert_array_equal(got.view(np.uint32), want.view(np.uint32))
 
 
+@pytest.fixture(scope="module")
+def qwen16_batch(gpu):
+    L = synth.qwen_layer(seed=1, n_experts=16)
+    return L, ResidentLayer(L, max_tokens=96, lib=gpu)
+
+
+def _abi_with_routing(gpu, L, N, idx, w):
+    T = N.shape[0]
+    sel = sorted({int(idx[t, j]) for t in range(T) for j in range(L.top_k) if w[t, j] != 0})
+    row_w = np.zeros((len(sel), T), np.float32)
+    for t in range(T):
+        for j in range(L.top_k):
+            if w[t, j] != 0:
+                row_w[sel.index(int(idx[t, j])), t] = w[t, j]
+    want = np.zeros_like(N)
+    M.moe_forward_rows_v2(gpu, [L.gates[e] for e in sel], [L.ups[e] for e in sel], [L.downs[e] for e in sel],
+                          L.gate_fmt, [L.down_fmts[e] for e in sel], None, None, None, L.act, row_w, N, want,
+                          L.embed_dim, L.inter_dim)
+    tg.check(gpu)
+    return want
+
+
+@pytest.mark.parametrize("T", [20, 64, 96])
+def test_tensor_core_step_bit_exact_vs_reference_abi(gpu, qwen16_batch, T):
+    """Batched steps on the tcgen05 grouped GEMMs (exact per-sub-block int32
+    sums read back from tensor memory, the reference's fp32 folds, the
+    ordered combine) equal the reference-ABI call on the step's routing."""
+    L, R = qwen16_batch
+    N = synth.rms_norm(np.random.default_rng(600 + T).standard_normal((T, 2048)).astype(np.float32))
+    got = R.forward(N, normalize=False)
+    idx, w = R.last_routing(T)
+    want = _abi_with_routing(gpu, L, N, idx, w)
+    np.testing.assert_array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
+def test_tensor_core_step_equals_matvec_step(gpu, qwen16_batch):
+    L, R = qwen16_batch
+    x = np.random.default_rng(700).standard_normal((40, 2048)).astype(np.float32)
+    outs = []
+    for tc in (True, False):
+        R.set_tc(tc)
+        outs.append(R.forward(x, normalize=True))
+    R.set_tc(True)
+    np.testing.assert_array_equal(outs[0].view(np.uint32), outs[1].view(np.uint32))
+
+
 def test_fused_step_more_experts_than_sms(gpu, oracle):
     """200 experts: some CTAs hold two router rows."""
     L = synth.qwen_layer(seed=7, n_experts=200, D=512, I=256)

@@ -42,6 +42,8 @@ struct Layer {
   int* counters = nullptr;
   unsigned long long* step_sync = nullptr;   // the fused step kernel's exchange block (step_sync_words)
   bool fused = true;               // use the fused step kernel when the shape allows
+  bool tc = true;                  // batched steps (T > 8) on the tensor-core grouped GEMMs
+  void* tc_scratch = nullptr;      // their intermediates (tc_moe_scratch_bytes)
   // tg_layer_forward's CUDA graph (copy in, step, copies out) for one
   // (rows, normalize, host staging buffers, stream)
   cudaGraphExec_t fwd_exec = nullptr;
@@ -84,6 +86,8 @@ static bool alloc_scratch(Layer* L) {
          (register_counters(L->counters, sizeof(int) * moe_counter_ints(L->max_slots, I)), true) &&
          dmalloc(L, (void**)&L->step_sync, sizeof(unsigned long long) * step_sync_words(T, E, L->top_k, I)) &&
          (register_counters(L->step_sync, sizeof(unsigned long long) * step_sync_words(T, E, L->top_k, I)), true) &&
+         (!(T > 8 && tc_moe_eligible(L->gate_fmt, L->down_fmt, D, I)) ||
+          dmalloc(L, &L->tc_scratch, tc_moe_scratch_bytes(L->max_rows, T, L->top_k, D, I))) &&
          dmalloc(L, (void**)&L->moe_out, sizeof(float) * 2 * (size_t)T * D) &&
          dmalloc(L, (void**)&L->xbuf, sizeof(float) * (size_t)T * D);
 }
@@ -185,6 +189,17 @@ static bool layer_enqueue(Layer* L, const float* x, const float* add, float* x_o
   a.sel_w = L->sel_w;
   a.st = status_ptr();
   cudaError_t e = launch_layer_route(a, s);
+  if (L->tc && L->tc_scratch && T > 8) {
+    if (e == cudaSuccess)
+      e = launch_tc_moe(L->plan, L->gate_fmt, L->down_fmt, T, L->top_k, L->D, L->I, T * L->top_k, L->xq8,
+                        L->tc_scratch, moe_out, status_ptr(), s);
+    count_launches(6);
+    if (e != cudaSuccess) {
+      set_host_error(100 + (int)e, "%s: %s", what, cudaGetErrorString(e));
+      return false;
+    }
+    return true;
+  }
   if (e == cudaSuccess)
     e = launch_moe_gateup(L->plan, std::min(L->max_slots, T * L->top_k), L->gate_fmt, L->D, L->I, L->xq8, L->hidden,
                           L->hq8, L->counters, status_ptr(), s);
@@ -305,6 +320,7 @@ void* tg_layer_clone(void* handle) {
   L->top_k = src->top_k;
   L->max_tokens = src->max_tokens;
   L->fused = src->fused;
+  L->tc = src->tc;
   L->experts = src->experts;
   auto copy_w = [&](WDesc& w) -> bool {
     if (!w.main) return true;   // expert held by another GPU
@@ -393,6 +409,16 @@ int tg_layer_set_router(void* handle, const float* router_w, const float* router
     return -1;
   }
   return 0;
+}
+
+// Selects the tensor-core grouped GEMMs (on = 1, the default) or the matvec
+// kernels (on = 0) for batched steps (T > 8).  Returns the previous setting.
+int tg_layer_set_tc(void* handle, int on) {
+  Layer* L = static_cast<Layer*>(handle);
+  if (!L) return -1;
+  const int prev = L->tc ? 1 : 0;
+  L->tc = on != 0;
+  return prev;
 }
 
 int tg_layer_set_fused(void* handle, int on) {

@@ -95,5 +95,14 @@ cudaError_t launch_layer_step(const StepLaunch& l, cudaStream_t s);
 // (device memory; null turns it off).
 void set_step_trace(void* p);
 cudaError_t launch_layer_route(const RouteArgs& a, cudaStream_t s);
+// Batched steps on the tensor cores (tg_gemm.cu): for a plan written by the
+// route kernel, the gate/up and down grouped GEMMs (tcgen05, exact per
+// sub-block int32 sums), the activation and Q8 of hidden, and the ordered
+// combine into out (which the route kernel zeroed).  K: top_k; max_rows:
+// T * top_k; scratch: tc_moe_scratch_bytes of device memory.
+bool tc_moe_eligible(int gate_fmt, int down_fmt, int D, int I);
+size_t tc_moe_scratch_bytes(int max_rows, int T, int K, int D, int I);
+cudaError_t launch_tc_moe(const PlanHdr* ph, int gate_fmt, int down_fmt, int T, int K, int D, int I, int max_rows,
+                          const Q8Dev* xq8, void* scratch, float* out, DevStatus* st, cudaStream_t s);
 
 }  // namespace tg

@@ -55,6 +55,10 @@ class ResidentLayer:
         if rc != 0:
             raise RuntimeError("tg_layer_set_router failed")
 
+    def set_tc(self, on=True):
+        """Tensor-core grouped GEMMs (default) or matvec kernels for batched steps (T > 8)."""
+        return bool(self.lib.tg_layer_set_tc(self.h, int(bool(on))))
+
     def set_fused(self, on=True):
         """Fused single-kernel steps (default) or the three-kernel path."""
         return bool(self.lib.tg_layer_set_fused(self.h, int(bool(on))))
