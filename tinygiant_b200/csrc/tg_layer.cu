@@ -44,6 +44,8 @@ struct Layer {
   bool fused = true;               // use the fused step kernel when the shape allows
   bool tc = true;                  // batched steps (T > 8) on the tensor-core grouped GEMMs
   void* tc_scratch = nullptr;      // their intermediates (tc_moe_scratch_bytes)
+  float* nbuf = nullptr;           // batched routing: normalized rows [max_tokens][D]
+  uint8_t* member = nullptr;       // batched routing: [max_tokens][E] selection membership
   // tg_layer_forward's CUDA graph (copy in, step, copies out) for one
   // (rows, normalize, host staging buffers, stream)
   cudaGraphExec_t fwd_exec = nullptr;
@@ -86,6 +88,8 @@ static bool alloc_scratch(Layer* L) {
          (register_counters(L->counters, sizeof(int) * moe_counter_ints(L->max_slots, I)), true) &&
          dmalloc(L, (void**)&L->step_sync, sizeof(unsigned long long) * step_sync_words(T, E, L->top_k, I)) &&
          (register_counters(L->step_sync, sizeof(unsigned long long) * step_sync_words(T, E, L->top_k, I)), true) &&
+         (T <= 8 || (dmalloc(L, (void**)&L->nbuf, sizeof(float) * (size_t)T * D) &&
+                     dmalloc(L, (void**)&L->member, (size_t)T * E))) &&
          (!(T > 8 && tc_moe_eligible(L->gate_fmt, L->down_fmt, D, I)) ||
           dmalloc(L, &L->tc_scratch, tc_moe_scratch_bytes(L->max_rows, T, L->top_k, D, I))) &&
          dmalloc(L, (void**)&L->moe_out, sizeof(float) * 2 * (size_t)T * D) &&
@@ -188,12 +192,49 @@ static bool layer_enqueue(Layer* L, const float* x, const float* add, float* x_o
   a.sel_idx = L->sel_idx;
   a.sel_w = L->sel_w;
   a.st = status_ptr();
-  cudaError_t e = launch_layer_route(a, s);
+  cudaError_t e;
+  if (T > 8 && L->nbuf) {
+    BatchRouteArgs b{};
+    b.x_in = x;
+    b.add_in = add;
+    b.x_out = x_out;
+    b.zero_out = moe_out;
+    b.norm_w = norm_w;
+    b.eps = 1e-6f;
+    b.normalize = normalize;
+    b.router_w = L->router_w;
+    b.router_b = L->router_b;
+    b.T = T;
+    b.D = L->D;
+    b.E = L->E;
+    b.top_k = L->top_k;
+    b.I = L->I;
+    b.act = L->act;
+    b.assoc_rule = ASSOC_MOE;
+    b.bias_term = 1;
+    b.experts = L->d_experts;
+    b.xq8 = L->xq8;
+    b.nbuf = L->nbuf;
+    b.member = L->member;
+    b.logits = L->logits;
+    b.plan = L->plan;
+    b.slots = L->slots;
+    b.rows = L->rows;
+    b.wts = L->wts;
+    b.row_slot = L->row_slot;
+    b.sel_idx = L->sel_idx;
+    b.sel_w = L->sel_w;
+    e = launch_batch_route(b, s);
+    count_launches(4);
+  } else {
+    e = launch_layer_route(a, s);
+    count_launches(1);
+  }
   if (L->tc && L->tc_scratch && T > 8) {
     if (e == cudaSuccess)
       e = launch_tc_moe(L->plan, L->gate_fmt, L->down_fmt, T, L->top_k, L->D, L->I, T * L->top_k, L->xq8,
                         L->tc_scratch, moe_out, status_ptr(), s);
-    count_launches(6);
+    count_launches(5);
     if (e != cudaSuccess) {
       set_host_error(100 + (int)e, "%s: %s", what, cudaGetErrorString(e));
       return false;
@@ -207,7 +248,7 @@ static bool layer_enqueue(Layer* L, const float* x, const float* add, float* x_o
     e = launch_moe_down(L->plan, std::min(L->max_slots, T * L->top_k), T * L->top_k, L->down_fmt, L->D, L->I, T, L->hq8,
                         L->hidden,
                         moe_out, nullptr, status_ptr(), s);
-  count_launches(3);
+  count_launches(2);
   if (e != cudaSuccess) {
     set_host_error(100 + (int)e, "%s: %s", what, cudaGetErrorString(e));
     return false;

@@ -49,6 +49,34 @@ struct RouteArgs {
 
 size_t route_smem_bytes(int D, int E, int T, int K);
 
+// Routing for batched steps (tg_route.cu): the RouteArgs fields plus the
+// normalized rows and a row x expert membership matrix.
+struct BatchRouteArgs {
+  const float* x_in;
+  const float* add_in;
+  float* x_out;
+  float* zero_out;
+  const float* norm_w;
+  float eps;
+  int normalize;
+  const float* router_w;
+  const float* router_b;
+  int T, D, E, top_k, I, act, assoc_rule, bias_term;
+  const ExpertDesc* experts;
+  Q8Dev* xq8;
+  float* nbuf;            // [T][D] normalized rows
+  uint8_t* member;        // [T][E] selection rank + 1 of each active (row, expert), else 0
+  float* logits;
+  PlanHdr* plan;
+  SlotDesc* slots;
+  int* rows;
+  float* wts;
+  int* row_slot;
+  int* sel_idx;
+  float* sel_w;
+};
+cudaError_t launch_batch_route(const BatchRouteArgs& a, cudaStream_t s);
+
 // One expert's weight pointers for the fused step kernel; the row layouts
 // follow from the layer's formats and shape.  A null gate marks an expert
 // held by another GPU.

@@ -19,6 +19,7 @@
 #include "tg_moe.h"
 #include "tg_ptx.cuh"
 #include "tg_q8.cuh"
+#include "tg_warpdot.cuh"
 
 namespace tg {
 
@@ -341,6 +342,269 @@ cudaError_t launch_layer_route(const RouteArgs& a, cudaStream_t s) {
   RouteArgs args = a;
   void* kargs[] = {(void*)&args};
   return cudaLaunchKernelExC(&cfg, reinterpret_cast<const void*>(layer_route_kernel), kargs);
+}
+
+// ---------------------------------------------------------------------
+// Routing for batched steps (many rows): the same results as
+// layer_route_kernel's, in four kernels that each use the whole GPU.
+//   norm_q8_kernel   one CTA per row: x' = x + add (x_out), N = x' / rr * w,
+//                    N's Q8 blocks; the row's MoE output zeroed
+//   logits_kernel    W_r N for tiles of 8 rows x 32 experts, a fixed order over D
+//   select_kernel    one warp per row: top-k (larger logit first, NaN last, ties
+//                    to the lower id), softmax over the selected, membership
+//   plan_kernel      one CTA: per expert its active rows in row order, slots in
+//                    expert order, the plan header (engine.py:297-318)
+
+__global__ void __launch_bounds__(256) norm_q8_kernel(BatchRouteArgs a) {
+  __shared__ float red[8];
+  __shared__ float rr_s;
+  pdl_wait();
+  pdl_trigger();
+  const int t = blockIdx.x, tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+  const int D = a.D, gbpr = (D + QK - 1) / QK;
+  const float* x = a.x_in + (size_t)t * D;
+  const float* ad = a.add_in ? a.add_in + (size_t)t * D : nullptr;
+  float* n = a.nbuf + (size_t)t * D;
+  float ss = 0.f;
+  for (int i = tid; i < D; i += 256) {
+    float v = x[i];
+    if (ad) v = fadd(v, ad[i]);
+    if (a.x_out) a.x_out[(size_t)t * D + i] = v;
+    if (a.zero_out) a.zero_out[(size_t)t * D + i] = 0.f;
+    n[i] = v;
+    ss = __fmaf_rn(v, v, ss);
+  }
+  if (a.normalize) {
+    ss = warp_sum(ss);
+    if (lane == 0) red[w] = ss;
+    __syncthreads();
+    if (tid == 0) {
+      float tot = 0.f;
+      for (int j = 0; j < 8; j++) tot = fadd(tot, red[j]);
+      rr_s = __fsqrt_rn(fadd(__fdiv_rn(tot, (float)D), a.eps));
+    }
+    __syncthreads();
+    const float rr = rr_s;
+    const double yd = 1.0 / (double)rr;
+    for (int i = tid; i < D; i += 256) {
+      float v = div_rn_d(n[i], rr, yd);
+      if (a.norm_w) v = fmul(v, a.norm_w[i]);
+      n[i] = v;
+    }
+  }
+  __syncthreads();
+  for (int b = w; b < gbpr; b += 8) quantize_block_warp(n + b * QK, min(QK, D - b * QK), a.xq8 + (size_t)t * gbpr + b);
+}
+
+__global__ void __launch_bounds__(256) logits_kernel(BatchRouteArgs a) {
+  __shared__ float Ws[32][129];
+  __shared__ float Ns[8][128];
+  pdl_wait();
+  pdl_trigger();
+  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+  const int D = a.D, E = a.E, T = a.T;
+  const int t0 = blockIdx.x * 8, e0 = blockIdx.y * 32;
+  const int t = t0 + w, e = e0 + lane;
+  float acc = 0.f;
+  for (int d0 = 0; d0 < D; d0 += 128) {
+    for (int i = tid; i < 32 * 128; i += 256) {
+      const int er = i >> 7, dc = i & 127;
+      Ws[er][dc] = e0 + er < E && d0 + dc < D ? a.router_w[(size_t)(e0 + er) * D + d0 + dc] : 0.f;
+    }
+    for (int i = tid; i < 8 * 128; i += 256) {
+      const int tr = i >> 7, dc = i & 127;
+      Ns[tr][dc] = t0 + tr < T && d0 + dc < D ? a.nbuf[(size_t)(t0 + tr) * D + d0 + dc] : 0.f;
+    }
+    __syncthreads();
+    const int nd = min(128, D - d0);
+    for (int dc = 0; dc < nd; dc++) acc = __fmaf_rn(Ws[lane][dc], Ns[w][dc], acc);
+    __syncthreads();
+  }
+  if (t < T && e < E) a.logits[(size_t)t * E + e] = a.router_b ? fadd(acc, a.router_b[e]) : acc;
+}
+
+__global__ void __launch_bounds__(256) select_kernel(BatchRouteArgs a) {
+  pdl_wait();
+  pdl_trigger();
+  const int lane = threadIdx.x & 31;
+  const int t = (int)(((long)blockIdx.x * blockDim.x + threadIdx.x) >> 5);
+  const int E = a.E, K = a.top_k;
+  if (t >= a.T) return;
+  float v[8], bvs[8];
+  uint32_t key[8];
+  int id[8], bis[8];
+#pragma unroll
+  for (int i = 0; i < 8; i++) {
+    const int e = lane + 32 * i;
+    v[i] = e < E ? __ldcg(a.logits + (size_t)t * E + e) : 0.f;
+    uint32_t u = __float_as_uint(v[i]);
+    if (u == 0x80000000u) u = 0u;
+    id[i] = e;
+    key[i] = e >= E ? 0u : v[i] != v[i] ? 1u : (u >> 31) ? ~u : (u | 0x80000000u);
+    if (e < E) a.member[(size_t)t * E + e] = 0;
+  }
+  // K rounds: the warp's largest key, the lowest id among equal keys
+#pragma unroll 1
+  for (int j = 0; j < K; j++) {
+    uint32_t best = 0u;
+    int bi = 0;
+    float bv = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; i++)
+      if (key[i] > best) {
+        best = key[i];
+        bi = i;
+        bv = v[i];
+      }
+    const uint32_t M = __reduce_max_sync(0xffffffffu, best);
+    const uint32_t I = __reduce_min_sync(0xffffffffu, best == M ? (uint32_t)(lane + 32 * bi) : 0xffffffffu);
+    float sel_v = 0.f;
+    if (I == (uint32_t)(lane + 32 * bi)) {
+#pragma unroll
+      for (int i = 0; i < 8; i++)
+        if (i == bi) key[i] = 0u;
+      sel_v = bv != bv ? -INFINITY : bv;
+    }
+    bvs[j] = __shfl_sync(0xffffffffu, sel_v, (int)(I & 31));
+    bis[j] = (int)I;
+  }
+  float sum = 0.f, ex[8];
+#pragma unroll
+  for (int j = 0; j < 8; j++)
+    if (j < K) {
+      ex[j] = expf(fsub(bvs[j], bvs[0]));
+      sum = fadd(sum, ex[j]);
+    }
+  __syncwarp();
+  if (lane < K) {
+    float wt = 0.f;
+    int bi = 0;
+#pragma unroll
+    for (int j = 0; j < 8; j++)
+      if (j == lane) {
+        wt = __fdiv_rn(ex[j], sum);
+        bi = bis[j];
+      }
+    a.sel_idx[(size_t)t * K + lane] = bi;
+    a.sel_w[(size_t)t * K + lane] = wt;
+    // experts held by another GPU (no local weights) are skipped
+    if (wt != 0.f && a.experts[bi].gate.main) a.member[(size_t)t * E + bi] = (uint8_t)(lane + 1);
+  }
+}
+
+__global__ void __launch_bounds__(1024) plan_kernel(BatchRouteArgs a) {
+  __shared__ int cnt[256], off[256], slot_of[256];
+  pdl_wait();
+  pdl_trigger();
+  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+  const int E = a.E, T = a.T, K = a.top_k;
+  // rows per expert: one warp per expert, 32 rows per ballot
+  for (int e = w; e < E; e += 32) {
+    int c = 0;
+    for (int t0 = 0; t0 < T; t0 += 32) {
+      const int t = t0 + lane;
+      c += __popc(__ballot_sync(0xffffffffu, t < T && a.member[(size_t)t * E + e] != 0));
+    }
+    if (lane == 0) cnt[e] = c;
+  }
+  __syncthreads();
+  if (w == 0) {   // exclusive scans of counts and of non-empty experts
+    int bc = 0, bz = 0;
+    for (int e0 = 0; e0 < E; e0 += 32) {
+      const int e = e0 + lane;
+      const int c = e < E ? cnt[e] : 0, nz = c > 0;
+      int sc = c, sz = nz;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int a1 = __shfl_up_sync(0xffffffffu, sc, o), a2 = __shfl_up_sync(0xffffffffu, sz, o);
+        if (lane >= o) {
+          sc += a1;
+          sz += a2;
+        }
+      }
+      if (e < E) {
+        off[e] = bc + sc - c;
+        slot_of[e] = nz ? bz + sz - 1 : -1;
+      }
+      bc += __shfl_sync(0xffffffffu, sc, 31);
+      bz += __shfl_sync(0xffffffffu, sz, 31);
+    }
+    if (lane == 0) {
+      PlanHdr* h = a.plan;
+      h->n_slots = bz;
+      h->total_rows = bc;
+      h->k = T;
+      h->embed_dim = a.D;
+      h->inter_dim = a.I;
+      h->act = a.act;
+      h->assoc_rule = a.assoc_rule;
+      h->bias_term = a.bias_term;
+      h->slots = a.slots;
+      h->rows = a.rows;
+      h->wts = a.wts;
+      h->row_slot = a.row_slot;
+    }
+  }
+  __syncthreads();
+  // each expert's active rows in row order
+  for (int e = w; e < E; e += 32) {
+    const int sl = slot_of[e];
+    if (sl < 0) continue;
+    int o = off[e];
+    for (int t0 = 0; t0 < T; t0 += 32) {
+      const int t = t0 + lane;
+      const int m = t < T ? a.member[(size_t)t * E + e] : 0;
+      const unsigned bal = __ballot_sync(0xffffffffu, m != 0);
+      if (m) {
+        const int pos = o + __popc(bal & ((1u << lane) - 1u));
+        a.rows[pos] = t;
+        a.wts[pos] = a.sel_w[(size_t)t * K + (m - 1)];
+        a.row_slot[pos] = sl;
+      }
+      o += __popc(bal);
+    }
+    if (lane == 0) {
+      const ExpertDesc& X = a.experts[e];
+      SlotDesc d;
+      d.gate = X.gate;
+      d.up = X.up;
+      d.down = X.down;
+      d.gb = X.gb;
+      d.ub = X.ub;
+      d.db = X.db;
+      d.n_rows = cnt[e];
+      d.row_off = off[e];
+      d.pad[0] = e;
+      d.pad[1] = 0;
+      a.slots[sl] = d;
+    }
+  }
+}
+
+static cudaError_t launch_cfg(const void* fn, dim3 grid, dim3 block, cudaStream_t s, BatchRouteArgs* a) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  void* kargs[] = {(void*)a};
+  return cudaLaunchKernelExC(&cfg, fn, kargs);
+}
+
+cudaError_t launch_batch_route(const BatchRouteArgs& args, cudaStream_t s) {
+  if (args.top_k < 1 || args.top_k > 8 || args.top_k > args.E || args.E > 256 || args.T < 1) return cudaErrorInvalidValue;
+  BatchRouteArgs a = args;
+  cudaError_t e = launch_cfg(reinterpret_cast<const void*>(norm_q8_kernel), dim3(a.T), dim3(256), s, &a);
+  if (e == cudaSuccess)
+    e = launch_cfg(reinterpret_cast<const void*>(logits_kernel), dim3((a.T + 7) / 8, (a.E + 31) / 32), dim3(256), s, &a);
+  if (e == cudaSuccess)
+    e = launch_cfg(reinterpret_cast<const void*>(select_kernel), dim3((a.T * 32 + 255) / 256), dim3(256), s, &a);
+  if (e == cudaSuccess) e = launch_cfg(reinterpret_cast<const void*>(plan_kernel), dim3(1), dim3(1024), s, &a);
+  return e;
 }
 
 }  // namespace tg
