@@ -73,28 +73,33 @@ struct TcArgs {
   DevStatus* st;
 };
 
+constexpr int TC_MAX_BPR = 16;    // 256-value blocks per input row (K <= 4096)
+
 struct TcShared {
   uint64_t wbar, mbar;
   uint32_t tmem;
   int n_units;
   int unit_end[TC_MAX_SLOTS];   // inclusive prefix of units per slot
-  float xscale[TC_N];
-  float xbsf[TC_N][8];
+  int src[TC_N];                // the chunk's active rows' Q8 source rows
   int x4[TC_N];
+  float xscale[TC_N][TC_MAX_BPR];
+  float xbsf[TC_N][TC_MAX_BPR][8];
 };
 
+// A step is 8 MMAs (256 tensor-memory columns): Q4_K one 256-value block
+// (its 8 sub-blocks), Q6_K half a block (its 8 16-value groups of half h).
+// Steps alternate between the two 256-column buffers, so the MMAs of step
+// s + 1 run while the epilogue reads step s.
 template <int WF>
 struct TcFmt;
 template <>
 struct TcFmt<FMT_Q4K> {
-  static constexpr int NMMA = 8;           // one per 32-value sub-block
-  static constexpr int ATILES = 8;         // int8 A tiles per block
+  static constexpr int SPB = 1;            // steps per block
   static constexpr bool A_SIGNED = false;  // nibbles 0..15
 };
 template <>
 struct TcFmt<FMT_Q6K> {
-  static constexpr int NMMA = 16;          // one per 16-value group
-  static constexpr int ATILES = 16;        // each 32-value chunk twice, the other half zero
+  static constexpr int SPB = 2;
   static constexpr bool A_SIGNED = true;   // q - 32
 };
 
@@ -108,9 +113,9 @@ __global__ void __launch_bounds__(TC_WARPS * 32, 1) tc_gemm_kernel(TcArgs a) {
   const int bpr = a.K / QK;
   const RowLayout lay = row_layout(WF, a.K);
   const int tiles = (a.R + TC_M - 1) / TC_M;
-  // shared memory: A tiles [ATILES][4 KB], B tiles [8][TC_N x 32 B], raw weight window
+  // shared memory: A tiles [8][4 KB], B tiles [8][TC_N x 32 B], raw weight window
   uint8_t* At = dsm;
-  uint8_t* Bt = At + F::ATILES * 4096;
+  uint8_t* Bt = At + 8 * 4096;
   uint8_t* raw = Bt + 8 * TC_N * 32;
 
   if (wid == 0) {
@@ -142,16 +147,20 @@ __global__ void __launch_bounds__(TC_WARPS * 32, 1) tc_gemm_kernel(TcArgs a) {
     }
     if (lane == 0) sh.n_units = run;
   }
-  // the zero halves of Q6_K's A tiles never change
+  // Q6_K's A tile m holds its group's 16 values in K-half m % 2 and zeros in
+  // the other half, which never change
   if (WF == FMT_Q6K)
-    for (int i = tid; i < F::ATILES * 4096 / 16; i += TC_WARPS * 32) reinterpret_cast<uint4*>(At)[i] = make_uint4(0, 0, 0, 0);
+    for (int i = tid; i < 8 * 4096 / 16; i += TC_WARPS * 32) reinterpret_cast<uint4*>(At)[i] = make_uint4(0, 0, 0, 0);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = sh.tmem;
   const int n_units = sh.n_units;
+  const int nsteps = bpr * F::SPB;
   uint32_t wphase = 0, mphase = 0;
   bool ok = true;
+  // epilogue coordinates: TMEM lane quarter q (rows 32 q ..), active rows 8 tg ..
+  const int q = wid & 3, tg = wid >> 2, r = 32 * q + lane;
 
   for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
     int s = 0;
@@ -169,21 +178,49 @@ __global__ void __launch_bounds__(TC_WARPS * 32, 1) tc_gemm_kernel(TcArgs a) {
       mbar_arrive_expect_tx(&sh.wbar, (uint32_t)nr * lay.rs);
       bulk_g2s(raw, src, (uint32_t)nr * lay.rs, &sh.wbar);
     }
-    // per active row of the chunk: source Q8 row, association
+    // the chunk's active rows: Q8 source rows, association, and every
+    // block's scale and 32-value sums (one round trip for the unit)
     if (tid < TC_N) {
       const int j = j0 + tid;
-      sh.x4[tid] = j < S.n_rows && use_x4(ph->assoc_rule, j & ~3, S.n_rows, ph->k);
+      sh.src[tid] = tid < nt ? (MODE == 0 ? ph->rows[off + j] : off + j) : -1;
+      sh.x4[tid] = tid < nt && use_x4(ph->assoc_rule, j & ~3, S.n_rows, ph->k);
     }
+    __syncthreads();
+    for (int i = tid; i < TC_N * bpr; i += TC_WARPS * 32) {
+      const int jj = i / bpr, b = i - jj * bpr, src = sh.src[jj];
+      float sc = 0.f;
+      float bs[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      if (src >= 0) {
+        const Q8Dev& xb = a.xsrc[(size_t)src * bpr + b];
+        sc = __ldcg(&xb.scale);
+        // bsums sit at byte 264 of the 320-byte block: 8-byte aligned
+#pragma unroll
+        for (int c = 0; c < 4; c++) {
+          const int2 v = __ldcg(reinterpret_cast<const int2*>(xb.bsums) + c);
+          bs[2 * c] = (float)v.x;
+          bs[2 * c + 1] = (float)v.y;
+        }
+      }
+      sh.xscale[jj][b] = sc;
+#pragma unroll
+      for (int c = 0; c < 8; c++) sh.xbsf[jj][b][c] = bs[c];
+    }
+    // B prefetch: thread (active row jj, 16-byte piece p) of a block's 256 values
+    const int bj = tid >> 4, bp = tid & 15;
+    auto load_b = [&](int b) -> uint4 {
+      const int src = sh.src[bj];
+      return src >= 0 ? __ldcg(reinterpret_cast<const uint4*>(a.xsrc[(size_t)src * bpr + b].qs) + bp)
+                      : make_uint4(0, 0, 0, 0);
+    };
+    uint4 bnext = load_b(0);
     bool wok = mbar_wait(&sh.wbar, wphase);
     if (!wok && tid == 0) set_error(a.st, ERR_WAIT_TIMEOUT, 60, blockIdx.x, u);
     wphase ^= 1u;
-    // epilogue coordinates: TMEM lane quarter, 8 active rows
-    const int q = wid & 3, tg = wid >> 2, r = 32 * q + lane;
-    float acc[8];
-#pragma unroll
-    for (int c = 0; c < 8; c++) acc[c] = 0.f;
-    for (int b = 0; b < bpr; b++) {
-      // A: unpack block b of every row into the int8 tiles
+
+    // stage step st: A tiles from the weight window, and at a block's first
+    // step its B tiles (the prefetched values) and the next block's prefetch
+    auto stage = [&](int st) {
+      const int b = st / F::SPB, h = st - b * F::SPB;
       if constexpr (WF == FMT_Q4K) {
         // thread: row rr, 16-byte piece p of the 128 nibble bytes -> 32 values
         for (int i = tid; i < TC_M * 8; i += TC_WARPS * 32) {
@@ -199,11 +236,9 @@ __global__ void __launch_bounds__(TC_WARPS * 32, 1) tc_gemm_kernel(TcArgs a) {
           *reinterpret_cast<uint4*>(At + (2 * g + 1) * 4096 + kmaj(rr, kb)) = hi;
         }
       } else {
-        // thread: row rr, 16-value group gq (ql / qh of the reference's layout)
-        for (int i = tid; i < TC_M * 16; i += TC_WARPS * 32) {
-          const int rr = i >> 4, gq = i & 15;
-          // group gq = 16 values 16 gq .. : half h, quarter k4, l-half lq
-          const int h = gq >> 3, k4 = (gq >> 1) & 3, lq = gq & 1;
+        // thread: row rr, group (lq, k4) of half h: tile m = 2 k4 + lq, values in K-half lq
+        for (int i = tid; i < TC_M * 8; i += TC_WARPS * 32) {
+          const int rr = i >> 3, m = i & 7, k4 = m >> 1, lq = m & 1;
           uint4 v = make_uint4(0, 0, 0, 0);
           if (rr < nr) {
             const uint8_t* mb = raw + (size_t)rr * lay.rs + b * 192;
@@ -222,67 +257,60 @@ __global__ void __launch_bounds__(TC_WARPS * 32, 1) tc_gemm_kernel(TcArgs a) {
             }
             v = make_uint4(o[0], o[1], o[2], o[3]);
           }
-          // the group's values sit in value positions 16 gq .. 16 gq + 15 of
-          // the block: chunk gq / 2, half gq % 2; its A tile is 2 (gq / 2) + gq % 2
-          // with the values in that half and zeros in the other
-          const int vpos = 128 * h + 32 * k4 + 16 * lq;   // first value of the group
-          const int chunk = vpos >> 5, half = (vpos >> 4) & 1;
-          *reinterpret_cast<uint4*>(At + (2 * chunk + half) * 4096 + kmaj(rr, 16 * half)) = v;
+          *reinterpret_cast<uint4*>(At + m * 4096 + kmaj(rr, 16 * lq)) = v;
         }
       }
-      // B: the chunk's active rows' Q8 block b (qs), and their scalars
-      for (int i = tid; i < TC_N * 16; i += TC_WARPS * 32) {
-        const int jj = i >> 4, p = i & 15;
-        const int j = j0 + jj;
-        uint4 v = make_uint4(0, 0, 0, 0);
-        if (jj < nt) {
-          const int src = MODE == 0 ? ph->rows[off + j] : off + j;
-          v = __ldcg(reinterpret_cast<const uint4*>(a.xsrc[(size_t)src * bpr + b].qs) + p);
-        }
-        // 16 bytes p = values 16 p .. 16 p + 15: sub-block p / 2, half p % 2
-        *reinterpret_cast<uint4*>(Bt + (p >> 1) * (TC_N * 32) + kmaj(jj, 16 * (p & 1))) = v;
+      if (h == 0) {
+        // 16 bytes bp = values 16 bp ..: sub-block bp / 2, K-half bp % 2
+        if (bj < TC_N) *reinterpret_cast<uint4*>(Bt + (bp >> 1) * (TC_N * 32) + kmaj(bj, 16 * (bp & 1))) = bnext;
+        if (b + 1 < bpr) bnext = load_b(b + 1);
       }
-      if (tid < TC_N) {
-        const int j = j0 + tid;
-        float sc = 0.f;
-        float bs[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-        if (tid < nt) {
-          const Q8Dev& xb = a.xsrc[(size_t)(MODE == 0 ? ph->rows[off + j] : off + j) * bpr + b];
-          sc = __ldcg(&xb.scale);
+    };
+    auto issue = [&](int st) {   // one thread
+      const int h = st % F::SPB;
+      constexpr uint32_t idesc = umma_idesc(F::A_SIGNED);
+      const uint32_t tb = tmem + (uint32_t)(st & 1) * 256;
 #pragma unroll
-          for (int c = 0; c < 8; c++) bs[c] = (float)__ldcg(&xb.bsums[c]);
-        }
-        sh.xscale[tid] = sc;
-#pragma unroll
-        for (int c = 0; c < 8; c++) sh.xbsf[tid][c] = bs[c];
+      for (int m = 0; m < 8; m++) {
+        // Q4_K: sub-block m; Q6_K: group (h, lq = m % 2, k4 = m / 2) of chunk 4 h + m / 2
+        const int bt = WF == FMT_Q4K ? m : 4 * h + (m >> 1);
+        const uint64_t da = umma_desc(smem_u32(At + m * 4096)), db = umma_desc(smem_u32(Bt + bt * (TC_N * 32)));
+        asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+                     "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(tb + m * TC_N),
+                     "l"(da), "l"(db), "r"(idesc), "r"(0));
       }
-      fence_proxy_async();
-      tc_fence_before();
-      ok = __syncthreads_and(wok) != 0;   // uniform: every thread leaves together
-      tc_fence_after();
-      if (!ok) break;
-      if (tid == 0) {
-        constexpr uint32_t idesc = umma_idesc(F::A_SIGNED);
+      asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+          smem_u32(&sh.mbar)));
+    };
+
+    float acc[8], fold[8];
 #pragma unroll
-        for (int m = 0; m < F::NMMA; m++) {
-          const int bt = WF == FMT_Q4K ? m : m >> 1;   // B tile: the 32-value chunk
-          const uint64_t da = umma_desc(smem_u32(At + m * 4096)), db = umma_desc(smem_u32(Bt + bt * (TC_N * 32)));
-          asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-                       "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem + m * TC_N),
-                       "l"(da), "l"(db), "r"(idesc), "r"(0));
-        }
-        asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-            smem_u32(&sh.mbar)));
-      }
+    for (int c = 0; c < 8; c++) acc[c] = fold[c] = 0.f;
+    if (wok) stage(0);
+    fence_proxy_async();
+    tc_fence_before();
+    ok = __syncthreads_and(wok) != 0;   // uniform: every thread leaves together
+    tc_fence_after();
+    if (ok && tid == 0) issue(0);
+    for (int st = 0; st < nsteps && ok; st++) {
       const bool mok = mbar_wait(&sh.mbar, mphase);
       if (!mok && tid == 0) set_error(a.st, ERR_WAIT_TIMEOUT, 61, blockIdx.x, u);
       mphase ^= 1u;
+      tc_fence_after();
+      // MMAs of step st are done: A / B are free for step st + 1
+      if (mok && st + 1 < nsteps) stage(st + 1);
+      fence_proxy_async();
+      tc_fence_before();
       ok = __syncthreads_and(mok) != 0;
       tc_fence_after();
       if (!ok) break;
-      // epilogue: row r, active rows 8 tg .. 8 tg + 7
-      const uint32_t tl = tmem + ((uint32_t)(32 * q) << 16) + 8 * tg;
-      if constexpr (WF == FMT_Q4K) {
+      if (tid == 0 && st + 1 < nsteps) issue(st + 1);
+      // epilogue of step st (row r, active rows 8 tg .. 8 tg + 7; warps past
+      // the chunk's rows idle)
+      const int b = st / F::SPB, h = st - b * F::SPB;
+      const uint32_t tl = tmem + (uint32_t)(st & 1) * 256 + ((uint32_t)(32 * q) << 16) + 8 * tg;
+      if (8 * tg >= nt) {
+      } else if constexpr (WF == FMT_Q4K) {
         const uint4 hd = *reinterpret_cast<const uint4*>(raw + (size_t)min(r, nr - 1) * lay.rs + b * Q4K_BYTES);
         const float d = f16_fast(hd.x & 0xFFFFu), dmin = f16_fast(hd.x >> 16);
         float bsum[8];
@@ -302,7 +330,7 @@ __global__ void __launch_bounds__(TC_WARPS * 32, 1) tc_gemm_kernel(TcArgs a) {
           for (int c = 0; c < 8; c++) {
             const int jj = 8 * tg + c;
             const float flo = i2f_small((int)il[c]), fhi = i2f_small((int)ih[c]);
-            const float blo = sh.xbsf[jj][2 * g], bhi = sh.xbsf[jj][2 * g + 1];
+            const float blo = sh.xbsf[jj][b][2 * g], bhi = sh.xbsf[jj][b][2 * g + 1];
             if (sh.x4[jj]) {
               bsum[c] = fadd(bsum[c], fsub(fadd(fsub(fmul(dsl, flo), fmul(dml, blo)), fmul(dsh, fhi)), fmul(dmh, bhi)));
             } else {
@@ -312,59 +340,36 @@ __global__ void __launch_bounds__(TC_WARPS * 32, 1) tc_gemm_kernel(TcArgs a) {
           }
         }
 #pragma unroll
-        for (int c = 0; c < 8; c++) acc[c] = fadd(acc[c], fmul(sh.xscale[8 * tg + c], bsum[c]));
+        for (int c = 0; c < 8; c++) acc[c] = fadd(acc[c], fmul(sh.xscale[8 * tg + c][b], bsum[c]));
       } else {
+        // the reference's fp32 fold of the block's 16 products sc * isum16,
+        // in its order (half h, l-half lq, quarter k4); each product is an
+        // exact integer in fp32
         const uint8_t* rowp = raw + (size_t)min(r, nr - 1) * lay.rs;
         const uint4 sv = *reinterpret_cast<const uint4*>(rowp + lay.a1 + b * 16);
         const uint32_t sw[4] = {sv.x, sv.y, sv.z, sv.w};
-        const float d = f16_fast((uint32_t)rowp[lay.a2 + 2 * b] | ((uint32_t)rowp[lay.a2 + 2 * b + 1] << 8));
-        int Ssum[8], Asum[8];
 #pragma unroll
-        for (int c = 0; c < 8; c++) Ssum[c] = Asum[c] = 0;
-        // products sc * isum16 in the reference's order (half, l-half, quarter)
+        for (int lq = 0; lq < 2; lq++)
 #pragma unroll
-        for (int gq = 0; gq < 16; gq++) {
-          const int h = gq >> 3, k4 = (gq >> 1) & 3, lq = gq & 1;
-          const int vpos = 128 * h + 32 * k4 + 16 * lq, m = 2 * (vpos >> 5) + ((vpos >> 4) & 1);
-          uint32_t is[8];
-          tc_ld8(tl + m * TC_N, is);
-          tc_wait_ld();
-          const int si = 8 * h + lq + 2 * k4;
-          const int sc = sbyte(sw[si >> 2], si & 3);
+          for (int k4 = 0; k4 < 4; k4++) {
+            uint32_t is[8];
+            tc_ld8(tl + (2 * k4 + lq) * TC_N, is);
+            tc_wait_ld();
+            const int si = 8 * h + lq + 2 * k4;
+            const int sc = sbyte(sw[si >> 2], si & 3);
+#pragma unroll
+            for (int c = 0; c < 8; c++) fold[c] = fadd(fold[c], (float)(sc * (int)is[c]));
+          }
+        if (h == 1) {
+          const float d = f16_fast((uint32_t)rowp[lay.a2 + 2 * b] | ((uint32_t)rowp[lay.a2 + 2 * b + 1] << 8));
 #pragma unroll
           for (int c = 0; c < 8; c++) {
-            const int p = sc * (int)is[c];
-            Ssum[c] += p;
-            Asum[c] += abs(p);
+            acc[c] = fadd(acc[c], fmul(fmul(d, sh.xscale[8 * tg + c][b]), fold[c]));
+            fold[c] = 0.f;
           }
-        }
-#pragma unroll
-        for (int c = 0; c < 8; c++) {
-          float bs = (float)Ssum[c];
-          if (Asum[c] >= (1 << 24)) {
-            // the reference's fp32 fold of the 16 products, in order
-            bs = 0.f;
-            for (int hl = 0; hl < 4; hl++)
-              for (int k4 = 0; k4 < 4; k4++) {
-                const int h = hl >> 1, lq = hl & 1;
-                const int vpos = 128 * h + 32 * k4 + 16 * lq, m = 2 * (vpos >> 5) + ((vpos >> 4) & 1);
-                uint32_t is[8];
-                tc_ld8(tl + m * TC_N, is);
-                tc_wait_ld();
-                const int si = 8 * h + lq + 2 * k4;
-                uint32_t isc = is[0];
-#pragma unroll
-                for (int cc = 1; cc < 8; cc++)
-                  if (cc == c) isc = is[cc];
-                bs = fadd(bs, (float)(sbyte(sw[si >> 2], si & 3) * (int)isc));
-              }
-          }
-          acc[c] = fadd(acc[c], fmul(fmul(d, sh.xscale[8 * tg + c]), bs));
         }
       }
       tc_fence_before();
-      __syncthreads();   // A / B tiles and tensor memory are reused by the next block
-      tc_fence_after();
     }
     // outputs of this unit
     if (ok && r < nr) {
@@ -383,7 +388,9 @@ __global__ void __launch_bounds__(TC_WARPS * 32, 1) tc_gemm_kernel(TcArgs a) {
         }
       }
     }
-    __syncthreads();   // the weight window is reused by the next unit
+    tc_fence_before();
+    __syncthreads();   // the weight window and tensor memory are reused by the next unit
+    tc_fence_after();
   }
   pdl_trigger();
   tc_fence_before();
@@ -419,28 +426,6 @@ __global__ void act_quant_kernel(const PlanHdr* __restrict__ ph, const float* __
     }
   }
   quantize_block_warp_vals(v, n, hq8 + (size_t)row * dbpr + b);
-}
-
-// tok_rows[t][c]: token t's active rows in slot order (c < its count, the
-// rest -1): one warp per token scanning the plan's rows.
-__global__ void token_rows_kernel(const PlanHdr* __restrict__ ph, int K, int* __restrict__ tok_rows) {
-  pdl_wait();
-  pdl_trigger();
-  const int lane = threadIdx.x & 31;
-  const int t = (int)(((long)blockIdx.x * blockDim.x + threadIdx.x) >> 5);
-  if (t >= ph->k) return;
-  int c = 0;
-  for (int s0 = 0; s0 < ph->total_rows; s0 += 32) {
-    const int sr = s0 + lane;
-    const bool hit = sr < ph->total_rows && ph->rows[sr] == t;
-    const unsigned m = __ballot_sync(FULL, hit);
-    if (hit) {
-      const int pos = c + __popc(m & ((1u << lane) - 1u));
-      if (pos < K) tok_rows[(size_t)t * K + pos] = sr;
-    }
-    c += __popc(m);
-  }
-  for (int i = c + lane; i < K; i += 32) tok_rows[(size_t)t * K + i] = -1;
 }
 
 // out[t][r] += the parts of token t's active rows, in slot order.
@@ -490,20 +475,20 @@ static cudaError_t pdl_launch(const void* fn, dim3 grid, dim3 block, size_t smem
 }
 
 static size_t tc_smem(int wf, int K) {
-  const int atiles = wf == FMT_Q4K ? 8 : 16;
-  return (size_t)atiles * 4096 + 8 * TC_N * 32 + (size_t)TC_M * row_layout(wf, K).rs + 64;
+  return (size_t)8 * 4096 + 8 * TC_N * 32 + (size_t)TC_M * row_layout(wf, K).rs + 64;
 }
 
 bool tc_moe_eligible(int gate_fmt, int down_fmt, int D, int I) {
   if (gate_fmt != FMT_Q4K || (down_fmt != FMT_Q4K && down_fmt != FMT_Q6K)) return false;
-  if (D % QK || I % QK) return false;
+  if (D % QK || I % QK || D / QK > TC_MAX_BPR || I / QK > TC_MAX_BPR) return false;
   return tc_smem(gate_fmt, D) <= 220 * 1024 && tc_smem(down_fmt, I) <= 220 * 1024;
 }
 
 size_t tc_moe_scratch_bytes(int max_rows, int T, int K, int D, int I) {
+  (void)T;
+  (void)K;
   const int dbpr = I / QK;
-  return (size_t)max_rows * 2 * I * 4 + (size_t)max_rows * dbpr * sizeof(Q8Dev) + (size_t)max_rows * D * 4 +
-         (size_t)T * K * 4 + 4 * 256;
+  return (size_t)max_rows * 2 * I * 4 + (size_t)max_rows * dbpr * sizeof(Q8Dev) + (size_t)max_rows * D * 4 + 3 * 256;
 }
 
 template <int WF, int MODE>
@@ -518,7 +503,8 @@ static cudaError_t tc_launch(const TcArgs& a, cudaStream_t s) {
 }
 
 cudaError_t launch_tc_moe(const PlanHdr* ph, int gate_fmt, int down_fmt, int T, int K, int D, int I, int max_rows,
-                          const Q8Dev* xq8, void* scratch, float* out, DevStatus* st, cudaStream_t s) {
+                          const Q8Dev* xq8, const int* tok_rows, void* scratch, float* out, DevStatus* st,
+                          cudaStream_t s) {
   uint8_t* p = static_cast<uint8_t*>(scratch);
   auto take = [&](size_t n) {
     uint8_t* q = p;
@@ -528,7 +514,6 @@ cudaError_t launch_tc_moe(const PlanHdr* ph, int gate_fmt, int down_fmt, int T, 
   float* gu = reinterpret_cast<float*>(take((size_t)max_rows * 2 * I * 4));
   Q8Dev* hq8 = reinterpret_cast<Q8Dev*>(take((size_t)max_rows * (I / QK) * sizeof(Q8Dev)));
   float* parts = reinterpret_cast<float*>(take((size_t)max_rows * D * 4));
-  int* tok_rows = reinterpret_cast<int*>(take((size_t)T * K * 4));
   TcArgs g{ph, xq8, gu, D, I, 2, st};
   cudaError_t e = tc_launch<FMT_Q4K, 0>(g, s);
   if (e != cudaSuccess) return e;
@@ -549,11 +534,6 @@ cudaError_t launch_tc_moe(const PlanHdr* ph, int gate_fmt, int down_fmt, int T, 
   {
     const PlanHdr* php = ph;
     int Kv = K;
-    int* tr = tok_rows;
-    void* a3[] = {(void*)&php, (void*)&Kv, (void*)&tr};
-    e = pdl_launch(reinterpret_cast<const void*>(token_rows_kernel), dim3((unsigned)((T * 32 + 255) / 256)), dim3(256),
-                   0, s, a3);
-    if (e != cudaSuccess) return e;
     const int* trc = tok_rows;
     const float* pp = parts;
     float* op = out;

@@ -46,6 +46,8 @@ struct Layer {
   void* tc_scratch = nullptr;      // their intermediates (tc_moe_scratch_bytes)
   float* nbuf = nullptr;           // batched routing: normalized rows [max_tokens][D]
   uint8_t* member = nullptr;       // batched routing: [max_tokens][E] selection membership
+  int* tpos = nullptr;             // batched routing: [max_tokens][top_k]
+  int* tok_rows = nullptr;         // batched routing: [max_tokens][top_k] active rows per token
   // tg_layer_forward's CUDA graph (copy in, step, copies out) for one
   // (rows, normalize, host staging buffers, stream)
   cudaGraphExec_t fwd_exec = nullptr;
@@ -89,7 +91,9 @@ static bool alloc_scratch(Layer* L) {
          dmalloc(L, (void**)&L->step_sync, sizeof(unsigned long long) * step_sync_words(T, E, L->top_k, I)) &&
          (register_counters(L->step_sync, sizeof(unsigned long long) * step_sync_words(T, E, L->top_k, I)), true) &&
          (T <= 8 || (dmalloc(L, (void**)&L->nbuf, sizeof(float) * (size_t)T * D) &&
-                     dmalloc(L, (void**)&L->member, (size_t)T * E))) &&
+                     dmalloc(L, (void**)&L->member, (size_t)T * E) &&
+                     dmalloc(L, (void**)&L->tpos, sizeof(int) * (size_t)L->max_rows) &&
+                     dmalloc(L, (void**)&L->tok_rows, sizeof(int) * (size_t)L->max_rows))) &&
          (!(T > 8 && tc_moe_eligible(L->gate_fmt, L->down_fmt, D, I)) ||
           dmalloc(L, &L->tc_scratch, tc_moe_scratch_bytes(L->max_rows, T, L->top_k, D, I))) &&
          dmalloc(L, (void**)&L->moe_out, sizeof(float) * 2 * (size_t)T * D) &&
@@ -216,6 +220,8 @@ static bool layer_enqueue(Layer* L, const float* x, const float* add, float* x_o
     b.xq8 = L->xq8;
     b.nbuf = L->nbuf;
     b.member = L->member;
+    b.tpos = L->tpos;
+    b.tok_rows = L->tok_rows;
     b.logits = L->logits;
     b.plan = L->plan;
     b.slots = L->slots;
@@ -233,8 +239,8 @@ static bool layer_enqueue(Layer* L, const float* x, const float* add, float* x_o
   if (L->tc && L->tc_scratch && T > 8) {
     if (e == cudaSuccess)
       e = launch_tc_moe(L->plan, L->gate_fmt, L->down_fmt, T, L->top_k, L->D, L->I, T * L->top_k, L->xq8,
-                        L->tc_scratch, moe_out, status_ptr(), s);
-    count_launches(5);
+                        L->tok_rows, L->tc_scratch, moe_out, status_ptr(), s);
+    count_launches(4);
     if (e != cudaSuccess) {
       set_host_error(100 + (int)e, "%s: %s", what, cudaGetErrorString(e));
       return false;

@@ -66,6 +66,8 @@ struct BatchRouteArgs {
   Q8Dev* xq8;
   float* nbuf;            // [T][D] normalized rows
   uint8_t* member;        // [T][E] selection rank + 1 of each active (row, expert), else 0
+  int* tpos;              // [T][top_k] each valid selection's place among its row's, in expert order
+  int* tok_rows;          // [T][top_k] each row's active rows (plan indices) in slot order, then -1
   float* logits;
   PlanHdr* plan;
   SlotDesc* slots;
@@ -131,6 +133,7 @@ cudaError_t launch_layer_route(const RouteArgs& a, cudaStream_t s);
 bool tc_moe_eligible(int gate_fmt, int down_fmt, int D, int I);
 size_t tc_moe_scratch_bytes(int max_rows, int T, int K, int D, int I);
 cudaError_t launch_tc_moe(const PlanHdr* ph, int gate_fmt, int down_fmt, int T, int K, int D, int I, int max_rows,
-                          const Q8Dev* xq8, void* scratch, float* out, DevStatus* st, cudaStream_t s);
+                          const Q8Dev* xq8, const int* tok_rows, void* scratch, float* out, DevStatus* st,
+                          cudaStream_t s);
 
 }  // namespace tg

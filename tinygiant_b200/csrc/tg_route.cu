@@ -487,9 +487,25 @@ __global__ void __launch_bounds__(256) select_kernel(BatchRouteArgs a) {
       }
     a.sel_idx[(size_t)t * K + lane] = bi;
     a.sel_w[(size_t)t * K + lane] = wt;
-    // experts held by another GPU (no local weights) are skipped
-    if (wt != 0.f && a.experts[bi].gate.main) a.member[(size_t)t * E + bi] = (uint8_t)(lane + 1);
   }
+  // experts held by another GPU (no local weights) are skipped; a valid
+  // selection's place among the row's valid selections in expert order is
+  // where the plan puts its active row in tok_rows
+  int bi = 0;
+  float wt = 0.f;
+  if (lane < K) {
+    bi = a.sel_idx[(size_t)t * K + lane];
+    wt = a.sel_w[(size_t)t * K + lane];
+  }
+  const bool valid = lane < K && wt != 0.f && a.experts[bi].gate.main != nullptr;
+  const unsigned vm = __ballot_sync(0xffffffffu, valid);
+  int p = 0;
+  for (int q = 0; q < K; q++) p += ((vm >> q) & 1u) && __shfl_sync(0xffffffffu, bi, q) < bi;
+  if (valid) {
+    a.member[(size_t)t * E + bi] = (uint8_t)(lane + 1);
+    a.tpos[(size_t)t * K + lane] = p;
+  }
+  if (lane < K && lane >= __popc(vm)) a.tok_rows[(size_t)t * K + lane] = -1;
 }
 
 __global__ void __launch_bounds__(1024) plan_kernel(BatchRouteArgs a) {
@@ -560,6 +576,7 @@ __global__ void __launch_bounds__(1024) plan_kernel(BatchRouteArgs a) {
         a.rows[pos] = t;
         a.wts[pos] = a.sel_w[(size_t)t * K + (m - 1)];
         a.row_slot[pos] = sl;
+        a.tok_rows[(size_t)t * K + a.tpos[(size_t)t * K + (m - 1)]] = pos;
       }
       o += __popc(bal);
     }
