@@ -280,6 +280,13 @@ def run_reference(a):
     print(json.dumps(line), flush=True)
 
 
+def quiet_nccl():
+    """Keep NCCL's banner ("NCCL version ...") off stdout, which carries only the
+    JSON line; INFO / TRACE debugging still goes through."""
+    if os.environ.get("NCCL_DEBUG", "").upper() not in ("INFO", "TRACE"):
+        os.environ["NCCL_DEBUG"] = "WARN"
+
+
 # ---- our arm ---------------------------------------------------------------
 
 def run_ours(a):
@@ -297,6 +304,7 @@ def run_ours(a):
     torch.cuda.set_device(local)
     if world > 1:
         from datetime import timedelta
+        quiet_nccl()
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
     lib = tg.load()
     lib.tg_cuda_set_device(local)
@@ -469,6 +477,7 @@ def run_stack(a):
     torch.cuda.set_device(local)
     if world > 1:
         from datetime import timedelta
+        quiet_nccl()
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
     lib = tg.load()
     lib.tg_cuda_set_device(local)
