@@ -66,6 +66,8 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--parallel", default="dp", choices=["dp", "ep"])
     ap.add_argument("--layers", type=int, default=48, help="C5: layers in the stack")
+    ap.add_argument("--ep-nccl", action="store_true",
+                    help="expert parallel: sum the shards with an NCCL all-reduce instead of inside the step kernel")
     return ap.parse_args()
 
 
@@ -320,6 +322,12 @@ def run_ours(a):
     base = ResidentLayer(L, max_tokens=T, lib=lib, shard=rank if ep else 0, n_shards=world if ep else 1)
     layers = [base] + [base.clone() for _ in range(R - 1)]
     tg.check(lib)
+    # expert parallel at decode size: the shards' parts are combined inside
+    # the step kernel over NVLink (no all-reduce launch) unless --ep-nccl
+    in_kernel = ep and T <= 8 and not a.ep_nccl
+    if in_kernel:
+        for lay in layers:
+            lay.ep_connect()
 
     S = a.warmup + a.steps
     # data-parallel ranks serve different tokens; expert-parallel ranks the same ones
@@ -330,7 +338,7 @@ def run_ours(a):
     def step(i):
         lay = layers[i % R]
         lib.tg_layer_forward_dev(lay.h, xs[i].data_ptr(), None, None, out.data_ptr(), T, 1, None)
-        if ep:
+        if ep and not in_kernel:
             dist.all_reduce(out)
 
     # warm-up (also exercises every copy once)
@@ -398,7 +406,9 @@ def run_ours(a):
                 "scaling": "strong" if ep or world == 1 else "weak",
                 "vs_baseline": None, "dtype": DTYPES.get(cfg, DTYPES["c2"]),
                 "data": "synthetic (seeded weights and inputs)",
-                "config": {**workload_desc(cfg, T, R, L), "parallelism": f"ep{world}" if ep else f"dp{world}"},
+                "config": {**workload_desc(cfg, T, R, L), "parallelism": f"ep{world}" if ep else f"dp{world}",
+                           **({"ep_combine": "in the step kernel over NVLink" if in_kernel else "NCCL all-reduce"}
+                              if ep else {})},
                 "gbps": achieved, "clocks": clk, "roofline": roof, "gpu_launches": int(launches)}
 
     # e2e: one GPU through the C-ABI entry tg_layer_forward with host buffers
@@ -428,7 +438,7 @@ def run_ours(a):
             with torch.cuda.stream(stream):
                 xd.copy_(xpin[i], non_blocking=True)
                 lib.tg_layer_forward_dev(layers[i % R].h, xd.data_ptr(), None, None, out.data_ptr(), T, 1, None)
-                if ep:
+                if ep and not in_kernel:
                     dist.all_reduce(out)
                 opin.copy_(out, non_blocking=True)
             stream.synchronize()
@@ -446,7 +456,8 @@ def run_ours(a):
         tg.check(lib)
         e2e = {"value": ranks_tokens * a.steps * T / el, "unit": UNIT, "h2d_bytes_per_step": int(xs_host[0].nbytes),
                "d2h_bytes_per_step": int(opin.numel() * 4),
-               "api": "tg_layer_forward_dev per rank, pinned host copies" + (" + NCCL all-reduce" if ep else ""),
+               "api": "tg_layer_forward_dev per rank, pinned host copies" +
+                      (" + NCCL all-reduce" if ep and not in_kernel else " (shards combined in the step kernel)" if ep else ""),
                "ms_per_step": el / a.steps * 1e3}
     if rank == 0:
         line["e2e"] = e2e

@@ -194,6 +194,15 @@ int tg_layer_forward_dev(void *layer, const float *x, const float *add, float *x
  * decode-sized (T <= 8) and the formats have one; 0: three kernels (router,
  * gate/up, down).  Same results either way.  Returns the previous setting. */
 int tg_layer_set_fused(void *layer, int on);
+/* Expert parallel with the combine inside the step kernel: each shard
+ * stores its part of the output into every shard's receive block over
+ * NVLink and sums the parts of its own block in shard order, so no separate
+ * all-reduce follows the step.  tg_layer_ep_handle writes the CUDA IPC handle
+ * (64 bytes) of this shard's block; tg_layer_ep_connect takes all shards'
+ * handles in shard order.  Decode-sized steps of a connected shard return
+ * the whole layer's output.  Return 0, or -1 on error. */
+int tg_layer_ep_handle(void *layer, void *handle_out);
+int tg_layer_ep_connect(void *layer, const void *handles);
 /* 1 (default): batched steps (T > 8) run the expert GEMMs on the tensor
  * cores (tcgen05); 0: the matvec kernels.  Same results either way.  Returns
  * the previous setting. */

@@ -77,7 +77,7 @@ def test_expert_shards_sum_to_whole_gloo():
     assert q.get(timeout=5) <= TOL
 
 
-def _nccl_rank(rank, world, port, q):
+def _nccl_rank(rank, world, port, q, in_kernel=False):
     import ctypes
 
     import torch
@@ -94,13 +94,17 @@ def _nccl_rank(rank, world, port, q):
         lib.tg_cuda_set_device(rank)
         L, N = _layer(), _rows()
         shard = ResidentLayer(L, max_tokens=N.shape[0], lib=lib, shard=rank, n_shards=world)
+        if in_kernel:
+            shard.ep_connect()
         x = torch.from_numpy(N).cuda()
         out = torch.zeros_like(x)
         stream = torch.cuda.current_stream()
         lib.tg_cuda_set_stream(ctypes.c_void_p(stream.cuda_stream))
-        assert lib.tg_layer_forward_dev(shard.h, ctypes.c_void_p(x.data_ptr()), None, None,
-                                        ctypes.c_void_p(out.data_ptr()), N.shape[0], 0, None) == 0
-        dist.all_reduce(out)
+        for _ in range(3 if in_kernel else 1):   # repeated steps reuse the receive blocks (new epochs)
+            assert lib.tg_layer_forward_dev(shard.h, ctypes.c_void_p(x.data_ptr()), None, None,
+                                            ctypes.c_void_p(out.data_ptr()), N.shape[0], 0, None) == 0
+        if not in_kernel:
+            dist.all_reduce(out)
         torch.cuda.synchronize()
         tg.check(lib)
         if rank == 0:
@@ -114,7 +118,11 @@ def _nccl_rank(rank, world, port, q):
 
 
 @pytest.mark.gpu
-def test_expert_shards_nccl_two_gpus():
+@pytest.mark.parametrize("in_kernel", [False, True])
+def test_expert_shards_two_gpus(in_kernel):
+    """Two GPUs, one process each: the shards' parts summed by an NCCL
+    all-reduce, or inside the step kernel over NVLink (tg_layer_ep_connect),
+    equal the unsharded layer."""
     import torch
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
@@ -122,7 +130,7 @@ def test_expert_shards_nccl_two_gpus():
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_nccl_rank, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_nccl_rank, args=(r, 2, port, q, in_kernel)) for r in range(2)]
     for p in procs:
         p.start()
     for p in procs:

@@ -67,6 +67,8 @@ EXT = {
     "tg_layer_expert_bytes": ([VP, CI], SZ),
     "tg_layer_forward_dev": ([VP, VP, VP, VP, VP, CI, CI, VP], CI),
     "tg_layer_set_fused": ([VP, CI], CI),
+    "tg_layer_ep_handle": ([VP, VP], CI),
+    "tg_layer_ep_connect": ([VP, VP], CI),
     "tg_layer_set_tc": ([VP, CI], CI),
     "tg_layer_set_router": ([VP, VP, VP], CI),
     "tg_cuda_step_trace": ([VP], CI),

@@ -55,6 +55,14 @@ struct Layer {
   const void* fwd_hx = nullptr;
   const void* fwd_ho = nullptr;
   cudaStream_t fwd_s = nullptr;
+  // expert-parallel combine inside the step kernel: this GPU's receive block
+  // [n_shards][max_tokens][D] of tagged words, and the blocks of every shard
+  // mapped into this process (tg_layer_ep_connect)
+  int shard = 0, n_shards = 1;
+  unsigned long long* ep_recv = nullptr;
+  unsigned long long** ep_peers_d = nullptr;   // device array [n_shards]
+  std::vector<void*> ep_opened;                // peer mappings to close
+  bool ep_connected = false;
   float* moe_out = nullptr;  // [2][max_tokens][D] for stacks and the host entry
   float* xbuf = nullptr;     // [max_tokens][D]
 };
@@ -68,6 +76,12 @@ static bool dmalloc(Layer* L, void** p, size_t n) {
   }
   L->owned.push_back(*p);
   return cudaMemset(*p, 0, n) == cudaSuccess;
+}
+
+// Receive block of the in-kernel expert-parallel combine: [n_shards][T][D]
+// tagged words for up to the fused step's 8 rows.
+static size_t ep_recv_bytes(const Layer* L) {
+  return sizeof(unsigned long long) * (size_t)L->n_shards * std::min(L->max_tokens, 8) * L->D;
 }
 
 static bool alloc_scratch(Layer* L) {
@@ -96,6 +110,10 @@ static bool alloc_scratch(Layer* L) {
                      dmalloc(L, (void**)&L->tok_rows, sizeof(int) * (size_t)L->max_rows))) &&
          (!(T > 8 && tc_moe_eligible(L->gate_fmt, L->down_fmt, D, I)) ||
           dmalloc(L, &L->tc_scratch, tc_moe_scratch_bytes(L->max_rows, T, L->top_k, D, I))) &&
+         (L->n_shards == 1 ||
+          (dmalloc(L, (void**)&L->ep_recv, ep_recv_bytes(L)) &&
+           (register_counters(L->ep_recv, ep_recv_bytes(L)), true) &&
+           dmalloc(L, (void**)&L->ep_peers_d, sizeof(void*) * (size_t)L->n_shards))) &&
          dmalloc(L, (void**)&L->moe_out, sizeof(float) * 2 * (size_t)T * D) &&
          dmalloc(L, (void**)&L->xbuf, sizeof(float) * (size_t)T * D);
 }
@@ -117,6 +135,8 @@ static bool upload_tables(Layer* L) {
 
 static void free_layer(Layer* L) {
   if (L->fwd_exec) cudaGraphExecDestroy(L->fwd_exec);
+  for (void* p : L->ep_opened) cudaIpcCloseMemHandle(p);
+  if (L->ep_recv) unregister_counters(L->ep_recv);
   if (L->counters) unregister_counters(L->counters);
   if (L->step_sync) unregister_counters(L->step_sync);
   for (void* p : L->owned) cudaFree(p);
@@ -157,6 +177,12 @@ static bool layer_enqueue(Layer* L, const float* x, const float* add, float* x_o
   sl.sel_w = L->sel_w;
   sl.sync = L->step_sync;
   sl.st = status_ptr();
+  if (L->ep_connected) {
+    sl.ep_rank = L->shard;
+    sl.ep_world = L->n_shards;
+    sl.ep_peers = L->ep_peers_d;
+    sl.ep_recv = L->ep_recv;
+  }
   if (L->fused && step_eligible(sl)) {
     const cudaError_t e = launch_layer_step(sl, s);
     count_launches(1);
@@ -310,6 +336,8 @@ void* tg_layer_create_shard(int n_experts, const uint8_t* const* gate_ptrs, cons
   L->act = act == ACT_GPTOSS ? ACT_GPTOSS : ACT_SILU;
   L->top_k = top_k;
   L->max_tokens = max_tokens;
+  L->shard = shard;
+  L->n_shards = n_shards;
   L->experts.resize(n_experts);
   for (int e = 0; e < n_experts; e++) {
     ExpertDesc& X = L->experts[e];
@@ -368,6 +396,8 @@ void* tg_layer_clone(void* handle) {
   L->max_tokens = src->max_tokens;
   L->fused = src->fused;
   L->tc = src->tc;
+  L->shard = src->shard;
+  L->n_shards = src->n_shards;
   L->experts = src->experts;
   auto copy_w = [&](WDesc& w) -> bool {
     if (!w.main) return true;   // expert held by another GPU
@@ -466,6 +496,58 @@ int tg_layer_set_tc(void* handle, int on) {
   const int prev = L->tc ? 1 : 0;
   L->tc = on != 0;
   return prev;
+}
+
+// Expert-parallel combine inside the step kernel.  tg_layer_ep_handle writes
+// the CUDA IPC handle of this shard's receive block (64 bytes);
+// tg_layer_ep_connect takes every shard's handle, in shard order, and maps
+// the other shards' blocks into this process.
+int tg_layer_ep_handle(void* handle, void* out) {
+  std::lock_guard<std::recursive_mutex> lk(ctx_mutex());
+  Layer* L = static_cast<Layer*>(handle);
+  if (!L || !out || !L->ep_recv) {
+    set_host_error(3, "tg_layer_ep_handle: not an expert-parallel shard");
+    return -1;
+  }
+  cudaIpcMemHandle_t h;
+  if (cudaIpcGetMemHandle(&h, L->ep_recv) != cudaSuccess) {
+    set_host_error(100, "tg_layer_ep_handle: %s", cudaGetErrorString(cudaGetLastError()));
+    return -1;
+  }
+  memcpy(out, &h, sizeof(h));
+  return 0;
+}
+
+int tg_layer_ep_connect(void* handle, const void* handles) {
+  std::lock_guard<std::recursive_mutex> lk(ctx_mutex());
+  const char* what = "tg_layer_ep_connect";
+  Layer* L = static_cast<Layer*>(handle);
+  if (!L || !handles || !L->ep_recv || L->ep_connected) {
+    set_host_error(3, "%s: not an unconnected expert-parallel shard", what);
+    return -1;
+  }
+  std::vector<unsigned long long*> ptrs(L->n_shards);
+  for (int p = 0; p < L->n_shards; p++) {
+    if (p == L->shard) {
+      ptrs[p] = L->ep_recv;
+      continue;
+    }
+    cudaIpcMemHandle_t h;
+    memcpy(&h, static_cast<const uint8_t*>(handles) + (size_t)p * sizeof(h), sizeof(h));
+    void* dp = nullptr;
+    if (cudaIpcOpenMemHandle(&dp, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+      set_host_error(100, "%s: shard %d: %s", what, p, cudaGetErrorString(cudaGetLastError()));
+      return -1;
+    }
+    L->ep_opened.push_back(dp);
+    ptrs[p] = static_cast<unsigned long long*>(dp);
+  }
+  if (cudaMemcpy(L->ep_peers_d, ptrs.data(), sizeof(void*) * ptrs.size(), cudaMemcpyHostToDevice) != cudaSuccess) {
+    set_host_error(100, "%s: upload failed", what);
+    return -1;
+  }
+  L->ep_connected = true;
+  return 0;
 }
 
 int tg_layer_set_fused(void* handle, int on) {

@@ -118,6 +118,13 @@ struct StepLaunch {
   float* sel_w;               // [T][top_k]
   unsigned long long* sync;   // the exchange block (step_sync_words), 256-byte aligned
   DevStatus* st;
+  // expert parallel, combined inside the kernel: every GPU stores its part of
+  // the output as tagged words into slot ep_rank of every GPU's receive block
+  // [ep_world][T][D] (ep_peers: those blocks, mapped into this process) and
+  // sums the ep_world parts of its own block in rank order.  ep_world 1: off.
+  int ep_rank = 0, ep_world = 1;
+  unsigned long long* const* ep_peers = nullptr;   // device array [ep_world]
+  const unsigned long long* ep_recv = nullptr;     // this GPU's receive block
 };
 bool step_eligible(const StepLaunch& l);
 cudaError_t launch_layer_step(const StepLaunch& l, cudaStream_t s);

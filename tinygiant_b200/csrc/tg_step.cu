@@ -93,6 +93,17 @@ __device__ __forceinline__ ulonglong2 ld_tagged2(const unsigned long long* p) {
 __device__ __forceinline__ bool tag_is(unsigned long long w, uint32_t ep) { return (uint32_t)(w >> 32) == ep; }
 __device__ __forceinline__ float tag_val(unsigned long long w) { return __uint_as_float((uint32_t)w); }
 
+// System-scope forms, for words another GPU writes over NVLink.
+__device__ __forceinline__ void st_tagged_sys(unsigned long long* p, uint32_t ep, float v) {
+  const unsigned long long w = ((unsigned long long)ep << 32) | __float_as_uint(v);
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_tagged_sys(const unsigned long long* p) {
+  unsigned long long w;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+  return w;
+}
+
 // Word of hidden value r (0 .. I-1) of active row o: each 256-value block is
 // stored so that lane l's values 8l .. 8l+7 are four 16-byte pairs at
 // 64-word strides (value p = 8l + j at word 64 (j / 2) + 2l + j % 2), which
@@ -100,6 +111,44 @@ __device__ __forceinline__ float tag_val(unsigned long long w) { return __uint_a
 __device__ __forceinline__ size_t hid_word(int o, int r, int dbpr) {
   const int b = r >> 8, p = r & 255;
   return ((size_t)o * dbpr + b) * 256 + ((p & 7) >> 1) * 64 + 2 * (p >> 3) + (p & 1);
+}
+
+// The expert-parallel combine of output row r (one warp; lane t < T holds
+// token t's part): stores the part as a tagged word into slot rank of every
+// shard's receive block over NVLink, then polls this shard's block until all
+// world parts of row r carry this launch's epoch, and writes their sum in
+// shard order (the same on every shard).  Not inlined, so the step's other
+// paths keep its registers.  False after the poll limit.
+static __device__ __noinline__ bool ep_combine_row(unsigned long long* const* peers, const unsigned long long* recv,
+                                                   int rank, int world, int T, int D, int r, float v, uint32_t ep,
+                                                   float* out) {
+  const int lane = threadIdx.x & 31;
+  constexpr int EPW = 8;
+  if (lane < T)
+    for (int p = 0; p < world; p++) st_tagged_sys(peers[p] + ((size_t)rank * T + lane) * D + r, ep, v);
+  float part[EPW];
+  for (int it = 0;; it++) {
+    bool ok = true;
+    if (lane < T)
+#pragma unroll
+      for (int p = 0; p < EPW; p++) {
+        part[p] = 0.f;
+        if (p < world) {
+          const unsigned long long w = ld_tagged_sys(recv + ((size_t)p * T + lane) * D + r);
+          ok &= tag_is(w, ep);
+          part[p] = tag_val(w);
+        }
+      }
+    if (__all_sync(FULL, ok)) break;
+    if (it >= STEP_POLLS) return false;
+    __nanosleep(64);
+  }
+  float sum = 0.f;
+#pragma unroll
+  for (int p = 0; p < EPW; p++)
+    if (p < world) sum = fadd(sum, part[p]);
+  if (lane < T) out[(size_t)lane * D + r] = sum;
+  return true;
 }
 
 // Matrix descriptor of format F with `rows` rows of `cols` values at m (row
@@ -136,6 +185,9 @@ struct StepArgs {
   unsigned long long* sync;   // launch counter
   unsigned long long* lgt;    // [T][E] tagged logits
   unsigned long long* hidt;   // [T*top_k][dbpr][256] tagged hidden
+  int ep_rank, ep_world;      // expert-parallel combine in the kernel (ep_world 1: off)
+  unsigned long long* const* ep_peers;   // [ep_world] every shard's receive block
+  const unsigned long long* ep_recv;     // this shard's receive block [ep_world][T][D]
   uint32_t stage_bytes;   // ring stage size
   int nst;                // ring stages per warp
   int xcap;               // active rows whose Q8 hidden blocks fit each CTA's shared memory
@@ -791,6 +843,17 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
   const int dbpr2 = DBLK ? dbpr : 1, SL = a.sl;
   const int b_b = lane / SL, b_sl = lane - b_b * SL;
   float* accw = sh.accw[wid];   // running output of the warp's row, per token
+  // Output row r (lane t < T holds token t's value); expert parallel: this
+  // shard's part, combined across shards by ep_combine_row.
+  auto emit_row = [&](int r, float v) {
+    if (dead) return;
+    if (a.ep_world == 1) {
+      if (lane < T) a.out[(size_t)lane * D + r] = v;
+    } else if (!ep_combine_row(a.ep_peers, a.ep_recv, a.ep_rank, a.ep_world, T, D, r, v, ep, a.out)) {
+      if (lane == 0) set_error(a.st, ERR_WAIT_TIMEOUT, 38, blockIdx.x, r);
+      dead = true;
+    }
+  };
   if (n_slots > 0)
     for (int r = gw; r < D; r += NW) {
       if (lane < T) accw[lane] = 0.f;
@@ -873,12 +936,11 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
         }
         refill(stg);
       }
-      if (lane < T && !dead) a.out[(size_t)lane * D + r] = accw[lane];
+      emit_row(r, lane < T ? accw[lane] : 0.f);
       __syncwarp();
     }
-  else if (!dead)
-    for (int r = gw; r < D; r += NW)
-      if (lane < T) a.out[(size_t)lane * D + r] = 0.f;
+  else
+    for (int r = gw; r < D; r += NW) emit_row(r, 0.f);
 
   if (wid == 0) TG_MARK(8);
   if (wid == SW - 1) TG_MARK(11);
@@ -927,7 +989,8 @@ static bool step_shape(const StepLaunch& l, StepShape& sh) {
   const void* ptrs[] = {l.x_in, l.add_in, l.x_out, l.norm_w, l.router_w, l.out, l.etab, l.sync};
   for (const void* q : ptrs)
     if (reinterpret_cast<uintptr_t>(q) & 15) return false;
-  if (!l.etab || !l.sync) return false;
+  if (!l.etab || !l.sync || l.ep_world < 1 || l.ep_world > 8 || (l.ep_world > 1 && (!l.ep_peers || !l.ep_recv)))
+    return false;
   // 256-block formats put a row's blocks on consecutive lanes: at most 16
   // blocks per gate / up row (a row pair fills the warp), 32 per down row
   const bool gblk = l.gate_fmt == FMT_Q4K || l.gate_fmt == FMT_Q6K;
@@ -1052,6 +1115,10 @@ cudaError_t launch_layer_step(const StepLaunch& l, cudaStream_t s) {
   a.hidt = a.lgt + (((size_t)std::min(l.T, STEP_T_MAX) * l.E + 31) & ~(size_t)31);
   a.st = l.st;
   a.trace = g_step_trace;
+  a.ep_rank = l.ep_rank;
+  a.ep_world = l.ep_world;
+  a.ep_peers = l.ep_peers;
+  a.ep_recv = l.ep_recv;
 #define TG_STEP_CASE(GFV, DFV) \
   if (l.gate_fmt == GFV && l.down_fmt == DFV) return step_launch<GFV, DFV>(a, sh, s);
   TG_STEP_PAIRS(TG_STEP_CASE)

@@ -55,6 +55,23 @@ class ResidentLayer:
         if rc != 0:
             raise RuntimeError("tg_layer_set_router failed")
 
+    def ep_connect(self):
+        """Expert-parallel shards (one process per GPU, torch.distributed
+        initialised): exchange the shards' receive-block handles and map them,
+        so decode-sized steps combine the shards' parts inside the step kernel
+        over NVLink and return the whole layer's output on every shard."""
+        import torch.distributed as dist
+        h = ctypes.create_string_buffer(64)
+        if self.lib.tg_layer_ep_handle(self.h, h) != 0:
+            check(self.lib)
+            raise RuntimeError("tg_layer_ep_handle failed")
+        handles = [None] * self.n_shards
+        dist.all_gather_object(handles, bytes(h.raw))
+        self._ep_handles = ctypes.create_string_buffer(b"".join(handles), 64 * self.n_shards)
+        if self.lib.tg_layer_ep_connect(self.h, self._ep_handles) != 0:
+            check(self.lib)
+            raise RuntimeError("tg_layer_ep_connect failed")
+
     def set_tc(self, on=True):
         """Tensor-core grouped GEMMs (default) or matvec kernels for batched steps (T > 8)."""
         return bool(self.lib.tg_layer_set_tc(self.h, int(bool(on))))
