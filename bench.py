@@ -66,6 +66,8 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--parallel", default="dp", choices=["dp", "ep"])
     ap.add_argument("--layers", type=int, default=48, help="C5: layers in the stack")
+    ap.add_argument("--matvec", action="store_true",
+                    help="batched steps (T > 8) on the matvec kernels instead of the tcgen05 grouped GEMMs")
     ap.add_argument("--ep-nccl", action="store_true",
                     help="expert parallel: sum the shards with an NCCL all-reduce instead of inside the step kernel")
     return ap.parse_args()
@@ -321,6 +323,9 @@ def run_ours(a):
     ep = world > 1 and a.parallel == "ep"
     base = ResidentLayer(L, max_tokens=T, lib=lib, shard=rank if ep else 0, n_shards=world if ep else 1)
     layers = [base] + [base.clone() for _ in range(R - 1)]
+    if a.matvec:
+        for lay in layers:
+            lay.set_tc(False)
     tg.check(lib)
     # expert parallel at decode size: the shards' parts are combined inside
     # the step kernel over NVLink (no all-reduce launch) unless --ep-nccl
@@ -407,6 +412,8 @@ def run_ours(a):
                 "vs_baseline": None, "dtype": DTYPES.get(cfg, DTYPES["c2"]),
                 "data": "synthetic (seeded weights and inputs)",
                 "config": {**workload_desc(cfg, T, R, L), "parallelism": f"ep{world}" if ep else f"dp{world}",
+                           "expert_path": "fused step kernel" if T <= 8 else
+                                          ("matvec kernels" if a.matvec else "tcgen05 grouped GEMMs"),
                            **({"ep_combine": "in the step kernel over NVLink" if in_kernel else "NCCL all-reduce"}
                               if ep else {})},
                 "gbps": achieved, "clocks": clk, "roofline": roof, "gpu_launches": int(launches)}

@@ -168,6 +168,40 @@ def test_tensor_core_step_equals_matvec_step(gpu, qwen16_batch):
     np.testing.assert_array_equal(outs[0].view(np.uint32), outs[1].view(np.uint32))
 
 
+@pytest.fixture(scope="module")
+def gptoss_batch(gpu):
+    L = synth.gptoss_layer(seed=3, n_experts=32)
+    return L, ResidentLayer(L, max_tokens=40, lib=gpu)
+
+
+@pytest.mark.parametrize("T", [12, 40])
+def test_tensor_core_step_bit_exact_vs_reference_abi_mxfp4(gpu, gptoss_batch, T):
+    """MXFP4 (gpt-oss, D = I = 2880: the last Q8 block of a row holds two
+    live sub-blocks) on the tcgen05 grouped GEMMs: codes unpacked to int8 in
+    shared memory, one int8 MMA per 32-value sub-block; T = 12 over 32
+    experts leaves one or two active rows per expert, T = 40 up to a dozen."""
+    L, R = gptoss_batch
+    N = synth.rms_norm(np.random.default_rng(800 + T).standard_normal((T, L.embed_dim)).astype(np.float32))
+    got = R.forward(N, normalize=False)
+    idx, w = R.last_routing(T)
+    want = _abi_with_routing(gpu, L, N, idx, w)
+    np.testing.assert_array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
+def test_tensor_core_step_mxfp4_vs_oracle_and_matvec(gpu, oracle, gptoss_batch):
+    L, R = gptoss_batch
+    N = synth.rms_norm(np.random.default_rng(900).standard_normal((16, L.embed_dim)).astype(np.float32))
+    outs = []
+    for tc in (True, False):
+        R.set_tc(tc)
+        outs.append(R.forward(N, normalize=False))
+    R.set_tc(True)
+    np.testing.assert_array_equal(outs[0].view(np.uint32), outs[1].view(np.uint32))
+    idx, w = R.last_routing(16)
+    routing_agrees(L, N, idx, w)
+    assert rel_err(outs[0], M.moe_layer_forward(oracle, L, N)) <= TOL
+
+
 def test_fused_step_more_experts_than_sms(gpu, oracle):
     """200 experts: some CTAs hold two router rows."""
     L = synth.qwen_layer(seed=7, n_experts=200, D=512, I=256)

@@ -44,6 +44,7 @@ struct Layer {
   bool fused = true;               // use the fused step kernel when the shape allows
   bool tc = true;                  // batched steps (T > 8) on the tensor-core grouped GEMMs
   void* tc_scratch = nullptr;      // their intermediates (tc_moe_scratch_bytes)
+  void* tc_tmaps = nullptr;        // MXFP4 layers: TMA tensor maps [E][3] of the expert matrices
   float* nbuf = nullptr;           // batched routing: normalized rows [max_tokens][D]
   uint8_t* member = nullptr;       // batched routing: [max_tokens][E] selection membership
   int* tpos = nullptr;             // batched routing: [max_tokens][top_k]
@@ -109,7 +110,10 @@ static bool alloc_scratch(Layer* L) {
                      dmalloc(L, (void**)&L->tpos, sizeof(int) * (size_t)L->max_rows) &&
                      dmalloc(L, (void**)&L->tok_rows, sizeof(int) * (size_t)L->max_rows))) &&
          (!(T > 8 && tc_moe_eligible(L->gate_fmt, L->down_fmt, D, I)) ||
-          dmalloc(L, &L->tc_scratch, tc_moe_scratch_bytes(L->max_rows, T, L->top_k, D, I))) &&
+          (dmalloc(L, &L->tc_scratch, tc_moe_scratch_bytes(L->max_rows, T, L->top_k, D, I)) &&
+           (!(L->gate_fmt == FMT_MXFP4 || L->down_fmt == FMT_MXFP4) ||
+            (dmalloc(L, &L->tc_tmaps, tc_tmap_bytes(E)) &&
+             tc_build_tmaps(L->experts.data(), E, L->tc_tmaps) == cudaSuccess)))) &&
          (L->n_shards == 1 ||
           (dmalloc(L, (void**)&L->ep_recv, ep_recv_bytes(L)) &&
            (register_counters(L->ep_recv, ep_recv_bytes(L)), true) &&
@@ -265,7 +269,7 @@ static bool layer_enqueue(Layer* L, const float* x, const float* add, float* x_o
   if (L->tc && L->tc_scratch && T > 8) {
     if (e == cudaSuccess)
       e = launch_tc_moe(L->plan, L->gate_fmt, L->down_fmt, T, L->top_k, L->D, L->I, T * L->top_k, L->xq8,
-                        L->tok_rows, L->tc_scratch, moe_out, status_ptr(), s);
+                        L->tok_rows, L->tc_tmaps, L->tc_scratch, moe_out, status_ptr(), s);
     count_launches(4);
     if (e != cudaSuccess) {
       set_host_error(100 + (int)e, "%s: %s", what, cudaGetErrorString(e));

@@ -137,10 +137,16 @@ cudaError_t launch_layer_route(const RouteArgs& a, cudaStream_t s);
 // sub-block int32 sums), the activation and Q8 of hidden, and the ordered
 // combine into out (which the route kernel zeroed).  K: top_k; max_rows:
 // T * top_k; scratch: tc_moe_scratch_bytes of device memory.
+// MXFP4 matrices are read through TMA tensor maps, [E][3] (gate, up, down)
+// in device memory: tc_tmap_bytes(E) of them, written by tc_build_tmaps
+// from the layer's expert table (entries of absent or other-format
+// matrices are zero).
 bool tc_moe_eligible(int gate_fmt, int down_fmt, int D, int I);
 size_t tc_moe_scratch_bytes(int max_rows, int T, int K, int D, int I);
+size_t tc_tmap_bytes(int E);
+cudaError_t tc_build_tmaps(const ExpertDesc* experts, int E, void* d_tmaps);
 cudaError_t launch_tc_moe(const PlanHdr* ph, int gate_fmt, int down_fmt, int T, int K, int D, int I, int max_rows,
-                          const Q8Dev* xq8, const int* tok_rows, void* scratch, float* out, DevStatus* st,
-                          cudaStream_t s);
+                          const Q8Dev* xq8, const int* tok_rows, const void* tmaps, void* scratch, float* out,
+                          DevStatus* st, cudaStream_t s);
 
 }  // namespace tg

@@ -20,7 +20,8 @@ struct SlotDesc {
   const float* db;   // down bias [embed] or null
   int n_rows;        // active input rows of this expert
   int row_off;       // offset of this slot's rows in the flat arrays
-  int pad[2];
+  int expert;        // GPU-routed plans: the expert's index in the layer's table
+  int pad;
 };
 
 // One expert of a resident layer (the GPU router selects among these).

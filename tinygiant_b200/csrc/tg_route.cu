@@ -304,8 +304,8 @@ __global__ void __launch_bounds__(RT_THREADS) layer_route_kernel(RouteArgs a) {
     d.db = X.db;
     d.n_rows = c;
     d.row_off = o;
-    d.pad[0] = ex_i;
-    d.pad[1] = 0;
+    d.expert = ex_i;
+    d.pad = 0;
     for (int q = 0; q < T * K; q++)
       if (sidx[q] == ex_i && sw[q] != 0.f) {
         a.rows[o] = q / K;
@@ -591,8 +591,8 @@ __global__ void __launch_bounds__(1024) plan_kernel(BatchRouteArgs a) {
       d.db = X.db;
       d.n_rows = cnt[e];
       d.row_off = off[e];
-      d.pad[0] = e;
-      d.pad[1] = 0;
+      d.expert = e;
+      d.pad = 0;
       a.slots[sl] = d;
     }
   }
