@@ -87,6 +87,7 @@ struct TcArgs {
   int mats;            // matrices per slot in this pass (2: gate, up; 1: down)
   DevStatus* st;
   const CUtensorMap* tmaps;   // MXFP4: [E][3] (gate, up, down) tensor maps
+  float negz;                 // -0.0f (the packed epilogue's product addend)
 };
 
 constexpr int TC_MAX_BPR = 16;    // 256-value blocks per input row (K <= 4096)
@@ -183,6 +184,35 @@ __device__ __forceinline__ void tc_ld<8>(uint32_t taddr, uint32_t (&r)[8]) {
 template <int V>
 using IC = std::integral_constant<int, V>;
 
+// Packed pairs of fp32 operations (sm_100 f32x2): each half rounds as the
+// scalar operation does, so pairs of independent accumulators keep their
+// exact values.  a - b is a + (-b).  A packed multiply feeding a packed add
+// is fused into one fma by the assembler even with .rn, so products are
+// formed as fma(a, b, z) with z = -0 from a kernel argument (not a constant
+// the assembler could fold): exactly the rounded product, and an fma is not
+// fused again.
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+__device__ __forceinline__ float2 fmul2z(float2 a, float2 b, float2 z) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "mov.b64 rc, {%6, %7};\n\tfma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(z.x), "f"(z.y));
+  return d;
+}
+__device__ __forceinline__ float2 splat2(float v) { return make_float2(v, v); }
+// i2f_small of two integers (|v| < 2^22): exact.
+__device__ __forceinline__ float2 i2f_small2(int a, int b) {
+  return fadd2(make_float2(__int_as_float(0x4B400000 + a), __int_as_float(0x4B400000 + b)), splat2(-12582912.0f));
+}
+
 template <int WF, int MODE>   // MODE 0: gate/up; 1: down
 __global__ void __launch_bounds__(TC_WARPS * 32, 1) tc_gemm_kernel(TcArgs a) {
   using F = TcFmt<WF>;
@@ -249,6 +279,7 @@ __global__ void __launch_bounds__(TC_WARPS * 32, 1) tc_gemm_kernel(TcArgs a) {
   // epilogue coordinates: TMEM lane quarter q (weight rows 32 q ..); the
   // four warps of a quarter split the chunk's active rows
   const int q = wid & 3, tg = wid >> 2, r = 32 * q + lane;
+  const float2 nz2 = splat2(a.negz);
 
   // unit u -> (slot, matrix, 128-row tile, chunk of TC_N active rows)
   auto coords = [&](int u, int& s, int& mat, int& tile, int& ch) {
@@ -490,34 +521,79 @@ __global__ void __launch_bounds__(TC_WARPS * 32, 1) tc_gemm_kernel(TcArgs a) {
       if constexpr (WF == FMT_Q4K) {
         const uint4 hd = sh.hdr[b & 1][r];
         const float d = f16_fast(hd.x & 0xFFFFu), dmin = f16_fast(hd.x >> 16);
-        float bsum[EW];
+        if constexpr (EW >= 2) {
+          // active rows in pairs (c, c + 1) on f32x2: a pair shares its x4
+          // group (c0 + c even, chunks start at multiples of 4)
+          constexpr int P = EW / 2;
+          float2 bs2[P];
 #pragma unroll
-        for (int c = 0; c < EW; c++) bsum[c] = 0.f;
+          for (int pp = 0; pp < P; pp++) bs2[pp] = splat2(0.f);
 #pragma unroll
-        for (int g = 0; g < 4; g++) {
-          uint32_t il[EW], ih[EW];
-          tc_ld<EW>(tl + (2 * g) * TC_N, il);
-          tc_ld<EW>(tl + (2 * g + 1) * TC_N, ih);
-          tc_wait_ld();
-          int sl, ml, shh, mh;
-          q4k_pair_scales(g, hd.y, hd.z, hd.w, sl, ml, shh, mh);
-          const float dsl = fmul(d, (float)sl), dml = fmul(dmin, (float)ml);
-          const float dsh = fmul(d, (float)shh), dmh = fmul(dmin, (float)mh);
+          for (int g = 0; g < 4; g++) {
+            uint32_t il[EW], ih[EW];
+            tc_ld<EW>(tl + (2 * g) * TC_N, il);
+            tc_ld<EW>(tl + (2 * g + 1) * TC_N, ih);
+            tc_wait_ld();
+            int sl, ml, shh, mh;
+            q4k_pair_scales(g, hd.y, hd.z, hd.w, sl, ml, shh, mh);
+            const float2 dsl = splat2(fmul(d, (float)sl)), ndml = splat2(-fmul(dmin, (float)ml));
+            const float2 dsh = splat2(fmul(d, (float)shh)), ndmh = splat2(-fmul(dmin, (float)mh));
 #pragma unroll
-          for (int c = 0; c < EW; c++) {
-            const int jj = c0 + c;
-            const float flo = i2f_small((int)il[c]), fhi = i2f_small((int)ih[c]);
-            const float blo = sh.xbsf[jj][b][2 * g], bhi = sh.xbsf[jj][b][2 * g + 1];
-            if (sh.x4[jj]) {
-              bsum[c] = fadd(bsum[c], fsub(fadd(fsub(fmul(dsl, flo), fmul(dml, blo)), fmul(dsh, fhi)), fmul(dmh, bhi)));
-            } else {
-              bsum[c] = fadd(bsum[c], fsub(fmul(dsl, flo), fmul(dml, blo)));
-              bsum[c] = fadd(bsum[c], fsub(fmul(dsh, fhi), fmul(dmh, bhi)));
+            for (int pp = 0; pp < P; pp++) {
+              const int jj = c0 + 2 * pp;
+              const float2 flo = i2f_small2((int)il[2 * pp], (int)il[2 * pp + 1]);
+              const float2 fhi = i2f_small2((int)ih[2 * pp], (int)ih[2 * pp + 1]);
+              const float2 ba = *reinterpret_cast<const float2*>(&sh.xbsf[jj][b][2 * g]);
+              const float2 bb = *reinterpret_cast<const float2*>(&sh.xbsf[jj + 1][b][2 * g]);
+              const float2 blo = make_float2(ba.x, bb.x), bhi = make_float2(ba.y, bb.y);
+              if (sh.x4[jj]) {
+                float2 t = fadd2(fmul2z(dsl, flo, nz2), fmul2z(ndml, blo, nz2));
+                t = fadd2(t, fmul2z(dsh, fhi, nz2));
+                t = fadd2(t, fmul2z(ndmh, bhi, nz2));
+                bs2[pp] = fadd2(bs2[pp], t);
+              } else {
+                bs2[pp] = fadd2(bs2[pp], fadd2(fmul2z(dsl, flo, nz2), fmul2z(ndml, blo, nz2)));
+                bs2[pp] = fadd2(bs2[pp], fadd2(fmul2z(dsh, fhi, nz2), fmul2z(ndmh, bhi, nz2)));
+              }
             }
           }
-        }
 #pragma unroll
-        for (int c = 0; c < EW; c++) acc[c] = fadd(acc[c], fmul(sh.xscale[c0 + c][b], bsum[c]));
+          for (int pp = 0; pp < P; pp++) {
+            const float2 xs = make_float2(sh.xscale[c0 + 2 * pp][b], sh.xscale[c0 + 2 * pp + 1][b]);
+            const float2 v = fadd2(make_float2(acc[2 * pp], acc[2 * pp + 1]), fmul2z(xs, bs2[pp], nz2));
+            acc[2 * pp] = v.x;
+            acc[2 * pp + 1] = v.y;
+          }
+        } else {
+          float bsum[EW];
+#pragma unroll
+          for (int c = 0; c < EW; c++) bsum[c] = 0.f;
+#pragma unroll
+          for (int g = 0; g < 4; g++) {
+            uint32_t il[EW], ih[EW];
+            tc_ld<EW>(tl + (2 * g) * TC_N, il);
+            tc_ld<EW>(tl + (2 * g + 1) * TC_N, ih);
+            tc_wait_ld();
+            int sl, ml, shh, mh;
+            q4k_pair_scales(g, hd.y, hd.z, hd.w, sl, ml, shh, mh);
+            const float dsl = fmul(d, (float)sl), dml = fmul(dmin, (float)ml);
+            const float dsh = fmul(d, (float)shh), dmh = fmul(dmin, (float)mh);
+#pragma unroll
+            for (int c = 0; c < EW; c++) {
+              const int jj = c0 + c;
+              const float flo = i2f_small((int)il[c]), fhi = i2f_small((int)ih[c]);
+              const float blo = sh.xbsf[jj][b][2 * g], bhi = sh.xbsf[jj][b][2 * g + 1];
+              if (sh.x4[jj]) {
+                bsum[c] = fadd(bsum[c], fsub(fadd(fsub(fmul(dsl, flo), fmul(dml, blo)), fmul(dsh, fhi)), fmul(dmh, bhi)));
+              } else {
+                bsum[c] = fadd(bsum[c], fsub(fmul(dsl, flo), fmul(dml, blo)));
+                bsum[c] = fadd(bsum[c], fsub(fmul(dsh, fhi), fmul(dmh, bhi)));
+              }
+            }
+          }
+#pragma unroll
+          for (int c = 0; c < EW; c++) acc[c] = fadd(acc[c], fmul(sh.xscale[c0 + c][b], bsum[c]));
+        }
       } else if constexpr (WF == FMT_Q6K) {
         // the reference's fp32 fold of the block's 16 products sc * isum16,
         // in its order (half h, l-half lq, quarter k4); each product is an
@@ -576,8 +652,18 @@ __global__ void __launch_bounds__(TC_WARPS * 32, 1) tc_gemm_kernel(TcArgs a) {
           for (int m = 0; m < MB; m++) {
             if (m0 + m >= nm) break;
             const float es = e8m0_half(e8[m0 + m]);
+            if constexpr (EW >= 2) {
 #pragma unroll
-            for (int c = 0; c < EW; c++) acc[c] = fadd(acc[c], fmul(fmul(xs[c], es), i2f_small((int)is[m][c])));
+              for (int pp = 0; pp < EW / 2; pp++) {
+                const float2 t = fmul2z(fmul2z(make_float2(xs[2 * pp], xs[2 * pp + 1]), splat2(es), nz2),
+                                       i2f_small2((int)is[m][2 * pp], (int)is[m][2 * pp + 1]), nz2);
+                const float2 v = fadd2(make_float2(acc[2 * pp], acc[2 * pp + 1]), t);
+                acc[2 * pp] = v.x;
+                acc[2 * pp + 1] = v.y;
+              }
+            } else {
+              acc[0] = fadd(acc[0], fmul(fmul(xs[0], es), i2f_small((int)is[m][0])));
+            }
           }
         }
       }
@@ -819,7 +905,7 @@ cudaError_t launch_tc_moe(const PlanHdr* ph, int gate_fmt, int down_fmt, int T, 
   float* gu = reinterpret_cast<float*>(take((size_t)max_rows * 2 * I * 4));
   Q8Dev* hq8 = reinterpret_cast<Q8Dev*>(take((size_t)max_rows * dbpr * sizeof(Q8Dev)));
   float* parts = reinterpret_cast<float*>(take((size_t)max_rows * D * 4));
-  TcArgs g{ph, xq8, gu, D, I, 2, st, tm};
+  TcArgs g{ph, xq8, gu, D, I, 2, st, tm, -0.0f};
   cudaError_t e = gate_fmt == FMT_MXFP4 ? tc_launch<FMT_MXFP4, 0>(g, s) : tc_launch<FMT_Q4K, 0>(g, s);
   if (e != cudaSuccess) return e;
   {
@@ -833,7 +919,7 @@ cudaError_t launch_tc_moe(const PlanHdr* ph, int gate_fmt, int down_fmt, int T, 
                    dim3(256), 0, s, a2);
     if (e != cudaSuccess) return e;
   }
-  TcArgs dn{ph, hq8, parts, I, D, 1, st, tm};
+  TcArgs dn{ph, hq8, parts, I, D, 1, st, tm, -0.0f};
   e = down_fmt == FMT_Q6K     ? tc_launch<FMT_Q6K, 1>(dn, s)
       : down_fmt == FMT_MXFP4 ? tc_launch<FMT_MXFP4, 1>(dn, s)
                               : tc_launch<FMT_Q4K, 1>(dn, s);
