@@ -65,7 +65,8 @@ def parse():
     ap.add_argument("--copies", type=int, default=R_COPIES)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--parallel", default="dp", choices=["dp", "ep"])
-    ap.add_argument("--layers", type=int, default=48, help="C5: layers in the stack")
+    ap.add_argument("--layers", type=int, default=None,
+                    help="C4 / C5: layers in the stack (default 36 / 48; C4 with 1: one layer over HBM copies)")
     ap.add_argument("--matvec", action="store_true",
                     help="batched steps (T > 8) on the matvec kernels instead of the tcgen05 grouped GEMMs")
     ap.add_argument("--ep-nccl", action="store_true",
@@ -89,7 +90,9 @@ def workload_desc(cfg, T, R, L):
         "c2": "C2: one Qwen3-30B-A3B MoE layer (128 experts, Q4_K gate/up, Q6_K down, top-8, D=2048, I=768)",
         "c3": "C3: Qwen3-30B-A3B MoE layer with Zipf(1.1)-skewed router bias",
         "c4": "C4: gpt-oss-120b-shaped MXFP4 MoE layer (128 experts, top-4, D=I=2880)",
-        "c5": "C5: 48-layer Qwen3-30B-A3B MoE-FFN stack (C2 experts per layer, per-layer routers, residual add)",
+        "c4s": "C4: gpt-oss-120b-shaped MXFP4 MoE stack (128 experts per layer, top-4, D=I=2880, per-layer routers, "
+               "residual add)",
+        "c5": "C5: Qwen3-30B-A3B MoE-FFN stack (C2 experts per layer, per-layer routers, residual add)",
     }
     return {"workload": names[cfg], "tokens_per_step": T, "experts": L.n_experts, "top_k": L.top_k,
             "embed_dim": L.embed_dim, "inter_dim": L.inter_dim, "layer_copies": R,
@@ -120,11 +123,13 @@ def stack_routers(n_layers, E, D, seed=4):
             for l in range(n_layers)]
 
 
-def stack_bytes(L, n_layers, T):
-    """C5 per step at T = 1: every layer reads its top_k selected experts once
-    (T = 1 selects top_k distinct experts), its router and x in / out."""
-    assert T == 1, "C5 is defined at batch 1"
-    return float(n_layers * (L.top_k * L.expert_bytes(0) + L.router_w.nbytes + 2 * T * L.embed_dim * 4))
+def stack_bytes(L, n_layers, T, uniq=None):
+    """A stack step: every layer reads each distinct selected expert once
+    (T = 1 selects top_k distinct experts; for T > 1, uniq = the mean distinct
+    experts per layer, read back from the layers' routing), its router and
+    x in / out."""
+    u = L.top_k if T == 1 else uniq
+    return float(n_layers * (u * L.expert_bytes(0) + L.router_w.nbytes + 2 * T * L.embed_dim * 4))
 
 
 # ---- clocks ------------------------------------------------------------------
@@ -246,11 +251,11 @@ def run_reference(a):
     cores = os.cpu_count() or 1
     lib.tg_set_threads(cores)
     out = np.zeros_like(xs[0])
-    if cfg == "c5":
+    if is_stack(a):
         # the engine's layer loop: x += MoE_l(rmsnorm(x)) for each layer's router
         import copy
         stack = []
-        for rw in stack_routers(a.layers, L.n_experts, L.embed_dim):
+        for rw in stack_routers(n_layers(a), L.n_experts, L.embed_dim):
             Ll = copy.copy(L)
             Ll.router_w = rw
             stack.append(Ll)
@@ -275,7 +280,8 @@ def run_reference(a):
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": a.gpus, "steps": a.steps,
             "warmup": a.warmup, "ms_per_step": el / a.steps * 1e3, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": DTYPES.get(cfg, DTYPES["c2"]), "data": "synthetic",
-            "config": workload_desc(cfg, T, 1, L),
+            "config": {**workload_desc("c4s" if cfg == "c4" and is_stack(a) else cfg, T, 1, L),
+                       **({"layers": n_layers(a)} if is_stack(a) else {})},
             "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": kind,
                              "sample": f"{a.steps} steps x {T} token(s); numpy router + "
                                        f"{'csrc/libtinygiant.c (reference source, NEON via oracle/neon_shim)' if kind == 'reference' else 'oracle port'}"
@@ -479,8 +485,17 @@ def run_ours(a):
         dist.destroy_process_group()
 
 
+def is_stack(a):
+    return a.config == "c5" or (a.config == "c4" and n_layers(a) > 1)
+
+
+def n_layers(a):
+    return a.layers if a.layers is not None else {"c4": 36, "c5": 48}.get(a.config, 1)
+
+
 def run_stack(a):
-    """C5: a token through an n-layer stack (x += MoE(rmsnorm(x)) per layer) per step."""
+    """C4 / C5: T tokens through an n-layer stack (x += MoE(rmsnorm(x)) per
+    layer) per step."""
     import torch
     import torch.distributed as dist
 
@@ -501,15 +516,25 @@ def run_stack(a):
     lib.tg_cuda_set_device(local)
     stream = torch.cuda.Stream()
     lib.tg_cuda_set_stream(ctypes.c_void_p(stream.cuda_stream))
-    T, NL = 1, a.layers
+    cfg = a.config
+    T, NL = a.tokens or 1, n_layers(a)
     ep = world > 1 and a.parallel == "ep"
-    L = synth.qwen_layer(seed=1)
+    L = make_layer(cfg)
     D = L.embed_dim
     base = ResidentLayer(L, max_tokens=T, lib=lib, shard=rank if ep else 0, n_shards=world if ep else 1)
     layers = [base] + [base.clone() for _ in range(NL - 1)]
     for lay, rw in zip(layers, stack_routers(NL, L.n_experts, D)):
         lay.set_router(rw)
+    if a.matvec:
+        for lay in layers:
+            lay.set_tc(False)
     tg.check(lib)
+    # expert parallel at decode size: every layer's shards are combined inside
+    # its step kernel over NVLink, so the stack runs as on one GPU
+    in_kernel = ep and T <= 8 and not a.ep_nccl
+    if in_kernel:
+        for lay in layers:
+            lay.ep_connect()
     handles = (ctypes.c_void_p * NL)(*[lay.h for lay in layers])
     S = a.warmup + a.steps
     xs_host = step_inputs(S, T, D, seed=4 if ep or world == 1 else 4 + 1000 * rank)
@@ -517,7 +542,7 @@ def run_stack(a):
     xb = [torch.zeros((T, D), dtype=torch.float32, device=f"cuda:{local}") for _ in range(4)]
 
     def step(i):
-        if not ep:
+        if not ep or in_kernel:
             xb[0].copy_(xs[i])
             lib.tg_stack_forward_dev(handles, NL, xb[0].data_ptr(), T, None)
             return
@@ -600,27 +625,42 @@ def run_stack(a):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         el = float(t.item())
     tg.check(lib)
+    # distinct experts per layer (T > 1): from every layer's routing of the last step
+    uniq = None
+    if T > 1:
+        per = []
+        for lay in layers:
+            idx, w = lay.last_routing(T)
+            per.append(len({int(e) for e, ww in zip(idx.ravel(), w.ravel()) if ww != 0}))
+        uniq = float(np.mean(per))
     if rank == 0:
-        nbytes = stack_bytes(L, NL, T)
+        nbytes = stack_bytes(L, NL, T, uniq)
         achieved = ranks_tokens * a.steps * nbytes / (ms / 1e3) / 1e9
         peak, peak_src = measured_peak()
         peak *= world
         roof = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                 "traffic": None, "kernel": f"fused MoE layer step x {NL} layers per token",
                 "algorithmic_bytes_per_step": nbytes, "peak_source": peak_src}
-        desc = workload_desc("c5", T, 1, L)
+        desc = workload_desc("c4s" if cfg == "c4" else "c5", T, 1, L)
         desc.update({"layers": NL, "l2": f"inputs larger than L2: {NL} distinct layers resident "
-                                       f"({NL * L.n_experts * L.expert_bytes(0) / 1e9:.1f} GB of experts)",
-                     "step": "one token through the stack: per layer rmsnorm + router + top-k + experts + residual add"})
+                                       f"({NL * L.n_experts * L.expert_bytes(0) / 1e9 / (world if ep else 1):.1f} GB "
+                                       f"of experts per GPU)",
+                     "step": f"{T} token(s) through the stack: per layer rmsnorm + router + top-k + experts + "
+                             f"residual add",
+                     "expert_path": "fused step kernel" if T <= 8 else
+                                    ("matvec kernels" if a.matvec else "tcgen05 grouped GEMMs"),
+                     **({"distinct_experts_per_layer": uniq} if uniq is not None else {}),
+                     **({"ep_combine": "in the step kernel over NVLink" if in_kernel else "NCCL all-reduce"}
+                        if ep else {})})
         line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": a.steps,
                 "warmup": a.warmup, "ms_per_step": ms / a.steps, "higher_is_better": True,
                 "scaling": "strong" if ep or world == 1 else "weak", "vs_baseline": None,
-                "dtype": DTYPES["c5"], "data": "synthetic (seeded weights and inputs)",
+                "dtype": DTYPES[cfg], "data": "synthetic (seeded weights and inputs)",
                 "config": {**desc, "parallelism": f"ep{world}" if ep else f"dp{world}"},
                 "gbps": achieved, "clocks": clk, "roofline": roof, "gpu_launches": int(launches),
                 "e2e": {"value": ranks_tokens * a.steps * T / el, "unit": UNIT,
                         "h2d_bytes_per_step": int(T * D * 4), "d2h_bytes_per_step": int(T * D * 4),
-                        "api": "tg_stack_forward_dev with pinned host copies" if not ep else
+                        "api": "tg_stack_forward_dev with pinned host copies" if not ep or in_kernel else
                                "tg_layer_forward_dev per layer + NCCL all-reduce, pinned host copies",
                         "ms_per_step": el / a.steps * 1e3}}
         print(json.dumps(line), flush=True)
@@ -635,7 +675,7 @@ def main():
     a = parse()
     if a.impl == "reference":
         run_reference(a)
-    elif a.config == "c5":
+    elif is_stack(a):
         run_stack(a)
     else:
         run_ours(a)
