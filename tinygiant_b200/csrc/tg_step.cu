@@ -493,6 +493,7 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
     cas(2, 4); cas(3, 5);
     cas(1, 4); cas(3, 6);
     cas(1, 2); cas(3, 4); cas(5, 6);
+    if (t == 0) TG_MARK(22);
     for (int jj = 0; jj < (sfail ? 0 : K); jj++) {
       const uint32_t M = __reduce_max_sync(FULL, key[0]);
       const uint32_t I = __reduce_min_sync(FULL, key[0] == M ? (uint32_t)id[0] : 0xffffffffu);
@@ -509,12 +510,14 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
       }
     }
     __syncwarp();
+    if (t == 0) TG_MARK(23);
     // softmax over the selected (lane j < K takes selection j; the sum runs
     // in j order)
     const float ex = lane < K ? expf(fsub(sh.sel_v[t][lane], sh.sel_v[t][0])) : 0.f;
     float sum = 0.f;
     for (int jj = 0; jj < K; jj++) sum = fadd(sum, shfl(ex, jj));
     const float w = lane < K ? __fdiv_rn(ex, sum) : 0.f;
+    if (t == 0) TG_MARK(24);
     if (lane < K) {
       sh.sel_w[t][lane] = w;
       if (blockIdx.x == 0) {

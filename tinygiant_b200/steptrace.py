@@ -21,6 +21,10 @@ PHASES = [
     ("R2: rr, logits (CTA)", 16, 17),
     ("logits poll (w0)", 2, 9),
     ("top-k, softmax (+plan) (w0)", 9, 14),
+    ("  sort network (w0)", 9, 22),
+    ("  top-k rounds (w0)", 22, 23),
+    ("  softmax (w0)", 23, 24),
+    ("  plan T=1 (w0)", 24, 14),
     ("R3: Q8 of N (first R3 warp)", 20, 18),
     ("S / R3 CTA sync (w0)", 14, 21),
     ("plan (T>1)", 21, 4),
