@@ -439,8 +439,6 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
     const int t = wid;
     constexpr int NV = STEP_E_MAX / 32;   // logits per lane: experts lane + 32 i
     float v[NV];
-    uint32_t key[NV];
-    int id[NV];
     for (int it = 0;; it++) {
       bool ok = true;
 #pragma unroll
@@ -467,74 +465,106 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
     if (t == 0) TG_MARK(9);
     // order keys: larger logit larger key, -0 as +0, NaN (1) below every
     // number, absent (0) below NaN; equal keys go to the lower expert id
-    // (router.py:35-38, NaN last)
+    // (router.py:35-38, NaN last).  Composite c = key << 32 | (255 - id):
+    // larger c first is that order, and the logit is recovered from the key.
+    unsigned long long c[NV];
 #pragma unroll
     for (int i = 0; i < NV; i++) {
       uint32_t u = __float_as_uint(v[i]);
       if (u == 0x80000000u) u = 0u;
-      id[i] = lane + 32 * i;
-      key[i] = id[i] >= E ? 0u : v[i] != v[i] ? 1u : (u >> 31) ? ~u : (u | 0x80000000u);
+      const int e = lane + 32 * i;   // < 256
+      const uint32_t k = e >= E ? 0u : v[i] != v[i] ? 1u : (u >> 31) ? ~u : (u | 0x80000000u);
+      c[i] = ((unsigned long long)k << 32) | (uint32_t)(255 - e);
     }
-    // the lane's 8 in that order (19-comparator sorting network), then K
-    // rounds: the warp's largest head, the lowest id among equal heads, and
-    // the winner's lane steps to its next
+    // the lane's list in that order (a sorting network: 5 comparators when
+    // E <= 128 leaves 4 entries per lane, else 19), then K rounds: the
+    // warp's largest head wins and its lane steps to its next
     auto cas = [&](int x, int y) {
-      const bool sw = key[y] > key[x] || (key[y] == key[x] && id[y] < id[x]);
-      const uint32_t kx = key[x], ky = key[y];
-      const float vx = v[x], vy = v[y];
-      const int ix = id[x], iy = id[y];
-      key[x] = sw ? ky : kx; key[y] = sw ? kx : ky;
-      v[x] = sw ? vy : vx; v[y] = sw ? vx : vy;
-      id[x] = sw ? iy : ix; id[y] = sw ? ix : iy;
+      const unsigned long long cx = c[x], cy = c[y];
+      c[x] = cx > cy ? cx : cy;
+      c[y] = cx > cy ? cy : cx;
     };
-    cas(0, 2); cas(1, 3); cas(4, 6); cas(5, 7);
-    cas(0, 4); cas(1, 5); cas(2, 6); cas(3, 7);
-    cas(0, 1); cas(2, 3); cas(4, 5); cas(6, 7);
-    cas(2, 4); cas(3, 5);
-    cas(1, 4); cas(3, 6);
-    cas(1, 2); cas(3, 4); cas(5, 6);
+    const bool four = E <= 128;
+    if (four) {
+      cas(0, 1); cas(2, 3); cas(0, 2); cas(1, 3); cas(1, 2);
+    } else {
+      cas(0, 2); cas(1, 3); cas(4, 6); cas(5, 7);
+      cas(0, 4); cas(1, 5); cas(2, 6); cas(3, 7);
+      cas(0, 1); cas(2, 3); cas(4, 5); cas(6, 7);
+      cas(2, 4); cas(3, 5);
+      cas(1, 4); cas(3, 6);
+      cas(1, 2); cas(3, 4); cas(5, 6);
+    }
     if (t == 0) TG_MARK(22);
-    for (int jj = 0; jj < (sfail ? 0 : K); jj++) {
-      const uint32_t M = __reduce_max_sync(FULL, key[0]);
-      const uint32_t I = __reduce_min_sync(FULL, key[0] == M ? (uint32_t)id[0] : 0xffffffffu);
-      if ((uint32_t)id[0] == I) {
-        sh.sel_e[t][jj] = (int)I;
-        sh.sel_v[t][jj] = v[0] != v[0] ? -INFINITY : v[0];
+    // round jj's winner (key M, 255 - id L) is kept by lane jj; the rounds
+    // run branch-free (the winner's lane shifts its list by selects)
+    uint32_t myM = 0u, myL = 0u;
+    const int kk = sfail ? 0 : K;
 #pragma unroll
-        for (int i = 0; i < NV - 1; i++) {
-          key[i] = key[i + 1];
-          v[i] = v[i + 1];
-          id[i] = id[i + 1];
+    for (int jj = 0; jj < STEP_K_MAX; jj++) {
+      if (jj < kk) {
+        const uint32_t hi = (uint32_t)(c[0] >> 32);
+        const uint32_t M = __reduce_max_sync(FULL, hi);
+        const uint32_t L = __reduce_max_sync(FULL, hi == M ? (uint32_t)c[0] : 0u);
+        const bool win = hi == M && (uint32_t)c[0] == L;
+        if (lane == jj) {
+          myM = M;
+          myL = L;
         }
-        key[NV - 1] = 0u;
+        if (four) {
+          c[0] = win ? c[1] : c[0];
+          c[1] = win ? c[2] : c[1];
+          c[2] = win ? c[3] : c[2];
+          c[3] = win ? 0ull : c[3];
+        } else {
+#pragma unroll
+          for (int i = 0; i < NV - 1; i++) c[i] = win ? c[i + 1] : c[i];
+          c[NV - 1] = win ? 0ull : c[NV - 1];
+        }
       }
+    }
+    // selection lane (lane < K): expert and logit (-0 comes back as +0,
+    // which no softmax term tells apart)
+    const int my_e = 255 - (int)myL;
+    const float my_v = myM == 1u ? -INFINITY : __uint_as_float(myM >= 0x80000000u ? (myM & 0x7FFFFFFFu) : ~myM);
+    if (lane < kk) {
+      sh.sel_e[t][lane] = my_e;
+      sh.sel_v[t][lane] = my_v;
     }
     __syncwarp();
     if (t == 0) TG_MARK(23);
     // softmax over the selected (lane j < K takes selection j; the sum runs
     // in j order)
-    const float ex = lane < K ? expf(fsub(sh.sel_v[t][lane], sh.sel_v[t][0])) : 0.f;
+    const float v0 = __shfl_sync(FULL, my_v, 0);   // every lane: a full-mask shuffle
+    const float ex = lane < K ? expf(fsub(my_v, v0)) : 0.f;
+    // the K shuffles are independent: issue them together, then the ordered sum
+    float exs[STEP_K_MAX];
+#pragma unroll
+    for (int jj = 0; jj < STEP_K_MAX; jj++) exs[jj] = shfl(ex, jj);
     float sum = 0.f;
-    for (int jj = 0; jj < K; jj++) sum = fadd(sum, shfl(ex, jj));
+#pragma unroll
+    for (int jj = 0; jj < STEP_K_MAX; jj++)
+      if (jj < K) sum = fadd(sum, exs[jj]);
     const float w = lane < K ? __fdiv_rn(ex, sum) : 0.f;
     if (t == 0) TG_MARK(24);
-    if (lane < K) {
+    if (lane < kk) {   // (no selection after a failed poll: the step returns below)
       sh.sel_w[t][lane] = w;
       if (blockIdx.x == 0) {
-        a.sel_idx[t * K + lane] = sh.sel_e[t][lane];
+        a.sel_idx[t * K + lane] = my_e;
         a.sel_w[t * K + lane] = w;
       }
     }
     if (T == 1) {
       // one token: its selected experts (nonzero weight, local) ascending by
       // id are the slots, one active row each
-      const int e = lane < K ? sh.sel_e[0][lane] : 0x7fffffff;
-      const bool valid = lane < K && w != 0.f && etab[lane < K ? e : 0].g != nullptr;
+      const int e = lane < kk ? my_e : 0x7fffffff;
+      const bool valid = lane < kk && w != 0.f && etab[lane < kk ? e : 0].g != nullptr;
       const unsigned vm = __ballot_sync(FULL, valid);
       int rank = 0;
-      for (int q = 0; q < K; q++) {
+#pragma unroll
+      for (int q = 0; q < STEP_K_MAX; q++) {
         const int eq = __shfl_sync(FULL, e, q);
-        rank += ((vm >> q) & 1u) && eq < e;
+        rank += q < K && ((vm >> q) & 1u) && eq < e;
       }
       if (valid) {
         sh.slot_e[rank] = e;
