@@ -408,7 +408,11 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
     const int t = i % T, r = i / T - 1;
     float ss = 0.f;
     for (int b = 0; b < gbpr; b++) ss = fadd(ss, sh.part_ss[t][b]);
-    const float rr = a.normalize ? __fsqrt_rn(fadd(__fdiv_rn(ss, (float)D), a.eps)) : 1.f;
+    // ss / D: for D a power of two the product with 2^-k, which rounds the
+    // same real number once, so it equals the division
+    const float msq = (D & (D - 1)) == 0 ? fmul(ss, __int_as_float((128 - __ffs(D)) << 23))   // 2^-log2(D)
+                                         : __fdiv_rn(ss, (float)D);
+    const float rr = a.normalize ? __fsqrt_rn(fadd(msq, a.eps)) : 1.f;
     if (r < 0) {
       sh.rrt[t] = rr;
       sh.yd[t] = 1.0 / (double)rr;
