@@ -585,14 +585,16 @@ int tg_layer_forward(void* handle, const float* x_host, float* out_host, int T, 
   }
   const size_t n = sizeof(float) * (size_t)T * L->D;
   float* hx = (float*)pinned_up(n);
-  float* ho = (float*)pinned_down(n);
+  float* ho = deliver_reserve((size_t)T * L->D);   // mapped: the device writes it
   if (!hx || !ho) return -1;
   cudaStream_t s = stream();
   memcpy(hx, x_host, n);
   float* moe = L->moe_out;
-  // The step's device work — the copy of x in, the step, the copies of its
-  // output and of the device status out — is one CUDA graph per (rows,
-  // normalize, staging buffers, stream), captured on first use and replayed.
+  // The step's device work — the copy of x in, the step, and the delivery of
+  // its output and of the device status into mapped host memory — is one
+  // CUDA graph per (rows, normalize, staging buffers, stream), captured on
+  // first use and replayed; the host then waits on the delivery's echo
+  // instead of synchronising the stream.
   const bool same = L->fwd_exec && L->fwd_T == T && L->fwd_norm == normalize && L->fwd_hx == hx &&
                     L->fwd_ho == ho && L->fwd_s == s;
   if (!same && s != nullptr && s != cudaStreamLegacy && s != cudaStreamPerThread) {
@@ -603,7 +605,7 @@ int tg_layer_forward(void* handle, const float* x_host, float* out_host, int T, 
     if (ok) {
       ok = cudaMemcpyAsync(L->xbuf, hx, n, cudaMemcpyHostToDevice, s) == cudaSuccess &&
            layer_enqueue(L, L->xbuf, nullptr, nullptr, moe, T, normalize, nullptr, s, what) &&
-           cudaMemcpyAsync(ho, moe, n, cudaMemcpyDeviceToHost, s) == cudaSuccess && status_copy_async(s, what);
+           deliver_async(moe, (size_t)T * L->D, s, what);
       ok = cudaStreamEndCapture(s, &graph) == cudaSuccess && ok;
     }
     if (ok) ok = cudaGraphInstantiate(&L->fwd_exec, graph, 0) == cudaSuccess;
@@ -622,17 +624,19 @@ int tg_layer_forward(void* handle, const float* x_host, float* out_host, int T, 
   }
   if (L->fwd_exec && L->fwd_T == T && L->fwd_norm == normalize && L->fwd_hx == hx && L->fwd_ho == ho &&
       L->fwd_s == s) {
+    deliver_begin();
     if (cudaGraphLaunch(L->fwd_exec, s) != cudaSuccess) {
       set_host_error(100, "%s: graph launch failed", what);
       return -1;
     }
     count_launches(1);
-    if (!finish_copied(what)) return -1;
+    if (!finish_delivered(what)) return -1;
   } else {
+    deliver_begin();
     if (cudaMemcpyAsync(L->xbuf, hx, n, cudaMemcpyHostToDevice, s) != cudaSuccess) return -1;
     if (!layer_enqueue(L, L->xbuf, nullptr, nullptr, moe, T, normalize, nullptr, s, what)) return -1;
-    if (cudaMemcpyAsync(ho, moe, n, cudaMemcpyDeviceToHost, s) != cudaSuccess) return -1;
-    if (!finish(what)) return -1;
+    if (!deliver_async(moe, (size_t)T * L->D, s, what)) return -1;
+    if (!finish_delivered(what)) return -1;
   }
   for (size_t i = 0; i < (size_t)T * L->D; i++) out_host[i] += ho[i];
   return 0;

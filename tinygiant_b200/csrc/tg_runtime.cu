@@ -12,6 +12,7 @@
 
 #include <algorithm>
 #include <atomic>
+#include <chrono>
 #include <cstdarg>
 #include <cstdio>
 #include <cstdlib>
@@ -94,6 +95,38 @@ struct PinBuf {
   }
 };
 
+// Pinned host memory mapped into the device's address space.
+struct MapBuf {
+  void* h = nullptr;
+  void* d = nullptr;
+  size_t n = 0;
+  bool reserve(size_t need) {
+    if (need <= n) return true;
+    size_t cap = std::max(need, n * 2);
+    cap = (cap + 4095) & ~(size_t)4095;
+    if (h) cudaFreeHost(h);
+    h = d = nullptr;
+    n = 0;
+    if (!cuda_ok(cudaHostAlloc(&h, cap, cudaHostAllocMapped | cudaHostAllocPortable), "cudaHostAlloc(result)") ||
+        !cuda_ok(cudaHostGetDevicePointer(&d, h, 0), "cudaHostGetDevicePointer(result)"))
+      return false;
+    memset(h, 0, cap);
+    n = cap;
+    return true;
+  }
+};
+
+// The head of the mapped result block: the request number the host set
+// before launching, echoed by the device after the result and the status
+// record are written.
+struct RetHdr {
+  unsigned int req;
+  unsigned int done;
+  unsigned int pad[2];
+  DevStatus st;
+};
+constexpr size_t RET_DATA = 64;   // the floats start here (16-byte aligned)
+
 // ---------------------------------------------------------------------
 // Context.
 
@@ -109,6 +142,8 @@ struct Ctx {
   DevStatus* h_status = nullptr;  // pinned
   DevBuf d_stage, d_xq8, d_hidden, d_hq8, d_tmp, d_counters, d_parts;
   PinBuf h_up, h_down;
+  MapBuf h_ret;                   // deliver_async's result block
+  unsigned int ret_seq = 0;
   int threads = 1;
 };
 
@@ -204,6 +239,86 @@ bool finish_copied(const char* what) {
 // Synchronises the stream and turns a device-side error record into a host error.
 bool finish(const char* what) {
   return status_copy_async(stream(), what) && finish_copied(what);
+}
+
+// ---------------------------------------------------------------------
+// Results without a stream synchronisation: one CTA copies n floats and the
+// status record into the mapped result block, then, after a system-scope
+// fence, echoes the host's request number; the host spins on that word.
+
+__global__ void deliver_kernel(const float* __restrict__ src, size_t n, const DevStatus* __restrict__ st,
+                               RetHdr* hdr, float* out) {
+  __shared__ unsigned int req;
+  if (threadIdx.x == 0) req = *reinterpret_cast<volatile unsigned int*>(&hdr->req);
+  const size_t n4 = n / 4;
+  for (size_t i = threadIdx.x; i < n4; i += blockDim.x)
+    reinterpret_cast<float4*>(out)[i] = __ldcg(reinterpret_cast<const float4*>(src) + i);
+  for (size_t i = n4 * 4 + threadIdx.x; i < n; i += blockDim.x) out[i] = __ldcg(src + i);
+  if (threadIdx.x == 0) {
+    volatile DevStatus* hs = &hdr->st;
+    hs->code = st->code;
+    hs->where = st->where;
+    hs->a = st->a;
+    hs->b = st->b;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    *reinterpret_cast<volatile unsigned int*>(&hdr->done) = req;
+  }
+}
+
+float* deliver_reserve(size_t n_floats) {
+  if (!g.h_ret.reserve(RET_DATA + sizeof(float) * n_floats)) return nullptr;
+  return reinterpret_cast<float*>(static_cast<uint8_t*>(g.h_ret.h) + RET_DATA);
+}
+
+bool deliver_async(const float* d_src, size_t n_floats, cudaStream_t s, const char* what) {
+  if (!g.h_ret.reserve(RET_DATA + sizeof(float) * n_floats)) return false;
+  RetHdr* hdr = static_cast<RetHdr*>(g.h_ret.d);
+  float* out = reinterpret_cast<float*>(static_cast<uint8_t*>(g.h_ret.d) + RET_DATA);
+  deliver_kernel<<<1, 512, 0, s>>>(d_src, n_floats, g.d_status, hdr, out);
+  count_launches(1);
+  return cuda_ok(cudaGetLastError(), what);
+}
+
+// Sets the next request number; call before launching the work that ends
+// with deliver_async.
+void deliver_begin() {
+  RetHdr* hdr = static_cast<RetHdr*>(g.h_ret.h);
+  __atomic_store_n(&hdr->req, ++g.ret_seq, __ATOMIC_RELEASE);
+}
+
+// Waits (spinning, bounded) until the device has echoed the request, then
+// turns a device-side error record into a host error as finish_copied does.
+// If the echo does not come (a failed launch or kernel), the stream is
+// synchronised to report the CUDA error.
+bool finish_delivered(const char* what) {
+  RetHdr* hdr = static_cast<RetHdr*>(g.h_ret.h);
+  const unsigned int want = g.ret_seq;
+  const auto t0 = std::chrono::steady_clock::now();
+  int spins = 0;
+  while (__atomic_load_n(&hdr->done, __ATOMIC_ACQUIRE) != want) {
+    if (++spins % 4096 == 0 && std::chrono::steady_clock::now() - t0 > std::chrono::seconds(10)) {
+      cudaStreamSynchronize(stream());
+      if (__atomic_load_n(&hdr->done, __ATOMIC_ACQUIRE) == want) break;
+      const cudaError_t e = cudaGetLastError();
+      set_host_error(100 + (int)e, "%s: the result was not delivered (%s)", what, cudaGetErrorString(e));
+      return false;
+    }
+  }
+  if (hdr->st.code != 0) {
+    const DevStatus st{hdr->st.code, hdr->st.where, hdr->st.a, hdr->st.b};
+    cudaStream_t s = stream();
+    cudaMemsetAsync(g.d_status, 0, sizeof(DevStatus), s);
+    if (g.d_counters.p) cudaMemsetAsync(g.d_counters.p, 0, g.d_counters.n, s);
+    for (auto& c : g_counter_bufs) cudaMemsetAsync(c.first, 0, c.second, s);
+    cudaStreamSynchronize(s);
+    hdr->st.code = 0;
+    set_host_error(200 + st.code, "%s: device error %d at site %d (%d, %d)", what, st.code, st.where, st.a, st.b);
+    return false;
+  }
+  return true;
 }
 
 // ---------------------------------------------------------------------
@@ -483,10 +598,13 @@ bool run_moe(std::vector<HostSlot>& slots, int gate_fmt, int act, int rule, int 
       return false;
   if (parts && !cuda_ok(launch_combine_parts(dph, D, k, parts, d_out, s), what)) return false;
   g_launches += 2 + (int)dfmts.size() + (parts ? 1 : 0);
-  if (!cuda_ok(cudaMemcpyAsync(g.h_down.p, d_out, sizeof(float) * (size_t)k * D, cudaMemcpyDeviceToHost, s), what))
-    return false;
-  if (!finish(what)) return false;
-  memcpy(output, g.h_down.p, sizeof(float) * (size_t)k * D);
+  // the output and the status record come back through the mapped result
+  // block; the host waits on its echo instead of synchronising the stream
+  const float* ho = deliver_reserve((size_t)k * D);
+  if (!ho) return false;
+  deliver_begin();
+  if (!deliver_async(d_out, (size_t)k * D, s, what) || !finish_delivered(what)) return false;
+  memcpy(output, ho, sizeof(float) * (size_t)k * D);
   return true;
 }
 

@@ -23,6 +23,15 @@ void count_launches(int n);
 void* pinned_up(size_t n);
 void* pinned_down(size_t n);
 void register_counters(void* p, size_t n);
+// Small results to the host without a stream synchronisation (mapped pinned
+// memory and a request number echoed by the device): deliver_reserve sizes
+// the block and returns the host copy of the floats; deliver_async enqueues
+// the copy (capturable); deliver_begin sets the request before a launch;
+// finish_delivered waits for it and checks the device status.
+float* deliver_reserve(size_t n_floats);
+bool deliver_async(const float* d_src, size_t n_floats, cudaStream_t s, const char* what);
+void deliver_begin();
+bool finish_delivered(const char* what);
 void unregister_counters(void* p);
 
 }  // namespace tg
