@@ -480,7 +480,7 @@ __device__ __forceinline__ float q4k_block_term(const uint8_t* blk, const XQ& xb
   const uint4 h = ld16(blk);
   const float d = f16_fast(h.x & 0xFFFFu), dmin = f16_fast(h.x >> 16);
   float bs = 0.f;
-#pragma unroll 1
+#pragma unroll 2
   for (int g = 0; g < 4; g++) {
     const uint4 q0 = ld16(blk + 16 + 32 * g), q1 = ld16(blk + 32 + 32 * g);
     const uint4 xa = ld16(xb.qs + 64 * g), xe = ld16(xb.qs + 64 * g + 16);
@@ -560,7 +560,7 @@ __device__ __forceinline__ float q6k_block_term(const uint8_t* mb, const uint8_t
                                                 const XQ& xb) {
   const uint4 sv = ld16(scb);
   int S = 0, A = 0;
-#pragma unroll 1
+#pragma unroll 2
   for (int hl = 0; hl < 4; hl++) {
     const int h = hl >> 1, lq = hl & 1;
     const uint4 va = ld16(mb + 64 * h + 16 * lq), vb = ld16(mb + 64 * h + 32 + 16 * lq);
