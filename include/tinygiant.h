@@ -75,7 +75,13 @@ void tg_prefetch_batch(const void **addrs, const size_t *lens, int count);
 int tg_mlock(const void *addr, size_t len);
 
 /* Generic attention decode step: any weight format per projection,
- * optional biases, QK norm, sinks and sliding window (libtinygiant.c:939-983). */
+ * optional biases, QK norm, sinks and sliding window (libtinygiant.c:939-983).
+ * These three run on the GPU.  kv_k / kv_v ([n_kv_heads][kv_max][head_dim]
+ * host floats) get a device mirror per pointer: positions below kv_len it
+ * has not seen are uploaded, and the new row is written to both.  A caller
+ * that writes a cache itself (or frees one and reuses its address) calls
+ * tg_cuda_unregister(kv_ptr) first.  head_dim even and <= 256;
+ * n_heads a multiple of n_kv_heads; kv_len < kv_max. */
 void tg_attention_v2(int fmt_q, int fmt_k, int fmt_v, int fmt_o, const void *wq, const void *wk,
                      const void *wv, const void *wo, const float *bq, const float *bk, const float *bv,
                      const float *bo, const float *q_norm_w, const float *k_norm_w, const float *sinks,
@@ -123,7 +129,7 @@ void tg_moe_forward(const uint8_t **expert_ptrs, const float *weights, int n_exp
                     float *output, int embed_dim, int inter_dim);
 
 /* Whole decoder layer with fp32 attention and pre-routed experts
- * (libtinygiant.c:1467-1507). */
+ * (libtinygiant.c:1467-1507).  Not built on the GPU: records error 5. */
 void tg_transformer_layer(const float *wq, const float *wk, const float *wv, const float *wo,
                           const float *attn_norm_w, const float *q_norm_w, const float *k_norm_w,
                           const float *ffn_norm_w, float *kv_k, float *kv_v, int kv_len, int kv_max,

@@ -666,6 +666,7 @@ int tg_cuda_register(const void* host_ptr, size_t nbytes) {
 
 int tg_cuda_unregister(const void* host_ptr) {
   std::lock_guard<std::recursive_mutex> lk(g.mu);
+  kv_mirror_forget(host_ptr);
   int n = (int)g_ranges.erase((uintptr_t)host_ptr);
   for (auto it = g_mats.begin(); it != g_mats.end();) {
     if (std::get<0>(it->first) == (uintptr_t)host_ptr) {
@@ -681,6 +682,7 @@ int tg_cuda_unregister(const void* host_ptr) {
 void tg_cuda_registry_clear(void) {
   std::lock_guard<std::recursive_mutex> lk(g.mu);
   if (g.inited) cudaStreamSynchronize(stream());
+  kv_mirror_clear();
   g_mats.clear();
   g_ranges.clear();
   g_slab.clear();

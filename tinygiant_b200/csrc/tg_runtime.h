@@ -33,5 +33,8 @@ bool deliver_async(const float* d_src, size_t n_floats, cudaStream_t s, const ch
 void deliver_begin();
 bool finish_delivered(const char* what);
 void unregister_counters(void* p);
+// Attention decode's KV-cache mirrors (tg_attention.cu), dropped with the registry.
+void kv_mirror_forget(const void* host);
+void kv_mirror_clear();
 
 }  // namespace tg
