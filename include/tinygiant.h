@@ -129,7 +129,8 @@ void tg_moe_forward(const uint8_t **expert_ptrs, const float *weights, int n_exp
                     float *output, int embed_dim, int inter_dim);
 
 /* Whole decoder layer with fp32 attention and pre-routed experts
- * (libtinygiant.c:1467-1507).  Not built on the GPU: records error 5. */
+ * (libtinygiant.c:1467-1507), built on the GPU entries above; x changes only
+ * if every step succeeded. */
 void tg_transformer_layer(const float *wq, const float *wk, const float *wv, const float *wo,
                           const float *attn_norm_w, const float *q_norm_w, const float *k_norm_w,
                           const float *ffn_norm_w, float *kv_k, float *kv_v, int kv_len, int kv_max,

@@ -24,7 +24,8 @@ def ref():
     if not O.REF_SO.exists():
         pytest.skip("oracle/_ref/libtinygiant_ref.so not built")
     lib = ctypes.CDLL(str(O.REF_SO))
-    for name in ("tg_attention_v2", "tg_attention_decode", "tg_attention_decode_q4", "tg_set_threads"):
+    for name in ("tg_attention_v2", "tg_attention_decode", "tg_attention_decode_q4", "tg_transformer_layer",
+                 "tg_set_threads"):
         fn = getattr(lib, name)
         fn.argtypes, fn.restype = ABI[name] if name in ABI else ([ctypes.c_int], None)
     lib.tg_set_threads(4)
@@ -139,6 +140,44 @@ def test_attention_decode_q4_matches_reference(gpu, ref):
                                    p(sin), p(x), p(out), D, H, KH, HD, pos)
 
     run_sequence(gpu, ref, call, steps=8, seed=2)
+
+
+def test_transformer_layer_matches_reference(gpu, ref):
+    """x += attention(rms_norm(x)); x += sum_e w_e expert_e(rms_norm(x)), the
+    experts pre-routed (Q4_K gate/up, Q4_K or F16 down), over 4 positions."""
+    rng = np.random.default_rng(31)
+    I = 256
+    wq, wk, wv, wo = (weights(rng, None, H * HD, D), weights(rng, None, KH * HD, D), weights(rng, None, KH * HD, D),
+                      weights(rng, None, D, H * HD))
+    an, fn = [(1.0 + 0.1 * rng.standard_normal(D)).astype(np.float32) for _ in range(2)]
+    qn, kn = [(1.0 + 0.1 * rng.standard_normal(HD)).astype(np.float32) for _ in range(2)]
+    cos, sin = rope_tables()
+    f16 = [0, 1, 0]
+    gates = [weights(rng, Q.FMT_Q4K, I, D) for _ in f16]
+    ups = [weights(rng, Q.FMT_Q4K, I, D) for _ in f16]
+    downs = [weights(rng, Q.FMT_F16 if f else Q.FMT_Q4K, D, I) for f in f16]
+    VPA = ctypes.c_void_p * len(f16)
+    gp, up_, dp = VPA(*[p(a) for a in gates]), VPA(*[p(a) for a in ups]), VPA(*[p(a) for a in downs])
+    isf = (ctypes.c_int * len(f16))(*f16)
+    ew = np.array([0.5, 0.3, 0.2], np.float32)
+    caches = {n: (np.zeros((KH, KV_MAX, HD), np.float32), np.zeros((KH, KV_MAX, HD), np.float32))
+              for n in ("ref", "gpu")}
+    for c in caches["gpu"]:
+        gpu.tg_cuda_unregister(p(c))
+    for pos in range(4):
+        x0 = rng.standard_normal(D).astype(np.float32)
+        xs = {}
+        for name, lib in (("ref", ref), ("gpu", gpu)):
+            x = x0.copy()
+            lib.tg_transformer_layer(p(wq), p(wk), p(wv), p(wo), p(an), p(qn), p(kn), p(fn), p(caches[name][0]),
+                                     p(caches[name][1]), pos, KV_MAX, p(cos), p(sin), ctypes.addressof(gp),
+                                     ctypes.addressof(up_), ctypes.addressof(dp), ctypes.addressof(isf), p(ew),
+                                     len(f16), p(x), D, I, H, KH, HD, pos)
+            xs[name] = x
+        msg = ctypes.create_string_buffer(512)
+        assert gpu.tg_cuda_last_error(msg, 512) == 0, msg.value
+        assert rel_err(xs["gpu"], xs["ref"]) <= TOL, pos
+        assert rel_err(caches["gpu"][0][:, pos], caches["ref"][0][:, pos]) <= TOL
 
 
 def test_attention_rejects_bad_shapes(gpu):

@@ -1,7 +1,7 @@
 // tg_attention.cu — the reference ABI's attention decode steps on the GPU
 // (csrc/libtinygiant.c:723-815 tg_attention_decode, 939-983 tg_attention_v2,
-// 985-1036 tg_attention_decode_q4), and the whole-layer entry, which is not
-// built (it records an error).
+// 985-1036 tg_attention_decode_q4), and the whole-layer entry built on them
+// (1467-1507 tg_transformer_layer).
 //
 // One decode step for one token:
 //   q, k, v = Wq x (+bq), Wk x (+bk), Wv x (+bv)   weights in any format, the
@@ -27,6 +27,7 @@
 #include <cmath>
 #include <cstring>
 #include <map>
+#include <vector>
 
 #include "../../include/tinygiant.h"
 #include "tg_kernels.h"
@@ -411,11 +412,40 @@ void tg_attention_v2(int fmt_q, int fmt_k, int fmt_v, int fmt_o, const void* wq,
                  n_heads, n_kv_heads, head_dim, pos, eps);
 }
 
-void tg_transformer_layer(const float*, const float*, const float*, const float*, const float*, const float*,
-                          const float*, const float*, float*, float*, int, int, const float*, const float*,
-                          const uint8_t**, const uint8_t**, const void**, const int*, const float*, int, float*, int,
-                          int, int, int, int, int) {
-  tg::set_host_error(5, "tg_transformer_layer is not implemented on the GPU in this build");
+// One decoder layer for one token (libtinygiant.c:1467-1507): x += attention
+// (rms_norm(x)), then x += the pre-routed experts' weighted outputs on
+// rms_norm(x), through the GPU entries above and tg_expert_forward_mixed.
+// x changes only if every step succeeded.
+void tg_transformer_layer(const float* wq, const float* wk, const float* wv, const float* wo,
+                          const float* attn_norm_w, const float* q_norm_w, const float* k_norm_w,
+                          const float* ffn_norm_w, float* kv_k, float* kv_v, int kv_len, int kv_max,
+                          const float* rope_cos, const float* rope_sin, const uint8_t** gate_ptrs,
+                          const uint8_t** up_ptrs, const void** down_ptrs, const int* down_is_f16,
+                          const float* expert_weights, int n_active, float* x, int embed_dim, int inter_dim,
+                          int n_heads, int n_kv_heads, int head_dim, int pos) {
+  std::lock_guard<std::recursive_mutex> lk(ctx_mutex());
+  const char* what = "tg_transformer_layer";
+  if (!x || embed_dim <= 0 || n_active < 0 || (n_active > 0 && (!gate_ptrs || !up_ptrs || !down_ptrs ||
+                                                                 !down_is_f16 || !expert_weights))) {
+    set_host_error(3, "%s: bad arguments", what);
+    return;
+  }
+  const unsigned seq0 = host_error_seq();
+  std::vector<float> xl(x, x + embed_dim), normed(embed_dim), part(embed_dim), moe(embed_dim, 0.f);
+  tg_rms_norm(xl.data(), attn_norm_w, normed.data(), embed_dim, 1e-6f);
+  if (host_error_seq() != seq0) return;
+  tg_attention_decode(wq, wk, wv, wo, q_norm_w, k_norm_w, kv_k, kv_v, kv_len, kv_max, rope_cos, rope_sin,
+                      normed.data(), part.data(), embed_dim, n_heads, n_kv_heads, head_dim, pos);
+  if (host_error_seq() != seq0) return;
+  for (int i = 0; i < embed_dim; i++) xl[i] += part[i];
+  tg_rms_norm(xl.data(), ffn_norm_w, normed.data(), embed_dim, 1e-6f);
+  if (host_error_seq() != seq0) return;
+  for (int e = 0; e < n_active; e++) {
+    tg_expert_forward_mixed(gate_ptrs[e], up_ptrs[e], down_ptrs[e], down_is_f16[e], normed.data(), moe.data(),
+                            expert_weights[e], embed_dim, inter_dim);
+    if (host_error_seq() != seq0) return;
+  }
+  for (int i = 0; i < embed_dim; i++) x[i] = xl[i] + moe[i];
 }
 
 }  // extern "C"

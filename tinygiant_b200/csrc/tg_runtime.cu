@@ -35,7 +35,13 @@ namespace tg {
 
 static std::mutex g_err_mu;
 static int g_err_code = 0;
+static unsigned g_err_seq = 0;   // errors recorded so far
 static std::string g_err_msg;
+
+unsigned host_error_seq() {
+  std::lock_guard<std::mutex> lk(g_err_mu);
+  return g_err_seq;
+}
 
 void set_host_error(int code, const char* fmt, ...) {
   char buf[512];
@@ -47,6 +53,7 @@ void set_host_error(int code, const char* fmt, ...) {
     std::lock_guard<std::mutex> lk(g_err_mu);
     g_err_code = code;
     g_err_msg = buf;
+    g_err_seq++;
   }
   fprintf(stderr, "libtinygiant(cuda): %s\n", buf);
   if (getenv("TG_CUDA_ABORT_ON_ERROR")) abort();

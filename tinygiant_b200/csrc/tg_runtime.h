@@ -9,6 +9,8 @@
 namespace tg {
 
 void set_host_error(int code, const char* fmt, ...);
+// Count of errors recorded so far (a call failed if it changed).
+unsigned host_error_seq();
 bool ensure_init();
 cudaStream_t stream();
 bool finish(const char* what);
