@@ -528,12 +528,21 @@ __global__ void __launch_bounds__(TC_WARPS * 32, 1) tc_gemm_kernel(TcArgs a) {
           float2 bs2[P];
 #pragma unroll
           for (int pp = 0; pp < P; pp++) bs2[pp] = splat2(0.f);
+          // two sub-block pairs' sums in flight per wait
 #pragma unroll
-          for (int g = 0; g < 4; g++) {
-            uint32_t il[EW], ih[EW];
-            tc_ld<EW>(tl + (2 * g) * TC_N, il);
-            tc_ld<EW>(tl + (2 * g + 1) * TC_N, ih);
-            tc_wait_ld();
+          for (int g2 = 0; g2 < 4; g2 += 2) {
+          uint32_t il2[2][EW], ih2[2][EW];
+#pragma unroll
+          for (int gg = 0; gg < 2; gg++) {
+            tc_ld<EW>(tl + (2 * (g2 + gg)) * TC_N, il2[gg]);
+            tc_ld<EW>(tl + (2 * (g2 + gg) + 1) * TC_N, ih2[gg]);
+          }
+          tc_wait_ld();
+#pragma unroll
+          for (int gg = 0; gg < 2; gg++) {
+            const int g = g2 + gg;
+            const uint32_t (&il)[EW] = il2[gg];
+            const uint32_t (&ih)[EW] = ih2[gg];
             int sl, ml, shh, mh;
             q4k_pair_scales(g, hd.y, hd.z, hd.w, sl, ml, shh, mh);
             const float2 dsl = splat2(fmul(d, (float)sl)), ndml = splat2(-fmul(dmin, (float)ml));
@@ -556,6 +565,7 @@ __global__ void __launch_bounds__(TC_WARPS * 32, 1) tc_gemm_kernel(TcArgs a) {
                 bs2[pp] = fadd2(bs2[pp], fadd2(fmul2z(dsh, fhi, nz2), fmul2z(ndmh, bhi, nz2)));
               }
             }
+          }
           }
 #pragma unroll
           for (int pp = 0; pp < P; pp++) {
