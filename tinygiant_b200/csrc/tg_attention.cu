@@ -304,7 +304,7 @@ static bool attention_step(const char* what, int fq, int fk, int fv, int fo, con
                o_a = take(4 * fa), o_o = take(4 * fo_), o_s = take(4 * fsc), o_xq = take(sizeof(Q8Dev) * nbx),
                o_aq = take(sizeof(Q8Dev) * nba);
   float* hin = (float*)pinned_up(4 * (fx + fr));
-  float* hout = (float*)pinned_down(4 * fo_);
+  const float* hout = deliver_reserve(fo_);   // mapped: output and the new K / V rows
   if (!hin || !hout || !g_att.reserve(off, what)) return false;
   uint8_t* b = (uint8_t*)g_att.p;
   float *x = (float*)(b + o_x), *rr = x + fx, *q = (float*)(b + o_q), *k = (float*)(b + o_k), *v = (float*)(b + o_v),
@@ -349,11 +349,16 @@ static bool attention_step(const char* what, int fq, int fk, int fv, int fo, con
     count_launches(1);
   }
   ok = ok && proj(Wo, fo, aq, att, dbo, ob);
-  if (!ok || cudaMemcpyAsync(hout, ob, 4 * fo_, cudaMemcpyDeviceToHost, s) != cudaSuccess) {
+  if (ok) {
+    deliver_begin();
+    ok = deliver_async(ob, fo_, s, what);
+  }
+  if (!ok) {
     set_host_error(100, "%s: launch failed (%s)", what, cudaGetErrorString(cudaGetLastError()));
+    cudaStreamSynchronize(s);
     return false;
   }
-  if (!finish(what)) return false;
+  if (!finish_delivered(what)) return false;
   mk->valid = mv->valid = std::max(mk->valid, kv_len + 1);
   memcpy(output, hout, 4 * (size_t)D);
   for (int h = 0; h < KH; h++) {
