@@ -221,13 +221,13 @@ static struct {
   size_t n = 0;
   bool reserve(size_t need, const char* what) {
     if (need <= n) return true;
+    const size_t cap = (std::max(need, 2 * n) + 4095) & ~(size_t)4095;
     if (p) {
       cudaStreamSynchronize(stream());
       cudaFree(p);
     }
     p = nullptr;
     n = 0;
-    const size_t cap = (std::max(need, 2 * n) + 4095) & ~(size_t)4095;
     if (cudaMalloc(&p, cap) != cudaSuccess) {
       set_host_error(100, "%s: cudaMalloc(%zu) failed", what, cap);
       return false;
