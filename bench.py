@@ -60,7 +60,9 @@ def parse():
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--config", default="c2", choices=["c2", "c3", "c4", "c5"])
+    ap.add_argument("--config", default="c2", choices=["c2", "c3", "c4", "c5", "attn", "cache"],
+                    help="c2-c5: the MoE workloads; attn: one attention decode step (tg_attention_v2); "
+                         "cache: an expert-cache directory loaded into HBM")
     ap.add_argument("--tokens", type=int, default=None)
     ap.add_argument("--copies", type=int, default=R_COPIES)
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -671,8 +673,156 @@ def run_stack(a):
         dist.destroy_process_group()
 
 
+# ---- around the path: attention decode and expert-cache loading ----------------
+
+def run_attn(a):
+    """One Qwen3-30B-A3B-shaped attention decode step (D 2048, 32 query / 4 KV
+    heads of 128, Q4_K q/k/o, Q6_K v, QK norm) per token through the C-ABI
+    tg_attention_v2 with host buffers, the context starting at --tokens
+    positions (default 1024) and growing by one per call; beside it the
+    reference's own C (oracle/_ref) on the same inputs, all host threads."""
+    import torch  # noqa: F401  (CUDA context first)
+
+    import tinygiant_b200 as tg
+    from oracle import oracle as O
+    from tinygiant_b200 import quants as Q
+    from tinygiant_b200._lib import ABI
+
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    D, H, KH, HD, KV_MAX = 2048, 32, 4, 128, 4096
+    L0 = a.tokens or 1024
+    rng = np.random.default_rng([9, 1])
+    mats = {"q": (Q.FMT_Q4K, H * HD, D), "k": (Q.FMT_Q4K, KH * HD, D), "v": (Q.FMT_Q6K, KH * HD, D),
+            "o": (Q.FMT_Q4K, D, H * HD)}
+    W = {}
+    for k, (f, r, c) in mats.items():
+        w = (rng.standard_normal((r, c)) * 0.02).astype(np.float32)
+        W[k] = Q.pack_q4k(w) if f == Q.FMT_Q4K else Q.pack_q6k(w)
+    qn, kn = [(1.0 + 0.1 * rng.standard_normal(HD)).astype(np.float32) for _ in range(2)]
+    half = HD // 2
+    ang = np.arange(KV_MAX)[:, None] * (1.0 / (1e6 ** (np.arange(half) * 2.0 / HD)))[None, :]
+    cos, sin = np.cos(ang).astype(np.float32), np.sin(ang).astype(np.float32)
+    kv0 = [(rng.standard_normal((KH, KV_MAX, HD)) * 0.5).astype(np.float32) for _ in range(2)]
+    n_calls = a.warmup + a.steps
+    xs = rng.standard_normal((n_calls, D)).astype(np.float32)
+
+    def p(x):
+        return None if x is None else x.ctypes.data
+
+    def call(lib, kv, pos, x, out):
+        lib.tg_attention_v2(mats["q"][0], mats["k"][0], mats["v"][0], mats["o"][0], p(W["q"]), p(W["k"]), p(W["v"]),
+                            p(W["o"]), None, None, None, None, p(qn), p(kn), None, p(kv[0]), p(kv[1]), pos, KV_MAX, 0,
+                            p(cos), p(sin), p(x), p(out), D, H, KH, HD, pos, 1e-6)
+
+    lib = tg.load()
+    ours_kv = [k.copy() for k in kv0]
+    out = np.zeros(D, np.float32)
+    for i in range(a.warmup):
+        call(lib, ours_kv, L0 + i, xs[i], out)
+    tg.check(lib)
+    t0 = time.perf_counter()
+    for i in range(a.warmup, n_calls):
+        call(lib, ours_kv, L0 + i, xs[i], out)
+    el = time.perf_counter() - t0
+    tg.check(lib)
+    ours_last = out.copy()
+
+    # the reference's C on the same sequence (a bounded sample), and the
+    # parity of the last step
+    ref = ctypes.CDLL(str(O.REF_SO)) if O.REF_SO.exists() else None
+    cpu = None
+    err = None
+    if ref is not None:
+        ref.tg_attention_v2.argtypes, ref.tg_attention_v2.restype = ABI["tg_attention_v2"]
+        ref.tg_set_threads.argtypes = [ctypes.c_int]
+        cores = os.cpu_count() or 1
+        ref.tg_set_threads(cores)
+        ref_kv = [k.copy() for k in kv0]
+        rout = np.zeros(D, np.float32)
+        n, t1 = 0, time.perf_counter()
+        for i in range(n_calls):
+            call(ref, ref_kv, L0 + i, xs[i], rout)
+            n += 1
+            if i >= a.warmup and time.perf_counter() - t1 > 20.0:
+                break
+        rel = time.perf_counter() - t1
+        if n == n_calls:
+            err = float(np.max(np.abs(ours_last - rout)) / max(float(np.max(np.abs(rout))), 1e-30))
+        cpu = {"value": n / rel, "unit": "tok/s", "cores": cores, "kind": "reference",
+               "sample": f"{n} steps from context {L0}; csrc/libtinygiant.c tg_attention_v2 (NEON via oracle/neon_shim)"}
+    wbytes = sum(w.nbytes for w in W.values())
+    kvb = lambda pos: 2 * KH * (pos + 1) * HD * 4
+    nbytes = float(np.mean([wbytes + kvb(L0 + i) for i in range(a.warmup, n_calls)]))
+    ms = el / a.steps * 1e3
+    peak, peak_src = measured_peak()
+    achieved = nbytes / (ms / 1e3) / 1e9
+    line = {"metric": "attention decode step tok/s (one layer)", "value": a.steps / el, "unit": "tok/s",
+            "n_gpus": 1, "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "int8xQ4_K/Q6_K projections, fp32 attention",
+            "data": "synthetic (seeded weights, KV cache and inputs)",
+            "config": {"workload": "Qwen3-30B-A3B attention decode: D 2048, 32 q / 4 kv heads x 128, Q4_K q/k/o, "
+                                   "Q6_K v, QK norm, RoPE", "context_start": L0, "kv_max": KV_MAX,
+                       "api": "tg_attention_v2 (C ABI, host buffers; the KV cache is the caller's host array, "
+                              "mirrored in HBM)"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                         "traffic": None, "algorithmic_bytes_per_step": nbytes, "peak_source": peak_src},
+            "e2e": {"value": a.steps / el, "unit": "tok/s", "h2d_bytes_per_step": int(D * 4 + HD * 4),
+                    "d2h_bytes_per_step": int(D * 4 + 2 * KH * HD * 4), "ms_per_step": ms},
+            "cpu_baseline": cpu, "parity_last_step_rel_err": err}
+    print(json.dumps(line), flush=True)
+
+
+def run_cache(a):
+    """--layers C2-shaped layers (default 2) written as an expert-cache
+    directory (the relayout format), then mapped and made resident in HBM:
+    GB/s of expert bytes from the (warm) page cache into HBM, and the first
+    layer's output checked against the same layer built in memory."""
+    import tempfile
+
+    import torch  # noqa: F401
+
+    import tinygiant_b200 as tg
+    from tinygiant_b200 import expert_cache, synth
+    from tinygiant_b200.layer import ResidentLayer
+
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    n = a.layers or 2
+    lib = tg.load()
+    layers = [synth.qwen_layer(seed=1, layer=l) for l in range(n)]
+    with tempfile.TemporaryDirectory() as d:
+        expert_cache.write_cache(d, layers)
+        t0 = time.perf_counter()
+        got = expert_cache.stack_from_cache(d, [L.router_w for L in layers])
+        res = [ResidentLayer(G, max_tokens=1, lib=lib) for G in got]
+        lib.tg_cuda_synchronize()
+        el = time.perf_counter() - t0
+        tg.check(lib)
+        nbytes = float(sum(G.n_experts * G.expert_bytes(0) for G in got))
+        x = np.random.default_rng(3).standard_normal((1, layers[0].embed_dim)).astype(np.float32)
+        mem = ResidentLayer(layers[0], max_tokens=1, lib=lib)
+        same = bool(np.array_equal(res[0].forward(x).view(np.uint32), mem.forward(x).view(np.uint32)))
+        for r in res + [mem]:
+            r.close()
+    line = {"metric": "expert-cache load into HBM GB/s", "value": nbytes / el / 1e9, "unit": "GB/s", "n_gpus": 1,
+            "steps": 1, "warmup": 0, "ms_per_step": el * 1e3, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "raw GGUF blocks (Q4_K, Q6_K)", "data": "synthetic C2 layers written as "
+            "layer_NNN.q4.bin + index.json in a temporary directory (warm page cache)",
+            "config": {"workload": f"{n} Qwen3-30B-A3B MoE layers, 128 experts each", "bytes": nbytes,
+                       "api": "tinygiant_b200.expert_cache.stack_from_cache + ResidentLayer"},
+            "first_layer_bit_identical": same}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     a = parse()
+    if a.config == "attn":
+        run_attn(a)
+        return
+    if a.config == "cache":
+        run_cache(a)
+        return
     if a.impl == "reference":
         run_reference(a)
     elif is_stack(a):

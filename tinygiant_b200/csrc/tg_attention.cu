@@ -112,46 +112,84 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_prep_kernel(float* q, float*
 }
 
 // Block h: query head h against KV head h / gqa over positions [start,
-// seq_len); scores in sc[h][.] (global scratch, kv_max per head).
+// seq_len); scores in sc[h][.] (global scratch, kv_max per head).  A thread
+// per position for the scores (float4 rows when head_dim % 4 == 0); for the
+// weighted sum of v, warp w takes positions w, w + nw, ..., its lanes the
+// dimensions, and the warps' partial sums add up in shared memory.
 __global__ void __launch_bounds__(ATT_THREADS) attn_heads_kernel(const float* q, const float* kv_k, const float* kv_v,
                                                                  int kv_max, int hd, int gqa, int start, int seq_len,
                                                                  float inv_sqrt, const float* sinks, float* sc,
                                                                  float* out) {
-  __shared__ float qs[ATT_MAX_HD];
+  __shared__ __align__(16) float qs[ATT_MAX_HD];
   __shared__ float red[ATT_THREADS / 32];
+  __shared__ float part[ATT_THREADS / 32][ATT_MAX_HD];
   const int h = blockIdx.x, t = threadIdx.x, lane = t & 31, w = t >> 5, nw = blockDim.x >> 5;
   const int kvh = h / gqa, n = seq_len - start;
-  const float* kc = kv_k + (size_t)kvh * kv_max * hd;
-  const float* vc = kv_v + (size_t)kvh * kv_max * hd;
+  const float* kc = kv_k + ((size_t)kvh * kv_max + start) * hd;
+  const float* vc = kv_v + ((size_t)kvh * kv_max + start) * hd;
   float* s = sc + (size_t)h * kv_max;
   for (int d = t; d < hd; d += blockDim.x) qs[d] = q[(size_t)h * hd + d];
   __syncthreads();
   float m = sinks ? sinks[h] : -1e30f;
-  for (int i = w; i < n; i += nw) {   // a warp per position
-    const float* kt = kc + (size_t)(start + i) * hd;
-    float dot = 0.f;
-    for (int d = lane; d < hd; d += 32) dot += qs[d] * kt[d];
-    for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
-    const float v = dot * inv_sqrt;
-    if (lane == 0) s[i] = v;
-    m = fmaxf(m, v);
+  if ((hd & 3) == 0) {
+    const float4* q4 = reinterpret_cast<const float4*>(qs);
+    for (int i = t; i < n; i += blockDim.x) {
+      const float4* kt = reinterpret_cast<const float4*>(kc + (size_t)i * hd);
+      float dot = 0.f;
+      for (int d4 = 0; d4 < hd / 4; d4++) {
+        const float4 kv = __ldg(kt + d4), qv = q4[d4];
+        dot += qv.x * kv.x + qv.y * kv.y + qv.z * kv.z + qv.w * kv.w;
+      }
+      const float v = dot * inv_sqrt;
+      s[i] = v;
+      m = fmaxf(m, v);
+    }
+  } else {
+    for (int i = t; i < n; i += blockDim.x) {
+      const float* kt = kc + (size_t)i * hd;
+      float dot = 0.f;
+      for (int d = 0; d < hd; d++) dot += qs[d] * kt[d];
+      const float v = dot * inv_sqrt;
+      s[i] = v;
+      m = fmaxf(m, v);
+    }
   }
   m = block_max(m, red);
   __syncthreads();   // every score is written
-  float part = 0.f;
+  float sp = 0.f;
   for (int i = t; i < n; i += blockDim.x) {
     const float e = expf(s[i] - m);
     s[i] = e;
-    part += e;
+    sp += e;
   }
-  float sum = block_sum(part, red);
+  float sum = block_sum(sp, red);
   if (sinks) sum += expf(sinks[h] - m);
   const float inv_sum = 1.f / sum;
   __syncthreads();   // every exponential is written
+  constexpr int DJ = ATT_MAX_HD / 32;
+  float acc[DJ];
+#pragma unroll
+  for (int j = 0; j < DJ; j++) acc[j] = 0.f;
+#pragma unroll 4
+  for (int i = w; i < n; i += nw) {
+    const float pw = s[i] * inv_sum;
+    const float* vt = vc + (size_t)i * hd;
+#pragma unroll
+    for (int j = 0; j < DJ; j++) {
+      const int d = lane + 32 * j;
+      if (d < hd) acc[j] += pw * __ldg(vt + d);
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < DJ; j++) {
+    const int d = lane + 32 * j;
+    if (d < hd) part[w][d] = acc[j];
+  }
+  __syncthreads();
   for (int d = t; d < hd; d += blockDim.x) {
-    float acc = 0.f;
-    for (int i = 0; i < n; i++) acc += (s[i] * inv_sum) * vc[(size_t)(start + i) * hd + d];
-    out[(size_t)h * hd + d] = acc;
+    float o = 0.f;
+    for (int ww = 0; ww < nw; ww++) o += part[ww][d];
+    out[(size_t)h * hd + d] = o;
   }
 }
 
