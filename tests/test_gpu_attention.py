@@ -142,6 +142,39 @@ def test_attention_decode_q4_matches_reference(gpu, ref):
     run_sequence(gpu, ref, call, steps=8, seed=2)
 
 
+@pytest.mark.parametrize("window,sinks", [(0, True), (700, False)])
+def test_attention_long_context_matches_reference(gpu, ref, window, sinks):
+    """A 1,000-position context, filled on the host, split over several CTAs
+    per head on the GPU (and a sliding window of 700)."""
+    rng = np.random.default_rng(41 + window)
+    L0, kv_max, steps = 1000, 1008, 3
+    fq = fk = fv = fo = Q.FMT_Q4K
+    wq, wk, wv, wo = (weights(rng, fq, H * HD, D), weights(rng, fk, KH * HD, D), weights(rng, fv, KH * HD, D),
+                      weights(rng, fo, D, H * HD))
+    qn, kn = [(1.0 + 0.1 * rng.standard_normal(HD)).astype(np.float32) for _ in range(2)]
+    sk = rng.standard_normal(H).astype(np.float32) if sinks else None
+    half = HD // 2
+    ang = np.arange(kv_max)[:, None] * (1.0 / (10000.0 ** (np.arange(half) * 2.0 / HD)))[None, :]
+    cos, sin = np.cos(ang).astype(np.float32), np.sin(ang).astype(np.float32)
+    kv0 = [(rng.standard_normal((KH, kv_max, HD)) * 0.5).astype(np.float32) for _ in range(2)]
+    caches = {n: [c.copy() for c in kv0] for n in ("ref", "gpu")}
+    for c in caches["gpu"]:
+        gpu.tg_cuda_unregister(p(c))
+    for pos in range(L0, L0 + steps):
+        x = rng.standard_normal(D).astype(np.float32)
+        outs = {}
+        for name, lib in (("ref", ref), ("gpu", gpu)):
+            out = np.zeros(D, np.float32)
+            kk, vv = caches[name]
+            lib.tg_attention_v2(fq, fk, fv, fo, p(wq), p(wk), p(wv), p(wo), None, None, None, None, p(qn), p(kn),
+                                p(sk), p(kk), p(vv), pos, kv_max, window, p(cos), p(sin), p(x), p(out),
+                                D, H, KH, HD, pos, 1e-6)
+            outs[name] = out
+        msg = ctypes.create_string_buffer(512)
+        assert gpu.tg_cuda_last_error(msg, 512) == 0, msg.value
+        assert rel_err(outs["gpu"], outs["ref"]) <= TOL, pos
+
+
 def test_transformer_layer_matches_reference(gpu, ref):
     """x += attention(rms_norm(x)); x += sum_e w_e expert_e(rms_norm(x)), the
     experts pre-routed (Q4_K gate/up, Q4_K or F16 down), over 4 positions."""

@@ -111,36 +111,44 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_prep_kernel(float* q, float*
   }
 }
 
-// Block h: query head h against KV head h / gqa over positions [start,
-// seq_len); scores in sc[h][.] (global scratch, kv_max per head).  A thread
-// per position for the scores (float4 rows when head_dim % 4 == 0); for the
-// weighted sum of v, warp w takes positions w, w + nw, ..., its lanes the
-// dimensions, and the warps' partial sums add up in shared memory.
-__global__ void __launch_bounds__(ATT_THREADS) attn_heads_kernel(const float* q, const float* kv_k, const float* kv_v,
+// Block (h, sp): query head h against KV head h / gqa over its share of the
+// positions [start, seq_len) (split sp of nsp, `chunk` positions each):
+// scores, their local maximum pm, the sum ps of exp(score - pm) and the
+// unnormalised sum pacc[d] of exp(score - pm) v[d].  A thread per score
+// (float4 rows when head_dim % 4 == 0; scores in sc[h][.], global scratch of
+// kv_max per head); for the weighted sum, warp w takes positions w, w + nw,
+// ..., its lanes the dimensions, and the warps' partial sums add up in
+// shared memory.
+__global__ void __launch_bounds__(ATT_THREADS) attn_split_kernel(const float* q, const float* kv_k, const float* kv_v,
                                                                  int kv_max, int hd, int gqa, int start, int seq_len,
-                                                                 float inv_sqrt, const float* sinks, float* sc,
-                                                                 float* out) {
+                                                                 int chunk, float inv_sqrt, float* sc, float* pm,
+                                                                 float* ps, float* pacc) {
   __shared__ __align__(16) float qs[ATT_MAX_HD];
   __shared__ float red[ATT_THREADS / 32];
   __shared__ float part[ATT_THREADS / 32][ATT_MAX_HD];
-  const int h = blockIdx.x, t = threadIdx.x, lane = t & 31, w = t >> 5, nw = blockDim.x >> 5;
-  const int kvh = h / gqa, n = seq_len - start;
-  const float* kc = kv_k + ((size_t)kvh * kv_max + start) * hd;
-  const float* vc = kv_v + ((size_t)kvh * kv_max + start) * hd;
-  float* s = sc + (size_t)h * kv_max;
+  const int h = blockIdx.x, sp = blockIdx.y, nsp = gridDim.y;
+  const int t = threadIdx.x, lane = t & 31, w = t >> 5, nw = blockDim.x >> 5;
+  const int kvh = h / gqa, p0 = start + sp * chunk, n = min(chunk, seq_len - p0);
+  const float* kc = kv_k + ((size_t)kvh * kv_max + p0) * hd;
+  const float* vc = kv_v + ((size_t)kvh * kv_max + p0) * hd;
+  float* s = sc + (size_t)h * kv_max + (p0 - start);
   for (int d = t; d < hd; d += blockDim.x) qs[d] = q[(size_t)h * hd + d];
   __syncthreads();
-  float m = sinks ? sinks[h] : -1e30f;
+  float m = -INFINITY;
   if ((hd & 3) == 0) {
     const float4* q4 = reinterpret_cast<const float4*>(qs);
     for (int i = t; i < n; i += blockDim.x) {
       const float4* kt = reinterpret_cast<const float4*>(kc + (size_t)i * hd);
-      float dot = 0.f;
+      float d0 = 0.f, d1 = 0.f, d2 = 0.f, d3 = 0.f;   // independent chains: loads stay in flight
+#pragma unroll 8
       for (int d4 = 0; d4 < hd / 4; d4++) {
         const float4 kv = __ldg(kt + d4), qv = q4[d4];
-        dot += qv.x * kv.x + qv.y * kv.y + qv.z * kv.z + qv.w * kv.w;
+        d0 += qv.x * kv.x;
+        d1 += qv.y * kv.y;
+        d2 += qv.z * kv.z;
+        d3 += qv.w * kv.w;
       }
-      const float v = dot * inv_sqrt;
+      const float v = ((d0 + d1) + (d2 + d3)) * inv_sqrt;
       s[i] = v;
       m = fmaxf(m, v);
     }
@@ -156,40 +164,62 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_heads_kernel(const float* q,
   }
   m = block_max(m, red);
   __syncthreads();   // every score is written
-  float sp = 0.f;
+  float sp_sum = 0.f;
   for (int i = t; i < n; i += blockDim.x) {
     const float e = expf(s[i] - m);
     s[i] = e;
-    sp += e;
+    sp_sum += e;
   }
-  float sum = block_sum(sp, red);
-  if (sinks) sum += expf(sinks[h] - m);
-  const float inv_sum = 1.f / sum;
+  const float sum = block_sum(sp_sum, red);
   __syncthreads();   // every exponential is written
   constexpr int DJ = ATT_MAX_HD / 32;
   float acc[DJ];
 #pragma unroll
-  for (int j = 0; j < DJ; j++) acc[j] = 0.f;
+  for (int jj = 0; jj < DJ; jj++) acc[jj] = 0.f;
 #pragma unroll 4
   for (int i = w; i < n; i += nw) {
-    const float pw = s[i] * inv_sum;
+    const float e = s[i];
     const float* vt = vc + (size_t)i * hd;
 #pragma unroll
-    for (int j = 0; j < DJ; j++) {
-      const int d = lane + 32 * j;
-      if (d < hd) acc[j] += pw * __ldg(vt + d);
+    for (int jj = 0; jj < DJ; jj++) {
+      const int d = lane + 32 * jj;
+      if (d < hd) acc[jj] += e * __ldg(vt + d);
     }
   }
 #pragma unroll
-  for (int j = 0; j < DJ; j++) {
-    const int d = lane + 32 * j;
-    if (d < hd) part[w][d] = acc[j];
+  for (int jj = 0; jj < DJ; jj++) {
+    const int d = lane + 32 * jj;
+    if (d < hd) part[w][d] = acc[jj];
   }
   __syncthreads();
+  const size_t o = (size_t)h * nsp + sp;
   for (int d = t; d < hd; d += blockDim.x) {
-    float o = 0.f;
-    for (int ww = 0; ww < nw; ww++) o += part[ww][d];
-    out[(size_t)h * hd + d] = o;
+    float v = 0.f;
+    for (int ww = 0; ww < nw; ww++) v += part[ww][d];
+    pacc[o * hd + d] = v;
+  }
+  if (t == 0) {
+    pm[o] = m;
+    ps[o] = sum;
+  }
+}
+
+// Block h: the splits of head h merged, with the sink logit:
+// out[d] = sum_s pacc_s[d] e^(pm_s - M) / (sum_s ps_s e^(pm_s - M) + e^(sink - M)),
+// M the largest of the split maxima and the sink.
+__global__ void attn_combine_kernel(const float* pm, const float* ps, const float* pacc, int nsp, int hd,
+                                    const float* sinks, float* out) {
+  const int h = blockIdx.x;
+  float M = sinks ? sinks[h] : -INFINITY;
+  for (int k = 0; k < nsp; k++) M = fmaxf(M, pm[(size_t)h * nsp + k]);
+  float tot = sinks ? expf(sinks[h] - M) : 0.f;
+  for (int k = 0; k < nsp; k++) tot += ps[(size_t)h * nsp + k] * expf(pm[(size_t)h * nsp + k] - M);
+  const float inv = 1.f / tot;
+  for (int d = threadIdx.x; d < hd; d += blockDim.x) {
+    float v = 0.f;
+    for (int k = 0; k < nsp; k++)
+      v += pacc[((size_t)h * nsp + k) * hd + d] * expf(pm[(size_t)h * nsp + k] - M);
+    out[(size_t)h * hd + d] = v * inv;
   }
 }
 
@@ -330,6 +360,8 @@ static bool attention_step(const char* what, int fq, int fk, int fv, int fo, con
   // device scratch: x | rope rows | q | k | v | attn | out, knew, vnew | scores | Q8 of x / of attn
   const size_t fx = D, fr = 2 * (size_t)half, fq_ = qd, fk_ = kd, fa = qd, fo_ = D + 2 * (size_t)kd;
   const size_t fsc = (size_t)H * kv_max;
+  constexpr int ATT_MAX_SPLIT = 8;   // position splits per head
+  const size_t fpm = (size_t)H * ATT_MAX_SPLIT, fpa = fpm * hd;
   const int nbx = (D + QK - 1) / QK, nba = (qd + QK - 1) / QK;
   size_t off = 0;
   auto take = [&](size_t bytes) {
@@ -340,7 +372,7 @@ static bool attention_step(const char* what, int fq, int fk, int fv, int fo, con
   // x and the two RoPE rows share one region (one upload)
   const size_t o_x = take(4 * (fx + fr)), o_q = take(4 * fq_), o_k = take(4 * fk_), o_v = take(4 * fk_),
                o_a = take(4 * fa), o_o = take(4 * fo_), o_s = take(4 * fsc), o_xq = take(sizeof(Q8Dev) * nbx),
-               o_aq = take(sizeof(Q8Dev) * nba);
+               o_aq = take(sizeof(Q8Dev) * nba), o_pm = take(4 * fpm), o_ps = take(4 * fpm), o_pa = take(4 * fpa);
   float* hin = (float*)pinned_up(4 * (fx + fr));
   const float* hout = deliver_reserve(fo_);   // mapped: output and the new K / V rows
   if (!hin || !hout || !g_att.reserve(off, what)) return false;
@@ -348,6 +380,7 @@ static bool attention_step(const char* what, int fq, int fk, int fv, int fo, con
   float *x = (float*)(b + o_x), *rr = x + fx, *q = (float*)(b + o_q), *k = (float*)(b + o_k), *v = (float*)(b + o_v),
         *att = (float*)(b + o_a), *ob = (float*)(b + o_o), *sc = (float*)(b + o_s);
   Q8Dev *xq = (Q8Dev*)(b + o_xq), *aq = (Q8Dev*)(b + o_aq);
+  float *pm = (float*)(b + o_pm), *ps = (float*)(b + o_ps), *pa = (float*)(b + o_pa);
 
   memcpy(hin, input, 4 * fx);
   memcpy(hin + fx, rope_cos + (size_t)pos * half, 4 * (size_t)half);
@@ -377,9 +410,14 @@ static bool attention_step(const char* what, int fq, int fk, int fv, int fo, con
     attn_prep_kernel<<<H + 2 * KH, ATT_THREADS, 0, s>>>(q, k, v, dqn, dkn, eps, rr, rr + half, H, KH, hd, mk->d,
                                                          mv->d, kv_len, kv_max, ob + D, ob + D + kd);
     const int seq_len = kv_len + 1, start = (window > 0 && seq_len > window) ? seq_len - window : 0;
-    attn_heads_kernel<<<H, ATT_THREADS, 0, s>>>(q, mk->d, mv->d, kv_max, hd, H / KH, start, seq_len,
-                                                1.f / sqrtf((float)hd), dsk, sc, att);
-    count_launches(2);
+    // positions split over up to ATT_MAX_SPLIT CTAs per head, >= 128 each
+    const int npos = seq_len - start;
+    const int nsp = std::max(1, std::min(ATT_MAX_SPLIT, npos / 128));
+    const int chunk = (npos + nsp - 1) / nsp;
+    attn_split_kernel<<<dim3(H, nsp), ATT_THREADS, 0, s>>>(q, mk->d, mv->d, kv_max, hd, H / KH, start, seq_len,
+                                                           chunk, 1.f / sqrtf((float)hd), sc, pm, ps, pa);
+    attn_combine_kernel<<<H, 128, 0, s>>>(pm, ps, pa, nsp, hd, dsk, att);
+    count_launches(3);
     ok = cudaGetLastError() == cudaSuccess;
   }
   if (ok && quantized(fo)) {

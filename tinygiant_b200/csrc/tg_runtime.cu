@@ -418,13 +418,41 @@ static bool in_registered_range(uintptr_t p, size_t n) {
 }
 
 // Copies raw host bytes to HBM in the layout of WDesc w (already allocated).
+// Host bytes (any memory: pageable, mapped files) to the device through two
+// pinned 4 MiB staging buffers, so the host copy of one chunk overlaps the
+// DMA of the previous one; an event guards each buffer's reuse.
+static bool upload_bytes(void* dst, const uint8_t* h, size_t n, cudaStream_t s) {
+  constexpr size_t CH = (size_t)4 << 20;
+  static void* pin[2] = {nullptr, nullptr};
+  static cudaEvent_t ev[2];
+  if (!pin[0]) {
+    for (int i = 0; i < 2; i++)
+      if (!cuda_ok(cudaMallocHost(&pin[i], CH), "cudaMallocHost(upload staging)") ||
+          !cuda_ok(cudaEventCreateWithFlags(&ev[i], cudaEventDisableTiming), "cudaEventCreate(upload)")) {
+        pin[0] = pin[1] = nullptr;
+        return false;
+      }
+  }
+  for (size_t off = 0, k = 0; off < n; off += CH, k++) {
+    const int b = (int)(k & 1);
+    const size_t len = std::min(CH, n - off);
+    if (!cuda_ok(cudaEventSynchronize(ev[b]), "upload weights")) return false;
+    memcpy(pin[b], h + off, len);
+    if (!cuda_ok(cudaMemcpyAsync(static_cast<uint8_t*>(dst) + off, pin[b], len, cudaMemcpyHostToDevice, s),
+                 "upload weights") ||
+        !cuda_ok(cudaEventRecord(ev[b], s), "upload weights"))
+      return false;
+  }
+  return true;
+}
+
 static bool upload_into(const uint8_t* h, size_t raw, const WDesc& w) {
   cudaStream_t s = stream();
   if (!(w.fmt == FMT_Q6K || w.fmt == FMT_MXFP4 || w.fmt == FMT_Q80)) {
-    if (!cuda_ok(cudaMemcpyAsync((void*)w.main, h, raw, cudaMemcpyHostToDevice, s), "upload weights")) return false;
+    if (!upload_bytes((void*)w.main, h, raw, s)) return false;
   } else {
     if (!g.d_tmp.reserve(raw)) return false;
-    if (!cuda_ok(cudaMemcpyAsync(g.d_tmp.p, h, raw, cudaMemcpyHostToDevice, s), "upload weights")) return false;
+    if (!upload_bytes(g.d_tmp.p, h, raw, s)) return false;
     launch_repack((const uint8_t*)g.d_tmp.p, w.fmt, w.rows, w.cols, (uint8_t*)w.main, s);
     g_launches++;
   }
