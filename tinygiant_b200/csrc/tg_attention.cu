@@ -405,7 +405,16 @@ static bool attention_step(const char* what, int fq, int fk, int fv, int fo, con
     launch_quantize_rows(x, 1, D, D, xq, s);
     count_launches(1);
   }
-  bool ok = proj(Wq, fq, xq, x, dbq, q) && proj(Wk, fk, xq, x, dbk, k) && proj(Wv, fv, xq, x, dbv, v);
+  bool ok;
+  if (fq != -1 && fk != -1 && fv != -1) {   // q, k, v in one launch
+    const WDesc W3[3] = {Wq, Wk, Wv};
+    const float* b3[3] = {dbq, dbk, dbv};
+    float* o3[3] = {q, k, v};
+    count_launches(1);
+    ok = launch_matvec3(W3, b3, o3, xq, x, 1, status_ptr(), s) == cudaSuccess;
+  } else {
+    ok = proj(Wq, fq, xq, x, dbq, q) && proj(Wk, fk, xq, x, dbk, k) && proj(Wv, fv, xq, x, dbv, v);
+  }
   if (ok) {
     attn_prep_kernel<<<H + 2 * KH, ATT_THREADS, 0, s>>>(q, k, v, dqn, dkn, eps, rr, rr + half, H, KH, hd, mk->d,
                                                          mv->d, kv_len, kv_max, ob + D, ob + D + kd);

@@ -10,6 +10,8 @@
 // (integer sub-block sums, max|x|) run in parallel.
 #include <cuda_fp16.h>
 
+#include <algorithm>
+
 #include "tg_dots.cuh"
 #include "tg_kernels.h"
 #include "tg_plan.cuh"
@@ -34,12 +36,11 @@ __global__ void __launch_bounds__(256) quantize_rows_kernel(const float* __restr
 // ---------------------------------------------------------------------
 // One matrix against one input: out[r] = dot (+ (bias ? bias[r] : 0.f)).
 
+// Rows r0 .. r0 + R - 1 of W (one CTA; smem: R x terms-per-row floats).
 template <int R>
-__global__ void __launch_bounds__(256) matvec_kernel(WDesc W, const Q8Dev* __restrict__ xq8, const float* __restrict__ x,
-                                                     const float* __restrict__ bias, int bias_term,
-                                                     float* __restrict__ out, DevStatus* st) {
-  extern __shared__ float smem[];
-  const int r0 = blockIdx.x * R;
+__device__ __forceinline__ void matvec_rows(const WDesc& W, int r0, const Q8Dev* __restrict__ xq8,
+                                            const float* __restrict__ x, const float* __restrict__ bias,
+                                            int bias_term, float* __restrict__ out, DevStatus* st, float* smem) {
   if (r0 >= W.rows) return;
   const int nr = min(R, W.rows - r0);
   if (W.fmt == FMT_F16) {
@@ -70,7 +71,32 @@ __global__ void __launch_bounds__(256) matvec_kernel(WDesc W, const Q8Dev* __res
   }
 }
 
-// f32 rows with the reference's lane structure (662-676).
+template <int R>
+__global__ void __launch_bounds__(256) matvec_kernel(WDesc W, const Q8Dev* __restrict__ xq8, const float* __restrict__ x,
+                                                     const float* __restrict__ bias, int bias_term,
+                                                     float* __restrict__ out, DevStatus* st) {
+  extern __shared__ float smem[];
+  matvec_rows<R>(W, blockIdx.x * R, xq8, x, bias, bias_term, out, st, smem);
+}
+
+// Three matrices against one input in one launch: blocks [0, nb0) take W0's
+// rows, the next nb1 W1's, the rest W2's.
+struct Matvec3 {
+  WDesc W[3];
+  const float* bias[3];
+  float* out[3];
+  int nb[3];
+};
+
+template <int R>
+__global__ void __launch_bounds__(256) matvec3_kernel(Matvec3 a, const Q8Dev* __restrict__ xq8,
+                                                      const float* __restrict__ x, int bias_term, DevStatus* st) {
+  extern __shared__ float smem[];
+  int b = blockIdx.x, m = 0;
+  while (m < 2 && b >= a.nb[m]) b -= a.nb[m++];
+  matvec_rows<R>(a.W[m], b * R, xq8, x, a.bias[m], bias_term, a.out[m], st, smem);
+}
+
 __global__ void f32_matvec_kernel(const float* __restrict__ A, const float* __restrict__ x, float* __restrict__ out,
                                   int nrows, int ncols) {
   const int r = blockIdx.x * blockDim.x + threadIdx.x;
@@ -214,6 +240,27 @@ cudaError_t launch_matvec(const WDesc& W, const Q8Dev* xq8, const float* x, cons
   cudaError_t e = ensure_smem(reinterpret_cast<const void*>(k), smem);
   if (e != cudaSuccess) return e;
   k<<<(W.rows + MV_R - 1) / MV_R, 256, smem, s>>>(W, xq8, x, bias, bias_term, out, st);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_matvec3(const WDesc* W, const float* const* bias, float* const* out, const Q8Dev* xq8,
+                           const float* x, int bias_term, DevStatus* st, cudaStream_t s) {
+  Matvec3 a{};
+  size_t smem = 0;
+  int blocks = 0;
+  for (int m = 0; m < 3; m++) {
+    a.W[m] = W[m];
+    a.bias[m] = bias[m];
+    a.out[m] = out[m];
+    a.nb[m] = (W[m].rows + MV_R - 1) / MV_R;
+    blocks += a.nb[m];
+    const int P = W[m].fmt == FMT_F16 ? 1 : terms_per_row(W[m].fmt, W[m].cols);
+    smem = std::max(smem, sizeof(float) * (size_t)MV_R * P);
+  }
+  auto k = matvec3_kernel<MV_R>;
+  cudaError_t e = ensure_smem(reinterpret_cast<const void*>(k), smem);
+  if (e != cudaSuccess) return e;
+  k<<<blocks, 256, smem, s>>>(a, xq8, x, bias_term, st);
   return cudaGetLastError();
 }
 
