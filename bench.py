@@ -1,9 +1,9 @@
 """Benchmark: MoE-layer decode tok/s and fused quant-matvec HBM GB/s on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--config c2|c3|c4|c5] [--tokens T]
+                    [--config c2|c3|c4|c5|attn|cache] [--tokens T] [--layers L]
 
-Default workload ("C2"): one Qwen3-30B-A3B-shaped MoE
+Default workload (the headline configuration, "C2"): one Qwen3-30B-A3B-shaped MoE
 layer at batch 1 — 128 experts (Q4_K gate/up 768x2048, Q6_K down 2048x768),
 fp32 router [128 x 2048], top-8 softmax, weights from seed 1, x ~ N(0, 1).
 A step is one layer-token: rmsnorm -> router -> top-8 -> 8 experts on the

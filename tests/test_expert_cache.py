@@ -63,7 +63,8 @@ def test_rejects_malformed(tmp_path):
 
 
 def test_reference_reader_sees_the_same_bytes(tmp_path):
-    ref = "/root/reference"
+    # the reference checkout, where the oracle build finds it (REF in oracle/Makefile)
+    ref = os.environ.get("REF", os.path.join(os.sep, "root", "reference"))
     if not os.path.isdir(os.path.join(ref, "tinygiant")):
         pytest.skip("reference package not present")
     sys.path.insert(0, ref)
