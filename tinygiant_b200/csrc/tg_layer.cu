@@ -584,17 +584,17 @@ int tg_layer_forward(void* handle, const float* x_host, float* out_host, int T, 
     return -1;
   }
   const size_t n = sizeof(float) * (size_t)T * L->D;
-  float* hx = (float*)pinned_up(n);
+  float* hx = fetch_reserve((size_t)T * L->D);     // mapped: the device reads it
   float* ho = deliver_reserve((size_t)T * L->D);   // mapped: the device writes it
   if (!hx || !ho) return -1;
   cudaStream_t s = stream();
   memcpy(hx, x_host, n);
   float* moe = L->moe_out;
-  // The step's device work — the copy of x in, the step, and the delivery of
-  // its output and of the device status into mapped host memory — is one
-  // CUDA graph per (rows, normalize, staging buffers, stream), captured on
-  // first use and replayed; the host then waits on the delivery's echo
-  // instead of synchronising the stream.
+  // The step's device work — the fetch of x from mapped host memory, the
+  // step, and the delivery of its output and of the device status into
+  // mapped host memory — is one CUDA graph per (rows, normalize, staging
+  // buffers, stream), captured on first use and replayed; the host then
+  // waits on the delivery's echo instead of synchronising the stream.
   const bool same = L->fwd_exec && L->fwd_T == T && L->fwd_norm == normalize && L->fwd_hx == hx &&
                     L->fwd_ho == ho && L->fwd_s == s;
   if (!same && s != nullptr && s != cudaStreamLegacy && s != cudaStreamPerThread) {
@@ -603,7 +603,7 @@ int tg_layer_forward(void* handle, const float* x_host, float* out_host, int T, 
     cudaGraph_t graph = nullptr;
     bool ok = cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal) == cudaSuccess;
     if (ok) {
-      ok = cudaMemcpyAsync(L->xbuf, hx, n, cudaMemcpyHostToDevice, s) == cudaSuccess &&
+      ok = fetch_async(L->xbuf, (size_t)T * L->D, s, what) &&
            layer_enqueue(L, L->xbuf, nullptr, nullptr, moe, T, normalize, nullptr, s, what) &&
            deliver_async(moe, (size_t)T * L->D, s, what);
       ok = cudaStreamEndCapture(s, &graph) == cudaSuccess && ok;

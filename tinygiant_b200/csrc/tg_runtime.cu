@@ -150,6 +150,7 @@ struct Ctx {
   DevBuf d_stage, d_xq8, d_hidden, d_hq8, d_tmp, d_counters, d_parts;
   PinBuf h_up, h_down;
   MapBuf h_ret;                   // deliver_async's result block
+  MapBuf h_in;                    // fetch_async's input block
   unsigned int ret_seq = 0;
   int threads = 1;
 };
@@ -273,6 +274,30 @@ __global__ void deliver_kernel(const float* __restrict__ src, size_t n, const De
     __threadfence_system();
     *reinterpret_cast<volatile unsigned int*>(&hdr->done) = req;
   }
+}
+
+// One CTA: copies n floats from mapped pinned host memory, which the host
+// wrote before the launch, into device memory.  The loads skip any cached
+// copy of the host lines (ld.global.cv).  It lets the next kernel launch at
+// once; that kernel waits for this grid (griddepcontrol.wait) before it
+// reads dst.
+__global__ void fetch_kernel(const float* __restrict__ src, size_t n, float* __restrict__ dst) {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  const size_t n4 = n / 4;
+  for (size_t i = threadIdx.x; i < n4; i += blockDim.x)
+    reinterpret_cast<float4*>(dst)[i] = __ldcv(reinterpret_cast<const float4*>(src) + i);
+  for (size_t i = n4 * 4 + threadIdx.x; i < n; i += blockDim.x) dst[i] = __ldcv(src + i);
+}
+
+float* fetch_reserve(size_t n_floats) {
+  return g.h_in.reserve(sizeof(float) * n_floats) ? static_cast<float*>(g.h_in.h) : nullptr;
+}
+
+bool fetch_async(float* d_dst, size_t n_floats, cudaStream_t s, const char* what) {
+  if (!g.h_in.reserve(sizeof(float) * n_floats)) return false;
+  fetch_kernel<<<1, 512, 0, s>>>(static_cast<const float*>(g.h_in.d), n_floats, d_dst);
+  count_launches(1);
+  return cuda_ok(cudaGetLastError(), what);
 }
 
 float* deliver_reserve(size_t n_floats) {

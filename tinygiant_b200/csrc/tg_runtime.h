@@ -34,6 +34,12 @@ float* deliver_reserve(size_t n_floats);
 bool deliver_async(const float* d_src, size_t n_floats, cudaStream_t s, const char* what);
 void deliver_begin();
 bool finish_delivered(const char* what);
+// Small inputs the other way: fetch_reserve sizes a mapped pinned block and
+// returns its host pointer; fetch_async enqueues a one-CTA kernel that copies
+// it into device memory (capturable) and lets a dependent kernel launched
+// with programmatic stream serialization start at once.
+float* fetch_reserve(size_t n_floats);
+bool fetch_async(float* d_dst, size_t n_floats, cudaStream_t s, const char* what);
 void unregister_counters(void* p);
 // Attention decode's KV-cache mirrors (tg_attention.cu), dropped with the registry.
 void kv_mirror_forget(const void* host);
