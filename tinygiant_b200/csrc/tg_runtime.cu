@@ -258,6 +258,7 @@ __global__ void deliver_kernel(const float* __restrict__ src, size_t n, const De
                                RetHdr* hdr, float* out) {
   __shared__ unsigned int req;
   if (threadIdx.x == 0) req = *reinterpret_cast<volatile unsigned int*>(&hdr->req);
+  asm volatile("griddepcontrol.wait;" ::: "memory");   // src and st come from the preceding kernel
   const size_t n4 = n / 4;
   for (size_t i = threadIdx.x; i < n4; i += blockDim.x)
     reinterpret_cast<float4*>(out)[i] = __ldcg(reinterpret_cast<const float4*>(src) + i);
@@ -309,9 +310,22 @@ bool deliver_async(const float* d_src, size_t n_floats, cudaStream_t s, const ch
   if (!g.h_ret.reserve(RET_DATA + sizeof(float) * n_floats)) return false;
   RetHdr* hdr = static_cast<RetHdr*>(g.h_ret.d);
   float* out = reinterpret_cast<float*>(static_cast<uint8_t*>(g.h_ret.d) + RET_DATA);
-  deliver_kernel<<<1, 512, 0, s>>>(d_src, n_floats, g.d_status, hdr, out);
+  // launched as a programmatic dependent: it is scheduled while the
+  // preceding kernel runs and waits for that grid before reading its output
+  const DevStatus* st = g.d_status;
+  void* args[] = {(void*)&d_src, (void*)&n_floats, (void*)&st, (void*)&hdr, (void*)&out};
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(1);
+  cfg.blockDim = dim3(512);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelExC(&cfg, (const void*)deliver_kernel, args);
   count_launches(1);
-  return cuda_ok(cudaGetLastError(), what);
+  return cuda_ok(e, what);
 }
 
 // Sets the next request number; call before launching the work that ends
