@@ -4,7 +4,7 @@
 //
 // Rules kept here: every cp.async.bulk starts and ends on 16-byte
 // boundaries (callers round tile sizes up; weight allocations are padded);
-// no copy uses .multicast::cluster; every wait has an iteration limit after
+// no copy uses cluster multicast; every wait has an iteration limit after
 // which it reports failure instead of spinning forever.
 #pragma once
 #include <cstdint>
