@@ -1,7 +1,7 @@
 """Benchmark: MoE-layer decode tok/s and fused quant-matvec HBM GB/s on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--config c2|c3|c4|c5|attn|cache] [--tokens T] [--layers L]
+                    [--config c1|c2|c3|c4|c5|attn|cache|trace] [--tokens T] [--layers L]
 
 Default workload (the headline configuration, "C2"): one Qwen3-30B-A3B-shaped MoE
 layer at batch 1 — 128 experts (Q4_K gate/up 768x2048, Q6_K down 2048x768),
@@ -16,18 +16,26 @@ so each step's 24.5 MB of experts were last touched 15 steps (~390 MB of
 traffic) earlier and are not L2-resident.
 
 e2e: the same step through the C-ABI entry tg_layer_forward with host
-buffers (x in, MoE output back), host<->device copies inside the timed region.
+buffers (x in, MoE output back), host<->device copies inside the timed
+region.  e2e_engine: the reference engine's own call sequence per step —
+numpy RMSNorm + router + top-k + union (engine.py:281-318) and
+tg_moe_forward_rows_v2 with host pointers (engine.py:323-341).
 
-Multi-GPU (torchrun), --parallel dp (default): every GPU holds the layer
-and serves its own tokens; no collective on the data path, per-GPU work is
-fixed ("weak").  --parallel ep: experts sharded by id (e % N == rank), router
-replicated, one NCCL all-reduce of the [T, D] output per step; total work is
-fixed ("strong").
+Multi-GPU (torchrun): --parallel ep (the default for N > 1) shards the experts
+by id (e % N == rank) with the router replicated; decode-sized steps sum the
+shards' parts inside the step kernel over NVLink (--ep-nccl: one NCCL
+all-reduce instead); total work is fixed ("strong").  --parallel dp: every
+GPU holds the whole layer and serves its own tokens ("weak").
+
+C1 (--config c1): one all-Q4_K expert (tg_expert_forward) over 64 copies
+(170 MB); the device-timed step is that expert as a one-expert resident layer
+without normalisation (weight 1), e2e is tg_expert_forward with host buffers.
 
 --impl reference: the reference's own CPU path on the host cores — its router
 (restated in synth.route, checked against tinygiant/router.py) + its
 csrc/libtinygiant.c tg_moe_forward_rows_v2 (oracle/_ref, compiled from the
-reference's source) with every host thread.
+reference's source) with every host thread, over the same R copies of the
+layer in host memory.
 """
 import argparse
 import ctypes
@@ -48,7 +56,9 @@ sys.path.insert(0, str(ROOT))
 METRIC = "MoE-layer decode tok/s; fused quant-matvec HBM GB/s vs ~8 TB/s B200 peak"
 UNIT = "tok/s"
 R_COPIES = 16
-DTYPES = {"c2": "int8xQ4_K/Q6_K (int32 accumulate), fp32 combine",
+C1_COPIES = 64      # C1: 64 x 2.65 MB = 170 MB of experts, beyond the 126 MB L2
+DTYPES = {"c1": "int8xQ4_K (int32 accumulate), fp32 combine",
+          "c2": "int8xQ4_K/Q6_K (int32 accumulate), fp32 combine",
           "c3": "int8xQ4_K/Q6_K (int32 accumulate), fp32 combine",
           "c4": "int8xMXFP4 (int32 accumulate), fp32 combine",
           "c5": "int8xQ4_K/Q6_K (int32 accumulate), fp32 combine"}
@@ -60,20 +70,27 @@ def parse():
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--config", default="c2", choices=["c2", "c3", "c4", "c5", "attn", "cache"],
-                    help="c2-c5: the MoE workloads; attn: one attention decode step (tg_attention_v2); "
-                         "cache: an expert-cache directory loaded into HBM")
+    ap.add_argument("--config", default="c2", choices=["c1", "c2", "c3", "c4", "c5", "attn", "cache", "trace"],
+                    help="c1-c5: the MoE workloads; attn: one attention decode step (tg_attention_v2); "
+                         "cache: an expert-cache directory loaded into HBM; trace: the fused step's phase "
+                         "timeline (diagnostics, no bench line)")
     ap.add_argument("--tokens", type=int, default=None)
     ap.add_argument("--copies", type=int, default=R_COPIES)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--parallel", default="dp", choices=["dp", "ep"])
+    ap.add_argument("--parallel", default=None, choices=["dp", "ep"],
+                    help="with several GPUs: ep (default) shards the experts by id, dp runs replicas")
+    ap.add_argument("--gptoss", action="store_true", help="--config trace: the C4 layer instead of C2")
+    ap.add_argument("--experts", type=int, default=None, help="--config trace: experts in the layer")
     ap.add_argument("--layers", type=int, default=None,
                     help="C4 / C5: layers in the stack (default 36 / 48; C4 with 1: one layer over HBM copies)")
     ap.add_argument("--matvec", action="store_true",
                     help="batched steps (T > 8) on the matvec kernels instead of the tcgen05 grouped GEMMs")
     ap.add_argument("--ep-nccl", action="store_true",
                     help="expert parallel: sum the shards with an NCCL all-reduce instead of inside the step kernel")
-    return ap.parse_args()
+    a = ap.parse_args()
+    if a.parallel is None:
+        a.parallel = "ep" if int(os.environ.get("WORLD_SIZE", "1")) > 1 else "dp"
+    return a
 
 
 # ---- workload ------------------------------------------------------------
@@ -87,8 +104,26 @@ def make_layer(cfg):
     return synth.qwen_layer(seed=1)
 
 
+def host_copies(L, R):
+    """R copies of layer L whose expert byte arrays are distinct host arrays
+    (the router is shared): the CPU arms cycle them as the GPU arm cycles its
+    R HBM copies."""
+    import copy
+    out = [L]
+    for _ in range(R - 1):
+        c = copy.copy(L)
+        c.gates = [g.copy() for g in L.gates]
+        c.ups = [u.copy() for u in L.ups]
+        c.downs = [d.copy() for d in L.downs]
+        out.append(c)
+    return out
+
+
 def workload_desc(cfg, T, R, L):
+    """The `config` of a bench line; both arms report the same one."""
     names = {
+        "c1": "C1: one Qwen3-30B-A3B-shaped expert SwiGLU FFN (all Q4_K: gate/up 768x2048, down 2048x768), "
+              "tg_expert_forward, weight 1",
         "c2": "C2: one Qwen3-30B-A3B MoE layer (128 experts, Q4_K gate/up, Q6_K down, top-8, D=2048, I=768)",
         "c3": "C3: Qwen3-30B-A3B MoE layer with Zipf(1.1)-skewed router bias",
         "c4": "C4: gpt-oss-120b-shaped MXFP4 MoE layer (128 experts, top-4, D=I=2880)",
@@ -96,9 +131,16 @@ def workload_desc(cfg, T, R, L):
                "residual add)",
         "c5": "C5: Qwen3-30B-A3B MoE-FFN stack (C2 experts per layer, per-layer routers, residual add)",
     }
+    if cfg == "c1":
+        return {"workload": names[cfg], "tokens_per_step": 1, "embed_dim": 2048, "inter_dim": 768,
+                "expert_copies": R,
+                "l2": f"inputs larger than L2: steps cycle {R} copies of the expert ({R * 2.654208:.0f} MB; "
+                      f"HBM on the GPU arm, host memory on the reference arm)",
+                "step": "one expert: gate/up, SiLU, down, out += 1.0 * y"}
     return {"workload": names[cfg], "tokens_per_step": T, "experts": L.n_experts, "top_k": L.top_k,
             "embed_dim": L.embed_dim, "inter_dim": L.inter_dim, "layer_copies": R,
-            "l2": f"inputs larger than L2: steps cycle {R} HBM copies of the layer",
+            "l2": f"inputs larger than L2: steps cycle {R} copies of the layer (HBM on the GPU arm, host memory "
+                  f"on the reference arm)",
             "step": "rmsnorm + router + top-k softmax + experts (gate/up/act/down/combine)"}
 
 
@@ -207,89 +249,132 @@ def traffic_from_profiles():
 
 # ---- CPU baseline (reference arm / cpu_baseline) ---------------------------
 
-def cpu_reference_run(L, xs, budget_s=12.0, max_steps=None):
-    """The reference's CPU path per step: its router + its C MoE call."""
+def reference_lib():
+    """The reference's own C (oracle/_ref, kind "reference"), else the oracle
+    port (kind "port")."""
     from oracle import oracle as O
-    from tinygiant_b200 import moe, synth
     lib = O.load_reference()
-    kind = "reference"
     if lib is None:
-        lib, kind = O.load_oracle(), "port"
-    cores = os.cpu_count() or 1
-    lib.tg_set_threads(cores)
-    out = np.zeros_like(xs[0])
-    moe.moe_layer_forward(lib, L, synth.rms_norm(xs[0]), out)    # warm
-    n, t0 = 0, time.perf_counter()
-    while True:
-        x = xs[n % len(xs)]
-        moe.moe_layer_forward(lib, L, synth.rms_norm(x), out)
-        n += 1
-        el = time.perf_counter() - t0
-        if (max_steps and n >= max_steps) or (not max_steps and el >= budget_s):
-            break
-    lib.tg_set_threads(1)
-    T = xs.shape[1]
-    return {"value": n * T / el, "unit": UNIT, "cores": cores, "kind": kind,
-            "sample": f"{n} steps x {T} token(s) of the same workload, {el:.1f} s; "
-                      f"{'reference csrc/libtinygiant.c built from source (NEON via oracle/neon_shim)' if kind == 'reference' else 'oracle port (tg_oracle.c)'}"
-                      f" + numpy router, all {cores} host threads"}, el / n
+        return O.load_oracle(), "port"
+    return lib, "reference"
 
 
-def run_reference(a):
-    rank = int(os.environ.get("RANK", "0"))
-    if rank != 0:
-        return
-    cfg = a.config
-    T = a.tokens or 1
-    L = make_layer(cfg)
-    xs = step_inputs(max(a.warmup, 1) + a.steps, T, L.embed_dim)
-    # warm-up steps, untimed
-    from oracle import oracle as O
+def ref_source(kind):
+    return ("csrc/libtinygiant.c built from the reference source (NEON via oracle/neon_shim)"
+            if kind == "reference" else "oracle port (oracle/tg_oracle.c)")
+
+
+def cpu_step(cfg, lib, copies, routers=None):
+    """One step of the reference's CPU path, as fn(i, x) -> output: C1 its
+    tg_expert_forward on copy i % R; a layer its router (synth.route, the
+    engine's numpy sequence) + tg_moe_forward_rows_v2 on layer copy i % R; a
+    stack (routers given) x += MoE_l(rmsnorm(x)) for each layer's router."""
+    import copy
     from tinygiant_b200 import moe, synth
-    lib = O.load_reference()
-    kind = "reference"
-    if lib is None:
-        lib, kind = O.load_oracle(), "port"
-    cores = os.cpu_count() or 1
-    lib.tg_set_threads(cores)
-    out = np.zeros_like(xs[0])
-    if is_stack(a):
-        # the engine's layer loop: x += MoE_l(rmsnorm(x)) for each layer's router
-        import copy
+    R = len(copies)
+    if cfg == "c1":
+        out = np.zeros(2048, np.float32)
+
+        def one(i, x):
+            out[:] = 0.0
+            lib.tg_expert_forward(copies[i % R].ctypes.data, x.ctypes.data, out.ctypes.data, 1.0, 2048, 768)
+            return out
+        return one
+    if routers is not None:
         stack = []
-        for rw in stack_routers(n_layers(a), L.n_experts, L.embed_dim):
-            Ll = copy.copy(L)
+        for rw in routers:
+            Ll = copy.copy(copies[0])
             Ll.router_w = rw
             stack.append(Ll)
 
-        def one(x):
+        def one(i, x):
             x = x.copy()
             for Ll in stack:
                 o = np.zeros_like(x)
                 moe.moe_layer_forward(lib, Ll, synth.rms_norm(x), o)
                 x += o
             return x
+        return one
+
+    def one(i, x):
+        out = np.zeros_like(x)
+        return moe.moe_layer_forward(lib, copies[i % R], synth.rms_norm(x), out)
+    return one
+
+
+def cpu_reference_run(cfg, copies, xs, budget_s=12.0, routers=None):
+    """The cpu_baseline leg: the reference's CPU path on the same workload,
+    all host threads, for about budget_s seconds of steps."""
+    lib, kind = reference_lib()
+    cores = os.cpu_count() or 1
+    lib.tg_set_threads(cores)
+    one = cpu_step(cfg, lib, copies, routers)
+    one(0, xs[0])    # warm
+    n, t0 = 0, time.perf_counter()
+    while True:
+        one(n, xs[n % len(xs)])
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= budget_s:
+            break
+    lib.tg_set_threads(1)
+    T = 1 if cfg == "c1" else xs.shape[1]
+    return {"value": n * T / el, "unit": UNIT, "cores": cores, "kind": kind,
+            "sample": f"{n} steps x {T} token(s) of the same workload, {el:.1f} s; {ref_source(kind)}"
+                      f"{'' if cfg == 'c1' else ' + numpy router'}, all {cores} host threads"}
+
+
+def run_reference(a):
+    """--impl reference: the reference's CPU path on this arm's config,
+    metric and unit; rank 0 only."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    cfg = a.config
+    T = 1 if cfg == "c1" else (a.tokens or 1)
+    from tinygiant_b200 import synth
+    stack = is_stack(a)
+    if cfg == "c1":
+        R = max(1, a.copies if a.copies != R_COPIES else C1_COPIES)
+        e0 = synth.c1_expert(seed=0)
+        copies = [e0] + [e0.copy() for _ in range(R - 1)]
+        xs = step_inputs(max(a.warmup, 1) + a.steps, 1, 2048)[:, 0]
+        desc = workload_desc("c1", 1, R, None)
+        routers = None
     else:
-        def one(x):
-            moe.moe_layer_forward(lib, L, synth.rms_norm(x), out)
+        L = make_layer(cfg)
+        R = 1 if stack else max(1, a.copies)
+        copies = host_copies(L, R)
+        xs = step_inputs(max(a.warmup, 1) + a.steps, T, L.embed_dim)
+        routers = stack_routers(n_layers(a), L.n_experts, L.embed_dim) if stack else None
+        desc = stack_desc(cfg, T, n_layers(a), L) if stack else workload_desc(cfg, T, R, L)
+    lib, kind = reference_lib()
+    cores = os.cpu_count() or 1
+    lib.tg_set_threads(cores)
+    one = cpu_step(cfg, lib, copies, routers)
     for i in range(a.warmup):
-        one(xs[i])
+        one(i, xs[i])
     t0 = time.perf_counter()
     for i in range(a.steps):
-        one(xs[a.warmup + i])
+        one(a.warmup + i, xs[a.warmup + i])
     el = time.perf_counter() - t0
     value = a.steps * T / el
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": a.gpus, "steps": a.steps,
-            "warmup": a.warmup, "ms_per_step": el / a.steps * 1e3, "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": DTYPES.get(cfg, DTYPES["c2"]), "data": "synthetic",
-            "config": {**workload_desc("c4s" if cfg == "c4" and is_stack(a) else cfg, T, 1, L),
-                       **({"layers": n_layers(a)} if is_stack(a) else {})},
+            "warmup": a.warmup, "ms_per_step": el / a.steps * 1e3, "higher_is_better": True,
+            "scaling": scaling_of(a, cfg), "vs_baseline": None, "dtype": DTYPES.get(cfg, DTYPES["c2"]),
+            "data": "synthetic (seeded weights and inputs)", "config": desc,
             "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": kind,
-                             "sample": f"{a.steps} steps x {T} token(s); numpy router + "
-                                       f"{'csrc/libtinygiant.c (reference source, NEON via oracle/neon_shim)' if kind == 'reference' else 'oracle port'}"
-                                       f", tg_set_threads({cores})"},
+                             "sample": f"{a.steps} steps x {T} token(s) of this workload; {ref_source(kind)}"
+                                       f"{'' if cfg == 'c1' else ' + numpy router'}, tg_set_threads({cores})"},
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
+
+
+def scaling_of(a, cfg):
+    """"strong" when the job's total work is fixed as GPUs are added (one GPU,
+    or experts sharded), "weak" for data-parallel replicas."""
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    return "weak" if world > 1 and a.parallel == "dp" else "strong"
 
 
 def quiet_nccl():
@@ -301,18 +386,16 @@ def quiet_nccl():
 
 # ---- our arm ---------------------------------------------------------------
 
-def run_ours(a):
+def setup_gpu(a):
+    """Per-rank set-up: device, process group (N > 1), library and its stream."""
     import torch
     import torch.distributed as dist
 
     import tinygiant_b200 as tg
-    from tinygiant_b200.layer import ResidentLayer
-
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
-    if world != a.gpus:
-        a.gpus = world
+    a.gpus = world
     torch.cuda.set_device(local)
     if world > 1:
         from datetime import timedelta
@@ -322,7 +405,121 @@ def run_ours(a):
     lib.tg_cuda_set_device(local)
     stream = torch.cuda.Stream()
     lib.tg_cuda_set_stream(ctypes.c_void_p(stream.cuda_stream))
+    return world, rank, local, lib, stream
 
+
+def time_graph(lib, step, first, last, stream, world, local):
+    """Captures steps first .. last-1 in one CUDA graph, replays it once
+    untimed, soaks ~1.5 s of replays while nvidia-smi samples the clocks, then
+    times one replay with CUDA events on the library's stream (barrier +
+    synchronize on both sides; the max over ranks).  Returns (ms, our kernel
+    launches in the graph, clocks, graph)."""
+    import torch
+    import torch.distributed as dist
+
+    import tinygiant_b200 as tg
+    g = torch.cuda.CUDAGraph()
+    launches0 = lib.tg_cuda_launch_count()
+    with torch.cuda.graph(g, stream=stream):
+        for i in range(first, last):
+            step(i)
+    launches = lib.tg_cuda_launch_count() - launches0
+    tg.check(lib)
+    g.replay()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    clocks.start()
+    t_soak = time.perf_counter()
+    with torch.cuda.stream(stream):
+        while time.perf_counter() - t_soak < 1.5:
+            g.replay()
+            torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        ev0.record(stream)
+        g.replay()
+        ev1.record(stream)
+    torch.cuda.synchronize()
+    ms = ev0.elapsed_time(ev1)
+    if world > 1:
+        t = torch.tensor([ms], device=f"cuda:{local}")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    clk = clocks.stop()
+    tg.check(lib)
+    return ms, int(launches), clk, g
+
+
+def max_over_ranks(v, world, local):
+    if world == 1:
+        return v
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([v], device=f"cuda:{local}", dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def ep_balance(L, xs, world):
+    """Expert parallel (e % world == rank): per step the largest number of
+    distinct selected experts that one GPU holds, averaged over the steps."""
+    from tinygiant_b200 import synth
+    per = []
+    for x in xs:
+        experts, _, _, _ = synth.route(L, synth.rms_norm(x))
+        counts = np.bincount(np.asarray(experts) % world, minlength=world)
+        per.append(int(counts.max()))
+    return float(np.mean(per)), int(max(per))
+
+
+def engine_e2e(lib, L, xs, R, warm):
+    """The reference engine's own call sequence per step on one GPU: numpy
+    RMSNorm + router + top-k + expert union and row weights (synth.route,
+    engine.py:281-318), then tg_moe_forward_rows_v2 with host pointers and a
+    zero-filled host output (engine.py:323-341).  The R host copies of the
+    layer are registered as immutable (tg_cuda_register, as an integration
+    does for its mapped expert files) and uploaded by one warm call each."""
+    import tinygiant_b200 as tg
+    from tinygiant_b200 import moe, synth
+    copies = host_copies(L, R)
+    for c in copies:
+        for arr in c.gates + c.ups + c.downs:
+            if lib.tg_cuda_register(arr.ctypes.data, arr.nbytes) != 0:
+                tg.check(lib)
+        allw = np.ones((c.n_experts, 1), np.float32)
+        o = np.zeros((1, c.embed_dim), np.float32)
+        moe.moe_forward_rows_v2(lib, c.gates, c.ups, c.downs, c.gate_fmt, c.down_fmts, None, None, None, c.act,
+                                allw, xs[0][:1], o, c.embed_dim, c.inter_dim)
+    tg.check(lib)
+    for i in range(warm):
+        moe.moe_layer_forward(lib, copies[i % R], synth.rms_norm(xs[i]))
+    t0 = time.perf_counter()
+    for i in range(warm, len(xs)):
+        moe.moe_layer_forward(lib, copies[i % R], synth.rms_norm(xs[i]))
+    el = time.perf_counter() - t0
+    tg.check(lib)
+    n = len(xs) - warm
+    T = xs.shape[1]
+    for c in copies:
+        for arr in c.gates + c.ups + c.downs:
+            lib.tg_cuda_unregister(arr.ctypes.data)
+    return {"value": n * T / el, "unit": UNIT, "h2d_bytes_per_step": int(xs[0].nbytes),
+            "d2h_bytes_per_step": int(xs[0].nbytes),
+            "api": "engine sequence: numpy rmsnorm + router + top-k + union, then tg_moe_forward_rows_v2 "
+                   "(reference ABI, host pointers)", "ms_per_step": el / n * 1e3}
+
+
+def run_ours(a):
+    import torch
+    import torch.distributed as dist
+
+    import tinygiant_b200 as tg
+    from tinygiant_b200.layer import ResidentLayer
+
+    world, rank, local, lib, stream = setup_gpu(a)
     cfg = a.config
     T = a.tokens or 1
     L = make_layer(cfg)
@@ -354,51 +551,13 @@ def run_ours(a):
         if ep and not in_kernel:
             dist.all_reduce(out)
 
-    # warm-up (also exercises every copy once)
+    # warm-up: the W steps, and at least one step on every copy
     with torch.cuda.stream(stream):
-        for i in range(a.warmup):
-            step(i)
+        for i in range(max(a.warmup, R)):
+            step(i % S)
     torch.cuda.synchronize()
     tg.check(lib)
-
-    # capture the K timed steps in one graph
-    g = torch.cuda.CUDAGraph()
-    launches0 = lib.tg_cuda_launch_count()
-    with torch.cuda.graph(g, stream=stream):
-        for i in range(a.warmup, S):
-            step(i)
-    launches = lib.tg_cuda_launch_count() - launches0
-    tg.check(lib)
-    # one untimed replay so the graph's first-launch cost is not timed
-    g.replay()
-    torch.cuda.synchronize()
-
-    # Clocks are sampled over a ~1.5 s soak of untimed replays of the same
-    # graph and the timed replay that follows it (the timed region alone is
-    # shorter than nvidia-smi's sampling period).
-    clocks = ClockSampler(local)
-    clocks.start()
-    t_soak = time.perf_counter()
-    with torch.cuda.stream(stream):
-        while time.perf_counter() - t_soak < 1.5:
-            g.replay()
-            torch.cuda.synchronize()
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    with torch.cuda.stream(stream):
-        ev0.record(stream)
-        g.replay()
-        ev1.record(stream)
-    torch.cuda.synchronize()
-    ms = ev0.elapsed_time(ev1)
-    if world > 1:
-        t = torch.tensor([ms], device=f"cuda:{local}")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-    clk = clocks.stop()
-    tg.check(lib)
+    ms, launches, clk, g = time_graph(lib, step, a.warmup, S, stream, world, local)
 
     ms_step = ms / a.steps
     ranks_tokens = 1 if ep else world   # data-parallel ranks each process their own tokens
@@ -407,35 +566,42 @@ def run_ours(a):
     if rank == 0:
         nbytes = algorithmic_bytes(L, xs_host[a.warmup:])
         achieved = ranks_tokens * nbytes.sum() / (ms / 1e3) / 1e9
-        peak, peak_src = measured_peak()
-        peak *= world            # whole-job bytes against every GPU's HBM
+        peak1, peak_src = measured_peak()
+        peak = peak1 * world            # whole-job bytes against every GPU's HBM
         tr = traffic_from_profiles()
         roof = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                "traffic": (tr or {}).get(cfg),
-                "kernel": "fused MoE layer step (router + gate/up + down kernels), per step",
+                "traffic": (tr or {}).get(cfg) if world == 1 else None,
+                "traffic_source": "dram__bytes_read.sum + dram__bytes_write.sum per launch from an earlier ncu "
+                                  "capture of this workload (profiles/traffic.json), not this run",
+                "kernel": "fused MoE layer step (one kernel: router + gate/up + down), per step" if T <= 8 else
+                          "batched MoE layer step (routing kernels + grouped GEMMs), per step",
                 "algorithmic_bytes_per_step": float(nbytes.mean()), "peak_source": peak_src}
         line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": a.steps,
                 "warmup": a.warmup, "ms_per_step": ms_step, "higher_is_better": True,
-                "scaling": "strong" if ep or world == 1 else "weak",
-                "vs_baseline": None, "dtype": DTYPES.get(cfg, DTYPES["c2"]),
-                "data": "synthetic (seeded weights and inputs)",
-                "config": {**workload_desc(cfg, T, R, L), "parallelism": f"ep{world}" if ep else f"dp{world}",
-                           "expert_path": "fused step kernel" if T <= 8 else
-                                          ("matvec kernels" if a.matvec else "tcgen05 grouped GEMMs"),
-                           **({"ep_combine": "in the step kernel over NVLink" if in_kernel else "NCCL all-reduce"}
-                              if ep else {})},
-                "gbps": achieved, "clocks": clk, "roofline": roof, "gpu_launches": int(launches)}
+                "scaling": scaling_of(a, cfg), "vs_baseline": None, "dtype": DTYPES.get(cfg, DTYPES["c2"]),
+                "data": "synthetic (seeded weights and inputs)", "config": workload_desc(cfg, T, R, L),
+                "parallelism": f"ep{world}" if ep else f"dp{world}",
+                "expert_path": "fused step kernel" if T <= 8 else
+                               ("matvec kernels" if a.matvec else "tcgen05 grouped GEMMs"),
+                "gbps": achieved, "clocks": clk, "roofline": roof, "gpu_launches": launches}
+        if ep:
+            mean_max, worst = ep_balance(L, xs_host[a.warmup:], world)
+            busiest = mean_max * L.expert_bytes(0) + L.router_w.nbytes + 2 * T * D * 4
+            line["ep"] = {"combine": "in the step kernel over NVLink" if in_kernel else "NCCL all-reduce",
+                          "shard_rule": "expert e on GPU e % N",
+                          "max_local_experts_per_step": {"mean": mean_max, "max": worst},
+                          "busiest_gpu_hbm_frac": busiest / (ms_step / 1e3) / 1e9 / peak1}
 
     # e2e: one GPU through the C-ABI entry tg_layer_forward with host buffers
     # (synchronous, x in / MoE output out every step); several GPUs through
     # tg_layer_forward_dev with each step's x copied from pinned host memory
     # and its output read back, plus the all-reduce for ep; max over ranks.
-    e2e = None
     if world == 1:
         xh = [np.ascontiguousarray(x) for x in xs_host]
         outh = np.zeros((T, D), np.float32)
-        for i in range(min(a.warmup, S)):
-            layers[i % R].forward(xh[i], outh)
+        # every copy's per-layer graph is instantiated before the timed calls
+        for i in range(max(a.warmup, R)):
+            layers[i % R].forward(xh[i % S], outh)
         t0 = time.perf_counter()
         for i in range(a.warmup, S):
             lib.tg_layer_forward(layers[i % R].h, xh[i].ctypes.data, outh.ctypes.data, T, 1)
@@ -458,32 +624,110 @@ def run_ours(a):
                 opin.copy_(out, non_blocking=True)
             stream.synchronize()
 
-        for i in range(min(a.warmup, S)):
-            e2e_step(i)
+        for i in range(max(a.warmup, R)):
+            e2e_step(i % S)
         dist.barrier()
         t0 = time.perf_counter()
         for i in range(a.warmup, S):
             e2e_step(i)
-        el = time.perf_counter() - t0
-        t = torch.tensor([el], device=f"cuda:{local}")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        el = float(t.item())
+        el = max_over_ranks(time.perf_counter() - t0, world, local)
         tg.check(lib)
         e2e = {"value": ranks_tokens * a.steps * T / el, "unit": UNIT, "h2d_bytes_per_step": int(xs_host[0].nbytes),
                "d2h_bytes_per_step": int(opin.numel() * 4),
                "api": "tg_layer_forward_dev per rank, pinned host copies" +
                       (" + NCCL all-reduce" if ep and not in_kernel else " (shards combined in the step kernel)" if ep else ""),
                "ms_per_step": el / a.steps * 1e3}
-    if rank == 0:
-        line["e2e"] = e2e
-        if world == 1 and not a.no_cpu_baseline:
-            cb, _ = cpu_reference_run(L, xs_host[a.warmup:], budget_s=12.0)
-            line["cpu_baseline"] = cb
-        print(json.dumps(line), flush=True)
     del g
     for lay in layers:
         lay.close()
+    if rank == 0:
+        line["e2e"] = e2e
+        if world == 1 and T <= 8:
+            line["e2e_engine"] = engine_e2e(lib, L, xs_host, R, max(a.warmup, 1))
+        if world == 1 and not a.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_reference_run(cfg, host_copies(L, R), xs_host[a.warmup:], budget_s=12.0)
+        print(json.dumps(line), flush=True)
     if world > 1:
+        dist.destroy_process_group()
+
+
+def run_c1(a):
+    """C1: one all-Q4_K expert.  Device-timed: the expert as a one-expert
+    resident layer stepped without normalisation (router weight 1, so the step
+    writes 1.0 * y, what tg_expert_forward adds to a zeroed output), cycling
+    64 HBM copies.  e2e: tg_expert_forward with host buffers, cycling 64 host
+    copies (uploaded on first sight)."""
+    import torch
+
+    import tinygiant_b200 as tg
+    from tinygiant_b200 import quants as Q, synth
+    from tinygiant_b200.layer import ResidentLayer
+
+    world, rank, local, lib, stream = setup_gpu(a)
+    R = max(1, a.copies if a.copies != R_COPIES else C1_COPIES)
+    D, I = 2048, 768
+    e0 = synth.c1_expert(seed=0)
+    gb = Q.row_bytes(Q.FMT_Q4K, D) * I
+    L1 = synth.MoeLayer(D, I, Q.FMT_Q4K, 0, 1, gates=[e0[:gb]], ups=[e0[gb:2 * gb]], downs=[e0[2 * gb:]],
+                        down_fmts=[Q.FMT_Q4K], router_w=np.zeros((1, D), np.float32))
+    base = ResidentLayer(L1, max_tokens=1, lib=lib)
+    layers = [base] + [base.clone() for _ in range(R - 1)]
+    tg.check(lib)
+    S = a.warmup + a.steps
+    xs_host = step_inputs(S, 1, D, seed=4 + 1000 * rank)
+    xs = torch.from_numpy(xs_host).to(f"cuda:{local}")
+    out = torch.zeros((1, D), dtype=torch.float32, device=f"cuda:{local}")
+
+    def step(i):
+        lib.tg_layer_forward_dev(layers[i % R].h, xs[i].data_ptr(), None, None, out.data_ptr(), 1, 0, None)
+
+    with torch.cuda.stream(stream):
+        for i in range(max(a.warmup, R)):
+            step(i % S)
+    torch.cuda.synchronize()
+    tg.check(lib)
+    ms, launches, clk, g = time_graph(lib, step, a.warmup, S, stream, world, local)
+    del g
+    for lay in layers:
+        lay.close()
+    ms_step = ms / a.steps
+    # e2e through the reference ABI: tg_expert_forward(x, out += y) on host copies
+    copies = [e0] + [e0.copy() for _ in range(R - 1)]
+    xh = [np.ascontiguousarray(x[0]) for x in xs_host]
+    outh = np.zeros(D, np.float32)
+    for i in range(R):
+        lib.tg_expert_forward(copies[i].ctypes.data, xh[i % S].ctypes.data, outh.ctypes.data, 1.0, D, I)
+    tg.check(lib)
+    t0 = time.perf_counter()
+    for i in range(a.warmup, S):
+        outh[:] = 0.0
+        lib.tg_expert_forward(copies[i % R].ctypes.data, xh[i].ctypes.data, outh.ctypes.data, 1.0, D, I)
+    el = max_over_ranks(time.perf_counter() - t0, world, local)
+    tg.check(lib)
+    if rank == 0:
+        nbytes = float(e0.nbytes + 3 * D * 4)   # weights, x, out, the layer's router row
+        achieved = world * nbytes / (ms_step / 1e3) / 1e9
+        peak, peak_src = measured_peak()
+        peak *= world
+        line = {"metric": METRIC, "value": world * a.steps / (ms / 1e3), "unit": UNIT, "n_gpus": world,
+                "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms_step, "higher_is_better": True,
+                "scaling": "weak" if world > 1 else "strong", "vs_baseline": None, "dtype": DTYPES["c1"],
+                "data": "synthetic (seeded weights and inputs)", "config": workload_desc("c1", 1, R, None),
+                "parallelism": f"dp{world}", "expert_path": "fused step kernel (one expert, weight 1)",
+                "gbps": achieved, "clocks": clk,
+                "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                             "frac": achieved / peak, "traffic": None,
+                             "kernel": "fused step kernel on a one-expert layer, per call",
+                             "algorithmic_bytes_per_step": nbytes, "peak_source": peak_src},
+                "gpu_launches": launches,
+                "e2e": {"value": world * a.steps / el, "unit": UNIT, "h2d_bytes_per_step": D * 4,
+                        "d2h_bytes_per_step": D * 4, "api": "tg_expert_forward (reference ABI, host buffers)",
+                        "ms_per_step": el / a.steps * 1e3}}
+        if world == 1 and not a.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_reference_run("c1", copies, xs_host[a.warmup:, 0], budget_s=12.0)
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
         dist.destroy_process_group()
 
 
@@ -495,6 +739,18 @@ def n_layers(a):
     return a.layers if a.layers is not None else {"c4": 36, "c5": 48}.get(a.config, 1)
 
 
+def stack_desc(cfg, T, NL, L):
+    """The `config` of a C4 / C5 stack line (both arms)."""
+    desc = workload_desc("c4s" if cfg == "c4" else "c5", T, 1, L)
+    desc.pop("layer_copies")
+    desc.update({"layers": NL,
+                 "l2": f"inputs larger than L2: {NL} layers with per-layer routers ({NL} HBM copies of the experts "
+                       f"on the GPU arm, one host copy on the reference arm)",
+                 "step": f"{T} token(s) through the stack: per layer rmsnorm + router + top-k + experts + "
+                         f"residual add"})
+    return desc
+
+
 def run_stack(a):
     """C4 / C5: T tokens through an n-layer stack (x += MoE(rmsnorm(x)) per
     layer) per step."""
@@ -502,22 +758,9 @@ def run_stack(a):
     import torch.distributed as dist
 
     import tinygiant_b200 as tg
-    from tinygiant_b200 import synth
     from tinygiant_b200.layer import ResidentLayer
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    a.gpus = world
-    torch.cuda.set_device(local)
-    if world > 1:
-        from datetime import timedelta
-        quiet_nccl()
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
-    lib = tg.load()
-    lib.tg_cuda_set_device(local)
-    stream = torch.cuda.Stream()
-    lib.tg_cuda_set_stream(ctypes.c_void_p(stream.cuda_stream))
+    world, rank, local, lib, stream = setup_gpu(a)
     cfg = a.config
     T, NL = a.tokens or 1, n_layers(a)
     ep = world > 1 and a.parallel == "ep"
@@ -525,7 +768,8 @@ def run_stack(a):
     D = L.embed_dim
     base = ResidentLayer(L, max_tokens=T, lib=lib, shard=rank if ep else 0, n_shards=world if ep else 1)
     layers = [base] + [base.clone() for _ in range(NL - 1)]
-    for lay, rw in zip(layers, stack_routers(NL, L.n_experts, D)):
+    routers = stack_routers(NL, L.n_experts, D)
+    for lay, rw in zip(layers, routers):
         lay.set_router(rw)
     if a.matvec:
         for lay in layers:
@@ -567,38 +811,7 @@ def run_stack(a):
             step(i)
     torch.cuda.synchronize()
     tg.check(lib)
-    g = torch.cuda.CUDAGraph()
-    launches0 = lib.tg_cuda_launch_count()
-    with torch.cuda.graph(g, stream=stream):
-        for i in range(a.warmup, S):
-            step(i)
-    launches = lib.tg_cuda_launch_count() - launches0
-    tg.check(lib)
-    g.replay()
-    torch.cuda.synchronize()
-    clocks = ClockSampler(local)
-    clocks.start()
-    t_soak = time.perf_counter()
-    with torch.cuda.stream(stream):
-        while time.perf_counter() - t_soak < 1.5:
-            g.replay()
-            torch.cuda.synchronize()
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    with torch.cuda.stream(stream):
-        ev0.record(stream)
-        g.replay()
-        ev1.record(stream)
-    torch.cuda.synchronize()
-    ms = ev0.elapsed_time(ev1)
-    if world > 1:
-        t = torch.tensor([ms], device=f"cuda:{local}")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-    clk = clocks.stop()
-    tg.check(lib)
+    ms, launches, clk, g = time_graph(lib, step, a.warmup, S, stream, world, local)
     ranks_tokens = 1 if ep else world
     value = ranks_tokens * a.steps * T / (ms / 1e3)
 
@@ -621,11 +834,7 @@ def run_stack(a):
     t0 = time.perf_counter()
     for i in range(a.warmup, S):
         e2e_step(i)
-    el = time.perf_counter() - t0
-    if world > 1:
-        t = torch.tensor([el], device=f"cuda:{local}")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        el = float(t.item())
+    el = max_over_ranks(time.perf_counter() - t0, world, local)
     tg.check(lib)
     # distinct experts per layer (T > 1): from every layer's routing of the last step
     uniq = None
@@ -643,28 +852,25 @@ def run_stack(a):
         roof = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                 "traffic": None, "kernel": f"fused MoE layer step x {NL} layers per token",
                 "algorithmic_bytes_per_step": nbytes, "peak_source": peak_src}
-        desc = workload_desc("c4s" if cfg == "c4" else "c5", T, 1, L)
-        desc.update({"layers": NL, "l2": f"inputs larger than L2: {NL} distinct layers resident "
-                                       f"({NL * L.n_experts * L.expert_bytes(0) / 1e9 / (world if ep else 1):.1f} GB "
-                                       f"of experts per GPU)",
-                     "step": f"{T} token(s) through the stack: per layer rmsnorm + router + top-k + experts + "
-                             f"residual add",
-                     "expert_path": "fused step kernel" if T <= 8 else
-                                    ("matvec kernels" if a.matvec else "tcgen05 grouped GEMMs"),
-                     **({"distinct_experts_per_layer": uniq} if uniq is not None else {}),
-                     **({"ep_combine": "in the step kernel over NVLink" if in_kernel else "NCCL all-reduce"}
-                        if ep else {})})
         line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": a.steps,
                 "warmup": a.warmup, "ms_per_step": ms / a.steps, "higher_is_better": True,
-                "scaling": "strong" if ep or world == 1 else "weak", "vs_baseline": None,
+                "scaling": scaling_of(a, cfg), "vs_baseline": None,
                 "dtype": DTYPES[cfg], "data": "synthetic (seeded weights and inputs)",
-                "config": {**desc, "parallelism": f"ep{world}" if ep else f"dp{world}"},
-                "gbps": achieved, "clocks": clk, "roofline": roof, "gpu_launches": int(launches),
+                "config": stack_desc(cfg, T, NL, L), "parallelism": f"ep{world}" if ep else f"dp{world}",
+                "expert_path": "fused step kernel" if T <= 8 else
+                               ("matvec kernels" if a.matvec else "tcgen05 grouped GEMMs"),
+                "experts_per_gpu_gb": NL * L.n_experts * L.expert_bytes(0) / 1e9 / (world if ep else 1),
+                **({"distinct_experts_per_layer": uniq} if uniq is not None else {}),
+                **({"ep": {"combine": "in the step kernel over NVLink" if in_kernel else "NCCL all-reduce",
+                           "shard_rule": "expert e on GPU e % N"}} if ep else {}),
+                "gbps": achieved, "clocks": clk, "roofline": roof, "gpu_launches": launches,
                 "e2e": {"value": ranks_tokens * a.steps * T / el, "unit": UNIT,
                         "h2d_bytes_per_step": int(T * D * 4), "d2h_bytes_per_step": int(T * D * 4),
                         "api": "tg_stack_forward_dev with pinned host copies" if not ep or in_kernel else
                                "tg_layer_forward_dev per layer + NCCL all-reduce, pinned host copies",
                         "ms_per_step": el / a.steps * 1e3}}
+        if world == 1 and not a.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_reference_run(cfg, [L], xs_host[a.warmup:], budget_s=12.0, routers=routers)
         print(json.dumps(line), flush=True)
     del g
     for lay in layers:
@@ -815,6 +1021,113 @@ def run_cache(a):
     print(json.dumps(line), flush=True)
 
 
+# ---- diagnostics: the fused step's phase timeline ---------------------------
+
+TRACE_PHASES = [
+    ("launch -> inputs ready", 0, 1),
+    ("R: x + router rows (w0)", 1, 3),
+    ("R1: sums, partial logits (w0)", 3, 16),
+    ("R2: rr, logits (CTA)", 16, 17),
+    ("logits poll (w0)", 2, 9),
+    ("top-k, softmax (+plan) (w0)", 9, 14),
+    ("  sort network (w0)", 9, 22),
+    ("  top-k rounds (w0)", 22, 23),
+    ("  softmax (w0)", 23, 24),
+    ("  plan T=1 (w0)", 24, 14),
+    ("R3: Q8 of N (first R3 warp)", 20, 18),
+    ("S / R3 CTA sync (w0)", 14, 21),
+    ("plan (T>1)", 21, 4),
+    ("phase A (warp 0)", 4, 5),
+    ("hidden poll (warp 0)", 5, 6),
+    ("Q8 of hidden (warp 0)", 6, 15),
+    ("CTA sync", 15, 7),
+    ("phase B (warp 0)", 7, 8),
+]
+TRACE_WARP = ["A wait", "A compute", "A issue", "B wait", "B compute", "B issue"]
+TRACE_SLOTS = 32   # trace words per CTA
+
+
+def step_trace(lib, step, n_steps=1):
+    """Runs step() n_steps times with the step kernel's trace hook
+    (tg_cuda_step_trace) on; returns (phases, warps, counts): name -> array
+    over CTAs / warps for the last step, in microseconds (SM cycles converted
+    with each CTA's own global-timer span) or poll counts."""
+    import torch
+    grid = lib.tg_cuda_step_trace(None)
+    buf = torch.zeros(grid * TRACE_SLOTS + grid * 16 * 8, dtype=torch.int64, device="cuda")
+    torch.cuda.synchronize()
+    lib.tg_cuda_step_trace(ctypes.c_void_p(buf.data_ptr()))
+    try:
+        for _ in range(n_steps):
+            step()
+        torch.cuda.synchronize()
+    finally:
+        lib.tg_cuda_step_trace(None)
+    v = buf.cpu().numpy().astype(np.int64)
+    t = v[: grid * TRACE_SLOTS].reshape(grid, TRACE_SLOTS)
+    span_ns = (t[:, 13] - t[:, 12]).astype(np.float64)
+    span_cyc = (t[:, 8] - t[:, 0]).astype(np.float64)
+    cyc_per_us = np.median(span_cyc / np.maximum(span_ns, 1.0)) * 1000.0
+    phases = {name: (t[:, b] - t[:, a]) / cyc_per_us for name, a, b in TRACE_PHASES}
+    phases["whole step (CTA)"] = span_ns / 1000.0
+    wv = v[grid * TRACE_SLOTS:].reshape(grid * 16, 8)
+    w = wv[:, :6] / cyc_per_us
+    warps = {name: w[:, i] for i, name in enumerate(TRACE_WARP)}
+    warps["A end -> hidden ready"] = wv[:, 7] / cyc_per_us
+    counts = {"logits polls (CTA)": t[:, 19], "hidden polls (warp)": wv[:, 6]}
+    return phases, warps, counts
+
+
+def run_trace(a):
+    """--config trace [--gptoss] [--experts E] [--copies R] [--tokens T]: the
+    fused step's phase timeline (median and max over CTAs / warps), after one
+    idle step and for the last of 8 back-to-back steps.  Diagnostics only."""
+    import torch
+
+    import tinygiant_b200 as tg
+    from tinygiant_b200 import synth
+    from tinygiant_b200.layer import ResidentLayer
+
+    lib = tg.load()
+    E = a.experts or 128
+    T = a.tokens or 1
+    R = a.copies if a.copies != R_COPIES else 4
+    L = synth.gptoss_layer(seed=3, n_experts=E) if a.gptoss else synth.qwen_layer(seed=1, n_experts=E)
+    base = ResidentLayer(L, max_tokens=T, lib=lib)
+    lays = [base] + [base.clone() for _ in range(R - 1)]
+    stream = torch.cuda.Stream()
+    lib.tg_cuda_set_stream(ctypes.c_void_p(stream.cuda_stream))
+    x = torch.randn(T, L.embed_dim, device="cuda")
+    out = torch.zeros_like(x)
+    it = [0]
+
+    def step():
+        lay = lays[it[0] % len(lays)]
+        it[0] += 1
+        lib.tg_layer_forward_dev(lay.h, ctypes.c_void_p(x.data_ptr()), None, None, ctypes.c_void_p(out.data_ptr()),
+                                 T, 1, None)
+
+    try:
+        with torch.cuda.stream(stream):
+            for _ in range(20):
+                step()
+            torch.cuda.synchronize()
+            for tag, n in (("one step after idle", 1), ("last of 8 back-to-back steps", 8)):
+                phases, warps, counts = step_trace(lib, step, n)
+                print(f"== {tag}")
+                for name, d in phases.items():
+                    print(f"  {name:28s} median {np.median(d):7.2f} us   max {d.max():7.2f}")
+                for name, d in warps.items():
+                    print(f"  per-warp {name:21s} median {np.median(d):7.2f} us   max {d.max():7.2f}")
+                for name, d in counts.items():
+                    print(f"  {name:28s} median {np.median(d):7.1f}      max {d.max():7.0f}")
+        tg.check(lib)
+    finally:
+        lib.tg_cuda_set_stream(None)
+        for lay in lays:
+            lay.close()
+
+
 def main():
     a = parse()
     if a.config == "attn":
@@ -823,8 +1136,13 @@ def main():
     if a.config == "cache":
         run_cache(a)
         return
+    if a.config == "trace":
+        run_trace(a)
+        return
     if a.impl == "reference":
         run_reference(a)
+    elif a.config == "c1":
+        run_c1(a)
     elif is_stack(a):
         run_stack(a)
     else:

@@ -156,14 +156,20 @@ void tg_cuda_set_stream(void *stream);
 /* Declares [host_ptr, host_ptr + nbytes) as immutable weight bytes (e.g. a
  * whole mmap'd expert file): matrices inside it are uploaded to HBM on first
  * use and never re-checked.  Matrices outside any declared range are
- * uploaded on first use too, but every later call compares a 96-byte sample
- * of their host bytes and re-uploads on a change; a change that misses the
- * sample needs tg_cuda_unregister / tg_cuda_registry_clear.  0 on success. */
+ * uploaded on first use too, but every later call fingerprints all of their
+ * host bytes (one host pass, ~14 GB/s) and re-uploads on any change, so a
+ * buffer refilled with another expert's bytes is never served stale; a
+ * registered range skips that pass.  0 on success. */
 int tg_cuda_register(const void *host_ptr, size_t nbytes);
 int tg_cuda_unregister(const void *host_ptr);
 void tg_cuda_registry_clear(void);
 /* Bytes of HBM the registry holds. */
 size_t tg_cuda_registry_bytes(void);
+/* Registry counters: matrices uploaded again because their host bytes changed
+ * (an unregistered matrix's whole content is fingerprinted on every call that
+ * uses it), entries dropped because their host address came back with another
+ * shape or format, and the entries held now.  Any pointer may be NULL. */
+void tg_cuda_registry_stats(uint64_t *reuploads, uint64_t *evictions, size_t *entries);
 
 /* Number of kernels this library has launched since load. */
 uint64_t tg_cuda_launch_count(void);
@@ -259,13 +265,6 @@ int tg_cuda_debug_row_isums(int fmt, const void *mat, int nrows, int ncols, cons
  * results that differ (0 expected).  Returns 0, or -1 on error. */
 int tg_cuda_debug_div_check(long long n, unsigned seed, unsigned long long *mismatches);
 
-/* Q4_K / Q6_K packers (host, multi-threaded): rows x cols fp32 (cols a
- * multiple of 256) -> rows * tg_row_bytes(fmt, cols) bytes.  A per-sub-block
- * min/max affine fit (Q4_K) or signed max-abs fit (Q6_K) with 6-/8-bit
- * sub-block scales; the block layouts are the ones the kernels decode. */
-void tg_pack_q4k(const float *w, int rows, int cols, uint8_t *out);
-void tg_pack_q6k(const float *w, int rows, int cols, uint8_t *out);
-
 /* ---- Allocation-free matvec -------------------------------------------- *
  * No counterpart in the reference: an extension for callers that cannot
  * allocate device memory.  out[r] = row r of a Q4_K matrix . input, the
@@ -280,7 +279,9 @@ void tg_pack_q6k(const float *w, int rows, int cols, uint8_t *out);
  * Calls that overlap on one device (several streams or host threads in
  * flight at once) race on that scratch: order them on one stream.  The first
  * call on each device looks up the scratch address; make it outside any
- * stream capture.  Returns 0 when enqueued, else the error code that
+ * stream capture.  The address is kept until exit, so a device that the
+ * process resets (cudaDeviceReset) must not be used with this entry point
+ * afterwards.  Returns 0 when enqueued, else the error code that
  * tg_cuda_last_error reports. */
 int tg_cuda_matmul_q4k_noalloc(const uint8_t *q4_matrix, const float *input, float *output, int nrows, int ncols,
                                void *stream);

@@ -62,10 +62,17 @@ _HOOKS = {
 }
 
 
+def reference_dir():
+    """The reference checkout: $TG_REFERENCE_DIR, else `reference` beside this
+    repository.  Only the CPU checkers are built from it; nothing reads it at
+    run time on a GPU host."""
+    return Path(os.environ.get("TG_REFERENCE_DIR", HERE.parent.parent / "reference"))
+
+
 def build(quiet=True):
     """Runs oracle/Makefile (the _ref targets only where the reference exists)."""
     targets = ["libtg_oracle.so"]
-    ref = os.environ.get("TG_REFERENCE_DIR", "/root/reference")
+    ref = reference_dir()
     if Path(ref, "csrc", "libtinygiant.c").exists():
         targets.append("ref")
     subprocess.run(["make", "-C", str(HERE), f"REF={ref}", *targets], check=True,

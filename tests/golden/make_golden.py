@@ -26,7 +26,7 @@ sys.path.insert(0, str(ROOT))
 from oracle import oracle as O  # noqa: E402
 
 OUT = Path(__file__).resolve().parent
-REF = Path(os.environ.get("TG_REFERENCE_DIR", "/root/reference"))
+REF = Path(os.environ.get("TG_REFERENCE_DIR", Path(__file__).resolve().parents[3] / "reference"))
 
 VP, CI, CF = ctypes.c_void_p, ctypes.c_int, ctypes.c_float
 

@@ -46,7 +46,8 @@ def test_loader_mirrors_reference_search(lib):
 def test_reference_loader_binds_this_library(lib):
     """tinygiant/_lib.py of the reference (when the checkout is present)
     loads this .so unchanged."""
-    ref = Path(os.environ.get("TG_REFERENCE_DIR", "/root/reference"))
+    from oracle import oracle as O
+    ref = O.reference_dir()
     if not (ref / "tinygiant" / "_lib.py").exists():
         pytest.skip("reference checkout not present")
     import importlib.util
@@ -119,3 +120,46 @@ def test_decoders_match_golden_gguf_fixture():
     for name, fmt, cols in (("q4k", 0, 512), ("q6k", 2, 512), ("mxfp4", 3, 64)):
         ours = Q.DEQUANT[fmt](g[f"{name}_mat"], 8, cols)
         np.testing.assert_array_equal(ours, g[f"{name}_deq"])
+
+
+def test_noalloc_return_code_is_the_reported_error(lib):
+    """tg_cuda_matmul_q4k_noalloc returns the same code that
+    tg_cuda_last_error reports, for size errors and (without a GPU) for the
+    missing device; nothing is written to the output."""
+    out = np.full(8, 5.0, np.float32)
+    x = np.ones(256, np.float32)
+    mat = np.zeros(8 * 144, np.uint8)
+    for rows, cols in ((8, 200), (8, 65536 + 256), (0, 256)):
+        rc = lib.tg_cuda_matmul_q4k_noalloc(mat.ctypes.data, x.ctypes.data, out.ctypes.data, rows, cols, None)
+        code, msg = tg.last_error(lib)
+        assert rc == code == 3, (rc, code, msg)
+    if lib.tg_cuda_device_count() == 0:
+        rc = lib.tg_cuda_matmul_q4k_noalloc(mat.ctypes.data, x.ctypes.data, out.ctypes.data, 8, 256, None)
+        code, msg = tg.last_error(lib)
+        assert rc != 0 and rc == code, (rc, code, msg)
+    assert np.all(out == 5.0)
+
+
+def test_numpy_packers_golden():
+    """The numpy Q4_K / Q6_K packers against committed packed bytes
+    (tests/golden/packers.npz), edge blocks included: all-zero, all-positive,
+    constant, tiny and huge values."""
+    from conftest import golden
+    from tinygiant_b200 import quants as Q
+    g = golden("packers")
+    np.testing.assert_array_equal(Q.pack_q4k(g["w"]), g["q4k"])
+    np.testing.assert_array_equal(Q.pack_q6k(g["w"]), g["q6k"])
+
+
+def test_bindings_match_the_reference_loader_signatures():
+    """tinygiant_b200._lib.ABI gives each of the 21 symbols the argtypes and
+    restype that the reference's loader gives it (tests/golden/ref_abi.json,
+    recorded from tinygiant/_lib.py by tests/golden/make_ref_abi.py)."""
+    import ctypes
+    import json
+    from pathlib import Path
+    ref = json.loads((Path(__file__).resolve().parent / "golden" / "ref_abi.json").read_text())
+    assert set(ref) == set(_lib.ABI)
+    for name, (args, res) in _lib.ABI.items():
+        assert [t.__name__ for t in args] == ref[name]["argtypes"], name
+        assert (None if res is None else res.__name__) == ref[name]["restype"], name

@@ -71,9 +71,11 @@ def test_fused_step_matches_three_kernel_path(gpu, qwen16, T):
 
 
 @pytest.mark.parametrize("T", [1, 5])
-def test_fused_step_bit_exact_vs_reference_abi(gpu, qwen16, T):
+def test_fused_step_bit_exact_vs_gpu_abi_path(gpu, qwen16, T):
     """Given the step's own routing, its output equals the reference-ABI call
-    (tg_moe_forward_rows_v2) on the same rows bit for bit: the dots, the
+    as this library runs it on the GPU (tg_moe_forward_rows_v2) on the same
+    rows bit for bit (a GPU-vs-GPU check; the oracle checks are in
+    test_gpu_full_configs.py): the dots, the
     activation and the ordered combine are the same arithmetic."""
     L, R = qwen16
     N = synth.rms_norm(np.random.default_rng(400 + T).standard_normal((T, 2048)).astype(np.float32))
@@ -100,9 +102,9 @@ def gptoss8(gpu):
 
 
 @pytest.mark.parametrize("T", [1, 3])
-def test_fused_step_bit_exact_vs_reference_abi_mxfp4(gpu, gptoss8, T):
+def test_fused_step_bit_exact_vs_gpu_abi_path_mxfp4(gpu, gptoss8, T):
     """The MXFP4 (gpt-oss) fused step, whose rows are split over half warps
-    with the sub-block fold chained through the lanes, equals the
+    with the sub-block fold chained through the lanes, equals the GPU
     reference-ABI call on the step's own routing bit for bit."""
     L, R = gptoss8
     N = synth.rms_norm(np.random.default_rng(500 + T).standard_normal((T, L.embed_dim)).astype(np.float32))
@@ -145,10 +147,10 @@ def _abi_with_routing(gpu, L, N, idx, w):
 
 
 @pytest.mark.parametrize("T", [20, 64, 96])
-def test_tensor_core_step_bit_exact_vs_reference_abi(gpu, qwen16_batch, T):
+def test_tensor_core_step_bit_exact_vs_gpu_abi_path(gpu, qwen16_batch, T):
     """Batched steps on the tcgen05 grouped GEMMs (exact per-sub-block int32
     sums read back from tensor memory, the reference's fp32 folds, the
-    ordered combine) equal the reference-ABI call on the step's routing."""
+    ordered combine) equal the GPU reference-ABI call on the step's routing."""
     L, R = qwen16_batch
     N = synth.rms_norm(np.random.default_rng(600 + T).standard_normal((T, 2048)).astype(np.float32))
     got = R.forward(N, normalize=False)
@@ -175,7 +177,7 @@ def gptoss_batch(gpu):
 
 
 @pytest.mark.parametrize("T", [12, 40])
-def test_tensor_core_step_bit_exact_vs_reference_abi_mxfp4(gpu, gptoss_batch, T):
+def test_tensor_core_step_bit_exact_vs_gpu_abi_path_mxfp4(gpu, gptoss_batch, T):
     """MXFP4 (gpt-oss, D = I = 2880: the last Q8 block of a row holds two
     live sub-blocks) on the tcgen05 grouped GEMMs: codes unpacked to int8 in
     shared memory, one int8 MMA per 32-value sub-block; T = 12 over 32

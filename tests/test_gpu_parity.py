@@ -280,6 +280,53 @@ def test_registry_sees_changed_weights(gpu, oracle):
     assert not np.array_equal(a, b)
 
 
+def _registry_stats(lib):
+    r, e, n = ctypes.c_uint64(), ctypes.c_uint64(), ctypes.c_size_t()
+    lib.tg_cuda_registry_stats(ctypes.byref(r), ctypes.byref(e), ctypes.byref(n))
+    return r.value, e.value, n.value
+
+
+def test_registry_sees_any_changed_byte_and_reused_addresses(gpu, oracle):
+    """An unregistered host matrix is fingerprinted whole on every call: one
+    nibble rewritten anywhere (here in the middle of a block, away from the
+    matrix's first, middle and last 32 bytes) is uploaded again.  The same
+    host address reused with another shape drops the old entry and reuses its
+    HBM."""
+    rng = np.random.default_rng(15)
+    from tests.golden.make_golden import rand_q4k
+    rows, cols = 64, 512
+    mat = rand_q4k(rng, rows, cols)
+    x = rng.standard_normal(cols).astype(np.float32)
+
+    def run(lib, m, r, c):
+        o = np.zeros(r, np.float32)
+        lib.tg_matmul_q4k(m.ctypes.data, x[:c].ctypes.data, o.ctypes.data, r, c)
+        return o
+
+    run(gpu, mat, rows, cols)
+    ok(gpu)
+    re0, ev0, _ = _registry_stats(gpu)
+    for off in (1000, 144 * 37 + 100, mat.nbytes - 40):   # nibble bytes of blocks 6, 37 and the last
+        mat[off] ^= 0x5A
+        got, want = run(gpu, mat, rows, cols), run(oracle, mat, rows, cols)
+        ok(gpu)
+        assert np.array_equal(bits(got), bits(want)), off
+    re1, _, _ = _registry_stats(gpu)
+    assert re1 - re0 == 3
+    got = run(gpu, mat, rows, cols)      # unchanged bytes: no upload
+    ok(gpu)
+    assert _registry_stats(gpu)[0] == re1
+    # the same buffer as a 32 x 1024 matrix: the 64 x 512 entry is dropped
+    mat2 = mat.reshape(-1)[: 32 * 4 * 144]
+    assert mat2.ctypes.data == mat.ctypes.data
+    mat2[:] = rand_q4k(rng, 32, 1024)
+    x = rng.standard_normal(1024).astype(np.float32)
+    got, want = run(gpu, mat2, 32, 1024), run(oracle, mat2, 32, 1024)
+    ok(gpu)
+    assert np.array_equal(bits(got), bits(want))
+    assert _registry_stats(gpu)[1] > ev0
+
+
 def test_unsupported_formats_fail_loudly(gpu):
     rng = np.random.default_rng(6)
     gates, ups, downs = _tiny_layer(rng, E=1)

@@ -14,11 +14,9 @@ pytestmark = pytest.mark.gpu
 MAX_COLS = 65536
 
 
-def _q4k_matrix(lib, rng, rows, cols):
-    w = rng.standard_normal((rows, cols)).astype(np.float32)
-    out = np.empty(rows * lib.tg_row_bytes(0, cols), np.uint8)
-    lib.tg_pack_q4k(w.ctypes.data, rows, cols, out.ctypes.data)
-    return out
+def _q4k_matrix(rng, rows, cols):
+    from tinygiant_b200 import quants as Q
+    return Q.pack_q4k(rng.standard_normal((rows, cols)).astype(np.float32))
 
 
 def _host_matmul(lib, mat, x, rows, cols):
@@ -39,7 +37,7 @@ def test_noalloc_matches_tg_matmul_q4k_two_calls_in_a_row(gpu):
     lib = gpu
     rng = np.random.default_rng(20261201)
     cases = [(300, 2048), (96, MAX_COLS)]
-    mats = [_q4k_matrix(lib, rng, r, c) for r, c in cases]
+    mats = [_q4k_matrix(rng, r, c) for r, c in cases]
     xs = [rng.standard_normal(c).astype(np.float32) for _, c in cases]
     want = [_host_matmul(lib, m, x, r, c) for m, x, (r, c) in zip(mats, xs, cases)]
 
@@ -68,11 +66,19 @@ def test_noalloc_matches_tg_matmul_q4k_two_calls_in_a_row(gpu):
             got = d_outs[i].cpu().numpy()
             np.testing.assert_array_equal(got.view(np.uint32), want[i].view(np.uint32))
 
-    # Once set up, further calls allocate no device memory.
-    free0 = torch.cuda.mem_get_info(dev)[0]
-    assert call(0) == 0 and call(1) == 0
-    stream.synchronize()
-    assert torch.cuda.mem_get_info(dev)[0] == free0
+    # Once set up, further calls allocate no device memory.  The free-memory
+    # figure is device-wide, so another process can move it: any device
+    # allocation takes at least 2 MiB, so a drop of 1 MiB or more in every
+    # one of three tries fails the test.
+    drops = []
+    for _ in range(3):
+        free0 = torch.cuda.mem_get_info(dev)[0]
+        assert call(0) == 0 and call(1) == 0
+        stream.synchronize()
+        drops.append(free0 - torch.cuda.mem_get_info(dev)[0])
+        if drops[-1] < (1 << 20):
+            break
+    assert min(drops) < (1 << 20), drops
 
 
 def test_noalloc_rejects_sizes_beyond_its_scratch(gpu):

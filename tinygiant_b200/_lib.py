@@ -3,7 +3,7 @@
 `find_library()` and `load_tinygiant_lib(lib_path)` behave as the
 reference's tinygiant/_lib.py:9-95: the same search order, the same 21
 symbols with the same argtypes/restype.  `load_tinygiant_lib` additionally
-binds the library's extension entry points (tg_cuda_*, tg_pack_*).
+binds the library's extension entry points (tg_cuda_*, tg_layer_*).
 """
 import ctypes
 from pathlib import Path
@@ -55,6 +55,7 @@ EXT = {
     "tg_cuda_unregister": ([VP], CI),
     "tg_cuda_registry_clear": ([], None),
     "tg_cuda_registry_bytes": ([], SZ),
+    "tg_cuda_registry_stats": ([VP, VP, VP], None),
     "tg_cuda_launch_count": ([], ctypes.c_uint64),
     "tg_cuda_device_count": ([], CI),
     "tg_cuda_debug_quantize_q8": ([VP, CI, CI, VP], CI),
@@ -81,8 +82,6 @@ EXT = {
     "tg_cuda_graph_destroy": ([VP], None),
     "tg_cuda_stream": ([], VP),
     "tg_cuda_synchronize": ([], CI),
-    "tg_pack_q4k": ([VP, CI, CI, VP], None),
-    "tg_pack_q6k": ([VP, CI, CI, VP], None),
     "tg_cuda_matmul_q4k_noalloc": ([VP, VP, VP, CI, CI, VP], CI),
 }
 

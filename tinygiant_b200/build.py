@@ -25,7 +25,7 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ARCH + ["-O3", "-lineinfo", "--fmad=false", "-std=c++17", "-Xcompiler", "-fPIC,-O3",
                      "-I", str(ROOT / "include")]
 SOURCES = ["tg_kernels.cu", "tg_moe.cu", "tg_route.cu", "tg_runtime.cu", "tg_layer.cu", "tg_step.cu", "tg_gemm.cu",
-           "tg_attention.cu", "tg_noalloc.cu", "tg_pack.cpp"]
+           "tg_attention.cu", "tg_noalloc.cu"]
 HEADERS = list(CSRC.glob("*.cuh")) + list(CSRC.glob("*.h")) + [ROOT / "include" / "tinygiant.h"]
 
 

@@ -6,6 +6,7 @@
 // re-laid out so each row is one 16-byte-aligned window (WDesc below); the
 // values are unchanged.
 #pragma once
+#include <mutex>
 #include <cstdint>
 #include <cuda_runtime.h>
 
@@ -143,6 +144,8 @@ inline cudaError_t ensure_smem(const void* fn, size_t bytes) {
   struct Entry { const void* fn; size_t bytes; };
   static Entry table[32];
   static int n = 0;
+  static std::mutex mu;   // entry points that run without the runtime lock reach this too
+  std::lock_guard<std::mutex> lk(mu);
   for (int i = 0; i < n; i++)
     if (table[i].fn == fn) {
       if (table[i].bytes >= bytes) return cudaSuccess;

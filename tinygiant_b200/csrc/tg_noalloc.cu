@@ -30,19 +30,26 @@ static std::mutex g_noalloc_mu;
 static Q8Dev* g_noalloc_ptr[NOALLOC_MAX_DEVICES];
 
 // Device address of the scratch on the current device, looked up once per
-// device.  Must first run outside stream capture.
-static Q8Dev* noalloc_scratch(int dev) {
+// device (the first call on a device must therefore run outside stream
+// capture).  The address is kept for the life of the process: after a
+// cudaDeviceReset it would be stale, so a process that resets a device must
+// not call this entry point on that device again.  Returns 0 with *out set,
+// or the error code it recorded.
+static int noalloc_scratch(int dev, Q8Dev** out) {
   std::lock_guard<std::mutex> lk(g_noalloc_mu);
-  if (g_noalloc_ptr[dev]) return g_noalloc_ptr[dev];
-  Q8Dev* ptr = nullptr;
-  cudaError_t e = cudaGetSymbolAddress((void**)&ptr, g_noalloc_xq8);
-  if (e != cudaSuccess || !ptr) {
-    set_host_error(100 + (int)e, "tg_cuda_matmul_q4k_noalloc: cudaGetSymbolAddress on device %d: %s", dev,
-                   cudaGetErrorString(e));
-    return nullptr;
+  if (!g_noalloc_ptr[dev]) {
+    Q8Dev* ptr = nullptr;
+    cudaError_t e = cudaGetSymbolAddress((void**)&ptr, g_noalloc_xq8);
+    if (e != cudaSuccess || !ptr) {
+      const int code = 100 + (int)(e != cudaSuccess ? e : cudaErrorInvalidSymbol);
+      set_host_error(code, "tg_cuda_matmul_q4k_noalloc: cudaGetSymbolAddress on device %d: %s", dev,
+                     cudaGetErrorString(e));
+      return code;
+    }
+    g_noalloc_ptr[dev] = ptr;
   }
-  g_noalloc_ptr[dev] = ptr;
-  return ptr;
+  *out = g_noalloc_ptr[dev];
+  return 0;
 }
 
 static bool device_pointer(const void* p, int dev) {
@@ -83,8 +90,8 @@ extern "C" int tg_cuda_matmul_q4k_noalloc(const uint8_t* q4_matrix, const float*
     set_host_error(3, "%s: matrix, input and output must be device memory on the current device %d", what, dev);
     return 3;
   }
-  Q8Dev* xq8 = noalloc_scratch(dev);
-  if (!xq8) return 100;
+  Q8Dev* xq8 = nullptr;
+  if (const int rc = noalloc_scratch(dev, &xq8)) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   WDesc w{q4_matrix, nullptr, nullptr, FMT_Q4K, nrows, ncols, (ncols / QK) * Q4K_BYTES};
   launch_quantize_rows(input, 1, ncols, ncols, xq8, s);

@@ -12,6 +12,7 @@
 
 #include <algorithm>
 #include <atomic>
+#include <climits>
 #include <chrono>
 #include <cstdarg>
 #include <cstdio>
@@ -412,31 +413,34 @@ struct Slab {
   }
 };
 
-struct Sample {
-  size_t off[3];
-  uint8_t bytes[3][32];
-  int len[3];
-};
-
-static void take_sample(const uint8_t* h, size_t n, Sample& s) {
-  size_t offs[3] = {0, n / 2, n > 32 ? n - 32 : 0};
-  for (int i = 0; i < 3; i++) {
-    s.off[i] = offs[i];
-    s.len[i] = (int)std::min<size_t>(32, n - std::min(n, offs[i]));
-    memcpy(s.bytes[i], h + offs[i], s.len[i]);
+// Content fingerprint of an unregistered host matrix: four lanes of 64-bit
+// xor-rotate-multiply over 32-byte strides, then the tail.  Each lane's step
+// is a bijection of the lane state for a fixed input word, so a change to any
+// one word always changes the result; the reference reuses host buffers for
+// different experts (a pread buffer refilled with another expert's bytes), so
+// every byte counts, not a sample of them.  ~14 GB/s on one host core.
+static inline uint64_t rotl64(uint64_t x, int r) { return (x << r) | (x >> (64 - r)); }
+static uint64_t content_hash(const uint8_t* p, size_t n) {
+  constexpr uint64_t K = 0x9E3779B97F4A7C15ull;
+  uint64_t h0 = n, h1 = n ^ 0x243F6A8885A308D3ull, h2 = n ^ 0x13198A2E03707344ull, h3 = n ^ 0xA4093822299F31D0ull;
+  size_t i = 0;
+  for (; i + 32 <= n; i += 32) {
+    uint64_t w[4];
+    memcpy(w, p + i, 32);
+    h0 = rotl64(h0 ^ w[0], 29) * K;
+    h1 = rotl64(h1 ^ w[1], 29) * K;
+    h2 = rotl64(h2 ^ w[2], 29) * K;
+    h3 = rotl64(h3 ^ w[3], 29) * K;
   }
-}
-
-static bool sample_matches(const uint8_t* h, const Sample& s) {
-  for (int i = 0; i < 3; i++)
-    if (memcmp(s.bytes[i], h + s.off[i], s.len[i]) != 0) return false;
-  return true;
+  for (; i < n; i++) h0 = rotl64(h0 ^ p[i], 29) * K;
+  return rotl64(h0, 1) ^ rotl64(h1, 17) ^ rotl64(h2, 33) ^ rotl64(h3, 49);
 }
 
 struct Entry {
   WDesc w;
   size_t raw_bytes;
-  Sample sample;
+  size_t dev_bytes;   // the device allocation's size
+  uint64_t hash;      // content_hash of the host bytes last uploaded
 };
 
 // A registered raw byte range (tg_cuda_register): matrices inside it are
@@ -446,6 +450,7 @@ struct Range {
 };
 
 static Slab g_slab;
+static std::atomic<uint64_t> g_reuploads{0}, g_evictions{0};
 static std::map<std::tuple<uintptr_t, int, int, int>, Entry> g_mats;
 static std::map<uintptr_t, Range> g_ranges;
 
@@ -508,35 +513,55 @@ bool lookup_matrix(const void* hp, int fmt, int rows, int cols, WDesc* out) {
   }
   size_t raw = fmt == -1 ? (size_t)rows * cols * 4 : fmt == -2 ? (size_t)rows * 4 : (size_t)rows * host_row_bytes(fmt, cols);
   auto key = std::make_tuple((uintptr_t)h, fmt, rows, cols);
+  const bool trusted = in_registered_range((uintptr_t)h, raw);
   auto it = g_mats.find(key);
   if (it != g_mats.end()) {
-    if (!in_registered_range((uintptr_t)h, raw) && !sample_matches(h, it->second.sample)) {
-      take_sample(h, raw, it->second.sample);
-      if (!upload_into(h, raw, it->second.w)) return false;
+    if (!trusted) {
+      const uint64_t hv = content_hash(h, raw);
+      if (hv != it->second.hash) {
+        if (!upload_into(h, raw, it->second.w)) return false;
+        it->second.hash = hv;
+        g_reuploads++;
+      }
     }
     *out = it->second.w;
     return true;
+  }
+  // The same host address seen before with another shape or format: the
+  // caller has reused the buffer, so the old entries go, and their device
+  // allocation is reused when it is large enough.
+  const size_t need = (fmt == FMT_Q4K || fmt == FMT_Q6K || fmt == FMT_MXFP4 || fmt == FMT_Q80 || fmt == FMT_F16)
+                          ? (size_t)rows * row_layout(fmt, cols).rs
+                          : raw;
+  uint8_t* reuse = nullptr;
+  size_t reuse_bytes = 0;
+  for (auto jt = g_mats.lower_bound(std::make_tuple((uintptr_t)h, INT_MIN, INT_MIN, INT_MIN));
+       jt != g_mats.end() && std::get<0>(jt->first) == (uintptr_t)h;) {
+    if (!reuse && jt->second.dev_bytes >= need) {
+      reuse = const_cast<uint8_t*>(jt->second.w.main);
+      reuse_bytes = jt->second.dev_bytes;
+    }
+    jt = g_mats.erase(jt);
+    g_evictions++;
   }
   Entry e{};
   e.raw_bytes = raw;
   e.w.fmt = fmt;
   e.w.rows = rows;
   e.w.cols = cols;
+  uint8_t* m = reuse ? reuse : g_slab.alloc(need);
+  if (!m) return false;
+  e.dev_bytes = reuse ? reuse_bytes : need;
+  e.w.main = m;
   if (fmt == FMT_Q4K || fmt == FMT_Q6K || fmt == FMT_MXFP4 || fmt == FMT_Q80 || fmt == FMT_F16) {
     const RowLayout L = row_layout(fmt, cols);
-    uint8_t* m = g_slab.alloc((size_t)rows * L.rs);
-    if (!m) return false;
-    e.w.main = m;
     e.w.aux1 = L.a1 >= 0 ? m + L.a1 : nullptr;
     e.w.aux2 = L.a2 >= 0 ? m + L.a2 : nullptr;
     e.w.rs = L.rs;
   } else {
-    uint8_t* m = g_slab.alloc(raw);
-    if (!m) return false;
-    e.w.main = m;
     e.w.rs = fmt == -1 ? cols * 4 : 4;
   }
-  take_sample(h, raw, e.sample);
+  e.hash = trusted ? 0 : content_hash(h, raw);
   if (!upload_into(h, raw, e.w)) return false;
   g_mats[key] = e;
   *out = e.w;
@@ -768,6 +793,13 @@ size_t tg_cuda_registry_bytes(void) {
 }
 
 uint64_t tg_cuda_launch_count(void) { return g_launches.load(); }
+
+void tg_cuda_registry_stats(uint64_t* reuploads, uint64_t* evictions, size_t* entries) {
+  std::lock_guard<std::recursive_mutex> lk(g.mu);
+  if (reuploads) *reuploads = g_reuploads.load();
+  if (evictions) *evictions = g_evictions.load();
+  if (entries) *entries = g_mats.size();
+}
 
 size_t tg_row_bytes(int fmt, int ncols) { return host_row_bytes(fmt, ncols); }
 

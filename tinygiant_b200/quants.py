@@ -4,12 +4,13 @@ Layouts are TinyGiant's (csrc/libtinygiant.c): Q4_K 144-byte blocks of 256
 values (fp16 d, fp16 dmin, 12 bytes of 6-bit scales/mins, 128 bytes of
 nibbles), Q6_K 210-byte blocks (ql[128], qh[64], int8 scales[16], fp16 d),
 MXFP4 17-byte blocks of 32 (e8m0 exponent, 16 bytes of e2m1 nibbles).
-The packers run in the library (tg_pack_q4k / tg_pack_q6k); the decoders
-here restate the reference's decode for building float references.
+The packers (numpy, host only) make the synthetic weights; the reference
+has no quantizer, so they fill its block layouts with a plain per-sub-block
+fit.  The decoders restate the reference's decode for building float
+references.  Nothing here is on the GPU path, and nothing here loads the
+product library.
 """
 import numpy as np
-
-from . import load
 
 FMT_Q4K, FMT_F16, FMT_Q6K, FMT_MXFP4, FMT_Q80 = 0, 1, 2, 3, 4
 BLOCK = {FMT_Q4K: (256, 144), FMT_Q6K: (256, 210), FMT_MXFP4: (32, 17), FMT_Q80: (32, 34)}
@@ -24,22 +25,116 @@ def row_bytes(fmt, cols):
     return cols * 2
 
 
-def _pack(fn, fmt, w):
-    w = np.ascontiguousarray(w, dtype=np.float32)
-    rows, cols = w.shape
-    if cols % 256:
-        raise ValueError("cols must be a multiple of 256")
-    out = np.empty(rows * row_bytes(fmt, cols), dtype=np.uint8)
-    fn(w.ctypes.data, rows, cols, out.ctypes.data)
+# ---- packers ----------------------------------------------------------------
+#
+#   Q4_K : value ~= d*sc_j*q - dmin*m_j, q in [0,15]; per 32-value sub-block
+#          lo = min(min(x), 0), scale_j = (max(x) - lo)/15, min_j = -lo; the
+#          block's d = max(scale_j)/63 and dmin = max(min_j)/63 are stored as
+#          fp16, and sc_j, m_j are 6-bit roundings against them
+#          (layout: csrc/libtinygiant.c:139-155, 210-222).
+#   Q6_K : value ~= d*sc_j*(q - 32), q-32 in [-32,31]; per 16-value
+#          sub-block scale_j = v/-32 with v its first largest-magnitude value;
+#          d = max|scale_j|/127 (fp16), sc_j an int8 rounding
+#          (layout: csrc/libtinygiant.c:382-401).
+# All arithmetic is fp32 with round-to-nearest-even, so the bytes are a
+# deterministic function of the weights.
+
+def _f16_round(x):
+    """fp32 -> nearest-even fp16 -> fp32 (the stored scale and its value)."""
+    h = np.asarray(x, dtype=np.float32).astype(np.float16)
+    return h, h.astype(np.float32)
+
+
+def _chain(v, better, start=None):
+    """Left fold over the last axis of v keeping `cur` while better(cur, next)
+    holds, else taking `next` (so ties, +0 against -0 included, go to the later
+    element): the fmin / fmax chains of the C fit."""
+    cur = v[..., 0] if start is None else start
+    for j in range(0 if start is not None else 1, v.shape[-1]):
+        cur = np.where(better(cur, v[..., j]), cur, v[..., j])
+    return cur.astype(np.float32)
+
+
+def _rint_clip(v, lo, hi):
+    return np.clip(np.rint(v), lo, hi).astype(np.int32)
+
+
+def _pack_q4k_blocks(x):
+    """x: fp32 [nb, 256] -> uint8 [nb, 144]."""
+    nb = x.shape[0]
+    xs = x.reshape(nb, 8, 32)
+    lo, hi = _chain(xs, np.less), _chain(xs, np.greater)
+    lo = np.where(lo > 0, np.float32(0), lo).astype(np.float32)
+    scale = ((hi - lo) / np.float32(15)).astype(np.float32)
+    minv = (-lo).astype(np.float32)
+    max_scale = _chain(scale, np.greater, np.zeros(nb, np.float32))
+    max_min = _chain(minv, np.greater, np.zeros(nb, np.float32))
+    dh, d = _f16_round(max_scale / np.float32(63))
+    mh, dmin = _f16_round(max_min / np.float32(63))
+    with np.errstate(divide="ignore", invalid="ignore"):
+        sc = np.where(d[:, None] > 0, _rint_clip(scale / d[:, None], 0, 63), 0).astype(np.int32)
+        mn = np.where(dmin[:, None] > 0, _rint_clip(minv / dmin[:, None], 0, 63), 0).astype(np.int32)
+        step = (d[:, None] * sc.astype(np.float32)).astype(np.float32)
+        off = (dmin[:, None] * mn.astype(np.float32)).astype(np.float32)
+        q = np.where(step[:, :, None] > 0,
+                     _rint_clip((xs + off[:, :, None]) / step[:, :, None], 0, 15), 0).astype(np.uint8)
+    out = np.zeros((nb, 144), np.uint8)
+    out[:, 0:2] = dh.view(np.uint8).reshape(nb, 2)
+    out[:, 2:4] = mh.view(np.uint8).reshape(nb, 2)
+    s = np.zeros((nb, 12), np.int32)
+    s[:, 0:4] = sc[:, 0:4] & 63
+    s[:, 4:8] = mn[:, 0:4] & 63
+    s[:, 8:12] = (sc[:, 4:8] & 0xF) | ((mn[:, 4:8] & 0xF) << 4)
+    s[:, 0:4] |= (sc[:, 4:8] >> 4) << 6
+    s[:, 4:8] |= (mn[:, 4:8] >> 4) << 6
+    out[:, 4:16] = s.astype(np.uint8)
+    q = q.reshape(nb, 4, 2, 32)
+    out[:, 16:144] = (q[:, :, 0, :] | (q[:, :, 1, :] << 4)).reshape(nb, 128)
     return out
 
 
+def _pack_q6k_blocks(x):
+    nb = x.shape[0]
+    xs = x.reshape(nb, 16, 16)
+    idx = np.abs(xs).argmax(axis=2)
+    v = np.take_along_axis(xs, idx[:, :, None], axis=2)[:, :, 0]
+    scale = (v / np.float32(-32)).astype(np.float32)
+    max_abs = _chain(np.abs(scale), np.greater, np.zeros(nb, np.float32))
+    dh, d = _f16_round(max_abs / np.float32(127))
+    with np.errstate(divide="ignore", invalid="ignore"):
+        sc = np.where(d[:, None] > 0, _rint_clip(scale / d[:, None], -127, 127), 0).astype(np.int32)
+        step = (d[:, None] * sc.astype(np.float32)).astype(np.float32)
+        l = np.where(step[:, :, None] != 0, _rint_clip(xs / step[:, :, None], -32, 31), 0)
+    q = (l + 32).astype(np.int32).reshape(nb, 2, 4, 32)   # [h][quarter][l]
+    q1, q2, q3, q4 = q[:, :, 0], q[:, :, 1], q[:, :, 2], q[:, :, 3]
+    out = np.zeros((nb, 210), np.uint8)
+    ql = np.concatenate([(q1 & 15) | ((q3 & 15) << 4), (q2 & 15) | ((q4 & 15) << 4)], axis=2)  # [nb][2][64]
+    out[:, 0:128] = ql.reshape(nb, 128).astype(np.uint8)
+    qh = (q1 >> 4) | ((q2 >> 4) << 2) | ((q3 >> 4) << 4) | ((q4 >> 4) << 6)
+    out[:, 128:192] = qh.reshape(nb, 64).astype(np.uint8)
+    out[:, 192:208] = sc.astype(np.int8).view(np.uint8)
+    out[:, 208:210] = dh.view(np.uint8).reshape(nb, 2)
+    return out
+
+
+def _pack(blocks_fn, fmt, w):
+    w = np.ascontiguousarray(w, dtype=np.float32)
+    if w.ndim != 2 or w.shape[1] % 256:
+        raise ValueError("weights must be [rows, cols] with cols a multiple of 256")
+    rows, cols = w.shape
+    out = blocks_fn(w.reshape(-1, 256))
+    assert out.nbytes == rows * row_bytes(fmt, cols)
+    return out.reshape(-1)
+
+
 def pack_q4k(w):
-    return _pack(load().tg_pack_q4k, FMT_Q4K, w)
+    """fp32 [rows, cols] -> Q4_K rows (144-byte blocks), uint8."""
+    return _pack(_pack_q4k_blocks, FMT_Q4K, w)
 
 
 def pack_q6k(w):
-    return _pack(load().tg_pack_q6k, FMT_Q6K, w)
+    """fp32 [rows, cols] -> Q6_K rows (210-byte blocks), uint8."""
+    return _pack(_pack_q6k_blocks, FMT_Q6K, w)
 
 
 def mxfp4_random(rows, cols, rng, exp_lo=119, exp_hi=123):
