@@ -156,10 +156,12 @@ void tg_cuda_set_stream(void *stream);
 /* Declares [host_ptr, host_ptr + nbytes) as immutable weight bytes (e.g. a
  * whole mmap'd expert file): matrices inside it are uploaded to HBM on first
  * use and never re-checked.  Matrices outside any declared range are
- * uploaded on first use too, but every later call fingerprints all of their
- * host bytes (one host pass, ~14 GB/s) and re-uploads on any change, so a
- * buffer refilled with another expert's bytes is never served stale; a
- * registered range skips that pass.  0 on success. */
+ * uploaded on first use too, and every later call checks their host bytes
+ * against what was uploaded and re-uploads on a change (the policy is
+ * tg_cuda_set_weight_check's).  Register only bytes that stay fixed while
+ * registered (a mapped expert file); a buffer that is refilled (a pread
+ * buffer reused for another expert) must be unregistered before it is
+ * refilled, or left unregistered.  0 on success. */
 int tg_cuda_register(const void *host_ptr, size_t nbytes);
 int tg_cuda_unregister(const void *host_ptr);
 void tg_cuda_registry_clear(void);
@@ -169,6 +171,18 @@ size_t tg_cuda_registry_bytes(void);
  * (an unregistered matrix's whole content is fingerprinted on every call that
  * uses it), entries dropped because their host address came back with another
  * shape or format, and the entries held now.  Any pointer may be NULL. */
+/* Policy for unregistered host matrices; returns the previous one.
+ *   2 (default)  every byte is fingerprinted on every call that uses the
+ *                matrix: any change is seen; costs one host pass over the
+ *                weights per call (~14 GB/s), about what the reference's CPU
+ *                path reads per call;
+ *   1            a 96-byte sample (first, middle, last 32 bytes): sees a
+ *                buffer refilled with another expert's bytes, not an edit
+ *                elsewhere; a few microseconds;
+ *   0            no check: host weights never change after first use (the
+ *                reference's own assumption for its hot path).
+ * Registered ranges (tg_cuda_register) are never checked. */
+int tg_cuda_set_weight_check(int mode);
 void tg_cuda_registry_stats(uint64_t *reuploads, uint64_t *evictions, size_t *entries);
 
 /* Number of kernels this library has launched since load. */

@@ -287,7 +287,8 @@ def _registry_stats(lib):
 
 
 def test_registry_sees_any_changed_byte_and_reused_addresses(gpu, oracle):
-    """An unregistered host matrix is fingerprinted whole on every call: one
+    """An unregistered host matrix is fingerprinted whole on every call (the
+    default policy): one
     nibble rewritten anywhere (here in the middle of a block, away from the
     matrix's first, middle and last 32 bytes) is uploaded again.  The same
     host address reused with another shape drops the old entry and reuses its
@@ -303,6 +304,7 @@ def test_registry_sees_any_changed_byte_and_reused_addresses(gpu, oracle):
         lib.tg_matmul_q4k(m.ctypes.data, x[:c].ctypes.data, o.ctypes.data, r, c)
         return o
 
+    assert gpu.tg_cuda_set_weight_check(2) == 2     # the default: every byte
     run(gpu, mat, rows, cols)
     ok(gpu)
     re0, ev0, _ = _registry_stats(gpu)
@@ -325,6 +327,19 @@ def test_registry_sees_any_changed_byte_and_reused_addresses(gpu, oracle):
     ok(gpu)
     assert np.array_equal(bits(got), bits(want))
     assert _registry_stats(gpu)[1] > ev0
+    # the sampled policy misses an edit away from its samples; the
+    # registered-range path never checks
+    assert gpu.tg_cuda_set_weight_check(1) == 2
+    try:
+        base = run(gpu, mat2, 32, 1024)
+        mat2[1000] ^= 0x5A
+        assert np.array_equal(bits(run(gpu, mat2, 32, 1024)), bits(base))
+        mat2[0] ^= 0x01                             # inside the sample: seen
+        got, want = run(gpu, mat2, 32, 1024), run(oracle, mat2, 32, 1024)
+        ok(gpu)
+        assert np.array_equal(bits(got), bits(want))
+    finally:
+        gpu.tg_cuda_set_weight_check(2)
 
 
 def test_unsupported_formats_fail_loudly(gpu):

@@ -56,6 +56,7 @@ EXT = {
     "tg_cuda_registry_clear": ([], None),
     "tg_cuda_registry_bytes": ([], SZ),
     "tg_cuda_registry_stats": ([VP, VP, VP], None),
+    "tg_cuda_set_weight_check": ([CI], CI),
     "tg_cuda_launch_count": ([], ctypes.c_uint64),
     "tg_cuda_device_count": ([], CI),
     "tg_cuda_debug_quantize_q8": ([VP, CI, CI, VP], CI),

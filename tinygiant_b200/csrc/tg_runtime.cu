@@ -436,11 +436,28 @@ static uint64_t content_hash(const uint8_t* p, size_t n) {
   return rotl64(h0, 1) ^ rotl64(h1, 17) ^ rotl64(h2, 33) ^ rotl64(h3, 49);
 }
 
+// The check policy for unregistered host matrices (tg_cuda_set_weight_check):
+// 2 every byte fingerprinted per call (default), 1 a 96-byte sample (first,
+// middle and last 32 bytes), 0 none.
+static int g_check = 2;
+
+static uint64_t sample_hash(const uint8_t* h, size_t n) {
+  uint8_t buf[96] = {};
+  const size_t offs[3] = {0, n / 2, n > 32 ? n - 32 : 0};
+  for (int i = 0; i < 3; i++) memcpy(buf + 32 * i, h + offs[i], std::min<size_t>(32, n - std::min(n, offs[i])));
+  return content_hash(buf, sizeof buf) ^ n;
+}
+
+static uint64_t check_hash(const uint8_t* h, size_t n) {
+  return g_check == 2 ? content_hash(h, n) : g_check == 1 ? sample_hash(h, n) : 0;
+}
+
 struct Entry {
   WDesc w;
   size_t raw_bytes;
   size_t dev_bytes;   // the device allocation's size
-  uint64_t hash;      // content_hash of the host bytes last uploaded
+  uint64_t hash;      // check_hash of the host bytes last uploaded
+  int check;          // the policy that hash was taken under
 };
 
 // A registered raw byte range (tg_cuda_register): matrices inside it are
@@ -516,11 +533,12 @@ bool lookup_matrix(const void* hp, int fmt, int rows, int cols, WDesc* out) {
   const bool trusted = in_registered_range((uintptr_t)h, raw);
   auto it = g_mats.find(key);
   if (it != g_mats.end()) {
-    if (!trusted) {
-      const uint64_t hv = content_hash(h, raw);
-      if (hv != it->second.hash) {
+    if (!trusted && g_check) {
+      const uint64_t hv = check_hash(h, raw);
+      if (hv != it->second.hash || it->second.check != g_check) {
         if (!upload_into(h, raw, it->second.w)) return false;
         it->second.hash = hv;
+        it->second.check = g_check;
         g_reuploads++;
       }
     }
@@ -561,7 +579,8 @@ bool lookup_matrix(const void* hp, int fmt, int rows, int cols, WDesc* out) {
   } else {
     e.w.rs = fmt == -1 ? cols * 4 : 4;
   }
-  e.hash = trusted ? 0 : content_hash(h, raw);
+  e.hash = trusted ? 0 : check_hash(h, raw);
+  e.check = trusted ? 0 : g_check;
   if (!upload_into(h, raw, e.w)) return false;
   g_mats[key] = e;
   *out = e.w;
@@ -793,6 +812,13 @@ size_t tg_cuda_registry_bytes(void) {
 }
 
 uint64_t tg_cuda_launch_count(void) { return g_launches.load(); }
+
+int tg_cuda_set_weight_check(int mode) {
+  std::lock_guard<std::recursive_mutex> lk(g.mu);
+  const int prev = g_check;
+  if (mode >= 0 && mode <= 2) g_check = mode;
+  return prev;
+}
 
 void tg_cuda_registry_stats(uint64_t* reuploads, uint64_t* evictions, size_t* entries) {
   std::lock_guard<std::recursive_mutex> lk(g.mu);
