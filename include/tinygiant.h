@@ -230,6 +230,12 @@ int tg_layer_set_fused(void *layer, int on);
  * the whole layer's output.  Return 0, or -1 on error. */
 int tg_layer_ep_handle(void *layer, void *handle_out);
 int tg_layer_ep_connect(void *layer, const void *handles);
+/* Restarts the layer's step epochs at 1 (clears its exchange block, arrival
+ * counters and, for a shard, its receive block; synchronises).  After any
+ * shard of a layer saw an error, every shard calls it, with none of their
+ * steps in flight (between two barriers), so that all shards tag and expect
+ * the same epochs again.  0 on success. */
+int tg_layer_ep_reset(void *layer);
 /* 1 (default): batched steps (T > 8) run the expert GEMMs on the tensor
  * cores (tcgen05); 0: the matvec kernels.  Same results either way.  Returns
  * the previous setting. */
@@ -243,6 +249,14 @@ int tg_layer_set_router(void *layer, const float *router_w, const float *router_
  * slots 12/13, the logits poll count in slot 19; then 8 uint64 per warp of
  * ring and poll counters); NULL stops it.  Returns the step's grid size. */
 int tg_cuda_step_trace(void *dev_buf);
+/* Tests of the fused step's bounded waits (no device fault is involved):
+ * steps launched after this call give up on a poll of another CTA's or GPU's
+ * words after poll_limit polls (<= 0: the default, about a second) and
+ * record a timeout in the device status; CTA skip_logit_cta (-1: none)
+ * publishes no router logits, so every CTA's logits poll runs out.  Steps
+ * already captured in a CUDA graph keep the settings they were captured
+ * with.  Returns 0. */
+int tg_cuda_debug_step_fault(int skip_logit_cta, int poll_limit);
 /* Host buffers, synchronous: out[T][D] += experts(normalize ? rmsnorm(x) : x). */
 int tg_layer_forward(void *layer, const float *x_host, float *out_host, int T, int normalize);
 /* Selected experts and weights [T][top_k] of the layer's last step. */

@@ -137,3 +137,145 @@ def test_expert_shards_two_gpus(in_kernel):
         p.join(timeout=180)
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
     assert q.get(timeout=5) <= TOL
+
+
+# ---- failure agreement across shards (layer.EpStepper) ----------------------
+
+class _FakeShardLayer:
+    """Stands in for a ResidentLayer: its epoch is the count of steps since
+    the last reset, as the step kernel's launch counter is."""
+
+    def __init__(self):
+        self.epoch = 0
+        self.resets = 0
+
+    def ep_reset(self):
+        self.epoch = 0
+        self.resets += 1
+
+
+def _stepper_rank(rank, world, port, q, fail_at, peer_sees_failure):
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+    from tinygiant_b200.layer import EpStepper
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=60))
+    try:
+        lay = _FakeShardLayer()
+        stepper = EpStepper([lay])
+        log = []
+        for i in range(1, 7):
+            def step():
+                lay.epoch += 1
+                epochs = [None] * world
+                dist.all_gather_object(epochs, lay.epoch)
+                if rank == 1 and i == fail_at:
+                    lay.epoch = 0          # the failing shard's runtime resets only itself
+                    raise RuntimeError("injected: a wait ran out")
+                # the in-kernel combine only completes when every shard tags the same epoch
+                same = len(set(epochs)) == 1
+                return same and not (peer_sees_failure and i == fail_at)
+            ok = stepper(step)
+            epochs = [None] * world
+            dist.all_gather_object(epochs, lay.epoch)
+            log.append((ok, tuple(epochs)))
+        if rank == 0:
+            q.put((log, lay.resets, stepper.resets))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("peer_sees_failure", [False, True])
+def test_ep_stepper_resyncs_epochs_on_cpu_ranks(peer_sees_failure):
+    """Rank 1's step fails at step 3 (its runtime resets its own epochs); with
+    or without rank 0 seeing a failure of its own, both shards agree the step
+    failed, both restart their epochs, and every later step succeeds with
+    equal epochs on both."""
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_stepper_rank, args=(r, 2, port, q, 3, peer_sees_failure)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    log, resets, stepper_resets = q.get(timeout=5)
+    assert [ok for ok, _ in log] == [True, True, False, True, True, True]
+    assert resets == 1 and stepper_resets == 1
+    for ok, epochs in log:
+        assert len(set(epochs)) == 1
+    assert [e[0] for _, e in log] == [1, 2, 0, 1, 2, 3]
+
+
+def _skip_rank(rank, world, port, q):
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+    import tinygiant_b200 as tg
+    from tinygiant_b200.layer import EpStepper, ResidentLayer
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        lib = tg.load()
+        lib.tg_cuda_set_device(rank)
+        L, N = _layer(), _rows()
+        shard = ResidentLayer(L, max_tokens=N.shape[0], lib=lib, shard=rank, n_shards=world)
+        shard.ep_connect()
+        lib.tg_cuda_set_stream(None)
+        lib.tg_cuda_debug_step_fault(-1, 1 << 14)     # waits give up after ~ms, not ~1 s
+        x = torch.from_numpy(N).cuda()
+        out = torch.zeros_like(x)
+        stepper = EpStepper([shard])
+        oks = []
+        for i in range(5):
+            def step():
+                if rank == 1 and i == 2:
+                    return True                      # this shard does not launch step 2
+                assert lib.tg_layer_forward_dev(shard.h, ctypes.c_void_p(x.data_ptr()), None, None,
+                                                ctypes.c_void_p(out.data_ptr()), N.shape[0], 0, None) == 0
+                ok = lib.tg_cuda_synchronize() == 0
+                code, msg = tg.last_error(lib)
+                if rank == 0 and i == 2:
+                    q.put(("peer", code, msg))
+                return ok and code == 0
+            oks.append(stepper(step))
+        lib.tg_cuda_debug_step_fault(-1, 0)
+        if rank == 0:
+            whole = ResidentLayer(L, max_tokens=N.shape[0], lib=lib).forward(N, normalize=False)
+            got = out.cpu().numpy()
+            q.put(("end", oks, float(np.max(np.abs(got - whole)) / np.max(np.abs(whole)))))
+        shard.close()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.gpu
+def test_shard_that_skips_a_step_makes_its_peer_time_out_then_both_recover():
+    """Two GPUs, the in-kernel combine: shard 1 skips step 2 (between steps,
+    nothing of it in flight); shard 0's combine poll runs out and is reported
+    (device error 2 at site 38); EpStepper restarts both shards' epochs and
+    steps 3 and 4 give the unsharded layer's output."""
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_skip_rank, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=180)
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    got = dict((m[0], m[1:]) for m in (q.get(timeout=5), q.get(timeout=5)))
+    code, msg = got["peer"]
+    assert code == 202 and "site 38" in msg, (code, msg)
+    oks, err = got["end"]
+    assert oks == [True, True, False, True, True]
+    assert err <= TOL

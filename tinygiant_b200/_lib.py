@@ -71,9 +71,11 @@ EXT = {
     "tg_layer_set_fused": ([VP, CI], CI),
     "tg_layer_ep_handle": ([VP, VP], CI),
     "tg_layer_ep_connect": ([VP, VP], CI),
+    "tg_layer_ep_reset": ([VP], CI),
     "tg_layer_set_tc": ([VP, CI], CI),
     "tg_layer_set_router": ([VP, VP, VP], CI),
     "tg_cuda_step_trace": ([VP], CI),
+    "tg_cuda_debug_step_fault": ([CI, CI], CI),
     "tg_layer_forward": ([VP, VP, VP, CI, CI], CI),
     "tg_layer_last_routing": ([VP, CI, VP, VP], CI),
     "tg_stack_forward_dev": ([VP, CI, VP, CI, VP], CI),

@@ -455,6 +455,37 @@ size_t tg_layer_expert_bytes(void* handle, int e) {
 // Diagnostics: fused steps launched after this call record per-CTA phase
 // timestamps into dev_buf ([grid][16] uint64, device memory); NULL stops it.
 // Returns the grid size a fused step uses.
+// Restarts the layer's step epochs at 1: clears its exchange block (launch
+// counter, tagged logits and hidden words), its arrival counters and, for an
+// expert-parallel shard, its receive block, then synchronises.  The shards of
+// one layer call it together, with no step of theirs in flight (between a
+// barrier after their last step and one before their next), after any of
+// them saw an error: a shard that reset alone would tag its words with
+// epochs its peers no longer wait for.
+int tg_layer_ep_reset(void* handle) {
+  std::lock_guard<std::recursive_mutex> lk(ctx_mutex());
+  Layer* L = (Layer*)handle;
+  if (!L || !ensure_init()) return -1;
+  cudaStream_t s = stream();
+  bool ok = cudaMemsetAsync(L->step_sync, 0, sizeof(unsigned long long) * step_sync_words(L->max_tokens, L->E,
+                                                                                          L->top_k, L->I), s) ==
+            cudaSuccess;
+  ok = ok && cudaMemsetAsync(L->counters, 0, sizeof(int) * moe_counter_ints(L->max_slots, L->I), s) == cudaSuccess;
+  if (L->ep_recv) ok = ok && cudaMemsetAsync(L->ep_recv, 0, ep_recv_bytes(L), s) == cudaSuccess;
+  ok = ok && cudaStreamSynchronize(s) == cudaSuccess;
+  if (!ok) {
+    const cudaError_t e = cudaGetLastError();
+    set_host_error(100 + (int)e, "tg_layer_ep_reset: %s", cudaGetErrorString(e));
+    return -1;
+  }
+  return 0;
+}
+
+int tg_cuda_debug_step_fault(int skip_logit_cta, int poll_limit) {
+  set_step_fault(skip_logit_cta, poll_limit);
+  return 0;
+}
+
 int tg_cuda_step_trace(void* dev_buf) {
   set_step_trace(dev_buf);
   int dev = 0, sms = 0;

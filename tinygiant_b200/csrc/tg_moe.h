@@ -131,6 +131,11 @@ cudaError_t launch_layer_step(const StepLaunch& l, cudaStream_t s);
 // Diagnostics: later step launches write [grid][16] phase timestamps to p
 // (device memory; null turns it off).
 void set_step_trace(void* p);
+// Tests of the bounded waits: later step launches give up after poll_limit
+// polls of another CTA's or GPU's words (<= 0: the default, about a second),
+// and CTA skip_logit_cta (-1: none) publishes no logits, so every CTA's
+// logits poll runs out and the step reports a timeout.
+void set_step_fault(int skip_logit_cta, int poll_limit);
 cudaError_t launch_layer_route(const RouteArgs& a, cudaStream_t s);
 // Batched steps on the tensor cores (tg_gemm.cu): for a plan written by the
 // route kernel, the gate/up and down grouped GEMMs (tcgen05, exact per

@@ -72,6 +72,13 @@ class ResidentLayer:
             check(self.lib)
             raise RuntimeError("tg_layer_ep_connect failed")
 
+    def ep_reset(self):
+        """Restart this layer's step epochs at 1 (tg_layer_ep_reset); see
+        EpStepper for when shards call it."""
+        if self.lib.tg_layer_ep_reset(self.h) != 0:
+            check(self.lib)
+            raise RuntimeError("tg_layer_ep_reset failed")
+
     def set_tc(self, on=True):
         """Tensor-core grouped GEMMs (default) or matvec kernels for batched steps (T > 8)."""
         return bool(self.lib.tg_layer_set_tc(self.h, int(bool(on))))
@@ -104,3 +111,49 @@ class ResidentLayer:
         if self.h:
             self.lib.tg_layer_destroy(self.h)
             self.h = None
+
+
+class EpStepper:
+    """Agreement on the outcome of expert-parallel steps across shards.
+
+    The shards of a layer combine their parts inside the step kernel, each
+    word tagged with the step's epoch (the layer's launch count), so every
+    shard must count the same steps.  A shard whose step fails (a bounded
+    wait ran out because a peer did not step, or any device error) resets its
+    own exchange state; its peers, whose steps may have failed or not, keep
+    counting.  So after every step the shards all-reduce a failure flag over
+    the host process group (torch.distributed, any backend), and on any
+    failure every shard resets the layers' epochs between two barriers
+    (ep_reset) and reports the step as failed; the next step starts at epoch
+    1 everywhere.
+
+    step: a callable running one step on this shard and returning True on
+    success (it synchronises and checks the device status itself); layers:
+    objects with ep_reset() (ResidentLayer).  The collectives are the same on
+    every shard and in the same order, whatever the outcome.
+    """
+
+    def __init__(self, layers, group=None):
+        self.layers = list(layers)
+        self.group = group
+        self.resets = 0
+
+    def __call__(self, step):
+        import torch
+        import torch.distributed as dist
+        try:
+            ok = bool(step())
+        except Exception:          # a failed step is reported, never skipped by peers
+            ok = False
+        backend = dist.get_backend(self.group)
+        dev = torch.device("cuda", torch.cuda.current_device()) if backend == "nccl" else torch.device("cpu")
+        flag = torch.tensor([0 if ok else 1], dtype=torch.int32, device=dev)
+        dist.all_reduce(flag, op=dist.ReduceOp.MAX, group=self.group)
+        if int(flag.item()) == 0:
+            return True
+        dist.barrier(group=self.group)
+        for lay in self.layers:
+            lay.ep_reset()
+        dist.barrier(group=self.group)
+        self.resets += 1
+        return False
