@@ -13,15 +13,11 @@
 //                                                      (moe_phase_b 1329-1384, 1428-1434)
 // One CTA per SM.  R runs one warp per expert (its router row); every CTA
 // quantizes N itself and repeats S on its own (both are tiny) instead of
-// waiting for one CTA to publish them.  For A and B each CTA owns an equal
-// share of the step: a contiguous run of the (slot, row) units of phase A
-// and a contiguous run of output rows of phase B.  Its weight rows arrive by
-// bulk asynchronous copies (cp.async.bulk, no multicast) as chunks in a
-// CTA-wide pool of shared-memory stages, in the order they are consumed
-// (phase A's, then phase B's); when the pool holds every chunk of the share
-// (a decode step at T = 1) all of them are issued at once, so the down
-// weights land while phase A computes, and otherwise each chunk's last
-// consumer issues the chunk that follows it into the freed stage.
+// waiting for one CTA to publish them.  A and B stream their weight rows
+// through a per-warp ring of shared-memory stages filled by bulk
+// asynchronous copies (cp.async.bulk, no multicast): the ring runs straight
+// from a warp's gate/up items into its down items, so the down weights are
+// in flight while phase A computes.
 //
 // There is no grid-wide barrier.  The two values CTAs exchange — router
 // logits and hidden activations — are written as 64-bit words holding the
@@ -44,7 +40,7 @@
 namespace tg {
 
 constexpr int SW = 16;             // warps per CTA
-constexpr int STEP_POOL_MAX = 32;  // pool stages per CTA
+constexpr int ST_MAX_NST = 8;      // ring stages per warp
 constexpr int STEP_T_MAX = 8;
 constexpr int STEP_K_MAX = 8;
 constexpr int STEP_R_MAX = STEP_T_MAX * STEP_K_MAX;   // active rows
@@ -74,11 +70,7 @@ struct StepShared {
   uint64_t xbar, ebar;
   float accw[SW][STEP_T_MAX];
   unsigned long long tw[SW][8];
-  uint64_t full[STEP_POOL_MAX];   // pool stage k: its current chunk has landed
-  int done[STEP_POOL_MAX];        // consumers finished with stage k's current chunk
-  int last_iss[STEP_POOL_MAX];    // the last chunk issued into stage k, or -1
-  int segc[STEP_R_MAX + 1];       // first phase-A chunk of each slot segment
-  int nach, nch;                  // phase-A chunks, all chunks
+  uint64_t bars[SW][ST_MAX_NST];
 };
 
 // ---------------------------------------------------------------------
@@ -196,12 +188,12 @@ struct StepArgs {
   int ep_rank, ep_world;      // expert-parallel combine in the kernel (ep_world 1: off)
   unsigned long long* const* ep_peers;   // [ep_world] every shard's receive block
   const unsigned long long* ep_recv;     // this shard's receive block [ep_world][T][D]
-  uint32_t stage_bytes;   // pool stage size
-  int nst;                // pool stages
+  uint32_t stage_bytes;   // ring stage size
+  int nst;                // ring stages per warp
   int xcap;               // active rows whose Q8 hidden blocks fit each CTA's shared memory
   int rwc;                // router rows staged per CTA
-  int cra, crb;           // rows per phase-A chunk (gate and up each), per phase-B chunk
-  int sb;                 // slots per phase-B group
+  int pa;                 // row pairs per phase-A item
+  int sb;                 // slots per phase-B item
   int sl;                 // phase-B lanes per block (slot lanes), a power of two
   DevStatus* st;
   unsigned long long* trace;   // [gridDim.x][16] phase timestamps, or null
@@ -223,6 +215,54 @@ __device__ __forceinline__ unsigned long long gtimer() {
       a.trace[blockIdx.x * 32 + (i)] = (unsigned long long)clock64();                       \
   } while (0)
 
+// A warp's position in its stream of items: phase 0 = gate/up item a (slot
+// a / I, row a % I); phase 1 = output row r, slots s .. s + SB - 1.
+struct SCur {
+  int ph;
+  int a, r;
+  int s;
+};
+
+__device__ __forceinline__ bool scur_next(SCur& c, int gw, int NW, int nA, int D, int n_slots, int SB) {
+  if (c.ph == 0) {
+    c.a += NW;
+    if (c.a < nA) return true;
+    c.ph = 1;
+    c.r = gw;
+    c.s = 0;
+    return n_slots > 0 && c.r < D;
+  }
+  c.s += SB;
+  if (c.s < n_slots) return true;
+  c.s = 0;
+  c.r += NW;
+  return c.r < D;
+}
+
+// Lane 0 of a warp: the bulk copies of item c into stage dst (completing on
+// bar).  Phase 0: rows r0 .. r0 + nr - 1 of the slot's gate (at dst) and up
+// (at dst + ghalf); phase 1: row c.r of the down matrices of slots c.s ..
+// c.s + SB - 1, dr bytes apart.  Not inlined: the ring calls it from three
+// places.
+template <int GF, int DF>
+static __device__ __noinline__ void step_issue(const StepExpert* sx, SCur c, uint8_t* dst, uint64_t* bar, int nrb,
+                                               int pa, int I, int D, uint32_t ghalf, uint32_t dr, int n_slots,
+                                               int SB) {
+  if (c.ph == 0) {
+    const int s = c.a / nrb, r0 = (c.a - s * nrb) * pa, nr = min(pa, I - r0);
+    const WDesc Gw = wdesc<GF>(sx[s].g, I, D), Uw = wdesc<GF>(sx[s].u, I, D);
+    mbar_arrive_expect_tx(bar, row_tx(Gw, r0, nr) + row_tx(Uw, r0, nr));
+    stage_row(Gw, r0, dst, bar, nr);
+    stage_row(Uw, r0, dst + ghalf, bar, nr);
+  } else {
+    const int s1 = min(n_slots, c.s + SB);
+    uint32_t tx = 0;
+    for (int s = c.s; s < s1; s++) tx += row_tx(wdesc<DF>(sx[s].d, D, I), (int)c.r);
+    mbar_arrive_expect_tx(bar, tx);
+    for (int s = c.s; s < s1; s++) stage_row(wdesc<DF>(sx[s].d, D, I), (int)c.r, dst + (s - c.s) * dr, bar);
+  }
+}
+
 template <int GF, int DF>
 __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
   extern __shared__ __align__(128) uint8_t dsm[];
@@ -230,15 +270,16 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, tid = threadIdx.x;
   const int T = a.T, D = a.D, E = a.E, K = a.top_k, I = a.I;
   const int G = gridDim.x;
+  // work items go to warps CTA-interleaved, so every SM gets an even share
+  const int gw = wid * G + blockIdx.x, NW = G * SW;
   const int gbpr = (D + QK - 1) / QK, dbpr = (I + QK - 1) / QK;
-  // the chunk pool [nst][stage_bytes] first; phase R borrows it for x (at its
-  // start) and this CTA's router rows (at its end) before any chunk is issued
-  const size_t pool_bytes = (size_t)a.nst * a.stage_bytes, rrow_bytes = round16((size_t)a.rwc * D * 4);
-  float* rrow = reinterpret_cast<float*>(dsm + pool_bytes - rrow_bytes);   // [rwc][D]
-  XQ* xa = reinterpret_cast<XQ*>(dsm + pool_bytes);   // [T][gbpr]
+  uint8_t* ring = dsm + (size_t)wid * a.nst * a.stage_bytes;
+  float* rrow = reinterpret_cast<float*>(dsm + (size_t)SW * a.nst * a.stage_bytes);   // [rwc][D]
+  XQ* xa = reinterpret_cast<XQ*>(reinterpret_cast<uint8_t*>(rrow) + round16((size_t)a.rwc * D * 4));   // [T][gbpr]
   XQ* xs = xa + (size_t)T * gbpr;   // [xcap][dbpr]
   StepExpert* sx = reinterpret_cast<StepExpert*>(xs + (size_t)a.xcap * dbpr);   // [xcap] the slots' experts
   StepExpert* etab = sx + a.xcap;                                                 // [E]
+  uint64_t* bar = sh.bars[wid];
   if (a.trace && tid == 0) a.trace[blockIdx.x * 32 + 12] = gtimer();
   if (wid == 0) TG_MARK(0);
 
@@ -249,9 +290,9 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
   const bool wbulk = wid < nrw;
   const float* wsrc = a.router_w + (size_t)(blockIdx.x + wid * G) * D;
   if (lane == 0) {
+    for (int i = 0; i < a.nst; i++) mbar_init(&bar[i], 1);
     mbar_init(&sh.rbar[wid], 1);
     if (wid == 0) {
-      for (int i = 0; i < a.nst; i++) mbar_init(&sh.full[i], 1);
       mbar_init(&sh.xbar, 1);
       mbar_init(&sh.ebar, 1);
       sh.ok = 1;
@@ -274,7 +315,7 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
   const uint32_t ep = sh.epoch;
   pdl_wait();      // x (and add) are written by the preceding kernel
   const uint32_t xbytes = (uint32_t)T * D * 4;
-  const bool xstaged = (size_t)xbytes * (a.add_in ? 2 : 1) <= pool_bytes - rrow_bytes;
+  const bool xstaged = (size_t)xbytes * (a.add_in ? 2 : 1) <= (size_t)SW * a.nst * a.stage_bytes;
   const float* xsm = reinterpret_cast<const float*>(dsm);
   const float* asm_ = a.add_in ? xsm + (size_t)T * D : nullptr;
   if (tid == 0 && xstaged) {
@@ -631,215 +672,112 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
   }
 
   if (wid == 0) TG_MARK(4);
-  // ---- A and B: the CTA's pool of staged chunks.
-  // This CTA's share of the step: the flat (slot, row) units [a0, a1) of
-  // phase A (gate and up row r of slot s, for each of the slot's tokens) and
-  // the output rows [b0, b1) of phase B (for every slot).  Its weight rows
-  // arrive as chunks, in the order they are consumed: phase A's in runs of
-  // up to CRA rows of one slot (the gate rows, then the up rows), then phase
-  // B's, output row group major (CRB rows), slot minor.  Chunk i goes to pool
-  // stage i % NS and completes on full[i % NS]; its consumers (one pass per
-  // row) count themselves off in done[], and the last one issues chunk i + NS
-  // into the freed stage.  With NS at least the chunk count every chunk is
-  // issued at once.  Passes go to warps round-robin in chunk order: phase A
-  // pass j (unit a0 + j) to warp j % SW, phase B row b0 + q to warp q % SW.
+  // ---- A and B: the per-warp ring
+  // Phase A items are (slot, block of pa consecutive rows of gate and of up);
+  // phase B items are (output row, group of sb consecutive slots).  With a
+  // 256-block format, phase A lanes are (row, gate|up, block) and phase B
+  // lanes (slot, block): each lane folds one block's term in the reference's
+  // order and the row's lanes fold the terms in block order.  Other formats
+  // split each row over half a warp (half_dot_sub32).
   const int n_slots = sh.n_slots, total = sh.total;
   const int grs = row_layout(GF, D).rs, drs = row_layout(DF, I).rs;
   constexpr bool GBLK = GF == FMT_Q4K || GF == FMT_Q6K;
   constexpr bool DBLK = DF == FMT_Q4K || DF == FMT_Q6K;
+  const int pa = a.pa, SB = a.sb;
+  const uint32_t ghalf = rows_stage_bytes(grs, pa), dr = rows_stage_bytes(drs, 1);
+  const int nrb = (I + pa - 1) / pa;   // row blocks per slot
+  const int nA = n_slots * nrb;
   const int k = T, rule = a.assoc_rule, act = a.act;
-  const int NS = a.nst, CRA = a.cra, CRB = a.crb;
-  const uint32_t SS = a.stage_bytes, ghalf = rows_stage_bytes(grs, CRA);
-  uint8_t* const pool = dsm;
-  const long nAu = (long)n_slots * I;
-  const int a0 = (int)(nAu * blockIdx.x / G), a1 = (int)(nAu * (blockIdx.x + 1) / G);
-  const int b0 = (int)((long)D * blockIdx.x / G), b1 = (int)((long)D * (blockIdx.x + 1) / G);
-  const int nqg = n_slots > 0 ? (b1 - b0 + CRB - 1) / CRB : 0;   // phase-B row groups
-  const int s_first = a0 / I;
-  if (tid == 0) {
-    // A chunk index of each slot segment's first chunk (segments of slots
-    // s_first .. in [a0, a1)), and the chunk count
-    int c = 0, ns = 0;
-    for (int s = s_first; s < n_slots && (long)s * I < a1; s++, ns++) {
-      sh.segc[ns] = c;
-      const int lo = max(a0, s * I), hi = min(a1, (s + 1) * I);
-      c += (hi - lo + CRA - 1) / CRA;
-    }
-    sh.segc[ns] = c;
-    sh.nach = c;
-    sh.nch = c + nqg * n_slots;
-  }
-  for (int i = tid; i < NS; i += SW * 32) {
-    sh.done[i] = 0;
-    sh.last_iss[i] = -1;
-  }
-  __syncthreads();
-  const int nAch = sh.nach, nch = sh.nch;
+  const int gbb = GF == FMT_Q4K ? Q4K_BYTES : 192, dbb = DF == FMT_Q4K ? Q4K_BYTES : 192;   // main bytes per block
 
-  // chunk i -> (phase-A: slot, first row of the slot, rows) or (phase-B: slot,
-  // first output row, rows); its consumer count is its rows
-  struct Chunk {
-    bool b;
-    int s, r0, n;
+  auto issue = [&](const SCur& c, int stg) {   // lane 0
+    step_issue<GF, DF>(sx, c, ring + (size_t)stg * a.stage_bytes, &bar[stg], nrb, pa, I, D, ghalf, dr, n_slots, SB);
   };
-  auto chunk_of = [&](int i) -> Chunk {
-    Chunk c;
-    if (i < nAch) {
-      int q = 0;
-      while (sh.segc[q + 1] <= i) q++;
-      const int s = s_first + q, lo = max(a0, s * I), hi = min(a1, (s + 1) * I);
-      const int r0 = lo - s * I + (i - sh.segc[q]) * CRA;
-      c.b = false;
-      c.s = s;
-      c.r0 = r0;
-      c.n = min(CRA, hi - s * I - r0);
-    } else {
-      const int j = i - nAch, g = j / n_slots;
-      c.b = true;
-      c.s = j - g * n_slots;
-      c.r0 = b0 + g * CRB;
-      c.n = min(CRB, b1 - c.r0);
+  SCur ic{0, gw - NW, 0, 0};
+  int issued = 0;
+  bool more = true;
+  for (int i = 0; i < a.nst && more; i++) {
+    more = scur_next(ic, gw, NW, nA, D, n_slots, SB);
+    if (more) {
+      if (lane == 0) issue(ic, i);
+      issued++;
     }
-    return c;
+  }
+  int j = 0;   // items consumed
+  // Stops the warp: no further copies are issued, and those in flight
+  // (items from .. issued-1) are waited for, each wait bounded.
+  auto stop = [&](int from) {
+    if (dead) return;
+    dead = true;
+    for (int i = from; i < issued; i++) mbar_wait(&bar[i % a.nst], (uint32_t)(i / a.nst) & 1u);
   };
-  // one thread: the bulk copies of chunk i into its pool stage
-  auto issue = [&](int i) {
-    const int st = i % NS;
-    uint8_t* dst = pool + (size_t)st * SS;
-    uint64_t* fb = &sh.full[st];
-    const Chunk c = chunk_of(i);
-    if (!c.b) {
-      const WDesc Gw = wdesc<GF>(sx[c.s].g, I, D), Uw = wdesc<GF>(sx[c.s].u, I, D);
-      mbar_arrive_expect_tx(fb, row_tx(Gw, c.r0, c.n) + row_tx(Uw, c.r0, c.n));
-      stage_row(Gw, c.r0, dst, fb, c.n);
-      stage_row(Uw, c.r0, dst + ghalf, fb, c.n);
-    } else {
-      const WDesc Dw = wdesc<DF>(sx[c.s].d, D, I);
-      mbar_arrive_expect_tx(fb, row_tx(Dw, c.r0, c.n));
-      stage_row(Dw, c.r0, dst, fb, c.n);
-    }
-    __threadfence_block();   // the barrier's expected bytes before the chunk's number
-    *reinterpret_cast<volatile int*>(&sh.last_iss[st]) = i;
-  };
-  // every chunk that fits the pool at once, spread over the warps' lane 0
-  // (the pool's bytes were last read through the generic proxy in phase R)
-  for (int i = wid; i < min(NS, nch); i += SW)
-    if (lane == 0) {
-      fence_proxy_async();
-      issue(i);
-    }
-
   unsigned long long* tw = sh.tw[wid];   // trace: wait / compute / issue cycles, phases A and B
   if (lane == 0)
     for (int q = 0; q < 8; q++) tw[q] = 0;
   int tph = 0;
   long long tc = 0;
-  // waits for chunk i (bounded); false (and the warp stops) on a timeout.
-  // A stage's barrier tells its consecutive phases apart by parity only, so
-  // the wait on chunk i's phase starts once chunk i has been issued into the
-  // stage (which happens after chunk i - NS has landed and been consumed).
-  auto wait_chunk = [&](int i) -> bool {
+  auto wait_stage = [&](int stg, int item) -> bool {
     if (dead) return false;
     if (a.trace) tc = clock64();
-    const int st = i % NS;
-    bool okw = true;
-    if (i >= NS) {
-      const volatile int* li = &sh.last_iss[st];
-      for (int it = 0; *li < i; it++) {
-        if (it >= a.poll_limit) {
-          okw = false;
-          break;
-        }
-        __nanosleep(32);
-      }
-      __threadfence_block();
-    }
-    okw = okw && mbar_wait(&sh.full[st], (uint32_t)(i / NS) & 1u);
+    const bool okw = mbar_wait(&bar[stg], (uint32_t)(item / a.nst) & 1u);
     if (a.trace) {
       const long long t1 = clock64();
       if (lane == 0) tw[3 * tph] += t1 - tc;
       tc = t1;
     }
     if (!okw) {
-      if (lane == 0) set_error(a.st, ERR_WAIT_TIMEOUT, 32, blockIdx.x, i);
-      dead = true;
+      if (lane == 0) set_error(a.st, ERR_WAIT_TIMEOUT, 32, blockIdx.x, wid);
+      stop(item + 1);
+      return false;
     }
-    return okw;
+    return true;
   };
-  // this warp has finished reading chunk i: count it off; the last consumer
-  // issues chunk i + NS into the freed stage
-  auto release = [&](int i, int consumers) {
+  auto refill = [&](int stg) {
     __syncwarp();
     long long t0 = 0;
     if (a.trace) {
       t0 = clock64();
       if (lane == 0) tw[3 * tph + 1] += t0 - tc;
     }
-    if (lane == 0) {
-      const int st = i % NS;
-      __threadfence_block();
-      if (atomicAdd(&sh.done[st], 1) == consumers - 1) {
-        __threadfence_block();
-        sh.done[st] = 0;
-        if (i + NS < nch && !dead) {
-          fence_proxy_async();
-          issue(i + NS);
-        }
-      }
+    if (dead || !more) return;
+    more = scur_next(ic, gw, NW, nA, D, n_slots, SB);
+    if (more) {
+      if (lane == 0) issue(ic, stg);
+      issued++;
     }
     if (a.trace && lane == 0) tw[3 * tph + 2] += clock64() - t0;
   };
 
-  // ---- phase A: pass j = the gate and up rows of unit a0 + j for each of
-  // the slot's tokens.  With a 256-block gate format the lanes are (matrix
-  // m, block b, part hh): LB = 32 / (2 gbpr) lanes (1, 2 or 4) share a
-  // block's term (q4k_split_term / q6k_split_term), and each matrix row
-  // folds its blocks' terms in block order (fold_row).  Other formats split
-  // the pair over the half warps (half_dot_sub32).
-  const int LB = GBLK ? (gbpr >= 16 ? 1 : gbpr >= 8 ? 2 : 4) : 1;
-  const int a_m = lane / (gbpr * LB), a_b = (lane / LB) % gbpr, a_hh = lane % LB;
-  const bool a_on = GBLK && a_m < 2;
-  const int gbb = GF == FMT_Q4K ? Q4K_BYTES : 192, dbb = DF == FMT_Q4K ? Q4K_BYTES : 192;   // main bytes per block
-  auto a_term = [&](const uint8_t* mb, const uint8_t* s1b, const uint8_t* s2b, const XQ& xb, bool x4) -> float {
-    if constexpr (GF == FMT_Q4K) {
-      if (LB == 1) return q4k_split_term<1>(mb, xb, x4, a_hh, a_on);
-      if (LB == 2) return q4k_split_term<2>(mb, xb, x4, a_hh, a_on);
-      return q4k_split_term<4>(mb, xb, x4, a_hh, a_on);
-    } else if constexpr (GF == FMT_Q6K) {
-      if (LB == 1) return q6k_split_term<1>(mb, s1b, s2b, xb, a_hh, a_on);
-      if (LB == 2) return q6k_split_term<2>(mb, s1b, s2b, xb, a_hh, a_on);
-      return q6k_split_term<4>(mb, s1b, s2b, xb, a_hh, a_on);
-    } else {
-      return 0.f;
-    }
-  };
-#pragma unroll 1
-  for (int j = wid; a0 + j < a1; j += SW) {
-    const int u = a0 + j, s = u / I, r = u - s * I;
-    const int q = s - s_first, lo = max(a0, s * I);
-    const int ci = sh.segc[q] + (u - lo) / CRA;
-    const int r0 = lo - s * I + ((u - lo) / CRA) * CRA;
-    if (!wait_chunk(ci)) break;
-    const uint8_t* dst = pool + (size_t)(ci % NS) * SS;
+  // phase A: items gw, gw + NW, ... < nA
+  const int gbpr2 = GBLK ? gbpr : 1;                 // lanes per row
+  const int a_pr = lane / (2 * gbpr2), a_m = (lane / gbpr2) & 1, a_b = lane - (lane / gbpr2) * gbpr2;
+  for (int it = gw; it < nA; it += NW, j++) {
+    const int stg = j % a.nst;
+    if (!wait_stage(stg, j)) continue;
+    const int s = it / nrb, r0 = (it - s * nrb) * pa, nr = min(pa, I - r0);
     const StepExpert& X = sx[s];
     const WDesc Gw = wdesc<GF>(X.g, I, D), Uw = wdesc<GF>(X.u, I, D);
+    const uint8_t* dst = ring + (size_t)stg * a.stage_bytes;
     const int n = sh.slot_n[s], off = sh.slot_off[s];
     if constexpr (GBLK) {
-      // this lane's block: row r of matrix a_m, staged at row r - r0 of the chunk
-      RowPtrs rp = row_ptrs(a_m ? Uw : Gw, r0, dst + (a_m ? ghalf : 0));
-      const size_t ro = (size_t)(r - r0) * grs;
-      const uint8_t* mb = rp.m + ro + (size_t)a_b * gbb;
-      const uint8_t* s1b = rp.a1 ? rp.a1 + ro + a_b * 16 : nullptr;
-      const uint8_t* s2b = rp.a2 ? rp.a2 + ro + a_b * 2 : nullptr;
-      const int lead = (lane / (gbpr * LB)) * (gbpr * LB) + LB - 1;
+      const bool on = a_pr < nr;
+      const RowPtrs rp = row_ptrs(a_m ? Uw : Gw, r0, dst + (a_m ? ghalf : 0));
+      const uint8_t* mb = rp.m + (size_t)a_pr * grs + (size_t)a_b * gbb;
+      const uint8_t* s1b = rp.a1 ? rp.a1 + (size_t)a_pr * grs + a_b * 16 : nullptr;
+      const uint8_t* s2b = rp.a2 ? rp.a2 + (size_t)a_pr * grs + a_b * 2 : nullptr;
+      const int r = r0 + a_pr;
 #pragma unroll 1
       for (int jj = 0; jj < n; jj++) {
         const bool x4 = use_x4(rule, jj & ~3, n, k);
-        const XQ& xb = xa[(size_t)sh.row_t[off + jj] * gbpr + (a_on ? a_b : 0)];
-        const float term = a_term(mb, s1b, s2b, xb, x4);
-        const float tot = fold_row(term, lead, gbpr, LB);
-        const float up = shfl(tot, min(gbpr * LB, 31));
-        if (lane == 0) {
+        float term = 0.f;
+        if (on) {
+          const XQ& xb = xa[(size_t)sh.row_t[off + jj] * gbpr + a_b];
+          if constexpr (GF == FMT_Q4K) term = q4k_block_term(mb, xb, x4);
+          else term = q6k_block_term(mb, s1b, s2b, xb);
+        }
+        const float tot = fold_row(term, lane - a_b, gbpr2);
+        const float up = shfl(tot, min(lane + gbpr2, 31));
+        if (on && a_m == 0 && a_b == 0) {
           float gt = tot, ut = up;
           if (X.gb) {
             gt = fadd(gt, X.gb[r]);
@@ -850,11 +788,7 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
       }
     } else {
       // one row: lanes 0-15 its gate row, lanes 16-31 its up row
-      RowPtrs rp = row_ptrs(lane < 16 ? Gw : Uw, r0, dst + (lane < 16 ? 0 : ghalf));
-      const size_t ro = (size_t)(r - r0) * grs;
-      rp.m += ro;
-      if (rp.a1) rp.a1 += ro;
-      if (rp.a2) rp.a2 += ro;
+      const RowPtrs rp = row_ptrs(lane < 16 ? Gw : Uw, r0, dst + (lane < 16 ? 0 : ghalf));
 #pragma unroll 1
       for (int jj = 0; jj < n; jj++) {
         const float v = half_dot_sub32<GF>(rp, D / 32, xa + (size_t)sh.row_t[off + jj] * gbpr);
@@ -862,14 +796,14 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
         if (lane == 0) {
           float gt = v, ut = up;
           if (X.gb) {
-            gt = fadd(gt, X.gb[r]);
-            ut = fadd(ut, X.ub[r]);
+            gt = fadd(gt, X.gb[r0]);
+            ut = fadd(ut, X.ub[r0]);
           }
-          st_tagged(a.hidt + hid_word(off + jj, r, dbpr), ep, act_fn(act, gt, ut));
+          st_tagged(a.hidt + hid_word(off + jj, r0, dbpr), ep, act_fn(act, gt, ut));
         }
       }
     }
-    release(ci, chunk_of(ci).n);
+    refill(stg);
   }
 
   if (wid == 0) TG_MARK(5);
@@ -939,16 +873,13 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
     }
   }
   if (wid == 0) TG_MARK(15);
-  if (!__syncthreads_and(okh)) dead = true;
+  if (!__syncthreads_and(okh)) stop(j);
   if (wid == 0) TG_MARK(7);
 
-  // ---- phase B: output row r of [b0, b1) (warp (r - b0) % SW), slots in
-  // groups of SB; its chunks are the ones of its row group g, one per slot.
-  // With a 256-block down format the lanes are (block, slot): the 8 lanes of
-  // a quarter warp read 8 different slots' rows (distinct banks); each lane
-  // folds one block's term in the reference's order, the slot's lanes fold
-  // the terms in block order, and the slots' parts are added in slot order.
-  const int dbpr2 = DBLK ? dbpr : 1, SL = a.sl, SB = a.sb;
+  // phase B: rows r = gw, gw + NW, ... < D; slots in groups of SB
+  // phase-B lanes: lane = block * SL + slot, so the 8 lanes of a quarter warp
+  // read 8 different slots' rows (distinct banks)
+  const int dbpr2 = DBLK ? dbpr : 1, SL = a.sl;
   const int b_b = lane / SL, b_sl = lane - b_b * SL;
   float* accw = sh.accw[wid];   // running output of the warp's row, per token
   // Output row r (lane t < T holds token t's value); expert parallel: this
@@ -963,28 +894,25 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
       dead = true;
     }
   };
-  auto stage_of = [&](int ci) { return pool + (size_t)(ci % NS) * SS; };
   if (n_slots > 0)
-    for (int qq = wid; b0 + qq < b1 && !dead; qq += SW) {
-      const int r = b0 + qq, g = qq / CRB, q0 = b0 + g * CRB, cb = nAch + g * n_slots;
-      const size_t ro = (size_t)(r - q0) * drs;
+    for (int r = gw; r < D; r += NW) {
       if (lane < T) accw[lane] = 0.f;
       __syncwarp();
-      for (int s0 = 0; s0 < n_slots; s0 += SB) {
+      for (int s0 = 0; s0 < n_slots; s0 += SB, j++) {
+        const int stg = j % a.nst;
+        if (!wait_stage(stg, j)) continue;
+        const uint8_t* dst = ring + (size_t)stg * a.stage_bytes;
         const int s1 = min(n_slots, s0 + SB);
-        bool okw = true;
-        for (int s = s0; s < s1 && okw; s++) okw = wait_chunk(cb + s);
-        if (!okw) break;
         if constexpr (DBLK) {
           const int s = s0 + b_sl;
           const bool in = s < s1, on = in && b_b < dbpr2;
           const int sc = in ? s : s0;
           const StepExpert& X = sx[sc];
           const int n = in ? sh.slot_n[sc] : 0, off = sh.slot_off[sc];
-          const RowPtrs rp = row_ptrs(wdesc<DF>(X.d, D, I), q0, stage_of(cb + sc));
-          const uint8_t* mb = rp.m + ro + (size_t)b_b * dbb;
-          const uint8_t* s1b = rp.a1 ? rp.a1 + ro + b_b * 16 : nullptr;
-          const uint8_t* s2b = rp.a2 ? rp.a2 + ro + b_b * 2 : nullptr;
+          const RowPtrs rp = row_ptrs(wdesc<DF>(X.d, D, I), (int)r, dst + (sc - s0) * dr);
+          const uint8_t* mb = rp.m + (size_t)b_b * dbb;
+          const uint8_t* s1b = rp.a1 ? rp.a1 + b_b * 16 : nullptr;
+          const uint8_t* s2b = rp.a2 ? rp.a2 + b_b * 2 : nullptr;
 #pragma unroll 1
           for (int t = 0; t < T; t++) {
             // this slot's active row for token t (a slot's rows are in token order)
@@ -1023,10 +951,7 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
             const bool in = s < s1;
             const int sc = in ? s : sp;
             const StepExpert& X = sx[sc];
-            RowPtrs rp = row_ptrs(wdesc<DF>(X.d, D, I), q0, stage_of(cb + sc));
-            rp.m += ro;
-            if (rp.a1) rp.a1 += ro;
-            if (rp.a2) rp.a2 += ro;
+            const RowPtrs rp = row_ptrs(wdesc<DF>(X.d, D, I), r, dst + (sc - s0) * dr);
             const int n = in ? sh.slot_n[sc] : 0, off = sh.slot_off[sc];
             const float db = X.db ? X.db[r] : 0.f;
 #pragma unroll 1
@@ -1049,24 +974,22 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
           }
           __syncwarp();
         }
-        for (int s = s0; s < s1; s++) release(cb + s, chunk_of(cb + s).n);
+        refill(stg);
       }
       emit_row(r, lane < T ? accw[lane] : 0.f);
       __syncwarp();
     }
   else
-    for (int r = b0 + wid; r < b1; r += SW) emit_row(r, 0.f);
+    for (int r = gw; r < D; r += NW) emit_row(r, 0.f);
 
   if (wid == 0) TG_MARK(8);
   if (wid == SW - 1) TG_MARK(11);
   if (a.trace && tid == 0) a.trace[blockIdx.x * 32 + 13] = gtimer();
   if (a.trace && lane == 0)
     for (int q = 0; q < 8; q++) a.trace[(size_t)gridDim.x * 32 + ((size_t)blockIdx.x * SW + wid) * 8 + q] = tw[q];
-  // bounded waits for copies still in flight before the CTA exits: only a
-  // stage's last issued chunk can be one (a chunk is issued into a stage
-  // after the stage's previous chunk was waited for and consumed)
-  __syncthreads();
-  if (tid < NS && sh.last_iss[tid] >= 0) mbar_wait(&sh.full[tid], (uint32_t)(sh.last_iss[tid] / NS) & 1u);
+  // bounded waits for any copies still in flight before the CTA exits
+  if (!dead)
+    for (int i = j; i < issued; i++) mbar_wait(&bar[i % a.nst], (uint32_t)(i / a.nst) & 1u);
 }
 
 // ---------------------------------------------------------------------
@@ -1080,7 +1003,7 @@ size_t step_sync_words(int T, int E, int top_k, int I) {
 // Shared-memory shape of one launch, or false when the step does not fit.
 struct StepShape {
   uint32_t stage;
-  int nst, rwc, xcap, cra, crb, sb, sl;
+  int nst, rwc, xcap, pa, sb, sl;
   size_t smem;
 };
 
@@ -1093,17 +1016,6 @@ static int step_sms() {
     if (sms < 1) sms = 1;
   }
   return sms;
-}
-
-static size_t step_smem_optin() {
-  static int v = 0;
-  if (!v) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
-    if (v < 48 * 1024) v = 48 * 1024;
-  }
-  return (size_t)v;
 }
 
 static bool step_shape(const StepLaunch& l, StepShape& sh) {
@@ -1126,53 +1038,32 @@ static bool step_shape(const StepLaunch& l, StepShape& sh) {
   const int bg = l.D / QK, bd = l.I / QK;
   if ((gblk && (bg < 1 || bg > 16)) || (dblk && (bd < 1 || bd > 32))) return false;
   const int G = step_sms();
+  sh.pa = gblk ? std::max(1, 16 / bg) : 1;
   sh.rwc = (l.E + G - 1) / G;
   if (sh.rwc > STEP_RW_MAX || (l.D + QK - 1) / QK > STEP_GB_MAX) return false;
   const int gbpr = (l.D + QK - 1) / QK, dbpr = (l.I + QK - 1) / QK;
   sh.xcap = l.T * l.top_k;
-  const size_t fixed = (size_t)l.T * gbpr * sizeof(XQ) + (size_t)sh.xcap * dbpr * sizeof(XQ) +
-                       (size_t)sh.xcap * sizeof(StepExpert) + (size_t)l.E * sizeof(StepExpert);
-  const size_t optin = step_smem_optin();
-  if (optin < sizeof(StepShared) + fixed + 1024) return false;
-  const size_t budget = optin - sizeof(StepShared) - 256 - fixed;   // for the chunk pool
-  // phase-B slot lanes and slots per group
+  const size_t fixed = round16((size_t)sh.rwc * l.D * 4) + (size_t)l.T * gbpr * sizeof(XQ) +
+                       (size_t)sh.xcap * dbpr * sizeof(XQ) + (size_t)sh.xcap * sizeof(StepExpert) +
+                       (size_t)l.E * sizeof(StepExpert);
+  const size_t budget = 220 * 1024 - sizeof(StepShared);
+  const uint32_t dr = rows_stage_bytes(row_layout(l.down_fmt, l.I).rs, 1);
+  const uint32_t sa = 2 * rows_stage_bytes(row_layout(l.gate_fmt, l.D).rs, sh.pa);
+  // phase-B slots per item: every slot of the step if the stage allows
   sh.sl = 1;
   if (dblk)
     while (2 * sh.sl * bd <= 32) sh.sl *= 2;
   const int max_slots = std::min(l.E, l.T * l.top_k);
-  sh.sb = dblk ? std::min(sh.sl, max_slots) : std::min(2, max_slots);   // 32-value formats: two slots per pass
-  // Chunk rows: the smallest phase-A chunk (>= 2 rows where possible) whose
-  // stages hold every chunk of a CTA's typical share at once; failing that,
-  // the one with the most stages.  A stage holds one phase-A chunk (gate and
-  // up rows) or one phase-B chunk (as many down rows as fit, up to the CTA's
-  // share of output rows).
-  const int grs = row_layout(l.gate_fmt, l.D).rs, drs = row_layout(l.down_fmt, l.I).rs;
-  const int ar = (int)(((long)max_slots * l.I + G - 1) / G), br = (l.D + G - 1) / G;
-  const size_t rrow = round16((size_t)sh.rwc * l.D * 4);
-  int best = -1;
-  long best_key = 0;
-  for (int cra = 1; cra <= 16; cra++) {
-    const uint32_t sa = 2 * rows_stage_bytes(grs, cra);
-    int crb = 1;
-    while (crb < br && rows_stage_bytes(drs, crb + 1) <= sa) crb++;
-    const uint32_t ss = std::max(sa, rows_stage_bytes(drs, crb));
-    const int ns = (int)std::min<size_t>(STEP_POOL_MAX, budget / ss);
-    if (ns < std::max(2, sh.sb) || (size_t)ns * ss < rrow + 16) continue;
-    const int chunks = (ar + cra - 1) / cra + std::min(max_slots, ar / std::max(1, l.I) + 1) +
-                       max_slots * ((br + crb - 1) / crb);
-    // all in flight: prefer the finest chunks (from 2 rows); else the most stages
-    const long key = chunks <= ns ? 1000000L - (cra >= 2 ? cra : 100) : (long)ns * 1000 - cra;
-    if (best < 0 || key > best_key) {
-      best = cra;
-      best_key = key;
-      sh.cra = cra;
-      sh.crb = crb;
-      sh.stage = ss;
-      sh.nst = ns;
-    }
+  int sb = dblk ? std::min(sh.sl, max_slots) : std::min(2, max_slots);   // 32-value formats: two slots per pass
+  for (;;) {
+    sh.stage = std::max(sa, (uint32_t)sb * dr);
+    if (fixed + (size_t)SW * 2 * sh.stage <= budget || sb == 1) break;
+    sb = std::max(1, sb / 2);
   }
-  if (best < 0) return false;
-  sh.smem = (size_t)sh.nst * sh.stage + fixed;
+  sh.sb = sb;
+  if (fixed + (size_t)SW * 2 * sh.stage > budget) return false;
+  sh.nst = (int)std::min<size_t>(ST_MAX_NST, (budget - fixed) / ((size_t)SW * sh.stage));
+  sh.smem = (size_t)SW * sh.nst * sh.stage + fixed;
   return true;
 }
 
@@ -1182,8 +1073,7 @@ static cudaError_t step_launch(StepArgs a, const StepShape& sh, cudaStream_t s) 
   a.nst = sh.nst;
   a.rwc = sh.rwc;
   a.xcap = sh.xcap;
-  a.cra = sh.cra;
-  a.crb = sh.crb;
+  a.pa = sh.pa;
   a.sb = sh.sb;
   a.sl = sh.sl;
   const void* fn = reinterpret_cast<const void*>(layer_step_kernel<GF, DF>);

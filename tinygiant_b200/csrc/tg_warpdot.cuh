@@ -598,140 +598,6 @@ __device__ __forceinline__ float q6k_block_term(const uint8_t* mb, const uint8_t
   return fmul(fmul(d, xb.scale), bs);
 }
 
-// ---------------------------------------------------------------------
-// A block term split over LB lanes (LB = 1, 2 or 4): lane part hh of the
-// block's LB lanes takes groups (Q4_K) or (half, l-half) pairs (Q6_K)
-// NG hh .. NG hh + NG - 1, NG = 4 / LB.
-
-// Q4_K: the reference's fold terms of groups g0 .. g0 + NG - 1 (x4: one per
-// group in t0; x1: two, t0 then t1), formed as in q4k_block_term.
-template <int NG>
-__device__ __forceinline__ void q4k_group_terms(const uint8_t* blk, const XQ& xb, bool x4, int g0, float (&t0)[NG],
-                                                float (&t1)[NG]) {
-  const uint4 h = ld16(blk);
-  const float d = f16_fast(h.x & 0xFFFFu), dmin = f16_fast(h.x >> 16);
-#pragma unroll
-  for (int gi = 0; gi < NG; gi++) {
-    const int g = g0 + gi;
-    const uint4 q0 = ld16(blk + 16 + 32 * g), q1 = ld16(blk + 32 + 32 * g);
-    const uint4 xa = ld16(xb.qs + 64 * g), xe = ld16(xb.qs + 64 * g + 16);
-    const uint4 xc = ld16(xb.qs + 64 * g + 32), xd = ld16(xb.qs + 64 * g + 48);
-    const float2 bf = *reinterpret_cast<const float2*>(xb.bsf + 2 * g);
-    const uint32_t qw[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
-    const uint32_t xl[8] = {xa.x, xa.y, xa.z, xa.w, xe.x, xe.y, xe.z, xe.w};
-    const uint32_t xh[8] = {xc.x, xc.y, xc.z, xc.w, xd.x, xd.y, xd.z, xd.w};
-    int ilo = 0, ihi16 = 0;
-#pragma unroll
-    for (int j = 0; j < 8; j++) {
-      ilo = dp4a_us(qw[j] & 0x0F0F0F0Fu, (int)xl[j], ilo);
-      ihi16 = dp4a_us(qw[j] & 0xF0F0F0F0u, (int)xh[j], ihi16);
-    }
-    int sl, ml, sh, mh;
-    q4k_pair_scales(g, h.y, h.z, h.w, sl, ml, sh, mh);
-    const float dsl = fmul(d, (float)sl), dml = fmul(dmin, (float)ml);
-    const float dsh = fmul(d, (float)sh), dmh = fmul(dmin, (float)mh);
-    const float flo = i2f_small(ilo), fhi = i2f_small(ihi16 >> 4);
-    if (x4) {
-      t0[gi] = fsub(fadd(fsub(fmul(dsl, flo), fmul(dml, bf.x)), fmul(dsh, fhi)), fmul(dmh, bf.y));
-      t1[gi] = 0.f;
-    } else {
-      t0[gi] = fsub(fmul(dsl, flo), fmul(dml, bf.x));
-      t1[gi] = fsub(fmul(dsh, fhi), fmul(dmh, bf.y));
-    }
-  }
-}
-
-// The Q4_K block term of the LB lanes lane0 .. lane0 + LB - 1 (this lane
-// is part hh): the reference's left fold of the block's terms runs through
-// the parts in order (each part adds its terms to the fold it receives),
-// then times x's scale.  Every lane of the warp calls (the shuffles are
-// warp-wide); the last part's lane returns the term.
-template <int LB>
-__device__ __forceinline__ float q4k_split_term(const uint8_t* blk, const XQ& xb, bool x4, int hh, bool on) {
-  constexpr int NG = 4 / LB;
-  float t0[NG], t1[NG];
-  if (on) q4k_group_terms<NG>(blk, xb, x4, NG * hh, t0, t1);
-  float carry = 0.f;
-#pragma unroll
-  for (int i = 0; i < LB; i++) {
-    const float in = LB > 1 ? __shfl_up_sync(FULL, carry, 1) : 0.f;
-    if (hh == i && on) {
-      float bs = i == 0 ? 0.f : in;
-#pragma unroll
-      for (int gi = 0; gi < NG; gi++) {
-        bs = fadd(bs, t0[gi]);
-        if (!x4) bs = fadd(bs, t1[gi]);
-      }
-      carry = bs;
-    }
-  }
-  return on ? fmul(xb.scale, carry) : 0.f;
-}
-
-// Q6_K: the exact integer sum S of the (half, l-half) pairs hl0 .. hl0 + NH
-// - 1 and the sum A of its products' magnitudes (q6k_block_term's S and A).
-template <int NH>
-__device__ __forceinline__ void q6k_partial(const uint8_t* mb, const uint4& sv, const XQ& xb, int hl0, int& S, int& A) {
-  S = 0;
-  A = 0;
-#pragma unroll
-  for (int i = 0; i < NH; i++) {
-    const int hl = hl0 + i, h = hl >> 1, lq = hl & 1;
-    const uint4 va = ld16(mb + 64 * h + 16 * lq), vb = ld16(mb + 64 * h + 32 + 16 * lq);
-    const uint4 vh = ld16(mb + 128 + 32 * h + 16 * lq);
-    const uint4 xs = ld16(xb.xs16 + 4 * hl);
-    const uint32_t qa[4] = {va.x, va.y, va.z, va.w}, qb[4] = {vb.x, vb.y, vb.z, vb.w};
-    const uint32_t qh[4] = {vh.x, vh.y, vh.z, vh.w};
-    const int xsv[4] = {(int)xs.x, (int)xs.y, (int)xs.z, (int)xs.w};
-    const uint32_t w0 = h ? sv.z : sv.x, w1 = h ? sv.w : sv.y;
-    const int8_t* xq = xb.qs + 128 * h + 16 * lq;
-#pragma unroll
-    for (int k = 0; k < 4; k++) {
-      const uint4 xv = ld16(xq + 32 * k);
-      const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w};
-      int raw = 0;
-#pragma unroll
-      for (int q = 0; q < 4; q++) {
-        uint32_t v;
-        if (k == 0) v = (qa[q] & 0x0F0F0F0Fu) | ((qh[q] & 0x03030303u) << 4);
-        else if (k == 1) v = (qb[q] & 0x0F0F0F0Fu) | ((qh[q] & 0x0C0C0C0Cu) << 2);
-        else if (k == 2) v = ((qa[q] >> 4) & 0x0F0F0F0Fu) | (qh[q] & 0x30303030u);
-        else v = ((qb[q] >> 4) & 0x0F0F0F0Fu) | ((qh[q] >> 2) & 0x30303030u);
-        raw = dp4a_us(v, (int)xw[q], raw);
-      }
-      const int sc = sbyte(k < 2 ? w0 : w1, lq + 2 * (k & 1));
-      const int p = sc * (raw - 32 * xsv[k]);
-      S += p;
-      A += abs(p);
-    }
-  }
-}
-
-// The Q6_K block term of LB lanes (this lane part hh): the parts' S and A
-// are added (integers, order-free), then the last part's lane forms the term
-// as q6k_block_term does.  Every lane calls.
-template <int LB>
-__device__ __forceinline__ float q6k_split_term(const uint8_t* mb, const uint8_t* scb, const uint8_t* db,
-                                                const XQ& xb, int hh, bool on) {
-  constexpr int NH = 4 / LB;
-  int S = 0, A = 0;
-  uint4 sv = make_uint4(0, 0, 0, 0);
-  if (on) {
-    sv = ld16(scb);
-    q6k_partial<NH>(mb, sv, xb, NH * hh, S, A);
-  }
-#pragma unroll
-  for (int o = 1; o < LB; o <<= 1) {
-    S += __shfl_xor_sync(FULL, S, o);
-    A += __shfl_xor_sync(FULL, A, o);
-  }
-  if (!on || hh != LB - 1) return 0.f;
-  const uint32_t sw[4] = {sv.x, sv.y, sv.z, sv.w};
-  const float bs = A < (1 << 24) ? (float)S : q6k_fold_slow(mb, sw, xb);
-  const float d = f16_fast((uint32_t)db[0] | ((uint32_t)db[1] << 8));
-  return fmul(fmul(d, xb.scale), bs);
-}
-
 // prmt with the PTX semantics of the selector's bit 3: the selected byte's
 // sign replicated.
 __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
