@@ -257,6 +257,16 @@ int tg_cuda_step_trace(void *dev_buf);
  * already captured in a CUDA graph keep the settings they were captured
  * with.  Returns 0. */
 int tg_cuda_debug_step_fault(int skip_logit_cta, int poll_limit);
+/* Test hook: batched steps on the tensor cores launched after this call write
+ * every int32 sub-block sum of their gate/up GEMM into gate_up and of their
+ * down GEMM into down (device buffers; NULL: off), at
+ * ((plan_row * mats + matrix) * rows + weight_row) * nsb + sub_block with
+ * mats 2 (gate, up) or 1 (down), rows the matrix's rows, nsb its row's
+ * sub-blocks (Q4_K, MXFP4: values / 32; Q6_K: values / 16 in the order
+ * (2 h + l-half) * 4 + quarter per block).  Plan rows are the step's active
+ * (expert, token) rows: experts ascending, tokens ascending within each.
+ * Layer graphs keep the pointers they were captured with.  Returns 0. */
+int tg_cuda_debug_tc_isums(void *gate_up, void *down);
 /* Host buffers, synchronous: out[T][D] += experts(normalize ? rmsnorm(x) : x). */
 int tg_layer_forward(void *layer, const float *x_host, float *out_host, int T, int normalize);
 /* Selected experts and weights [T][top_k] of the layer's last step. */

@@ -331,3 +331,45 @@ def test_stack_forward_and_graph_replay(gpu, oracle):
         gpu.tg_cuda_set_stream(None)
         for r in res:
             r.close()
+
+
+@pytest.mark.parametrize("kind", ["q4k", "mxfp4"])
+def test_tensor_core_int32_sums_bit_exact_vs_oracle(gpu, oracle, kind):
+    """The tcgen05 grouped GEMM's int32 sub-block sums (read back from tensor
+    memory) equal the oracle's (tgo_row_isums) bit for bit for every gate and
+    up row of every active (expert, token) row of a batched step (T = 16):
+    Q4_K sub-blocks of 32 values, and MXFP4 sub-blocks at D = 2880, whose
+    last Q8 block holds two live sub-blocks."""
+    import torch
+    from tinygiant_b200 import quants as Q
+    if kind == "q4k":
+        L = synth.qwen_layer(seed=7, n_experts=8, top_k=2)
+    else:
+        L = synth.gptoss_layer(seed=3, layer=2, n_experts=8, top_k=2)
+    T, D, I = 16, L.embed_dim, L.inter_dim
+    nsb, rb = D // 32, Q.row_bytes(L.gate_fmt, D)
+    R = ResidentLayer(L, max_tokens=T, lib=gpu)
+    buf = torch.full((T * L.top_k * 2 * I * nsb,), -(2 ** 31), dtype=torch.int32, device="cuda")
+    try:
+        gpu.tg_cuda_debug_tc_isums(ctypes.c_void_p(buf.data_ptr()), None)
+        N = synth.rms_norm(np.random.default_rng([71, T]).standard_normal((T, D)).astype(np.float32))
+        R.forward(N, normalize=False)          # a fresh layer: its graph is captured with the hook on
+    finally:
+        gpu.tg_cuda_debug_tc_isums(None, None)
+        R_idx, R_w = R.last_routing(T)
+        R.close()
+    dbg = buf.cpu().numpy().reshape(T * L.top_k, 2, I, nsb)
+    xq = O.quantize_q8(oracle, N)
+    sel = sorted({int(R_idx[t, j]) for t in range(T) for j in range(L.top_k) if R_w[t, j] != 0})
+    p = 0
+    want = np.zeros((I, nsb), np.int32)
+    for e in sel:
+        toks = [t for t in range(T) if any(int(R_idx[t, j]) == e and R_w[t, j] != 0 for j in range(L.top_k))]
+        for t in toks:
+            xt = np.ascontiguousarray(xq[t])
+            for mat, Mx in enumerate((L.gates[e], L.ups[e])):
+                for r in range(I):
+                    oracle.tgo_row_isums(L.gate_fmt, Mx[r * rb:].ctypes.data, xt.ctypes.data, D, want[r].ctypes.data)
+                np.testing.assert_array_equal(dbg[p, mat], want, err_msg=f"expert {e} token {t} matrix {mat}")
+            p += 1
+    assert p > T   # every token's rows were checked

@@ -88,7 +88,17 @@ struct TcArgs {
   DevStatus* st;
   const CUtensorMap* tmaps;   // MXFP4: [E][3] (gate, up, down) tensor maps
   float negz;                 // -0.0f (the packed epilogue's product addend)
+  int* dbg;                   // test hook: every int32 sub-block sum, or null (tc_debug_isum_index)
 };
+
+// Test hook layout: the int32 sum of sub-block sb (the oracle's order: Q4_K
+// and MXFP4 32-value sub-blocks in value order, Q6_K the 16-value groups
+// (h, l-half, quarter) as (2 h + l-half) 4 + quarter) of weight row wr of
+// matrix mat (gate/up pass: 0 gate, 1 up) against plan row prow.
+__host__ __device__ __forceinline__ size_t tc_debug_isum_index(int prow, int mats, int mat, int R, int wr, int nsb,
+                                                              int sb) {
+  return (((size_t)prow * mats + mat) * R + wr) * nsb + sb;
+}
 
 constexpr int TC_MAX_BPR = 16;    // 256-value blocks per input row (K <= 4096)
 constexpr int TC_NS = 4;          // MXFP4 code ring: stages of 128 rows x 128 bytes
@@ -511,6 +521,16 @@ __global__ void __launch_bounds__(TC_WARPS * 32, 1) tc_gemm_kernel(TcArgs a) {
 #pragma unroll
     for (int c = 0; c < 8; c++) acc[c] = fold[c] = 0.f;
 
+    // test hook: this thread's sums (weight row r0 + r, active row c0 + c)
+    const int nsb_dbg = WF == FMT_Q6K ? a.K / 16 : a.K / 32;
+    auto dbg_put1 = [&](int c, int sb, int v) {
+      if (r < nr && c0 + c < nt)
+        a.dbg[tc_debug_isum_index(off + j0 + c0 + c, a.mats, MODE == 0 ? mat : 0, a.R, r0 + r, nsb_dbg, sb)] = v;
+    };
+    auto dbg_put = [&](int c, int sb, int lo, int hi) {
+      dbg_put1(c, sb, lo);
+      dbg_put1(c, sb + 1, hi);
+    };
     // epilogue of step st for this warp's EW active rows c0 .. c0 + EW - 1
     // (weight row r): the reference's fp32 fold of the integer sums
     auto epilogue = [&](auto ewc, int st) {
@@ -538,6 +558,12 @@ __global__ void __launch_bounds__(TC_WARPS * 32, 1) tc_gemm_kernel(TcArgs a) {
             tc_ld<EW>(tl + (2 * (g2 + gg) + 1) * TC_N, ih2[gg]);
           }
           tc_wait_ld();
+          if (a.dbg) {
+#pragma unroll
+            for (int gg = 0; gg < 2; gg++)
+#pragma unroll
+              for (int c = 0; c < EW; c++) dbg_put(c, 8 * b + 2 * (g2 + gg), (int)il2[gg][c], (int)ih2[gg][c]);
+          }
 #pragma unroll
           for (int gg = 0; gg < 2; gg++) {
             const int g = g2 + gg;
@@ -584,6 +610,9 @@ __global__ void __launch_bounds__(TC_WARPS * 32, 1) tc_gemm_kernel(TcArgs a) {
             tc_ld<EW>(tl + (2 * g) * TC_N, il);
             tc_ld<EW>(tl + (2 * g + 1) * TC_N, ih);
             tc_wait_ld();
+            if (a.dbg)
+#pragma unroll
+              for (int c = 0; c < EW; c++) dbg_put(c, 8 * b + 2 * g, (int)il[c], (int)ih[c]);
             int sl, ml, shh, mh;
             q4k_pair_scales(g, hd.y, hd.z, hd.w, sl, ml, shh, mh);
             const float dsl = fmul(d, (float)sl), dml = fmul(dmin, (float)ml);
@@ -617,6 +646,9 @@ __global__ void __launch_bounds__(TC_WARPS * 32, 1) tc_gemm_kernel(TcArgs a) {
             uint32_t is[EW];
             tc_ld<EW>(tl + (2 * k4 + lq) * TC_N, is);
             tc_wait_ld();
+            if (a.dbg)
+#pragma unroll
+              for (int c = 0; c < EW; c++) dbg_put1(c, 16 * b + (2 * h + lq) * 4 + k4, (int)is[c]);
             const int si = lq + 2 * k4;
             const int sc = sbyte(sw[si >> 2], si & 3);
 #pragma unroll
@@ -658,6 +690,12 @@ __global__ void __launch_bounds__(TC_WARPS * 32, 1) tc_gemm_kernel(TcArgs a) {
           for (int m = 0; m < MB; m++)
             if (m0 + m < nm) tc_ld<EW>(tl + (m0 + m) * TC_N, is[m]);
           tc_wait_ld();
+          if (a.dbg)
+#pragma unroll
+            for (int m = 0; m < MB; m++)
+              if (m0 + m < nm)
+#pragma unroll
+                for (int c = 0; c < EW; c++) dbg_put1(c, 8 * b + m0 + m, (int)is[m][c]);
 #pragma unroll
           for (int m = 0; m < MB; m++) {
             if (m0 + m >= nm) break;
@@ -900,6 +938,13 @@ cudaError_t tc_build_tmaps(const ExpertDesc* experts, int E, void* d_tmaps) {
   return cudaMemcpy(d_tmaps, maps.data(), maps.size() * sizeof(CUtensorMap), cudaMemcpyHostToDevice);
 }
 
+static int* g_tc_dbg_gu = nullptr;
+static int* g_tc_dbg_dn = nullptr;
+void set_tc_debug(int* gate_up, int* down) {
+  g_tc_dbg_gu = gate_up;
+  g_tc_dbg_dn = down;
+}
+
 cudaError_t launch_tc_moe(const PlanHdr* ph, int gate_fmt, int down_fmt, int T, int K, int D, int I, int max_rows,
                           const Q8Dev* xq8, const int* tok_rows, const void* tmaps, void* scratch, float* out,
                           DevStatus* st, cudaStream_t s) {
@@ -915,7 +960,7 @@ cudaError_t launch_tc_moe(const PlanHdr* ph, int gate_fmt, int down_fmt, int T, 
   float* gu = reinterpret_cast<float*>(take((size_t)max_rows * 2 * I * 4));
   Q8Dev* hq8 = reinterpret_cast<Q8Dev*>(take((size_t)max_rows * dbpr * sizeof(Q8Dev)));
   float* parts = reinterpret_cast<float*>(take((size_t)max_rows * D * 4));
-  TcArgs g{ph, xq8, gu, D, I, 2, st, tm, -0.0f};
+  TcArgs g{ph, xq8, gu, D, I, 2, st, tm, -0.0f, g_tc_dbg_gu};
   cudaError_t e = gate_fmt == FMT_MXFP4 ? tc_launch<FMT_MXFP4, 0>(g, s) : tc_launch<FMT_Q4K, 0>(g, s);
   if (e != cudaSuccess) return e;
   {
@@ -929,7 +974,7 @@ cudaError_t launch_tc_moe(const PlanHdr* ph, int gate_fmt, int down_fmt, int T, 
                    dim3(256), 0, s, a2);
     if (e != cudaSuccess) return e;
   }
-  TcArgs dn{ph, hq8, parts, I, D, 1, st, tm, -0.0f};
+  TcArgs dn{ph, hq8, parts, I, D, 1, st, tm, -0.0f, g_tc_dbg_dn};
   e = down_fmt == FMT_Q6K     ? tc_launch<FMT_Q6K, 1>(dn, s)
       : down_fmt == FMT_MXFP4 ? tc_launch<FMT_MXFP4, 1>(dn, s)
                               : tc_launch<FMT_Q4K, 1>(dn, s);

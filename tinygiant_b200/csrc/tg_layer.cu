@@ -481,6 +481,11 @@ int tg_layer_ep_reset(void* handle) {
   return 0;
 }
 
+int tg_cuda_debug_tc_isums(void* gate_up, void* down) {
+  set_tc_debug(static_cast<int*>(gate_up), static_cast<int*>(down));
+  return 0;
+}
+
 int tg_cuda_debug_step_fault(int skip_logit_cta, int poll_limit) {
   set_step_fault(skip_logit_cta, poll_limit);
   return 0;

@@ -150,6 +150,10 @@ bool tc_moe_eligible(int gate_fmt, int down_fmt, int D, int I);
 size_t tc_moe_scratch_bytes(int max_rows, int T, int K, int D, int I);
 size_t tc_tmap_bytes(int E);
 cudaError_t tc_build_tmaps(const ExpertDesc* experts, int E, void* d_tmaps);
+// Test hook: later grouped-GEMM passes write every int32 sub-block sum of the
+// gate/up pass into gate_up and of the down pass into down (device memory,
+// [plan row][matrix][weight row][sub-block], tc_debug_isum_index); null: off.
+void set_tc_debug(int* gate_up, int* down);
 cudaError_t launch_tc_moe(const PlanHdr* ph, int gate_fmt, int down_fmt, int T, int K, int D, int I, int max_rows,
                           const Q8Dev* xq8, const int* tok_rows, const void* tmaps, void* scratch, float* out,
                           DevStatus* st, cudaStream_t s);
