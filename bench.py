@@ -237,6 +237,27 @@ def measured_peak():
     return 6650.0, "fallback 6.65 TB/s"
 
 
+def measured_int8_peak():
+    """Dense int8 tensor ops/s: twice the measured bf16 GEMM rate (the
+    nominal int8 : bf16 dense ratio of B200, 4.5 : 2.25 POPS), burst figure."""
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return 2.0 * float(d["bf16_tflops"]), "2 x measured bf16 cuBLAS (MEASURED_PEAKS.json bf16_tflops)"
+    return 2.0 * 1590.0, "2 x fallback 1.59 PFLOP/s bf16"
+
+
+def batched_ops(L, xs):
+    """Per step: int8 multiply-adds x 2 of the active (expert, token) rows'
+    gate, up and down dots (3 D I each), from the reference routing."""
+    from tinygiant_b200 import synth
+    out = []
+    for x in xs:
+        _, row_w, _, _ = synth.route(L, synth.rms_norm(x))
+        out.append(2.0 * float(np.count_nonzero(row_w)) * 3 * L.embed_dim * L.inter_dim)
+    return np.array(out)
+
+
 def traffic_from_profiles():
     p = ROOT / "profiles" / "traffic.json"
     if p.exists():
@@ -584,6 +605,17 @@ def run_ours(a):
                 "expert_path": "fused step kernel" if T <= 8 else
                                ("matvec kernels" if a.matvec else "tcgen05 grouped GEMMs"),
                 "gbps": achieved, "clocks": clk, "roofline": roof, "gpu_launches": launches}
+        if T > 8:
+            # batched steps: the tensor-pipe roofline of the grouped GEMMs
+            ops = batched_ops(L, xs_host[a.warmup:])
+            tops = ranks_tokens * ops.sum() / (ms / 1e3) / 1e12
+            ipeak, ipsrc = measured_int8_peak()
+            ipeak *= world
+            line["roofline"] = {"bound": "tensor", "achieved": tops, "peak": ipeak, "unit": "TOPS (int8)",
+                                "frac": tops / ipeak, "traffic": None,
+                                "kernel": "batched MoE layer step (routing kernels + tcgen05 kind::i8 grouped "
+                                          "GEMMs), per step", "ops_per_step": float(ops.mean()),
+                                "peak_source": ipsrc, "hbm": roof}
         if ep:
             mean_max, worst = ep_balance(L, xs_host[a.warmup:], world)
             busiest = mean_max * L.expert_bytes(0) + L.router_w.nbytes + 2 * T * D * 4
