@@ -46,7 +46,8 @@ struct Layer {
   void* tc_scratch = nullptr;      // their intermediates (tc_moe_scratch_bytes)
   void* tc_tmaps = nullptr;        // MXFP4 layers: TMA tensor maps [E][3] of the expert matrices
   float* nbuf = nullptr;           // batched routing: normalized rows [max_tokens][D]
-  uint8_t* member = nullptr;       // batched routing: [max_tokens][E] selection membership
+  uint8_t* member = nullptr;       // batched routing: [E][rows of the step] selection membership
+  int* ecnt = nullptr;             // batched routing: [E] active rows per expert
   int* tpos = nullptr;             // batched routing: [max_tokens][top_k]
   int* tok_rows = nullptr;         // batched routing: [max_tokens][top_k] active rows per token
   // tg_layer_forward's CUDA graph (copy in, step, copies out) for one
@@ -107,6 +108,7 @@ static bool alloc_scratch(Layer* L) {
          (register_counters(L->step_sync, sizeof(unsigned long long) * step_sync_words(T, E, L->top_k, I)), true) &&
          (T <= 8 || (dmalloc(L, (void**)&L->nbuf, sizeof(float) * (size_t)T * D) &&
                      dmalloc(L, (void**)&L->member, (size_t)T * E) &&
+                     dmalloc(L, (void**)&L->ecnt, sizeof(int) * 256) &&
                      dmalloc(L, (void**)&L->tpos, sizeof(int) * (size_t)L->max_rows) &&
                      dmalloc(L, (void**)&L->tok_rows, sizeof(int) * (size_t)L->max_rows))) &&
          (!(T > 8 && tc_moe_eligible(L->gate_fmt, L->down_fmt, D, I)) ||
@@ -250,6 +252,7 @@ static bool layer_enqueue(Layer* L, const float* x, const float* add, float* x_o
     b.xq8 = L->xq8;
     b.nbuf = L->nbuf;
     b.member = L->member;
+    b.ecnt = L->ecnt;
     b.tpos = L->tpos;
     b.tok_rows = L->tok_rows;
     b.logits = L->logits;

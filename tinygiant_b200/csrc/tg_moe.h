@@ -50,7 +50,7 @@ struct RouteArgs {
 size_t route_smem_bytes(int D, int E, int T, int K);
 
 // Routing for batched steps (tg_route.cu): the RouteArgs fields plus the
-// normalized rows and a row x expert membership matrix.
+// normalized rows and an expert x row membership matrix.
 struct BatchRouteArgs {
   const float* x_in;
   const float* add_in;
@@ -65,7 +65,8 @@ struct BatchRouteArgs {
   const ExpertDesc* experts;
   Q8Dev* xq8;
   float* nbuf;            // [T][D] normalized rows
-  uint8_t* member;        // [T][E] selection rank + 1 of each active (row, expert), else 0
+  uint8_t* member;        // [E][T] selection rank + 1 of each active (expert, row), else 0
+  int* ecnt;              // [E] active rows per expert (zeroed by the norm kernel, counted by select)
   int* tpos;              // [T][top_k] each valid selection's place among its row's, in expert order
   int* tok_rows;          // [T][top_k] each row's active rows (plan indices) in slot order, then -1
   float* logits;

@@ -349,10 +349,11 @@ cudaError_t launch_layer_route(const RouteArgs& a, cudaStream_t s) {
 // layer_route_kernel's, in four kernels that each use the whole GPU.
 //   norm_q8_kernel   one CTA per row: x' = x + add (x_out), N = x' / rr * w,
 //                    N's Q8 blocks; the row's MoE output zeroed
-//   logits_kernel    W_r N for tiles of 8 rows x 32 experts, a fixed order over D
+//   logits_kernel    W_r N for tiles of 16 rows x 32 experts, a fixed order over D
 //   select_kernel    one warp per row: top-k (larger logit first, NaN last, ties
 //                    to the lower id), softmax over the selected, membership
-//   plan_kernel      one CTA: per expert its active rows in row order, slots in
+//                    (stored expert-major, so each expert's rows are contiguous)
+//   plan_kernel      one CTA per expert: its active rows in row order, slots in
 //                    expert order, the plan header (engine.py:297-318)
 
 __global__ void __launch_bounds__(256) norm_q8_kernel(BatchRouteArgs a) {
@@ -362,6 +363,8 @@ __global__ void __launch_bounds__(256) norm_q8_kernel(BatchRouteArgs a) {
   pdl_trigger();
   const int t = blockIdx.x, tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
   const int D = a.D, gbpr = (D + QK - 1) / QK;
+  if (t == 0)
+    for (int e = tid; e < a.E; e += 256) a.ecnt[e] = 0;   // select_kernel counts each expert's rows
   const float* x = a.x_in + (size_t)t * D;
   const float* ad = a.add_in ? a.add_in + (size_t)t * D : nullptr;
   float* n = a.nbuf + (size_t)t * D;
@@ -396,31 +399,78 @@ __global__ void __launch_bounds__(256) norm_q8_kernel(BatchRouteArgs a) {
   for (int b = w; b < gbpr; b += 8) quantize_block_warp(n + b * QK, min(QK, D - b * QK), a.xq8 + (size_t)t * gbpr + b);
 }
 
+// Tile: 16 rows x 32 experts per CTA; lane = expert, warp w = rows 2w and
+// 2w + 1.  Per 128-value chunk of D the router rows and the normalized rows
+// are staged in shared memory (router rows padded to 132 floats, so a
+// quarter warp's 16-byte loads hit distinct banks); each lane keeps its two
+// rows' dots in four chains each (value d in chain d % 4) and adds the chains
+// in a fixed order per chunk.
+constexpr int LG_T = 16, LG_E = 32, LG_D = 128, LG_WP = 132;
 __global__ void __launch_bounds__(256) logits_kernel(BatchRouteArgs a) {
-  __shared__ float Ws[32][129];
-  __shared__ float Ns[8][128];
+  __shared__ __align__(16) float Ws[LG_E][LG_WP];
+  __shared__ __align__(16) float Ns[LG_T][LG_D];
   pdl_wait();
   pdl_trigger();
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
   const int D = a.D, E = a.E, T = a.T;
-  const int t0 = blockIdx.x * 8, e0 = blockIdx.y * 32;
-  const int t = t0 + w, e = e0 + lane;
-  float acc = 0.f;
-  for (int d0 = 0; d0 < D; d0 += 128) {
-    for (int i = tid; i < 32 * 128; i += 256) {
-      const int er = i >> 7, dc = i & 127;
-      Ws[er][dc] = e0 + er < E && d0 + dc < D ? a.router_w[(size_t)(e0 + er) * D + d0 + dc] : 0.f;
+  const int t0 = blockIdx.x * LG_T, e0 = blockIdx.y * LG_E;
+  const int e = e0 + lane, ta = t0 + 2 * w, tb = ta + 1;
+  float acc_a = 0.f, acc_b = 0.f;
+  // this thread's share of a chunk: router values i = tid + 256 q, row values
+  // likewise; the next chunk's are loaded into registers while this one is
+  // computed from shared memory
+  constexpr int NWQ = LG_E * LG_D / 256, NNQ = LG_T * LG_D / 256;
+  float wr[NWQ], nr[NNQ];
+  auto fetch = [&](int d0) {
+#pragma unroll
+    for (int q = 0; q < NWQ; q++) {
+      const int i = tid + 256 * q, er = i / LG_D, dc = i % LG_D;
+      wr[q] = e0 + er < E && d0 + dc < D ? __ldg(a.router_w + (size_t)(e0 + er) * D + d0 + dc) : 0.f;
     }
-    for (int i = tid; i < 8 * 128; i += 256) {
-      const int tr = i >> 7, dc = i & 127;
-      Ns[tr][dc] = t0 + tr < T && d0 + dc < D ? a.nbuf[(size_t)(t0 + tr) * D + d0 + dc] : 0.f;
+#pragma unroll
+    for (int q = 0; q < NNQ; q++) {
+      const int i = tid + 256 * q, tr = i / LG_D, dc = i % LG_D;
+      nr[q] = t0 + tr < T && d0 + dc < D ? __ldcg(a.nbuf + (size_t)(t0 + tr) * D + d0 + dc) : 0.f;
+    }
+  };
+  fetch(0);
+  for (int d0 = 0; d0 < D; d0 += LG_D) {
+#pragma unroll
+    for (int q = 0; q < NWQ; q++) {
+      const int i = tid + 256 * q;
+      Ws[i / LG_D][i % LG_D] = wr[q];
+    }
+#pragma unroll
+    for (int q = 0; q < NNQ; q++) {
+      const int i = tid + 256 * q;
+      Ns[i / LG_D][i % LG_D] = nr[q];
     }
     __syncthreads();
-    const int nd = min(128, D - d0);
-    for (int dc = 0; dc < nd; dc++) acc = __fmaf_rn(Ws[lane][dc], Ns[w][dc], acc);
+    if (d0 + LG_D < D) fetch(d0 + LG_D);
+    float ca[4] = {0.f, 0.f, 0.f, 0.f}, cb[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 8
+    for (int dc = 0; dc < LG_D; dc += 4) {
+      const float4 wv = *reinterpret_cast<const float4*>(&Ws[lane][dc]);
+      const float4 na = *reinterpret_cast<const float4*>(&Ns[2 * w][dc]);
+      const float4 nb = *reinterpret_cast<const float4*>(&Ns[2 * w + 1][dc]);
+      ca[0] = __fmaf_rn(wv.x, na.x, ca[0]);
+      ca[1] = __fmaf_rn(wv.y, na.y, ca[1]);
+      ca[2] = __fmaf_rn(wv.z, na.z, ca[2]);
+      ca[3] = __fmaf_rn(wv.w, na.w, ca[3]);
+      cb[0] = __fmaf_rn(wv.x, nb.x, cb[0]);
+      cb[1] = __fmaf_rn(wv.y, nb.y, cb[1]);
+      cb[2] = __fmaf_rn(wv.z, nb.z, cb[2]);
+      cb[3] = __fmaf_rn(wv.w, nb.w, cb[3]);
+    }
+    acc_a = fadd(acc_a, fadd(fadd(ca[0], ca[1]), fadd(ca[2], ca[3])));
+    acc_b = fadd(acc_b, fadd(fadd(cb[0], cb[1]), fadd(cb[2], cb[3])));
     __syncthreads();
   }
-  if (t < T && e < E) a.logits[(size_t)t * E + e] = a.router_b ? fadd(acc, a.router_b[e]) : acc;
+  if (e < E) {
+    const float b = a.router_b ? a.router_b[e] : 0.f;
+    if (ta < T) a.logits[(size_t)ta * E + e] = a.router_b ? fadd(acc_a, b) : acc_a;
+    if (tb < T) a.logits[(size_t)tb * E + e] = a.router_b ? fadd(acc_b, b) : acc_b;
+  }
 }
 
 __global__ void __launch_bounds__(256) select_kernel(BatchRouteArgs a) {
@@ -441,7 +491,7 @@ __global__ void __launch_bounds__(256) select_kernel(BatchRouteArgs a) {
     if (u == 0x80000000u) u = 0u;
     id[i] = e;
     key[i] = e >= E ? 0u : v[i] != v[i] ? 1u : (u >> 31) ? ~u : (u | 0x80000000u);
-    if (e < E) a.member[(size_t)t * E + e] = 0;
+    if (e < E) a.member[(size_t)e * a.T + t] = 0;
   }
   // K rounds: the warp's largest key, the lowest id among equal keys
 #pragma unroll 1
@@ -502,53 +552,57 @@ __global__ void __launch_bounds__(256) select_kernel(BatchRouteArgs a) {
   int p = 0;
   for (int q = 0; q < K; q++) p += ((vm >> q) & 1u) && __shfl_sync(0xffffffffu, bi, q) < bi;
   if (valid) {
-    a.member[(size_t)t * E + bi] = (uint8_t)(lane + 1);
+    a.member[(size_t)bi * a.T + t] = (uint8_t)(lane + 1);
     a.tpos[(size_t)t * K + lane] = p;
+    atomicAdd(a.ecnt + bi, 1);
   }
   if (lane < K && lane >= __popc(vm)) a.tok_rows[(size_t)t * K + lane] = -1;
 }
 
-__global__ void __launch_bounds__(1024) plan_kernel(BatchRouteArgs a) {
-  __shared__ int cnt[256], off[256], slot_of[256];
+// One CTA per expert e (blockIdx.x).  Every CTA scans the experts' row
+// counts (select_kernel's) into row offsets and slot numbers; CTA e then
+// lists its expert's active rows in row order: each warp counts the members
+// of its 32-row chunks of the expert's membership column, the chunks' counts
+// are scanned, and each member row is written at the expert's offset plus
+// the members before it.  CTA 0 writes the plan header.
+constexpr int PLAN_THREADS = 512, PLAN_MAX_CHUNKS = 256;   // rows up to 8192
+__global__ void __launch_bounds__(PLAN_THREADS) plan_kernel(BatchRouteArgs a) {
+  __shared__ int off[256], slot_of[256], chunk[PLAN_MAX_CHUNKS];
+  __shared__ int wsum[2][PLAN_THREADS / 32];
   pdl_wait();
   pdl_trigger();
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
-  const int E = a.E, T = a.T, K = a.top_k;
-  // rows per expert: one warp per expert, 32 rows per ballot
-  for (int e = w; e < E; e += 32) {
-    int c = 0;
-    for (int t0 = 0; t0 < T; t0 += 32) {
-      const int t = t0 + lane;
-      c += __popc(__ballot_sync(0xffffffffu, t < T && a.member[(size_t)t * E + e] != 0));
-    }
-    if (lane == 0) cnt[e] = c;
-  }
-  __syncthreads();
-  if (w == 0) {   // exclusive scans of counts and of non-empty experts
-    int bc = 0, bz = 0;
-    for (int e0 = 0; e0 < E; e0 += 32) {
-      const int e = e0 + lane;
-      const int c = e < E ? cnt[e] : 0, nz = c > 0;
-      int sc = c, sz = nz;
+  constexpr int NW = PLAN_THREADS / 32;
+  const int E = a.E, T = a.T, K = a.top_k, e = blockIdx.x;
+  {   // exclusive scans of the counts and of the non-empty experts (E <= 256 <= threads)
+    const int c = tid < E ? __ldcg(a.ecnt + tid) : 0, nz = c > 0;
+    int sc = c, sz = nz;
 #pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const int a1 = __shfl_up_sync(0xffffffffu, sc, o), a2 = __shfl_up_sync(0xffffffffu, sz, o);
-        if (lane >= o) {
-          sc += a1;
-          sz += a2;
-        }
+    for (int o = 1; o < 32; o <<= 1) {
+      const int a1 = __shfl_up_sync(0xffffffffu, sc, o), a2 = __shfl_up_sync(0xffffffffu, sz, o);
+      if (lane >= o) {
+        sc += a1;
+        sz += a2;
       }
-      if (e < E) {
-        off[e] = bc + sc - c;
-        slot_of[e] = nz ? bz + sz - 1 : -1;
-      }
-      bc += __shfl_sync(0xffffffffu, sc, 31);
-      bz += __shfl_sync(0xffffffffu, sz, 31);
     }
-    if (lane == 0) {
+    if (lane == 31) {
+      wsum[0][w] = sc;
+      wsum[1][w] = sz;
+    }
+    __syncthreads();
+    int bc = 0, bz = 0;
+    for (int j = 0; j < w; j++) {
+      bc += wsum[0][j];
+      bz += wsum[1][j];
+    }
+    if (tid < E) {
+      off[tid] = bc + sc - c;
+      slot_of[tid] = nz ? bz + sz - 1 : -1;
+    }
+    if (e == 0 && tid == PLAN_THREADS - 1) {
       PlanHdr* h = a.plan;
-      h->n_slots = bz;
-      h->total_rows = bc;
+      h->n_slots = bz + sz;
+      h->total_rows = bc + sc;
       h->k = T;
       h->embed_dim = a.D;
       h->inter_dim = a.I;
@@ -560,41 +614,60 @@ __global__ void __launch_bounds__(1024) plan_kernel(BatchRouteArgs a) {
       h->wts = a.wts;
       h->row_slot = a.row_slot;
     }
+    __syncthreads();
+  }
+  const int sl = slot_of[e];
+  if (sl < 0) return;   // uniform over the CTA
+  const uint8_t* col = a.member + (size_t)e * T;
+  const int nch = (T + 31) / 32;
+  for (int c = w; c < nch; c += NW) {
+    const int t = 32 * c + lane;
+    const unsigned bal = __ballot_sync(0xffffffffu, t < T && __ldcg(col + t) != 0);
+    if (lane == 0) chunk[c] = __popc(bal);
   }
   __syncthreads();
-  // each expert's active rows in row order
-  for (int e = w; e < E; e += 32) {
-    const int sl = slot_of[e];
-    if (sl < 0) continue;
-    int o = off[e];
-    for (int t0 = 0; t0 < T; t0 += 32) {
-      const int t = t0 + lane;
-      const int m = t < T ? a.member[(size_t)t * E + e] : 0;
-      const unsigned bal = __ballot_sync(0xffffffffu, m != 0);
-      if (m) {
-        const int pos = o + __popc(bal & ((1u << lane) - 1u));
-        a.rows[pos] = t;
-        a.wts[pos] = a.sel_w[(size_t)t * K + (m - 1)];
-        a.row_slot[pos] = sl;
-        a.tok_rows[(size_t)t * K + a.tpos[(size_t)t * K + (m - 1)]] = pos;
+  if (w == 0) {   // exclusive scan over the chunks
+    int run = 0;
+    for (int c0 = 0; c0 < nch; c0 += 32) {
+      const int c = c0 + lane;
+      const int v = c < nch ? chunk[c] : 0;
+      int sc = v;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int a1 = __shfl_up_sync(0xffffffffu, sc, o);
+        if (lane >= o) sc += a1;
       }
-      o += __popc(bal);
+      if (c < nch) chunk[c] = run + sc - v;
+      run += __shfl_sync(0xffffffffu, sc, 31);
     }
-    if (lane == 0) {
-      const ExpertDesc& X = a.experts[e];
-      SlotDesc d;
-      d.gate = X.gate;
-      d.up = X.up;
-      d.down = X.down;
-      d.gb = X.gb;
-      d.ub = X.ub;
-      d.db = X.db;
-      d.n_rows = cnt[e];
-      d.row_off = off[e];
-      d.expert = e;
-      d.pad = 0;
-      a.slots[sl] = d;
+  }
+  __syncthreads();
+  for (int c = w; c < nch; c += NW) {
+    const int t = 32 * c + lane;
+    const int m = t < T ? __ldcg(col + t) : 0;
+    const unsigned bal = __ballot_sync(0xffffffffu, m != 0);
+    if (m) {
+      const int pos = off[e] + chunk[c] + __popc(bal & ((1u << lane) - 1u));
+      a.rows[pos] = t;
+      a.wts[pos] = a.sel_w[(size_t)t * K + (m - 1)];
+      a.row_slot[pos] = sl;
+      a.tok_rows[(size_t)t * K + a.tpos[(size_t)t * K + (m - 1)]] = pos;
     }
+  }
+  if (tid == 0) {
+    const ExpertDesc& X = a.experts[e];
+    SlotDesc d;
+    d.gate = X.gate;
+    d.up = X.up;
+    d.down = X.down;
+    d.gb = X.gb;
+    d.ub = X.ub;
+    d.db = X.db;
+    d.n_rows = __ldcg(a.ecnt + e);
+    d.row_off = off[e];
+    d.expert = e;
+    d.pad = 0;
+    a.slots[sl] = d;
   }
 }
 
@@ -613,14 +686,17 @@ static cudaError_t launch_cfg(const void* fn, dim3 grid, dim3 block, cudaStream_
 }
 
 cudaError_t launch_batch_route(const BatchRouteArgs& args, cudaStream_t s) {
-  if (args.top_k < 1 || args.top_k > 8 || args.top_k > args.E || args.E > 256 || args.T < 1) return cudaErrorInvalidValue;
+  if (args.top_k < 1 || args.top_k > 8 || args.top_k > args.E || args.E > 256 || args.T < 1 ||
+      args.T > 32 * PLAN_MAX_CHUNKS || !args.ecnt)
+    return cudaErrorInvalidValue;
   BatchRouteArgs a = args;
   cudaError_t e = launch_cfg(reinterpret_cast<const void*>(norm_q8_kernel), dim3(a.T), dim3(256), s, &a);
   if (e == cudaSuccess)
-    e = launch_cfg(reinterpret_cast<const void*>(logits_kernel), dim3((a.T + 7) / 8, (a.E + 31) / 32), dim3(256), s, &a);
+    e = launch_cfg(reinterpret_cast<const void*>(logits_kernel), dim3((a.T + LG_T - 1) / LG_T, (a.E + LG_E - 1) / LG_E),
+                   dim3(256), s, &a);
   if (e == cudaSuccess)
     e = launch_cfg(reinterpret_cast<const void*>(select_kernel), dim3((a.T * 32 + 255) / 256), dim3(256), s, &a);
-  if (e == cudaSuccess) e = launch_cfg(reinterpret_cast<const void*>(plan_kernel), dim3(1), dim3(1024), s, &a);
+  if (e == cudaSuccess) e = launch_cfg(reinterpret_cast<const void*>(plan_kernel), dim3(a.E), dim3(PLAN_THREADS), s, &a);
   return e;
 }
 

@@ -148,6 +148,7 @@ struct Ctx {
   bool user_stream_set = false;
   DevStatus* d_status = nullptr;
   DevStatus* h_status = nullptr;  // pinned
+  unsigned int* d_arrived = nullptr;   // deliver_kernel's CTA count (zero between launches)
   DevBuf d_stage, d_xq8, d_hidden, d_hq8, d_tmp, d_counters, d_parts;
   PinBuf h_up, h_down;
   MapBuf h_ret;                   // deliver_async's result block
@@ -213,10 +214,13 @@ bool ensure_init() {
   if (!cuda_ok(cudaStreamCreateWithFlags(&g.own_stream, cudaStreamNonBlocking), "cudaStreamCreate") ||
       !cuda_ok(cudaMalloc(&g.d_status, sizeof(DevStatus)), "cudaMalloc(status)") ||
       !cuda_ok(cudaMallocHost(&g.h_status, sizeof(DevStatus)), "cudaMallocHost(status)") ||
-      !cuda_ok(cudaMemset(g.d_status, 0, sizeof(DevStatus)), "cudaMemset(status)")) {
+      !cuda_ok(cudaMemset(g.d_status, 0, sizeof(DevStatus)), "cudaMemset(status)") ||
+      !cuda_ok(cudaMalloc(&g.d_arrived, sizeof(unsigned int)), "cudaMalloc(arrivals)") ||
+      !cuda_ok(cudaMemset(g.d_arrived, 0, sizeof(unsigned int)), "cudaMemset(arrivals)")) {
     g.init_failed = true;
     return false;
   }
+  register_counters(g.d_arrived, sizeof(unsigned int));   // cleared again after a device error
   g.inited = true;
   return true;
 }
@@ -256,39 +260,57 @@ bool finish(const char* what) {
 // fence, echoes the host's request number; the host spins on that word.
 
 __global__ void deliver_kernel(const float* __restrict__ src, size_t n, const DevStatus* __restrict__ st,
-                               RetHdr* hdr, float* out) {
+                               RetHdr* hdr, float* out, unsigned int* arrived) {
   __shared__ unsigned int req;
+  __shared__ bool last;
   if (threadIdx.x == 0) req = *reinterpret_cast<volatile unsigned int*>(&hdr->req);
   asm volatile("griddepcontrol.wait;" ::: "memory");   // src and st come from the preceding kernel
-  const size_t n4 = n / 4;
-  for (size_t i = threadIdx.x; i < n4; i += blockDim.x)
+  const size_t n4 = n / 4, step = (size_t)gridDim.x * blockDim.x, i0 = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  for (size_t i = i0; i < n4; i += step)
     reinterpret_cast<float4*>(out)[i] = __ldcg(reinterpret_cast<const float4*>(src) + i);
-  for (size_t i = n4 * 4 + threadIdx.x; i < n; i += blockDim.x) out[i] = __ldcg(src + i);
+  for (size_t i = n4 * 4 + i0; i < n; i += step) out[i] = __ldcg(src + i);
+  // the last CTA to finish its share writes the status and the echo (one
+  // CTA: no count)
+  __syncthreads();
   if (threadIdx.x == 0) {
+    if (gridDim.x == 1) {
+      last = true;
+    } else {
+      __threadfence_system();
+      last = atomicAdd(arrived, 1u) == gridDim.x - 1;
+      if (last) *arrived = 0;
+      __threadfence();
+    }
+  }
+  __syncthreads();
+  if (last && threadIdx.x == 0) {
     volatile DevStatus* hs = &hdr->st;
     hs->code = st->code;
     hs->where = st->where;
     hs->a = st->a;
     hs->b = st->b;
-  }
-  __syncthreads();
-  if (threadIdx.x == 0) {
     __threadfence_system();
     *reinterpret_cast<volatile unsigned int*>(&hdr->done) = req;
   }
 }
 
-// One CTA: copies n floats from mapped pinned host memory, which the host
-// wrote before the launch, into device memory.  The loads skip any cached
-// copy of the host lines (ld.global.cv).  It lets the next kernel launch at
-// once; that kernel waits for this grid (griddepcontrol.wait) before it
-// reads dst.
+// Copies n floats from mapped pinned host memory, which the host wrote
+// before the launch, into device memory (one CTA for a decode step's rows,
+// more for large batches).  The loads skip any cached copy of the host lines
+// (ld.global.cv).  It lets the next kernel launch at once; that kernel waits
+// for this grid (griddepcontrol.wait) before it reads dst.
 __global__ void fetch_kernel(const float* __restrict__ src, size_t n, float* __restrict__ dst) {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-  const size_t n4 = n / 4;
-  for (size_t i = threadIdx.x; i < n4; i += blockDim.x)
+  const size_t n4 = n / 4, step = (size_t)gridDim.x * blockDim.x, i0 = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  for (size_t i = i0; i < n4; i += step)
     reinterpret_cast<float4*>(dst)[i] = __ldcv(reinterpret_cast<const float4*>(src) + i);
-  for (size_t i = n4 * 4 + threadIdx.x; i < n; i += blockDim.x) dst[i] = __ldcv(src + i);
+  for (size_t i = n4 * 4 + i0; i < n; i += step) dst[i] = __ldcv(src + i);
+}
+
+// CTAs of the fetch and delivery copies: one up to 64 K floats (a decode
+// step's rows), then one per 64 K floats, at most 32.
+static unsigned copy_ctas(size_t n_floats) {
+  return (unsigned)std::min<size_t>(32, std::max<size_t>(1, (n_floats + 65535) / 65536));
 }
 
 float* fetch_reserve(size_t n_floats) {
@@ -297,7 +319,7 @@ float* fetch_reserve(size_t n_floats) {
 
 bool fetch_async(float* d_dst, size_t n_floats, cudaStream_t s, const char* what) {
   if (!g.h_in.reserve(sizeof(float) * n_floats)) return false;
-  fetch_kernel<<<1, 512, 0, s>>>(static_cast<const float*>(g.h_in.d), n_floats, d_dst);
+  fetch_kernel<<<copy_ctas(n_floats), 512, 0, s>>>(static_cast<const float*>(g.h_in.d), n_floats, d_dst);
   count_launches(1);
   return cuda_ok(cudaGetLastError(), what);
 }
@@ -314,9 +336,10 @@ bool deliver_async(const float* d_src, size_t n_floats, cudaStream_t s, const ch
   // launched as a programmatic dependent: it is scheduled while the
   // preceding kernel runs and waits for that grid before reading its output
   const DevStatus* st = g.d_status;
-  void* args[] = {(void*)&d_src, (void*)&n_floats, (void*)&st, (void*)&hdr, (void*)&out};
+  unsigned int* arrived = g.d_arrived;
+  void* args[] = {(void*)&d_src, (void*)&n_floats, (void*)&st, (void*)&hdr, (void*)&out, (void*)&arrived};
   cudaLaunchConfig_t cfg{};
-  cfg.gridDim = dim3(1);
+  cfg.gridDim = dim3(copy_ctas(n_floats));
   cfg.blockDim = dim3(512);
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
