@@ -211,6 +211,8 @@ def test_ep_stepper_resyncs_epochs_on_cpu_ranks(peer_sees_failure):
 
 
 def _skip_rank(rank, world, port, q):
+    import ctypes
+
     import torch
     import torch.distributed as dist
     from datetime import timedelta
@@ -253,7 +255,7 @@ def _skip_rank(rank, world, port, q):
             got = out.cpu().numpy()
             err = float(np.max(np.abs(got - whole)) / np.max(np.abs(whole)))
         shard.close()
-        q.put((rank, oks, err, log))
+        q.put((rank, oks, err, log + stepper.errors))
     except Exception as ex:             # reported to the test, which fails on it
         q.put((rank, None, None, log + [repr(ex)]))
     finally:

@@ -137,13 +137,15 @@ class EpStepper:
         self.layers = list(layers)
         self.group = group
         self.resets = 0
+        self.errors = []           # (step number, repr of the exception) of steps that raised
 
     def __call__(self, step):
         import torch
         import torch.distributed as dist
         try:
             ok = bool(step())
-        except Exception:          # a failed step is reported, never skipped by peers
+        except Exception as ex:    # a failed step is reported to the peers, never skipped
+            self.errors.append((self.resets, repr(ex)))
             ok = False
         backend = dist.get_backend(self.group)
         dev = torch.device("cuda", torch.cuda.current_device()) if backend == "nccl" else torch.device("cpu")
