@@ -1094,7 +1094,8 @@ def step_trace(lib, step, n_steps=1):
     with each CTA's own global-timer span) or poll counts."""
     import torch
     grid = lib.tg_cuda_step_trace(None)
-    buf = torch.zeros(grid * TRACE_SLOTS + grid * 16 * 8, dtype=torch.int64, device="cuda")
+    nw = lib.tg_cuda_step_trace_warps()
+    buf = torch.zeros(grid * TRACE_SLOTS + grid * nw * 8, dtype=torch.int64, device="cuda")
     torch.cuda.synchronize()
     lib.tg_cuda_step_trace(ctypes.c_void_p(buf.data_ptr()))
     try:
@@ -1110,7 +1111,8 @@ def step_trace(lib, step, n_steps=1):
     cyc_per_us = np.median(span_cyc / np.maximum(span_ns, 1.0)) * 1000.0
     phases = {name: (t[:, b] - t[:, a]) / cyc_per_us for name, a, b in TRACE_PHASES}
     phases["whole step (CTA)"] = span_ns / 1000.0
-    wv = v[grid * TRACE_SLOTS:].reshape(grid * 16, 8)
+    wv = v[grid * TRACE_SLOTS:].reshape(grid * nw, 8)
+    wv = wv[wv.any(axis=1)]   # records of warps a narrower step does not have stay zero
     w = wv[:, :6] / cyc_per_us
     warps = {name: w[:, i] for i, name in enumerate(TRACE_WARP)}
     warps["A end -> hidden ready"] = wv[:, 7] / cyc_per_us

@@ -247,8 +247,11 @@ int tg_layer_set_router(void *layer, const float *router_w, const float *router_
 /* Diagnostics: fused steps launched after this call write per-CTA phase
  * timestamps into dev_buf (32 uint64 per CTA: SM clocks, the global timer in
  * slots 12/13, the logits poll count in slot 19; then 8 uint64 per warp of
- * ring and poll counters); NULL stops it.  Returns the step's grid size. */
+ * ring and poll counters, tg_cuda_step_trace_warps() warps per CTA); NULL
+ * stops it.  Returns the step's grid size. */
 int tg_cuda_step_trace(void *dev_buf);
+/* Warps per CTA of the fused step, i.e. the per-warp trace records per CTA. */
+int tg_cuda_step_trace_warps(void);
 /* Tests of the fused step's bounded waits (no device fault is involved):
  * steps launched after this call give up on a poll of another CTA's or GPU's
  * words after poll_limit polls (<= 0: the default, about a second) and

@@ -502,6 +502,8 @@ int tg_cuda_step_trace(void* dev_buf) {
   return sms;
 }
 
+int tg_cuda_step_trace_warps(void) { return step_warps(); }
+
 // Selects the fused single-kernel step (on = 1, the default) or the
 // three-kernel step (on = 0) for this layer.  Returns the previous setting.
 // Replaces a layer's router with host arrays router_w [E][D] and router_b

@@ -132,6 +132,8 @@ cudaError_t launch_layer_step(const StepLaunch& l, cudaStream_t s);
 // Diagnostics: later step launches write [grid][16] phase timestamps to p
 // (device memory; null turns it off).
 void set_step_trace(void* p);
+// Warps per CTA of the fused step kernel (the trace's per-warp records).
+int step_warps();
 // Tests of the bounded waits: later step launches give up after poll_limit
 // polls of another CTA's or GPU's words (<= 0: the default, about a second),
 // and CTA skip_logit_cta (-1: none) publishes no logits, so every CTA's

@@ -39,7 +39,8 @@
 
 namespace tg {
 
-constexpr int SW = 16;             // warps per CTA
+constexpr int SW_MAX = 20;         // warps per CTA: 20 for MXFP4 steps (their phase A decodes on the
+                                   // integer pipes and gains from more warps), 16 otherwise
 constexpr int ST_MAX_NST = 8;      // ring stages per warp
 constexpr int STEP_T_MAX = 8;
 constexpr int STEP_K_MAX = 8;
@@ -56,7 +57,7 @@ struct StepShared {
   int cnt[STEP_E_MAX];
   int slot_of[STEP_E_MAX];
   int off[STEP_E_MAX];
-  int wsum[2][SW];
+  int wsum[2][SW_MAX];
   int n_slots, total, ok;
   uint32_t epoch;
   int slot_e[STEP_R_MAX], slot_n[STEP_R_MAX], slot_off[STEP_R_MAX];
@@ -66,11 +67,11 @@ struct StepShared {
   float part_dot[STEP_RW_MAX][STEP_T_MAX][STEP_GB_MAX];
   float rrt[STEP_T_MAX];
   double yd[STEP_T_MAX];
-  uint64_t rbar[SW];
+  uint64_t rbar[SW_MAX];
   uint64_t xbar, ebar;
-  float accw[SW][STEP_T_MAX];
-  unsigned long long tw[SW][8];
-  uint64_t bars[SW][ST_MAX_NST];
+  float accw[SW_MAX][STEP_T_MAX];
+  unsigned long long tw[SW_MAX][8];
+  uint64_t bars[SW_MAX][ST_MAX_NST];
 };
 
 // ---------------------------------------------------------------------
@@ -263,7 +264,7 @@ static __device__ __noinline__ void step_issue(const StepExpert* sx, SCur c, uin
   }
 }
 
-template <int GF, int DF>
+template <int GF, int DF, int SW>
 __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
   extern __shared__ __align__(128) uint8_t dsm[];
   __shared__ StepShared sh;
@@ -274,8 +275,11 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
   const int gw = wid * G + blockIdx.x, NW = G * SW;
   const int gbpr = (D + QK - 1) / QK, dbpr = (I + QK - 1) / QK;
   uint8_t* ring = dsm + (size_t)wid * a.nst * a.stage_bytes;
-  float* rrow = reinterpret_cast<float*>(dsm + (size_t)SW * a.nst * a.stage_bytes);   // [rwc][D]
-  XQ* xa = reinterpret_cast<XQ*>(reinterpret_cast<uint8_t*>(rrow) + round16((size_t)a.rwc * D * 4));   // [T][gbpr]
+  // phase R borrows the rings' bytes: x (and add) at their start, this CTA's
+  // router rows at their end; no ring item is issued before R has read them
+  const size_t rings = (size_t)SW * a.nst * a.stage_bytes, rrow_bytes = round16((size_t)a.rwc * D * 4);
+  float* rrow = reinterpret_cast<float*>(dsm + rings - rrow_bytes);   // [rwc][D]
+  XQ* xa = reinterpret_cast<XQ*>(dsm + rings);   // [T][gbpr]
   XQ* xs = xa + (size_t)T * gbpr;   // [xcap][dbpr]
   StepExpert* sx = reinterpret_cast<StepExpert*>(xs + (size_t)a.xcap * dbpr);   // [xcap] the slots' experts
   StepExpert* etab = sx + a.xcap;                                                 // [E]
@@ -315,7 +319,7 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
   const uint32_t ep = sh.epoch;
   pdl_wait();      // x (and add) are written by the preceding kernel
   const uint32_t xbytes = (uint32_t)T * D * 4;
-  const bool xstaged = (size_t)xbytes * (a.add_in ? 2 : 1) <= (size_t)SW * a.nst * a.stage_bytes;
+  const bool xstaged = (size_t)xbytes * (a.add_in ? 2 : 1) + rrow_bytes <= rings;
   const float* xsm = reinterpret_cast<const float*>(dsm);
   const float* asm_ = a.add_in ? xsm + (size_t)T * D : nullptr;
   if (tid == 0 && xstaged) {
@@ -696,6 +700,7 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
   SCur ic{0, gw - NW, 0, 0};
   int issued = 0;
   bool more = true;
+  if (lane == 0) fence_proxy_async();   // the rings' bytes were read through the generic proxy in phase R
   for (int i = 0; i < a.nst && more; i++) {
     more = scur_next(ic, gw, NW, nA, D, n_slots, SB);
     if (more) {
@@ -986,7 +991,7 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
   if (wid == SW - 1) TG_MARK(11);
   if (a.trace && tid == 0) a.trace[blockIdx.x * 32 + 13] = gtimer();
   if (a.trace && lane == 0)
-    for (int q = 0; q < 8; q++) a.trace[(size_t)gridDim.x * 32 + ((size_t)blockIdx.x * SW + wid) * 8 + q] = tw[q];
+    for (int q = 0; q < 8; q++) a.trace[(size_t)gridDim.x * 32 + ((size_t)blockIdx.x * SW_MAX + wid) * 8 + q] = tw[q];
   // bounded waits for any copies still in flight before the CTA exits
   if (!dead)
     for (int i = j; i < issued; i++) mbar_wait(&bar[i % a.nst], (uint32_t)(i / a.nst) & 1u);
@@ -1007,6 +1012,17 @@ struct StepShape {
   size_t smem;
 };
 
+static size_t step_smem_optin() {
+  static int v = 0;
+  if (!v) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    if (v < 48 * 1024) v = 48 * 1024;
+  }
+  return (size_t)v;
+}
+
 static int step_sms() {
   static int sms = 0;
   if (!sms) {
@@ -1018,7 +1034,11 @@ static int step_sms() {
   return sms;
 }
 
+// Warps per CTA of a step with this gate format.
+static int step_warps_for(int gate_fmt) { return gate_fmt == FMT_MXFP4 ? SW_MAX : 16; }
+
 static bool step_shape(const StepLaunch& l, StepShape& sh) {
+  const int SW = step_warps_for(l.gate_fmt);
   const bool gf = l.gate_fmt == FMT_Q4K || l.gate_fmt == FMT_Q6K || l.gate_fmt == FMT_MXFP4 || l.gate_fmt == FMT_Q80;
   const bool df = l.down_fmt == FMT_Q4K || l.down_fmt == FMT_Q6K || l.down_fmt == FMT_MXFP4 || l.down_fmt == FMT_Q80;
   if (!gf || !df || l.T < 1 || l.T > STEP_T_MAX || l.E < 1 || l.E > STEP_E_MAX || l.top_k < 1 ||
@@ -1043,10 +1063,13 @@ static bool step_shape(const StepLaunch& l, StepShape& sh) {
   if (sh.rwc > STEP_RW_MAX || (l.D + QK - 1) / QK > STEP_GB_MAX) return false;
   const int gbpr = (l.D + QK - 1) / QK, dbpr = (l.I + QK - 1) / QK;
   sh.xcap = l.T * l.top_k;
-  const size_t fixed = round16((size_t)sh.rwc * l.D * 4) + (size_t)l.T * gbpr * sizeof(XQ) +
-                       (size_t)sh.xcap * dbpr * sizeof(XQ) + (size_t)sh.xcap * sizeof(StepExpert) +
-                       (size_t)l.E * sizeof(StepExpert);
-  const size_t budget = 220 * 1024 - sizeof(StepShared);
+  // the router rows live at the end of the rings' bytes during phase R
+  const size_t rrow = round16((size_t)sh.rwc * l.D * 4);
+  const size_t fixed = (size_t)l.T * gbpr * sizeof(XQ) + (size_t)sh.xcap * dbpr * sizeof(XQ) +
+                       (size_t)sh.xcap * sizeof(StepExpert) + (size_t)l.E * sizeof(StepExpert);
+  const size_t optin = step_smem_optin();
+  if (optin < sizeof(StepShared) + fixed + rrow + 4096) return false;
+  const size_t budget = optin - 256 - sizeof(StepShared);
   const uint32_t dr = rows_stage_bytes(row_layout(l.down_fmt, l.I).rs, 1);
   const uint32_t sa = 2 * rows_stage_bytes(row_layout(l.gate_fmt, l.D).rs, sh.pa);
   // phase-B slots per item: every slot of the step if the stage allows
@@ -1061,7 +1084,7 @@ static bool step_shape(const StepLaunch& l, StepShape& sh) {
     sb = std::max(1, sb / 2);
   }
   sh.sb = sb;
-  if (fixed + (size_t)SW * 2 * sh.stage > budget) return false;
+  if (fixed + (size_t)SW * 2 * sh.stage > budget || (size_t)SW * 2 * sh.stage < rrow) return false;
   sh.nst = (int)std::min<size_t>(ST_MAX_NST, (budget - fixed) / ((size_t)SW * sh.stage));
   sh.smem = (size_t)SW * sh.nst * sh.stage + fixed;
   return true;
@@ -1069,6 +1092,7 @@ static bool step_shape(const StepLaunch& l, StepShape& sh) {
 
 template <int GF, int DF>
 static cudaError_t step_launch(StepArgs a, const StepShape& sh, cudaStream_t s) {
+  constexpr int SW = GF == FMT_MXFP4 ? SW_MAX : 16;
   a.stage_bytes = sh.stage;
   a.nst = sh.nst;
   a.rwc = sh.rwc;
@@ -1076,7 +1100,7 @@ static cudaError_t step_launch(StepArgs a, const StepShape& sh, cudaStream_t s) 
   a.pa = sh.pa;
   a.sb = sh.sb;
   a.sl = sh.sl;
-  const void* fn = reinterpret_cast<const void*>(layer_step_kernel<GF, DF>);
+  const void* fn = reinterpret_cast<const void*>(layer_step_kernel<GF, DF, SW>);
   cudaError_t e = ensure_smem(fn, sh.smem);
   if (e != cudaSuccess) return e;
   static size_t fits = 0;   // largest shared-memory size known to fit one CTA per SM
@@ -1121,6 +1145,7 @@ bool step_eligible(const StepLaunch& l) {
 
 static unsigned long long* g_step_trace = nullptr;
 void set_step_trace(void* p) { g_step_trace = static_cast<unsigned long long*>(p); }
+int step_warps() { return SW_MAX; }
 static int g_poll_limit = STEP_POLLS, g_skip_logit_cta = -1;
 void set_step_fault(int skip_logit_cta, int poll_limit) {
   g_skip_logit_cta = skip_logit_cta;
