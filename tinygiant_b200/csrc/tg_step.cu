@@ -61,7 +61,8 @@ struct StepShared {
   int n_slots, total, ok;
   uint32_t epoch;
   int slot_e[STEP_R_MAX], slot_n[STEP_R_MAX], slot_off[STEP_R_MAX];
-  int row_t[STEP_R_MAX];
+  int row_t[STEP_R_MAX];   // active row -> token
+  int row_s[STEP_R_MAX];   // active row -> slot
   float row_w[STEP_R_MAX];
   float part_ss[STEP_T_MAX][STEP_GB_MAX];
   float part_dot[STEP_RW_MAX][STEP_T_MAX][STEP_GB_MAX];
@@ -69,7 +70,6 @@ struct StepShared {
   double yd[STEP_T_MAX];
   uint64_t rbar[SW_MAX];
   uint64_t xbar, ebar;
-  float accw[SW_MAX][STEP_T_MAX];
   unsigned long long tw[SW_MAX][8];
   uint64_t bars[SW_MAX][ST_MAX_NST];
 };
@@ -186,16 +186,19 @@ struct StepArgs {
   unsigned long long* sync;   // launch counter
   unsigned long long* lgt;    // [T][E] tagged logits
   unsigned long long* hidt;   // [T*top_k][dbpr][256] tagged hidden
+  unsigned long long* hflag;  // [T*top_k*dbpr] tagged: block q of hq is this epoch's
+  XQ* hq;                     // [T*top_k*dbpr] Q8 of hidden, each block quantized once in the grid
   int ep_rank, ep_world;      // expert-parallel combine in the kernel (ep_world 1: off)
   unsigned long long* const* ep_peers;   // [ep_world] every shard's receive block
   const unsigned long long* ep_recv;     // this shard's receive block [ep_world][T][D]
   uint32_t stage_bytes;   // ring stage size
   int nst;                // ring stages per warp
   int xcap;               // active rows whose Q8 hidden blocks fit each CTA's shared memory
+  int xq_n;               // XQ blocks in shared memory: T gbpr + xcap dbpr, or the larger if alias_x
+  int alias_x;            // the Q8 of hidden overlays the Q8 of the inputs (written after phase A)
   int rwc;                // router rows staged per CTA
   int pa;                 // row pairs per phase-A item
   int sb;                 // slots per phase-B item
-  int sl;                 // phase-B lanes per block (slot lanes), a power of two
   DevStatus* st;
   unsigned long long* trace;   // [gridDim.x][16] phase timestamps, or null
   int poll_limit;         // polls of another CTA's (or GPU's) words before giving up
@@ -279,9 +282,9 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
   // router rows at their end; no ring item is issued before R has read them
   const size_t rings = (size_t)SW * a.nst * a.stage_bytes, rrow_bytes = round16((size_t)a.rwc * D * 4);
   float* rrow = reinterpret_cast<float*>(dsm + rings - rrow_bytes);   // [rwc][D]
-  XQ* xa = reinterpret_cast<XQ*>(dsm + rings);   // [T][gbpr]
-  XQ* xs = xa + (size_t)T * gbpr;   // [xcap][dbpr]
-  StepExpert* sx = reinterpret_cast<StepExpert*>(xs + (size_t)a.xcap * dbpr);   // [xcap] the slots' experts
+  XQ* xa = reinterpret_cast<XQ*>(dsm + rings);           // [T][gbpr]
+  XQ* xs = a.alias_x ? xa : xa + (size_t)T * gbpr;         // [xcap][dbpr]
+  StepExpert* sx = reinterpret_cast<StepExpert*>(xa + a.xq_n);   // [xcap] the slots' experts
   StepExpert* etab = sx + a.xcap;                                                 // [E]
   uint64_t* bar = sh.bars[wid];
   if (a.trace && tid == 0) a.trace[blockIdx.x * 32 + 12] = gtimer();
@@ -581,6 +584,7 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
         sh.slot_n[rank] = 1;
         sh.slot_off[rank] = rank;
         sh.row_t[rank] = 0;
+        sh.row_s[rank] = rank;
         sh.row_w[rank] = w;
         sx[rank] = etab[e];
       }
@@ -610,7 +614,7 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
         v[jj] = i0 + jj < D ? x : 0.f;
       }
     }
-    quantize_xq<GF == FMT_MXFP4>(v, n, xa + q);
+    quantize_xq<GF == FMT_MXFP4, GF>(v, n, xa + q);
   }
   if (wid == T) TG_MARK(18);
   for (int i = tid; i < E; i += SW * 32) sh.cnt[i] = 0;
@@ -619,14 +623,15 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
   if (T > 1) {
     // experts held by another GPU (no local weights) are skipped; their
     // contribution arrives through the cross-GPU sum
+    // cnt[e]: the tokens that selected expert e, as a bit mask
     for (int i = tid; i < T * K; i += SW * 32) {
       const int t = i / K, j = i - t * K;
       const int e = sh.sel_e[t][j];
-      if (sh.sel_w[t][j] != 0.f && etab[e].g) atomicAdd(&sh.cnt[e], 1);
+      if (sh.sel_w[t][j] != 0.f && etab[e].g) atomicOr(&sh.cnt[e], 1 << t);
     }
     __syncthreads();
     {   // exclusive scans of row counts and of non-empty experts over e < E <= 256
-      const int c = tid < E ? sh.cnt[tid] : 0, nz = c > 0;
+      const int c = tid < E ? __popc(sh.cnt[tid]) : 0, nz = c > 0;
       int sc = c, sz = nz;
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
@@ -659,18 +664,21 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
     for (int e = tid; e < E; e += SW * 32) {
       const int s = sh.slot_of[e];
       if (s < 0) continue;
-      int o = sh.off[e];
       sh.slot_e[s] = e;
-      sh.slot_n[s] = sh.cnt[e];
-      sh.slot_off[s] = o;
-      for (int t = 0; t < T; t++)
-        for (int j = 0; j < K; j++)
-          if (sh.sel_e[t][j] == e && sh.sel_w[t][j] != 0.f) {
-            sh.row_t[o] = t;
-            sh.row_w[o] = sh.sel_w[t][j];
-            o++;
-          }
+      sh.slot_n[s] = __popc(sh.cnt[e]);
+      sh.slot_off[s] = sh.off[e];
       sx[s] = etab[e];
+    }
+    // a slot's rows in token order: (t, j) goes after the slot's earlier tokens
+    for (int i = tid; i < T * K; i += SW * 32) {
+      const int t = i / K, j = i - t * K;
+      const int e = sh.sel_e[t][j];
+      const int m = sh.cnt[e];
+      if (!((m >> t) & 1) || sh.sel_w[t][j] == 0.f) continue;   // (a token selects an expert at most once)
+      const int o = sh.off[e] + __popc(m & ((1 << t) - 1));
+      sh.row_t[o] = t;
+      sh.row_s[o] = sh.slot_of[e];
+      sh.row_w[o] = sh.sel_w[t][j];
     }
     __syncthreads();
   }
@@ -814,9 +822,9 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
   if (wid == 0) TG_MARK(5);
   if (wid == SW - 1) TG_MARK(10);
   tph = 1;
-  // ---- hidden: every CTA polls the active rows' hidden blocks (tagged with
-  // this epoch) and quantizes them into its shared memory, two blocks per
-  // warp at a time.
+  // ---- hidden: every CTA needs the Q8 of every active row's hidden blocks
+  // (tagged with this epoch) in its shared memory.  A few blocks: each CTA
+  // polls and quantizes them itself, two blocks per warp at a time.
   bool okh = !dead;
   if (total > a.xcap) {
     if (tid == 0) set_error(a.st, ERR_BAD_PLAN, 35, total, a.xcap);
@@ -824,69 +832,142 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
   }
   const int nh = okh ? total * dbpr : 0;   // hidden blocks
   const long long ta = a.trace ? clock64() : 0;
-  for (int q0 = wid; q0 < nh; q0 += 2 * SW) {
-    float v[2][8];
-    int nn[2];
-#pragma unroll
-    for (int h = 0; h < 2; h++) {
-      const int q = q0 + h * SW;
-      nn[h] = q < nh ? min(QK, I - (q % dbpr) * QK) : 0;
-    }
-    for (int it = 0;; it++) {
-      bool ok = true;
-#pragma unroll
-      for (int h = 0; h < 2; h++) {
-        const unsigned long long* src = a.hidt + (size_t)(q0 + h * SW) * 256 + 2 * lane;
+  if (a.alias_x) __syncthreads();   // xs overlays xa: every warp of this CTA is past phase A
+  if (nh > 4 * SW) {
+    // Many blocks: each is quantized once in the grid (block q by warp q / G
+    // of CTA q % G) into hq, published by its tagged flag; every CTA then
+    // copies all of them, each warp's lanes polling 32 flags at a time.
+    for (int q = (int)blockIdx.x + wid * G; q < nh && okh; q += NW) {
+      const int nq = min(QK, I - (q % dbpr) * QK);
+      const unsigned long long* src = a.hidt + (size_t)q * 256 + 2 * lane;
+      float v[8];
+      for (int it = 0;; it++) {
+        bool ok = true;
 #pragma unroll
         for (int p = 0; p < 4; p++) {
           const int i = 8 * lane + 2 * p;
-          v[h][2 * p] = v[h][2 * p + 1] = 0.f;
-          if (i < nn[h]) {
+          v[2 * p] = v[2 * p + 1] = 0.f;
+          if (i < nq) {
             const ulonglong2 w = ld_tagged2(src + 64 * p);
             ok &= tag_is(w.x, ep);
-            v[h][2 * p] = tag_val(w.x);
-            if (i + 1 < nn[h]) {
+            v[2 * p] = tag_val(w.x);
+            if (i + 1 < nq) {
               ok &= tag_is(w.y, ep);
-              v[h][2 * p + 1] = tag_val(w.y);
+              v[2 * p + 1] = tag_val(w.y);
             }
           }
         }
-      }
-      if (__all_sync(FULL, ok)) {
-        if (a.trace && lane == 0) {
-          tw[6] += it + 1;
-          if (q0 == wid) tw[7] = clock64() - ta;
+        if (__all_sync(FULL, ok)) break;
+        if (it >= a.poll_limit) {
+          if (lane == 0) set_error(a.st, ERR_WAIT_TIMEOUT, 33, blockIdx.x, wid);
+          okh = false;
+          break;
         }
-        break;
+        __nanosleep(64);
       }
-      if (it >= a.poll_limit) {
-        if (lane == 0) set_error(a.st, ERR_WAIT_TIMEOUT, 33, blockIdx.x, wid);
-        okh = false;
-        break;
+      if (!okh) break;
+      quantize_xq<DF == FMT_MXFP4, DF>(v, nq, a.hq + q);
+      __syncwarp();
+      if (lane == 0) {
+        __threadfence();   // the warp's stores of block q before its flag
+        st_tagged(a.hflag + q, ep, 0.f);
       }
-      __nanosleep(64);
     }
-    if (!okh) break;
-    if (wid == 0 && q0 == 0) TG_MARK(6);
-#pragma unroll 1
-    for (int h = 0; h < 2 && nn[h] > 0; h++) {
-      XQ& xb = xs[q0 + h * SW];
-      float vv[8];
+    if (wid == 0) TG_MARK(6);
+    for (int q0 = wid; q0 < nh && okh; q0 += 32 * SW) {
+      const int q = q0 + SW * lane;
+      bool seen = q >= nh;
+      for (int it = 0;; it++) {
+        if (!seen) seen = tag_is(ld_tagged(a.hflag + q), ep);
+        if (__all_sync(FULL, seen)) {
+          if (a.trace && lane == 0) {
+            tw[6] += it + 1;
+            if (q0 == wid) tw[7] = clock64() - ta;
+          }
+          break;
+        }
+        if (it >= a.poll_limit) {
+          if (lane == 0) set_error(a.st, ERR_WAIT_TIMEOUT, 34, blockIdx.x, wid);
+          okh = false;
+          break;
+        }
+        __nanosleep(64);
+      }
+      if (!okh) break;
+      __threadfence();   // each lane's flag observed before the warp reads the blocks
+      __syncwarp();
+      constexpr int QW = sizeof(XQ) / 16;
+      const int nb = min(32, (nh - q0 + SW - 1) / SW);   // blocks q0 + SW i, i < nb
+      for (int i = lane; i < nb * QW; i += 32) {
+        const int bi = i / QW, c = i - bi * QW;
+        reinterpret_cast<uint4*>(xs + q0 + SW * bi)[c] = __ldcg(reinterpret_cast<const uint4*>(a.hq + q0 + SW * bi) + c);
+      }
+    }
+  } else {
+    for (int q0 = wid; q0 < nh; q0 += 2 * SW) {
+      float v[2][8];
+      int nn[2];
 #pragma unroll
-      for (int jj = 0; jj < 8; jj++) vv[jj] = h ? v[1][jj] : v[0][jj];
-      quantize_xq<DF == FMT_MXFP4>(vv, nn[h], &xb);
+      for (int h = 0; h < 2; h++) {
+        const int q = q0 + h * SW;
+        nn[h] = q < nh ? min(QK, I - (q % dbpr) * QK) : 0;
+      }
+      for (int it = 0;; it++) {
+        bool ok = true;
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+          const unsigned long long* src = a.hidt + (size_t)(q0 + h * SW) * 256 + 2 * lane;
+#pragma unroll
+          for (int p = 0; p < 4; p++) {
+            const int i = 8 * lane + 2 * p;
+            v[h][2 * p] = v[h][2 * p + 1] = 0.f;
+            if (i < nn[h]) {
+              const ulonglong2 w = ld_tagged2(src + 64 * p);
+              ok &= tag_is(w.x, ep);
+              v[h][2 * p] = tag_val(w.x);
+              if (i + 1 < nn[h]) {
+                ok &= tag_is(w.y, ep);
+                v[h][2 * p + 1] = tag_val(w.y);
+              }
+            }
+          }
+        }
+        if (__all_sync(FULL, ok)) {
+          if (a.trace && lane == 0) {
+            tw[6] += it + 1;
+            if (q0 == wid) tw[7] = clock64() - ta;
+          }
+          break;
+        }
+        if (it >= a.poll_limit) {
+          if (lane == 0) set_error(a.st, ERR_WAIT_TIMEOUT, 33, blockIdx.x, wid);
+          okh = false;
+          break;
+        }
+        __nanosleep(64);
+      }
+      if (!okh) break;
+      if (wid == 0 && q0 == 0) TG_MARK(6);
+#pragma unroll 1
+      for (int h = 0; h < 2 && nn[h] > 0; h++) {
+        XQ& xb = xs[q0 + h * SW];
+        float vv[8];
+#pragma unroll
+        for (int jj = 0; jj < 8; jj++) vv[jj] = h ? v[1][jj] : v[0][jj];
+        quantize_xq<DF == FMT_MXFP4, DF>(vv, nn[h], &xb);
+      }
     }
   }
   if (wid == 0) TG_MARK(15);
   if (!__syncthreads_and(okh)) stop(j);
   if (wid == 0) TG_MARK(7);
 
-  // phase B: rows r = gw, gw + NW, ... < D; slots in groups of SB
-  // phase-B lanes: lane = block * SL + slot, so the 8 lanes of a quarter warp
-  // read 8 different slots' rows (distinct banks)
-  const int dbpr2 = DBLK ? dbpr : 1, SL = a.sl;
-  const int b_b = lane / SL, b_sl = lane - b_b * SL;
-  float* accw = sh.accw[wid];   // running output of the warp's row, per token
+  // phase B: rows r = gw, gw + NW, ... < D; slots in groups of SB (one ring
+  // stage), the group's active rows in rounds of rpr: lane = block * rpr +
+  // row, so the 8 lanes of a quarter warp read 8 different rows (distinct
+  // slots' bytes, or one slot's bytes broadcast)
+  const int dbpr2 = DBLK ? dbpr : 1, rpr = 32 / dbpr2;
+  const int b_b = lane / rpr, b_r = lane - b_b * rpr;
   // Output row r (lane t < T holds token t's value); expert parallel: this
   // shard's part, combined across shards by ep_combine_row.
   auto emit_row = [&](int r, float v) {
@@ -901,87 +982,65 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
   };
   if (n_slots > 0)
     for (int r = gw; r < D; r += NW) {
-      if (lane < T) accw[lane] = 0.f;
-      __syncwarp();
+      float acc = 0.f;   // lane t < T: token t's output, parts added in slot order
       for (int s0 = 0; s0 < n_slots; s0 += SB, j++) {
         const int stg = j % a.nst;
         if (!wait_stage(stg, j)) continue;
         const uint8_t* dst = ring + (size_t)stg * a.stage_bytes;
         const int s1 = min(n_slots, s0 + SB);
+        // the group's active rows ra .. rb - 1 (slot-major, each slot's in token order)
+        const int ra = sh.slot_off[s0], rb = sh.slot_off[s1 - 1] + sh.slot_n[s1 - 1];
         if constexpr (DBLK) {
-          const int s = s0 + b_sl;
-          const bool in = s < s1, on = in && b_b < dbpr2;
-          const int sc = in ? s : s0;
-          const StepExpert& X = sx[sc];
-          const int n = in ? sh.slot_n[sc] : 0, off = sh.slot_off[sc];
-          const RowPtrs rp = row_ptrs(wdesc<DF>(X.d, D, I), (int)r, dst + (sc - s0) * dr);
-          const uint8_t* mb = rp.m + (size_t)b_b * dbb;
-          const uint8_t* s1b = rp.a1 ? rp.a1 + b_b * 16 : nullptr;
-          const uint8_t* s2b = rp.a2 ? rp.a2 + b_b * 2 : nullptr;
-#pragma unroll 1
-          for (int t = 0; t < T; t++) {
-            // this slot's active row for token t (a slot's rows are in token order)
-            int jr = -1;
-            for (int jj = 0; jj < n; jj++)
-              if (sh.row_t[off + jj] == t) jr = jj;
-            float term = 0.f;
-            if (on && jr >= 0) {
-              const XQ& xb = xs[(size_t)(off + jr) * dbpr + b_b];
-              if constexpr (DF == FMT_Q4K) term = q4k_block_term(mb, xb, use_x4(rule, jr & ~3, n, k));
-              else term = q6k_block_term(mb, s1b, s2b, xb);
-            }
-            const float tot = fold_row(term, b_sl, dbpr2, SL);
-            float part = 0.f;
-            if (in && jr >= 0 && b_b == 0) {
-              const float w = sh.row_w[off + jr];
-              part = a.bias_term ? fmul(w, fadd(tot, X.db ? X.db[r] : 0.f)) : fmul(w, tot);
-            }
-            const int has = in && jr >= 0;
-            // the parts of the group's slots, added in slot order
-            float acc = accw[t];
-            for (int q = 0; q < s1 - s0; q++) {
-              const float pv = shfl(part, q);
-              if (__shfl_sync(FULL, has, q)) acc = fadd(acc, pv);
-            }
-            __syncwarp();
-            if (lane == 0) accw[t] = acc;
-            __syncwarp();
-          }
-        } else {
-          // two slots per pass: lanes 0-15 slot sp, lanes 16-31 slot sp + 1;
-          // their parts are added in slot order
-#pragma unroll 1
-          for (int sp = s0; sp < s1; sp += 2) {
-            const int s = sp + (lane >> 4);
-            const bool in = s < s1;
-            const int sc = in ? s : sp;
+          // rounds of rpr rows: lane = block * rpr + row, each lane one block term
+          for (int q0 = ra; q0 < rb; q0 += rpr) {
+            const int rho = q0 + b_r, rc = rho < rb ? rho : q0;
+            const bool on = b_b < dbpr2 && rho < rb;
+            const int sc = sh.row_s[rc];
             const StepExpert& X = sx[sc];
-            const RowPtrs rp = row_ptrs(wdesc<DF>(X.d, D, I), r, dst + (sc - s0) * dr);
-            const int n = in ? sh.slot_n[sc] : 0, off = sh.slot_off[sc];
-            const float db = X.db ? X.db[r] : 0.f;
-#pragma unroll 1
-            for (int t = 0; t < T; t++) {
-              int jr = -1;
-              for (int jj = 0; jj < n; jj++)
-                if (sh.row_t[off + jj] == t) jr = jj;
-              const float v = half_dot_sub32<DF>(rp, I / 32, xs + (size_t)(off + max(jr, 0)) * dbpr);
-              const float w = jr >= 0 ? sh.row_w[off + jr] : 0.f;
-              const float part = a.bias_term ? fmul(w, fadd(v, db)) : fmul(w, v);
-              const float p0 = shfl(part, 0), p1 = shfl(part, 16);
-              const int h0 = __shfl_sync(FULL, jr >= 0, 0), h1 = __shfl_sync(FULL, jr >= 0, 16);
-              if (lane == 0) {
-                float acc = accw[t];
-                if (h0) acc = fadd(acc, p0);
-                if (h1) acc = fadd(acc, p1);
-                accw[t] = acc;
+            const RowPtrs rp = row_ptrs(wdesc<DF>(X.d, D, I), (int)r, dst + (sc - s0) * dr);
+            const int bb = min(b_b, dbpr2 - 1);
+            float term = 0.f;
+            if (on) {
+              const XQ& xb = xs[(size_t)rc * dbpr + bb];
+              const uint8_t* mb = rp.m + (size_t)bb * dbb;
+              if constexpr (DF == FMT_Q4K) {
+                term = q4k_block_term(mb, xb, use_x4(rule, (rc - sh.slot_off[sc]) & ~3, sh.slot_n[sc], k));
+              } else {
+                term = q6k_block_term(mb, rp.a1 ? rp.a1 + bb * 16 : nullptr, rp.a2 ? rp.a2 + bb * 2 : nullptr, xb);
               }
             }
+            const float tot = fold_row(term, b_r, dbpr2, rpr);
+            float part = 0.f;
+            if (rho < rb) {
+              const float w = sh.row_w[rc];
+              part = a.bias_term ? fmul(w, fadd(tot, X.db ? X.db[r] : 0.f)) : fmul(w, tot);
+            }
+            // row q0 + i's part on lane i: token t's lane adds the round's rows in order
+            const int nr = min(rpr, rb - q0);
+            for (int i = 0; i < nr; i++) {
+              const float v = shfl(part, i);
+              if (lane == sh.row_t[q0 + i]) acc = fadd(acc, v);
+            }
           }
-          __syncwarp();
+        } else {
+          // two rows per pass: lanes 0-15 row q0, lanes 16-31 row q0 + 1
+#pragma unroll 1
+          for (int q0 = ra; q0 < rb; q0 += 2) {
+            const int rho = q0 + (lane >> 4), rc = rho < rb ? rho : q0;
+            const int sc = sh.row_s[rc];
+            const StepExpert& X = sx[sc];
+            const RowPtrs rp = row_ptrs(wdesc<DF>(X.d, D, I), r, dst + (sc - s0) * dr);
+            const float v = half_dot_sub32<DF>(rp, I / 32, xs + (size_t)rc * dbpr);
+            const float w = sh.row_w[rc], db = X.db ? X.db[r] : 0.f;
+            const float part = a.bias_term ? fmul(w, fadd(v, db)) : fmul(w, v);
+            const float p0 = shfl(part, 0), p1 = shfl(part, 16);
+            if (lane == sh.row_t[q0]) acc = fadd(acc, p0);
+            if (q0 + 1 < rb && lane == sh.row_t[q0 + 1]) acc = fadd(acc, p1);
+          }
         }
         refill(stg);
       }
-      emit_row(r, lane < T ? accw[lane] : 0.f);
+      emit_row(r, lane < T ? acc : 0.f);
       __syncwarp();
     }
   else
@@ -1000,15 +1059,20 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
 // ---------------------------------------------------------------------
 // Launcher.
 
+// The exchange block: launch counter (32 words), tagged logits [t][E], tagged
+// hidden [t top_k][dbpr][256], hidden blocks' flags [t top_k dbpr] and their
+// Q8 [t top_k dbpr] (XQ), each region from a 256-byte boundary.
+static size_t round32(size_t n) { return (n + 31) & ~(size_t)31; }
 size_t step_sync_words(int T, int E, int top_k, int I) {
   const int t = std::min(T, STEP_T_MAX), dbpr = (I + QK - 1) / QK;
-  return 32 + (((size_t)t * E + 31) & ~(size_t)31) + (size_t)t * top_k * dbpr * 256;
+  const size_t nh = (size_t)t * top_k * dbpr;
+  return 32 + round32((size_t)t * E) + nh * 256 + round32(nh) + round32(nh * sizeof(XQ) / 8);
 }
 
 // Shared-memory shape of one launch, or false when the step does not fit.
 struct StepShape {
   uint32_t stage;
-  int nst, rwc, xcap, pa, sb, sl;
+  int nst, rwc, xcap, pa, sb, alias, xq_n;
   size_t smem;
 };
 
@@ -1065,29 +1129,37 @@ static bool step_shape(const StepLaunch& l, StepShape& sh) {
   sh.xcap = l.T * l.top_k;
   // the router rows live at the end of the rings' bytes during phase R
   const size_t rrow = round16((size_t)sh.rwc * l.D * 4);
-  const size_t fixed = (size_t)l.T * gbpr * sizeof(XQ) + (size_t)sh.xcap * dbpr * sizeof(XQ) +
-                       (size_t)sh.xcap * sizeof(StepExpert) + (size_t)l.E * sizeof(StepExpert);
+  const size_t nxa = (size_t)l.T * gbpr, nxh = (size_t)sh.xcap * dbpr;
+  const size_t tabs = (size_t)sh.xcap * sizeof(StepExpert) + (size_t)l.E * sizeof(StepExpert);
   const size_t optin = step_smem_optin();
-  if (optin < sizeof(StepShared) + fixed + rrow + 4096) return false;
   const size_t budget = optin - 256 - sizeof(StepShared);
   const uint32_t dr = rows_stage_bytes(row_layout(l.down_fmt, l.I).rs, 1);
   const uint32_t sa = 2 * rows_stage_bytes(row_layout(l.gate_fmt, l.D).rs, sh.pa);
-  // phase-B slots per item: every slot of the step if the stage allows
-  sh.sl = 1;
-  if (dblk)
-    while (2 * sh.sl * bd <= 32) sh.sl *= 2;
+  // phase-B slots per item (one stage): as many as fit; 32-value formats at
+  // most what the phase-A stage holds
   const int max_slots = std::min(l.E, l.T * l.top_k);
-  int sb = dblk ? std::min(sh.sl, max_slots) : std::min(2, max_slots);   // 32-value formats: two slots per pass
-  for (;;) {
-    sh.stage = std::max(sa, (uint32_t)sb * dr);
-    if (fixed + (size_t)SW * 2 * sh.stage <= budget || sb == 1) break;
-    sb = std::max(1, sb / 2);
+  const int sb_cap = std::max(1, std::min(max_slots, dblk ? 32 : std::max(2, (int)(sa / dr))));
+  // the Q8 of the inputs and of hidden side by side, else (larger steps)
+  // overlaid: hidden is quantized after phase A
+  for (int alias = 0; alias < 2; alias++) {
+    const size_t nxq = alias ? std::max(nxa, nxh) : nxa + nxh;
+    const size_t fixed = nxq * sizeof(XQ) + tabs;
+    if (optin < sizeof(StepShared) + fixed + rrow + 4096) continue;
+    int sb = sb_cap;
+    for (;;) {
+      sh.stage = std::max(sa, (uint32_t)sb * dr);
+      if (fixed + (size_t)SW * 2 * sh.stage <= budget || sb == 1) break;
+      sb--;
+    }
+    sh.sb = sb;
+    if (fixed + (size_t)SW * 2 * sh.stage > budget || (size_t)SW * 2 * sh.stage < rrow) continue;
+    sh.nst = (int)std::min<size_t>(ST_MAX_NST, (budget - fixed) / ((size_t)SW * sh.stage));
+    sh.smem = (size_t)SW * sh.nst * sh.stage + fixed;
+    sh.alias = alias;
+    sh.xq_n = (int)nxq;
+    return true;
   }
-  sh.sb = sb;
-  if (fixed + (size_t)SW * 2 * sh.stage > budget || (size_t)SW * 2 * sh.stage < rrow) return false;
-  sh.nst = (int)std::min<size_t>(ST_MAX_NST, (budget - fixed) / ((size_t)SW * sh.stage));
-  sh.smem = (size_t)SW * sh.nst * sh.stage + fixed;
-  return true;
+  return false;
 }
 
 template <int GF, int DF>
@@ -1099,7 +1171,8 @@ static cudaError_t step_launch(StepArgs a, const StepShape& sh, cudaStream_t s) 
   a.xcap = sh.xcap;
   a.pa = sh.pa;
   a.sb = sh.sb;
-  a.sl = sh.sl;
+  a.alias_x = sh.alias;
+  a.xq_n = sh.xq_n;
   const void* fn = reinterpret_cast<const void*>(layer_step_kernel<GF, DF, SW>);
   cudaError_t e = ensure_smem(fn, sh.smem);
   if (e != cudaSuccess) return e;
@@ -1182,7 +1255,12 @@ cudaError_t launch_layer_step(const StepLaunch& l, cudaStream_t s) {
   // layer sized for its largest T); words left there by earlier launches
   // carry older epochs and are never taken
   a.lgt = l.sync + 32;
-  a.hidt = a.lgt + (((size_t)std::min(l.T, STEP_T_MAX) * l.E + 31) & ~(size_t)31);
+  a.hidt = a.lgt + round32((size_t)std::min(l.T, STEP_T_MAX) * l.E);
+  {
+    const size_t nh = (size_t)std::min(l.T, STEP_T_MAX) * l.top_k * ((l.I + QK - 1) / QK);
+    a.hflag = a.hidt + nh * 256;
+    a.hq = reinterpret_cast<XQ*>(a.hflag + round32(nh));
+  }
   a.st = l.st;
   a.trace = g_step_trace;
   a.poll_limit = g_poll_limit;

@@ -358,13 +358,13 @@ __device__ __forceinline__ void warp_dot(const RowPtrs& rp, int cols, const Q8De
 struct __align__(16) XQ {
   int8_t qs[QK];        // 0
   float scale;          // 256
-  int32_t sum;          // 260
-  int32_t pad0[2];
-  int32_t bsums[8];     // 272
-  int32_t xs16[16];     // 304: sum of 16-value group g = 8h + 2k + lq at 4 (2h + lq) + k
-  float bsf[8];         // 368: bsums as fp32 (exact: |bsum| <= 4064)
+  int32_t pad0[3];
+  union {               // 272: the sums the consuming format's block terms use
+    float bsf[8];       // Q4_K: 32-value sums as fp32 (exact: |bsum| <= 4064)
+    int32_t xs16[16];   // Q6_K: sum of 16-value group g = 8h + 2k + lq at 4 (2h + lq) + k
+  };
 };
-static_assert(sizeof(XQ) == 400, "XQ layout");
+static_assert(sizeof(XQ) == 336, "XQ layout");
 
 // Slot of the sum of 16-value group g (values 16g .. 16g + 15) in XQ.xs16.
 __host__ __device__ __forceinline__ int xs16_slot(int g) { return 4 * (2 * (g >> 3) + (g & 1)) + ((g & 7) >> 1); }
@@ -392,8 +392,9 @@ __device__ __forceinline__ float fmax_nan(float a, float b) {
 }
 
 // The quantizer of tg_q8.cuh (quantize_q8, csrc/libtinygiant.c:169-208) run
-// by one warp into the staged form XQ, its extra fields (sums of each 16
-// values, 32-value sums as fp32) formed from the same lane sums.  Lane l
+// by one warp into the staged form XQ, its extra field for the consuming
+// format CF (Q6_K: sums of each 16 values; Q4_K: 32-value sums as fp32)
+// formed from the same lane sums.  Lane l
 // holds v[j] = value 8l + j of the block; positions at or past n are stored
 // as 0.  The amax reduction is a tree (max is order-free); a NaN in the block
 // gives the canonical NaN scale, where the reference propagates the NaN it
@@ -402,7 +403,7 @@ __device__ __forceinline__ float fmax_nan(float a, float b) {
 // PERM stores each 32-value sub-block's qs in the MXFP4 order: word 2k + h
 // holds values (4k + 2h, 16 + 4k + 2h, 4k + 2h + 1, 17 + 4k + 2h), the
 // order in which mxfp4_isum reads a code word's nibbles.
-template <bool PERM = false>
+template <bool PERM = false, int CF = FMT_Q4K>
 __device__ __forceinline__ void quantize_xq(const float (&v)[8], int n, XQ* o) {
   const int lane = threadIdx.x & 31;
   float m[8];
@@ -447,18 +448,12 @@ __device__ __forceinline__ void quantize_xq(const float (&v)[8], int n, XQ* o) {
   }
   const int s16 = s + __shfl_xor_sync(FULL, s, 1);        // values 16 (l / 2) .. + 15
   const int s32 = s16 + __shfl_xor_sync(FULL, s16, 2);    // sub-block l / 4
-  int tot = s32 + __shfl_xor_sync(FULL, s32, 4);
-  tot += __shfl_xor_sync(FULL, tot, 8);
-  tot += __shfl_xor_sync(FULL, tot, 16);
-  if ((lane & 1) == 0) o->xs16[xs16_slot(lane >> 1)] = s16;
-  if ((lane & 3) == 0) {
-    o->bsums[lane >> 2] = s32;
-    o->bsf[lane >> 2] = (float)s32;
+  if constexpr (CF == FMT_Q6K) {
+    if ((lane & 1) == 0) o->xs16[xs16_slot(lane >> 1)] = s16;
+  } else if constexpr (CF == FMT_Q4K) {
+    if ((lane & 3) == 0) o->bsf[lane >> 2] = (float)s32;
   }
-  if (lane == 0) {
-    o->scale = div_rn_d(a, 127.f, 1.0 / 127.0);
-    o->sum = tot;
-  }
+  if (lane == 0) o->scale = div_rn_d(a, 127.f, 1.0 / 127.0);
 }
 
 // Exact int -> fp32 for |v| < 2^22 on the integer and fp32 pipes: the bits of
