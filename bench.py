@@ -1079,7 +1079,12 @@ TRACE_PHASES = [
     ("plan (T>1)", 21, 4),
     ("phase A (warp 0)", 4, 5),
     ("hidden poll (warp 0)", 5, 6),
+    ("  CTA barrier (w0, T > 5)", 5, 25),
+    ("  poll of its block (w0, T > 2)", 25, 26),
+    ("  Q8 + publish (w0, T > 2)", 26, 6),
     ("Q8 of hidden (warp 0)", 6, 15),
+    ("  flags poll (w0, T > 2)", 6, 27),
+    ("  copy (w0, T > 2)", 27, 15),
     ("CTA sync", 15, 7),
     ("phase B (warp 0)", 7, 8),
 ]
@@ -1109,12 +1114,14 @@ def step_trace(lib, step, n_steps=1):
     span_ns = (t[:, 13] - t[:, 12]).astype(np.float64)
     span_cyc = (t[:, 8] - t[:, 0]).astype(np.float64)
     cyc_per_us = np.median(span_cyc / np.maximum(span_ns, 1.0)) * 1000.0
-    phases = {name: (t[:, b] - t[:, a]) / cyc_per_us for name, a, b in TRACE_PHASES}
+    # phases whose marks this step does not set (other T) are left out
+    phases = {name: (t[:, b] - t[:, a]) / cyc_per_us for name, a, b in TRACE_PHASES if t[:, a].all() and t[:, b].all()}
     phases["whole step (CTA)"] = span_ns / 1000.0
     wv = v[grid * TRACE_SLOTS:].reshape(grid * nw, 8)
     wv = wv[wv.any(axis=1)]   # records of warps a narrower step does not have stay zero
     w = wv[:, :6] / cyc_per_us
     warps = {name: w[:, i] for i, name in enumerate(TRACE_WARP)}
+    warps["A total"] = w[:, 0] + w[:, 1] + w[:, 2]
     warps["A end -> hidden ready"] = wv[:, 7] / cyc_per_us
     counts = {"logits polls (CTA)": t[:, 19], "hidden polls (warp)": wv[:, 6]}
     return phases, warps, counts
@@ -1122,7 +1129,7 @@ def step_trace(lib, step, n_steps=1):
 
 def run_trace(a):
     """--config trace [--gptoss] [--experts E] [--copies R] [--tokens T]: the
-    fused step's phase timeline (median and max over CTAs / warps), after one
+    fused step's phase timeline (percentiles over CTAs / warps), after one
     idle step and for the last of 8 back-to-back steps.  Diagnostics only."""
     import torch
 
@@ -1157,12 +1164,17 @@ def run_trace(a):
             for tag, n in (("one step after idle", 1), ("last of 8 back-to-back steps", 8)):
                 phases, warps, counts = step_trace(lib, step, n)
                 print(f"== {tag}")
+                print(f"  {'':37s}{'min':>8s}{'p10':>8s}{'median':>8s}{'p90':>8s}{'max':>8s}")
+
+                def row(name, d, fmt="8.2f"):
+                    q = np.percentile(d, [0, 10, 50, 90, 100])
+                    print(f"  {name:37s}" + "".join(format(x, fmt) for x in q))
                 for name, d in phases.items():
-                    print(f"  {name:28s} median {np.median(d):7.2f} us   max {d.max():7.2f}")
+                    row(name + " (us)", d)
                 for name, d in warps.items():
-                    print(f"  per-warp {name:21s} median {np.median(d):7.2f} us   max {d.max():7.2f}")
+                    row("per-warp " + name + " (us)", d)
                 for name, d in counts.items():
-                    print(f"  {name:28s} median {np.median(d):7.1f}      max {d.max():7.0f}")
+                    row(name, d, "8.0f")
         tg.check(lib)
     finally:
         lib.tg_cuda_set_stream(None)

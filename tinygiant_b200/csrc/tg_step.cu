@@ -92,6 +92,19 @@ __device__ __forceinline__ ulonglong2 ld_tagged2(const unsigned long long* p) {
   return w;
 }
 __device__ __forceinline__ bool tag_is(unsigned long long w, uint32_t ep) { return (uint32_t)(w >> 32) == ep; }
+// A flag that publishes other data: released by its writer (after the data,
+// which the warp's other lanes wrote before a __syncwarp), acquired by its
+// readers.  (A full fence instead would also wait, on the lane that issues
+// the ring's bulk copies, for those copies.)
+__device__ __forceinline__ void st_flag_release(unsigned long long* p, uint32_t ep) {
+  const unsigned long long w = (unsigned long long)ep << 32;
+  asm volatile("st.release.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_flag_acquire(const unsigned long long* p) {
+  unsigned long long w;
+  asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+  return w;
+}
 __device__ __forceinline__ float tag_val(unsigned long long w) { return __uint_as_float((uint32_t)w); }
 
 // System-scope forms, for words another GPU writes over NVLink.
@@ -596,11 +609,9 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
     if (t == 0) TG_MARK(14);
   }
   if (wid == T) TG_MARK(20);
-  // R3, warps T.. first
-#pragma unroll 1
-  for (int q = (wid + SW - T) % SW; q < nq; q += SW) {
-    const int t = q / gbpr, b = q - t * gbpr, i0 = b * QK + 8 * lane, n = min(QK, D - b * QK);
-    float v[8];
+  // R3, warps T.. first: N of block q, quantized
+  auto r3_prep = [&](int q, float (&v)[8]) {
+    const int t = q / gbpr, b = q - t * gbpr, i0 = b * QK + 8 * lane;
     load_block(q, v, false);
     if (a.normalize) {
       const float rr = sh.rrt[t];
@@ -614,7 +625,27 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
         v[jj] = i0 + jj < D ? x : 0.f;
       }
     }
-    quantize_xq<GF == FMT_MXFP4, GF>(v, n, xa + q);
+  };
+  auto r3_n = [&](int q) { return min(QK, D - (q % gbpr) * QK); };
+  if (nq <= SW) {
+#pragma unroll 1
+    for (int q = (wid + SW - T) % SW; q < nq; q += SW) {
+      float v[8];
+      r3_prep(q, v);
+      quantize_xq<GF == FMT_MXFP4, GF>(v, r3_n(q), xa + q);
+    }
+  } else {
+    // two blocks per pass (independent chains; a missing second block
+    // repeats the first, rewriting the same bytes)
+#pragma unroll 1
+    for (int q = (wid + SW - T) % SW; q < nq; q += 2 * SW) {
+      const int q2 = q + SW < nq ? q + SW : q;
+      float v[8], v2[8];
+      r3_prep(q, v);
+      r3_prep(q2, v2);
+      quantize_xq<GF == FMT_MXFP4, GF>(v, r3_n(q), xa + q);
+      quantize_xq<GF == FMT_MXFP4, GF>(v2, r3_n(q2), xa + q2);
+    }
   }
   if (wid == T) TG_MARK(18);
   for (int i = tid; i < E; i += SW * 32) sh.cnt[i] = 0;
@@ -833,6 +864,7 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
   const int nh = okh ? total * dbpr : 0;   // hidden blocks
   const long long ta = a.trace ? clock64() : 0;
   if (a.alias_x) __syncthreads();   // xs overlays xa: every warp of this CTA is past phase A
+  if (wid == 0) TG_MARK(25);
   if (nh > 4 * SW) {
     // Many blocks: each is quantized once in the grid (block q by warp q / G
     // of CTA q % G) into hq, published by its tagged flag; every CTA then
@@ -857,7 +889,10 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
             }
           }
         }
-        if (__all_sync(FULL, ok)) break;
+        if (__all_sync(FULL, ok)) {
+          if (wid == 0 && q == (int)blockIdx.x) TG_MARK(26);
+          break;
+        }
         if (it >= a.poll_limit) {
           if (lane == 0) set_error(a.st, ERR_WAIT_TIMEOUT, 33, blockIdx.x, wid);
           okh = false;
@@ -867,19 +902,17 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
       }
       if (!okh) break;
       quantize_xq<DF == FMT_MXFP4, DF>(v, nq, a.hq + q);
-      __syncwarp();
-      if (lane == 0) {
-        __threadfence();   // the warp's stores of block q before its flag
-        st_tagged(a.hflag + q, ep, 0.f);
-      }
+      __syncwarp();   // the warp's stores of block q before its flag
+      if (lane == 31) st_flag_release(a.hflag + q, ep);
     }
     if (wid == 0) TG_MARK(6);
     for (int q0 = wid; q0 < nh && okh; q0 += 32 * SW) {
       const int q = q0 + SW * lane;
       bool seen = q >= nh;
       for (int it = 0;; it++) {
-        if (!seen) seen = tag_is(ld_tagged(a.hflag + q), ep);
+        if (!seen) seen = tag_is(ld_flag_acquire(a.hflag + q), ep);
         if (__all_sync(FULL, seen)) {
+          if (wid == 0 && q0 == 0) TG_MARK(27);
           if (a.trace && lane == 0) {
             tw[6] += it + 1;
             if (q0 == wid) tw[7] = clock64() - ta;
@@ -894,8 +927,7 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
         __nanosleep(64);
       }
       if (!okh) break;
-      __threadfence();   // each lane's flag observed before the warp reads the blocks
-      __syncwarp();
+      __syncwarp();   // each lane's acquired flag before the warp reads the blocks
       constexpr int QW = sizeof(XQ) / 16;
       const int nb = min(32, (nh - q0 + SW - 1) / SW);   // blocks q0 + SW i, i < nb
       for (int i = lane; i < nb * QW; i += 32) {
