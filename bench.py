@@ -1127,11 +1127,66 @@ def step_trace(lib, step, n_steps=1):
     return phases, warps, counts
 
 
+TC_TRACE = ["producer: waits for a free weight stage", "producer: span",
+            "MMA: waits for A/B operands", "MMA: waits for a free accumulator", "MMA: span",
+            "unpack: waits for weights", "unpack: waits for a free A/B stage", "unpack: waits for free epilogue data",
+            "unpack: waits for row tails", "unpack: span",
+            "epilogue: waits for its data", "epilogue: waits for accumulators", "epilogue: span"]
+
+
+def run_tc_trace(a, T):
+    """--config trace --tokens T > 8 [--gptoss]: the tensor-core GEMMs' role
+    counters per CTA (kilocycles; percentiles over CTAs) for one batched step
+    of C3 (or C4 with --gptoss).  Diagnostics only."""
+    import torch
+
+    import tinygiant_b200 as tg
+    from tinygiant_b200.layer import ResidentLayer
+
+    lib = tg.load()
+    L = make_layer("c4" if a.gptoss else "c3")
+    lay = ResidentLayer(L, max_tokens=T, lib=lib)
+    stream = torch.cuda.Stream()
+    lib.tg_cuda_set_stream(ctypes.c_void_p(stream.cuda_stream))
+    x = torch.randn(T, L.embed_dim, device="cuda")
+    out = torch.zeros_like(x)
+    try:
+        with torch.cuda.stream(stream):
+            for _ in range(3):
+                lib.tg_layer_forward_dev(lay.h, ctypes.c_void_p(x.data_ptr()), None, None,
+                                         ctypes.c_void_p(out.data_ptr()), T, 1, None)
+            torch.cuda.synchronize()
+            grid = lib.tg_cuda_tc_trace(None)
+            buf = torch.zeros(2 * grid * 16, dtype=torch.int64, device="cuda")
+            torch.cuda.synchronize()
+            lib.tg_cuda_tc_trace(ctypes.c_void_p(buf.data_ptr()))
+            lib.tg_layer_forward_dev(lay.h, ctypes.c_void_p(x.data_ptr()), None, None,
+                                     ctypes.c_void_p(out.data_ptr()), T, 1, None)
+            torch.cuda.synchronize()
+            lib.tg_cuda_tc_trace(None)
+        tg.check(lib)
+        v = buf.cpu().numpy().reshape(2, grid, 16).astype(np.float64)
+        for p, name in enumerate(("gate/up", "down")):
+            print(f"== {name} GEMM, T = {T}: units per CTA median {np.median(v[p, :, 13]):.0f}, "
+                  f"steps per CTA median {np.median(v[p, :, 14]):.0f}")
+            print(f"  {'(kcycles)':44s}{'min':>8s}{'p10':>8s}{'median':>8s}{'p90':>8s}{'max':>8s}")
+            for i, n in enumerate(TC_TRACE):
+                q = np.percentile(v[p, :, i] / 1000.0, [0, 10, 50, 90, 100])
+                print(f"  {n:44s}" + "".join(f"{x:8.1f}" for x in q))
+    finally:
+        lib.tg_cuda_set_stream(None)
+        lay.close()
+
+
 def run_trace(a):
     """--config trace [--gptoss] [--experts E] [--copies R] [--tokens T]: the
     fused step's phase timeline (percentiles over CTAs / warps), after one
-    idle step and for the last of 8 back-to-back steps.  Diagnostics only."""
+    idle step and for the last of 8 back-to-back steps; with T > 8 the
+    tensor-core GEMMs' role counters (run_tc_trace).  Diagnostics only."""
     import torch
+    if (a.tokens or 1) > 8:
+        run_tc_trace(a, a.tokens)
+        return
 
     import tinygiant_b200 as tg
     from tinygiant_b200 import synth

@@ -252,6 +252,12 @@ int tg_layer_set_router(void *layer, const float *router_w, const float *router_
 int tg_cuda_step_trace(void *dev_buf);
 /* Warps per CTA of the fused step, i.e. the per-warp trace records per CTA. */
 int tg_cuda_step_trace_warps(void);
+/* Diagnostics: batched steps' tensor-core GEMM launches after this call write
+ * per-CTA role counters into dev_buf ([2][grid][16] uint64: the gate/up pass,
+ * then the down pass; cycles the producer, MMA, unpack and epilogue roles
+ * waited on each ring, each role's span, units and steps); NULL stops it.
+ * Returns the GEMMs' grid size. */
+int tg_cuda_tc_trace(void *dev_buf);
 /* Tests of the fused step's bounded waits (no device fault is involved):
  * steps launched after this call give up on a poll of another CTA's or GPU's
  * words after poll_limit polls (<= 0: the default, about a second) and

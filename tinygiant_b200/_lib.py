@@ -76,6 +76,7 @@ EXT = {
     "tg_layer_set_router": ([VP, VP, VP], CI),
     "tg_cuda_step_trace": ([VP], CI),
     "tg_cuda_step_trace_warps": ([], CI),
+    "tg_cuda_tc_trace": ([VP], CI),
     "tg_cuda_debug_step_fault": ([CI, CI], CI),
     "tg_cuda_debug_tc_isums": ([VP, VP], CI),
     "tg_layer_forward": ([VP, VP, VP, CI, CI], CI),

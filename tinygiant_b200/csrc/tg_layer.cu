@@ -44,7 +44,7 @@ struct Layer {
   bool fused = true;               // use the fused step kernel when the shape allows
   bool tc = true;                  // batched steps (T > 8) on the tensor-core grouped GEMMs
   void* tc_scratch = nullptr;      // their intermediates (tc_moe_scratch_bytes)
-  void* tc_tmaps = nullptr;        // MXFP4 layers: TMA tensor maps [E][3] of the expert matrices
+  void* tc_tmaps = nullptr;        // batched layers: TMA tensor maps [E][6] of the expert matrices (tc_build_tmaps)
   float* nbuf = nullptr;           // batched routing: normalized rows [max_tokens][D]
   uint8_t* member = nullptr;       // batched routing: [E][rows of the step] selection membership
   int* ecnt = nullptr;             // batched routing: [E] active rows per expert
@@ -113,9 +113,8 @@ static bool alloc_scratch(Layer* L) {
                      dmalloc(L, (void**)&L->tok_rows, sizeof(int) * (size_t)L->max_rows))) &&
          (!(T > 8 && tc_moe_eligible(L->gate_fmt, L->down_fmt, D, I)) ||
           (dmalloc(L, &L->tc_scratch, tc_moe_scratch_bytes(L->max_rows, T, L->top_k, D, I)) &&
-           (!(L->gate_fmt == FMT_MXFP4 || L->down_fmt == FMT_MXFP4) ||
-            (dmalloc(L, &L->tc_tmaps, tc_tmap_bytes(E)) &&
-             tc_build_tmaps(L->experts.data(), E, L->tc_tmaps) == cudaSuccess)))) &&
+           dmalloc(L, &L->tc_tmaps, tc_tmap_bytes(E)) &&
+           tc_build_tmaps(L->experts.data(), E, L->tc_tmaps) == cudaSuccess)) &&
          (L->n_shards == 1 ||
           (dmalloc(L, (void**)&L->ep_recv, ep_recv_bytes(L)) &&
            (register_counters(L->ep_recv, ep_recv_bytes(L)), true) &&
@@ -487,6 +486,12 @@ int tg_layer_ep_reset(void* handle) {
 int tg_cuda_debug_tc_isums(void* gate_up, void* down) {
   set_tc_debug(static_cast<int*>(gate_up), static_cast<int*>(down));
   return 0;
+}
+
+int tg_cuda_tc_trace(void* dev_buf) {
+  std::lock_guard<std::recursive_mutex> lk(ctx_mutex());
+  set_tc_trace(dev_buf);
+  return tc_trace_ctas();
 }
 
 int tg_cuda_debug_step_fault(int skip_logit_cta, int poll_limit) {

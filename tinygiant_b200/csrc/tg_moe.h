@@ -157,6 +157,10 @@ cudaError_t tc_build_tmaps(const ExpertDesc* experts, int E, void* d_tmaps);
 // gate/up pass into gate_up and of the down pass into down (device memory,
 // [plan row][matrix][weight row][sub-block], tc_debug_isum_index); null: off.
 void set_tc_debug(int* gate_up, int* down);
+// Diagnostics: per-CTA role counters of later grouped-GEMM launches into p
+// ([2][tc_trace_ctas()][16]: gate/up pass, then down), or off (null).
+void set_tc_trace(void* p);
+int tc_trace_ctas();
 cudaError_t launch_tc_moe(const PlanHdr* ph, int gate_fmt, int down_fmt, int T, int K, int D, int I, int max_rows,
                           const Q8Dev* xq8, const int* tok_rows, const void* tmaps, void* scratch, float* out,
                           DevStatus* st, cudaStream_t s);
