@@ -256,27 +256,34 @@ __device__ __forceinline__ bool scur_next(SCur& c, int gw, int NW, int nA, int D
   return c.r < D;
 }
 
-// Lane 0 of a warp: the bulk copies of item c into stage dst (completing on
-// bar).  Phase 0: rows r0 .. r0 + nr - 1 of the slot's gate (at dst) and up
-// (at dst + ghalf); phase 1: row c.r of the down matrices of slots c.s ..
-// c.s + SB - 1, dr bytes apart.  Not inlined: the ring calls it from three
-// places.
+// The whole warp: the bulk copies of item c into stage dst (completing on
+// bar): lane 0 sets the stage's byte count, then each copy comes from its own
+// lane.  Phase 0: rows r0 .. r0 + nr - 1 of the slot's gate (lane 0, at dst)
+// and up (lane 1, at dst + ghalf); phase 1: row c.r of the down matrices of
+// slots c.s .. c.s + SB - 1 (lane j: slot c.s + j, dr bytes apart; SB <= 32).
+// Not inlined: the ring calls it from two places.
 template <int GF, int DF>
 static __device__ __noinline__ void step_issue(const StepExpert* sx, SCur c, uint8_t* dst, uint64_t* bar, int nrb,
                                                int pa, int I, int D, uint32_t ghalf, uint32_t dr, int n_slots,
                                                int SB) {
+  const int lane = threadIdx.x & 31;
   if (c.ph == 0) {
     const int s = c.a / nrb, r0 = (c.a - s * nrb) * pa, nr = min(pa, I - r0);
     const WDesc Gw = wdesc<GF>(sx[s].g, I, D), Uw = wdesc<GF>(sx[s].u, I, D);
-    mbar_arrive_expect_tx(bar, row_tx(Gw, r0, nr) + row_tx(Uw, r0, nr));
-    stage_row(Gw, r0, dst, bar, nr);
-    stage_row(Uw, r0, dst + ghalf, bar, nr);
+    if (lane == 0) mbar_arrive_expect_tx(bar, row_tx(Gw, r0, nr) + row_tx(Uw, r0, nr));
+    __syncwarp();
+    if (lane == 0) stage_row(Gw, r0, dst, bar, nr);
+    else if (lane == 1) stage_row(Uw, r0, dst + ghalf, bar, nr);
   } else {
-    const int s1 = min(n_slots, c.s + SB);
-    uint32_t tx = 0;
-    for (int s = c.s; s < s1; s++) tx += row_tx(wdesc<DF>(sx[s].d, D, I), (int)c.r);
-    mbar_arrive_expect_tx(bar, tx);
-    for (int s = c.s; s < s1; s++) stage_row(wdesc<DF>(sx[s].d, D, I), (int)c.r, dst + (s - c.s) * dr, bar);
+    const int s = c.s + lane;
+    const bool on = s < min(n_slots, c.s + SB);
+    const WDesc Dw = wdesc<DF>(sx[on ? s : c.s].d, D, I);
+    uint32_t tx = on ? row_tx(Dw, (int)c.r) : 0u;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) tx += __shfl_xor_sync(FULL, tx, o);
+    if (lane == 0) mbar_arrive_expect_tx(bar, tx);
+    __syncwarp();
+    if (on) stage_row(Dw, (int)c.r, dst + lane * dr, bar);
   }
 }
 
@@ -733,17 +740,17 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
   const int k = T, rule = a.assoc_rule, act = a.act;
   const int gbb = GF == FMT_Q4K ? Q4K_BYTES : 192, dbb = DF == FMT_Q4K ? Q4K_BYTES : 192;   // main bytes per block
 
-  auto issue = [&](const SCur& c, int stg) {   // lane 0
+  auto issue = [&](const SCur& c, int stg) {   // the whole warp
     step_issue<GF, DF>(sx, c, ring + (size_t)stg * a.stage_bytes, &bar[stg], nrb, pa, I, D, ghalf, dr, n_slots, SB);
   };
   SCur ic{0, gw - NW, 0, 0};
   int issued = 0;
   bool more = true;
-  if (lane == 0) fence_proxy_async();   // the rings' bytes were read through the generic proxy in phase R
+  fence_proxy_async();   // the rings' bytes were read through the generic proxy in phase R (any lane may issue)
   for (int i = 0; i < a.nst && more; i++) {
     more = scur_next(ic, gw, NW, nA, D, n_slots, SB);
     if (more) {
-      if (lane == 0) issue(ic, i);
+      issue(ic, i);
       issued++;
     }
   }
@@ -786,7 +793,7 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
     if (dead || !more) return;
     more = scur_next(ic, gw, NW, nA, D, n_slots, SB);
     if (more) {
-      if (lane == 0) issue(ic, stg);
+      issue(ic, stg);
       issued++;
     }
     if (a.trace && lane == 0) tw[3 * tph + 2] += clock64() - t0;
