@@ -56,7 +56,10 @@ struct StepShared {
   float sel_w[STEP_T_MAX][STEP_K_MAX];
   int cnt[STEP_E_MAX];
   int slot_of[STEP_E_MAX];
-  int off[STEP_E_MAX];
+  union {
+    int off[STEP_E_MAX];     // the plan (T > 1): each expert's first active row
+    int slot_a[STEP_R_MAX];  // after it: phase A's slot order, most active rows first
+  };
   int wsum[2][SW_MAX];
   int n_slots, total, ok;
   uint32_t epoch;
@@ -258,17 +261,17 @@ __device__ __forceinline__ bool scur_next(SCur& c, int gw, int NW, int nA, int D
 
 // The whole warp: the bulk copies of item c into stage dst (completing on
 // bar): lane 0 sets the stage's byte count, then each copy comes from its own
-// lane.  Phase 0: rows r0 .. r0 + nr - 1 of the slot's gate (lane 0, at dst)
+// lane.  Phase 0: rows r0 .. r0 + nr - 1 of slot aord[c.a / nrb]'s gate (lane 0, at dst)
 // and up (lane 1, at dst + ghalf); phase 1: row c.r of the down matrices of
 // slots c.s .. c.s + SB - 1 (lane j: slot c.s + j, dr bytes apart; SB <= 32).
 // Not inlined: the ring calls it from two places.
 template <int GF, int DF>
-static __device__ __noinline__ void step_issue(const StepExpert* sx, SCur c, uint8_t* dst, uint64_t* bar, int nrb,
-                                               int pa, int I, int D, uint32_t ghalf, uint32_t dr, int n_slots,
-                                               int SB) {
+static __device__ __noinline__ void step_issue(const StepExpert* sx, const int* aord, SCur c, uint8_t* dst,
+                                               uint64_t* bar, int nrb, int pa, int I, int D, uint32_t ghalf,
+                                               uint32_t dr, int n_slots, int SB) {
   const int lane = threadIdx.x & 31;
   if (c.ph == 0) {
-    const int s = c.a / nrb, r0 = (c.a - s * nrb) * pa, nr = min(pa, I - r0);
+    const int sq = c.a / nrb, s = aord[sq], r0 = (c.a - sq * nrb) * pa, nr = min(pa, I - r0);
     const WDesc Gw = wdesc<GF>(sx[s].g, I, D), Uw = wdesc<GF>(sx[s].u, I, D);
     if (lane == 0) mbar_arrive_expect_tx(bar, row_tx(Gw, r0, nr) + row_tx(Uw, r0, nr));
     __syncwarp();
@@ -605,6 +608,7 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
         sh.slot_off[rank] = rank;
         sh.row_t[rank] = 0;
         sh.row_s[rank] = rank;
+        sh.slot_a[rank] = rank;
         sh.row_w[rank] = w;
         sx[rank] = etab[e];
       }
@@ -719,6 +723,19 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
       sh.row_w[o] = sh.sel_w[t][j];
     }
     __syncthreads();
+    // phase A takes the slots with the most rows first, so that their longer
+    // items spread over the warps (ties in slot order)
+    if (wid == 0)
+      for (int q = lane; q < sh.n_slots; q += 32) {
+        const int nq = sh.slot_n[q];
+        int rk = 0;
+        for (int t = 0; t < sh.n_slots; t++) {
+          const int nt2 = sh.slot_n[t];
+          rk += nt2 > nq || (nt2 == nq && t < q);
+        }
+        sh.slot_a[rk] = q;
+      }
+    __syncthreads();
   }
 
   if (wid == 0) TG_MARK(4);
@@ -741,7 +758,8 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
   const int gbb = GF == FMT_Q4K ? Q4K_BYTES : 192, dbb = DF == FMT_Q4K ? Q4K_BYTES : 192;   // main bytes per block
 
   auto issue = [&](const SCur& c, int stg) {   // the whole warp
-    step_issue<GF, DF>(sx, c, ring + (size_t)stg * a.stage_bytes, &bar[stg], nrb, pa, I, D, ghalf, dr, n_slots, SB);
+    step_issue<GF, DF>(sx, sh.slot_a, c, ring + (size_t)stg * a.stage_bytes, &bar[stg], nrb, pa, I, D, ghalf, dr,
+                       n_slots, SB);
   };
   SCur ic{0, gw - NW, 0, 0};
   int issued = 0;
@@ -805,7 +823,7 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
   for (int it = gw; it < nA; it += NW, j++) {
     const int stg = j % a.nst;
     if (!wait_stage(stg, j)) continue;
-    const int s = it / nrb, r0 = (it - s * nrb) * pa, nr = min(pa, I - r0);
+    const int sq = it / nrb, s = sh.slot_a[sq], r0 = (it - sq * nrb) * pa, nr = min(pa, I - r0);
     const StepExpert& X = sx[s];
     const WDesc Gw = wdesc<GF>(X.g, I, D), Uw = wdesc<GF>(X.u, I, D);
     const uint8_t* dst = ring + (size_t)stg * a.stage_bytes;
@@ -1115,6 +1133,37 @@ struct StepShape {
   size_t smem;
 };
 
+#define TG_STEP_PAIRS(X)       \
+  X(FMT_Q4K, FMT_Q6K)          \
+  X(FMT_Q4K, FMT_Q4K)          \
+  X(FMT_MXFP4, FMT_MXFP4)      \
+  X(FMT_Q6K, FMT_Q6K)          \
+  X(FMT_Q80, FMT_Q80)
+
+template <int GF, int DF>
+static const void* step_fn() {
+  constexpr int SW = GF == FMT_MXFP4 ? SW_MAX : 16;
+  return reinterpret_cast<const void*>(layer_step_kernel<GF, DF, SW>);
+}
+
+// The step kernel's static shared memory for a format pair (StepShared and
+// whatever the compiler adds to it), cached; 0 if it cannot be read.
+static size_t step_static_smem(int gf, int df) {
+  static size_t cache[16][16] = {};
+  if (gf < 0 || gf >= 16 || df < 0 || df >= 16) return 0;
+  if (!cache[gf][df]) {
+    const void* fn = nullptr;
+#define TG_STEP_FN(GFV, DFV) \
+  if (gf == GFV && df == DFV) fn = step_fn<GFV, DFV>();
+    TG_STEP_PAIRS(TG_STEP_FN)
+#undef TG_STEP_FN
+    cudaFuncAttributes at{};
+    if (!fn || cudaFuncGetAttributes(&at, fn) != cudaSuccess) return 0;
+    cache[gf][df] = at.sharedSizeBytes;
+  }
+  return cache[gf][df];
+}
+
 static size_t step_smem_optin() {
   static int v = 0;
   if (!v) {
@@ -1171,7 +1220,8 @@ static bool step_shape(const StepLaunch& l, StepShape& sh) {
   const size_t nxa = (size_t)l.T * gbpr, nxh = (size_t)sh.xcap * dbpr;
   const size_t tabs = (size_t)sh.xcap * sizeof(StepExpert) + (size_t)l.E * sizeof(StepExpert);
   const size_t optin = step_smem_optin();
-  const size_t budget = optin - 256 - sizeof(StepShared);
+  const size_t stat = std::max(sizeof(StepShared), step_static_smem(l.gate_fmt, l.down_fmt));
+  const size_t budget = optin - 256 - stat;
   const uint32_t dr = rows_stage_bytes(row_layout(l.down_fmt, l.I).rs, 1);
   const uint32_t sa = 2 * rows_stage_bytes(row_layout(l.gate_fmt, l.D).rs, sh.pa);
   // phase-B slots per item (one stage): as many as fit; 32-value formats at
@@ -1183,7 +1233,7 @@ static bool step_shape(const StepLaunch& l, StepShape& sh) {
   for (int alias = 0; alias < 2; alias++) {
     const size_t nxq = alias ? std::max(nxa, nxh) : nxa + nxh;
     const size_t fixed = nxq * sizeof(XQ) + tabs;
-    if (optin < sizeof(StepShared) + fixed + rrow + 4096) continue;
+    if (optin < stat + fixed + rrow + 4096) continue;
     int sb = sb_cap;
     for (;;) {
       sh.stage = std::max(sa, (uint32_t)sb * dr);
@@ -1212,7 +1262,7 @@ static cudaError_t step_launch(StepArgs a, const StepShape& sh, cudaStream_t s) 
   a.sb = sh.sb;
   a.alias_x = sh.alias;
   a.xq_n = sh.xq_n;
-  const void* fn = reinterpret_cast<const void*>(layer_step_kernel<GF, DF, SW>);
+  const void* fn = step_fn<GF, DF>();
   cudaError_t e = ensure_smem(fn, sh.smem);
   if (e != cudaSuccess) return e;
   static size_t fits = 0;   // largest shared-memory size known to fit one CTA per SM
@@ -1238,13 +1288,6 @@ static cudaError_t step_launch(StepArgs a, const StepShape& sh, cudaStream_t s) 
 }
 
 // Gate / down format pairs with a fused step kernel.
-#define TG_STEP_PAIRS(X)       \
-  X(FMT_Q4K, FMT_Q6K)          \
-  X(FMT_Q4K, FMT_Q4K)          \
-  X(FMT_MXFP4, FMT_MXFP4)      \
-  X(FMT_Q6K, FMT_Q6K)          \
-  X(FMT_Q80, FMT_Q80)
-
 bool step_eligible(const StepLaunch& l) {
   StepShape sh;
   if (!step_shape(l, sh)) return false;
