@@ -373,3 +373,39 @@ def test_tensor_core_int32_sums_bit_exact_vs_oracle(gpu, oracle, kind):
                 np.testing.assert_array_equal(dbg[p, mat], want, err_msg=f"expert {e} token {t} matrix {mat}")
             p += 1
     assert p > T   # every token's rows were checked
+
+
+def test_tensor_core_role_trace(gpu):
+    """tg_cuda_tc_trace: one batched step fills the per-CTA role counters of
+    both grouped-GEMM passes; on every CTA with units the units and steps
+    match the unit count and steps per unit, and no role waited longer than
+    its own span."""
+    import torch
+    L = synth.qwen_layer(seed=5, n_experts=16)
+    T = 48
+    R = ResidentLayer(L, max_tokens=T, lib=gpu)
+    N = synth.rms_norm(np.random.default_rng(48).standard_normal((T, 2048)).astype(np.float32))
+    try:
+        R.forward(N, normalize=False)   # graph captured without the hook
+        grid = gpu.tg_cuda_tc_trace(None)
+        assert grid > 0
+        buf = torch.zeros(2 * grid * 16, dtype=torch.int64, device="cuda")
+        gpu.tg_cuda_tc_trace(ctypes.c_void_p(buf.data_ptr()))
+        R2 = R.clone()                  # a fresh layer: its graph is captured with the hook on
+        try:
+            R2.forward(N, normalize=False)
+        finally:
+            gpu.tg_cuda_tc_trace(None)
+            R2.close()
+        tg.check(gpu)
+    finally:
+        R.close()
+    v = buf.cpu().numpy().reshape(2, grid, 16)
+    for p, steps_per_unit in ((0, 2048 // 256), (1, 2 * (768 // 256))):
+        units, steps = v[p, :, 13], v[p, :, 14]
+        busy = units > 0
+        assert busy.any()
+        np.testing.assert_array_equal(steps[busy], units[busy] * steps_per_unit)
+        for wait, span in ((0, 1), (2, 4), (3, 4), (10, 12), (11, 12)):
+            assert (v[p, busy, wait] <= v[p, busy, span]).all()
+        assert (v[p, busy, 12] > 0).all()
