@@ -751,9 +751,8 @@ __global__ void __launch_bounds__(TcRoles<WF>::WARPS * 32, 1) tc_gemm_kernel(TcA
       };
       // epilogue of step st for this warp's EW active rows c0 .. c0 + EW - 1
       // (weight row r), from accumulator columns tl
-      auto epilogue = [&](auto ewc, auto oc, int st, const TcEMeta<WF>& E, uint32_t tl) {
-        constexpr int EW = decltype(ewc)::value, O = decltype(oc)::value;
-        const int cb = c0 + O;   // this call's first column (active row)
+      auto epilogue = [&](auto ewc, int st, const TcEMeta<WF>& E, uint32_t tl) {
+        constexpr int EW = decltype(ewc)::value;
         const int b = st / F::SPB, h = st - b * F::SPB;
         (void)h;
         if constexpr (WF == FMT_Q4K) {
@@ -779,7 +778,7 @@ __global__ void __launch_bounds__(TcRoles<WF>::WARPS * 32, 1) tc_gemm_kernel(TcA
 #pragma unroll
                 for (int gg = 0; gg < GW; gg++)
 #pragma unroll
-                  for (int c = 0; c < EW; c++) dbg_put(O + c, 8 * b + 2 * (g2 + gg), (int)il2[gg][c], (int)ih2[gg][c]);
+                  for (int c = 0; c < EW; c++) dbg_put(c, 8 * b + 2 * (g2 + gg), (int)il2[gg][c], (int)ih2[gg][c]);
               }
 #pragma unroll
               for (int gg = 0; gg < GW; gg++) {
@@ -790,9 +789,9 @@ __global__ void __launch_bounds__(TcRoles<WF>::WARPS * 32, 1) tc_gemm_kernel(TcA
                 for (int pp = 0; pp < P; pp++) {
                   const float2 flo = i2f_small2((int)il2[gg][2 * pp], (int)il2[gg][2 * pp + 1]);
                   const float2 fhi = i2f_small2((int)ih2[gg][2 * pp], (int)ih2[gg][2 * pp + 1]);
-                  const float4 b4 = E.xb4[(cb >> 1) + pp][g];
+                  const float4 b4 = E.xb4[(c0 >> 1) + pp][g];
                   const float2 blo = make_float2(b4.x, b4.y), bhi = make_float2(b4.z, b4.w);
-                  if ((x4m >> (O + 2 * pp)) & 1u) {
+                  if ((x4m >> (2 * pp)) & 1u) {
                     float2 t = fadd2(fmul2z(dsl, flo, nz2), fmul2z(ndml, blo, nz2));
                     t = fadd2(t, fmul2z(dsh, fhi, nz2));
                     t = fadd2(t, fmul2z(ndmh, bhi, nz2));
@@ -806,34 +805,34 @@ __global__ void __launch_bounds__(TcRoles<WF>::WARPS * 32, 1) tc_gemm_kernel(TcA
             }
 #pragma unroll
             for (int pp = 0; pp < P; pp++) {
-              const float2 xs = make_float2(E.xscale[cb + 2 * pp], E.xscale[cb + 2 * pp + 1]);
-              const float2 v = fadd2(make_float2(acc[O + 2 * pp], acc[O + 2 * pp + 1]), fmul2z(xs, bs2[pp], nz2));
-              acc[O + 2 * pp] = v.x;
-              acc[O + 2 * pp + 1] = v.y;
+              const float2 xs = make_float2(E.xscale[c0 + 2 * pp], E.xscale[c0 + 2 * pp + 1]);
+              const float2 v = fadd2(make_float2(acc[2 * pp], acc[2 * pp + 1]), fmul2z(xs, bs2[pp], nz2));
+              acc[2 * pp] = v.x;
+              acc[2 * pp + 1] = v.y;
             }
           } else {
             // (x - y = x + (-y) exactly: the negated products are the reference's subtrahends)
             float bsum = 0.f;
-            const int hi1 = cb & 1;
+            const int hi1 = c0 & 1;
 #pragma unroll
             for (int g = 0; g < 4; g++) {
               uint32_t il[1], ih[1];
               tc_ld<1>(tl + (2 * g) * TC_N, il);
               tc_ld<1>(tl + (2 * g + 1) * TC_N, ih);
               tc_wait_ld();
-              if (a.dbg) dbg_put(O, 8 * b + 2 * g, (int)il[0], (int)ih[0]);
+              if (a.dbg) dbg_put(0, 8 * b + 2 * g, (int)il[0], (int)ih[0]);
               const float4 s4 = sc[g];
               const float flo = i2f_small((int)il[0]), fhi = i2f_small((int)ih[0]);
-              const float4 b4 = E.xb4[cb >> 1][g];
+              const float4 b4 = E.xb4[c0 >> 1][g];
               const float blo = hi1 ? b4.y : b4.x, bhi = hi1 ? b4.w : b4.z;
-              if ((x4m >> O) & 1u) {
+              if (x4m & 1u) {
                 bsum = fadd(bsum, fadd(fadd(fadd(fmul(s4.x, flo), fmul(s4.y, blo)), fmul(s4.z, fhi)), fmul(s4.w, bhi)));
               } else {
                 bsum = fadd(bsum, fadd(fmul(s4.x, flo), fmul(s4.y, blo)));
                 bsum = fadd(bsum, fadd(fmul(s4.z, fhi), fmul(s4.w, bhi)));
               }
             }
-            acc[O] = fadd(acc[O], fmul(E.xscale[cb], bsum));
+            acc[0] = fadd(acc[0], fmul(E.xscale[c0], bsum));
           }
         } else if constexpr (WF == FMT_Q6K) {
           // the reference's fp32 fold of the block's 16 products sc * isum16,
@@ -856,19 +855,19 @@ __global__ void __launch_bounds__(TcRoles<WF>::WARPS * 32, 1) tc_gemm_kernel(TcA
                 const uint32_t (&is)[EW] = is2[kk];
                 if (a.dbg)
 #pragma unroll
-                  for (int c = 0; c < EW; c++) dbg_put1(O + c, 16 * b + (2 * h + lq) * 4 + k4, (int)is[c]);
+                  for (int c = 0; c < EW; c++) dbg_put1(c, 16 * b + (2 * h + lq) * 4 + k4, (int)is[c]);
                 const int si = lq + 2 * k4;
                 const float scf = (float)sbyte(sw[si >> 2], si & 3);
                 if constexpr (EW >= 2) {
 #pragma unroll
                   for (int pp = 0; pp < EW / 2; pp++) {
-                    const float2 v = fadd2(make_float2(fold[O + 2 * pp], fold[O + 2 * pp + 1]),
+                    const float2 v = fadd2(make_float2(fold[2 * pp], fold[2 * pp + 1]),
                                            fmul2z(splat2(scf), i2f_small2((int)is[2 * pp], (int)is[2 * pp + 1]), nz2));
-                    fold[O + 2 * pp] = v.x;
-                    fold[O + 2 * pp + 1] = v.y;
+                    fold[2 * pp] = v.x;
+                    fold[2 * pp + 1] = v.y;
                   }
                 } else {
-                  fold[O] = fadd(fold[O], fmul(scf, i2f_small((int)is[0])));
+                  fold[0] = fadd(fold[0], fmul(scf, i2f_small((int)is[0])));
                 }
               }
             }
@@ -876,8 +875,8 @@ __global__ void __launch_bounds__(TcRoles<WF>::WARPS * 32, 1) tc_gemm_kernel(TcA
             const float d = E.dq[r];
 #pragma unroll
             for (int c = 0; c < EW; c++) {
-              acc[O + c] = fadd(acc[O + c], fmul(fmul(d, E.xscale[cb + c]), fold[O + c]));
-              fold[O + c] = 0.f;
+              acc[c] = fadd(acc[c], fmul(fmul(d, E.xscale[c0 + c]), fold[c]));
+              fold[c] = 0.f;
             }
           }
         } else {
@@ -887,7 +886,7 @@ __global__ void __launch_bounds__(TcRoles<WF>::WARPS * 32, 1) tc_gemm_kernel(TcA
           const uint2 eh = E.e8[r];
           float xs[EW];
 #pragma unroll
-          for (int c = 0; c < EW; c++) xs[c] = E.xscale[cb + c];
+          for (int c = 0; c < EW; c++) xs[c] = E.xscale[c0 + c];
           constexpr int MB = EW >= 8 ? 2 : EW >= 4 ? 4 : 8;   // accumulator loads in flight per wait
 #pragma unroll
           for (int m0 = 0; m0 < 8; m0 += MB) {
@@ -902,7 +901,7 @@ __global__ void __launch_bounds__(TcRoles<WF>::WARPS * 32, 1) tc_gemm_kernel(TcA
               for (int m = 0; m < MB; m++)
                 if (m0 + m < nm)
 #pragma unroll
-                  for (int c = 0; c < EW; c++) dbg_put1(O + c, 8 * b + m0 + m, (int)is[m][c]);
+                  for (int c = 0; c < EW; c++) dbg_put1(c, 8 * b + m0 + m, (int)is[m][c]);
 #pragma unroll
             for (int m = 0; m < MB; m++) {
               if (m0 + m >= nm) break;
@@ -913,12 +912,12 @@ __global__ void __launch_bounds__(TcRoles<WF>::WARPS * 32, 1) tc_gemm_kernel(TcA
                 for (int pp = 0; pp < EW / 2; pp++) {
                   const float2 t = fmul2z(fmul2z(make_float2(xs[2 * pp], xs[2 * pp + 1]), splat2(es), nz2),
                                           i2f_small2((int)is[m][2 * pp], (int)is[m][2 * pp + 1]), nz2);
-                  const float2 v = fadd2(make_float2(acc[O + 2 * pp], acc[O + 2 * pp + 1]), t);
-                  acc[O + 2 * pp] = v.x;
-                  acc[O + 2 * pp + 1] = v.y;
+                  const float2 v = fadd2(make_float2(acc[2 * pp], acc[2 * pp + 1]), t);
+                  acc[2 * pp] = v.x;
+                  acc[2 * pp + 1] = v.y;
                 }
               } else {
-                acc[O] = fadd(acc[O], fmul(fmul(xs[0], es), i2f_small((int)is[m][0])));
+                acc[0] = fadd(acc[0], fmul(fmul(xs[0], es), i2f_small((int)is[m][0])));
               }
             }
           }
@@ -942,12 +941,12 @@ __global__ void __launch_bounds__(TcRoles<WF>::WARPS * 32, 1) tc_gemm_kernel(TcA
           const uint32_t tl = tmem + (uint32_t)kt * 256 + ((uint32_t)(32 * q) << 16) + c0;
           const TcEMeta<WF>& E = sh.em[ke];
           switch (ew) {
-            case 1: epilogue(IC<1>{}, IC<0>{}, st, E, tl); break;
-            case 2: epilogue(IC<2>{}, IC<0>{}, st, E, tl); break;
-            case 4: epilogue(IC<4>{}, IC<0>{}, st, E, tl); break;
-            case 8: epilogue(IC<8>{}, IC<0>{}, st, E, tl); break;
+            case 1: epilogue(IC<1>{}, st, E, tl); break;
+            case 2: epilogue(IC<2>{}, st, E, tl); break;
+            case 4: epilogue(IC<4>{}, st, E, tl); break;
+            case 8: epilogue(IC<8>{}, st, E, tl); break;
             default:
-              if constexpr (RL::EWMAX >= 16) epilogue(IC<16>{}, IC<0>{}, st, E, tl);
+              if constexpr (RL::EWMAX >= 16) epilogue(IC<16>{}, st, E, tl);
               break;
           }
         }

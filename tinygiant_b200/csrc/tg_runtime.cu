@@ -299,18 +299,34 @@ __global__ void deliver_kernel(const float* __restrict__ src, size_t n, const De
 // more for large batches).  The loads skip any cached copy of the host lines
 // (ld.global.cv).  It lets the next kernel launch at once; that kernel waits
 // for this grid (griddepcontrol.wait) before it reads dst.
+// Reads of mapped host memory cross PCIe (about a microsecond each): each
+// thread keeps four in flight before it stores them.
 __global__ void fetch_kernel(const float* __restrict__ src, size_t n, float* __restrict__ dst) {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const size_t n4 = n / 4, step = (size_t)gridDim.x * blockDim.x, i0 = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
-  for (size_t i = i0; i < n4; i += step)
-    reinterpret_cast<float4*>(dst)[i] = __ldcv(reinterpret_cast<const float4*>(src) + i);
+  const float4* s4 = reinterpret_cast<const float4*>(src);
+  float4* d4 = reinterpret_cast<float4*>(dst);
+  for (size_t i = i0; i < n4; i += 4 * step) {
+    float4 v[4];
+#pragma unroll
+    for (int k = 0; k < 4; k++)
+      if (i + k * step < n4) v[k] = __ldcv(s4 + i + k * step);
+#pragma unroll
+    for (int k = 0; k < 4; k++)
+      if (i + k * step < n4) d4[i + k * step] = v[k];
+  }
   for (size_t i = n4 * 4 + i0; i < n; i += step) dst[i] = __ldcv(src + i);
 }
 
-// CTAs of the fetch and delivery copies: one up to 64 K floats (a decode
-// step's rows), then one per 64 K floats, at most 32.
+// CTAs of the delivery copy: one up to 64 K floats (a decode step's rows),
+// then one per 64 K floats, at most 32.
 static unsigned copy_ctas(size_t n_floats) {
   return (unsigned)std::min<size_t>(32, std::max<size_t>(1, (n_floats + 65535) / 65536));
+}
+// CTAs of the fetch: one per 8 K floats (each thread then reads at most four
+// float4 at once), at most 64.
+static unsigned fetch_ctas(size_t n_floats) {
+  return (unsigned)std::min<size_t>(64, std::max<size_t>(1, (n_floats + 8191) / 8192));
 }
 
 float* fetch_reserve(size_t n_floats) {
@@ -319,7 +335,7 @@ float* fetch_reserve(size_t n_floats) {
 
 bool fetch_async(float* d_dst, size_t n_floats, cudaStream_t s, const char* what) {
   if (!g.h_in.reserve(sizeof(float) * n_floats)) return false;
-  fetch_kernel<<<copy_ctas(n_floats), 512, 0, s>>>(static_cast<const float*>(g.h_in.d), n_floats, d_dst);
+  fetch_kernel<<<fetch_ctas(n_floats), 512, 0, s>>>(static_cast<const float*>(g.h_in.d), n_floats, d_dst);
   count_launches(1);
   return cuda_ok(cudaGetLastError(), what);
 }
