@@ -563,10 +563,9 @@ __global__ void __launch_bounds__(TcRoles<WF>::WARPS * 32, 1) tc_gemm_kernel(TcA
         if constexpr (WF == FMT_Q4K) {
           // thread: row rr, 16-byte piece p of the 128 nibble bytes -> 32 values
           // (rows 144 bytes apart: a phase's 8 reads hit 8 distinct 16-byte columns)
-#pragma unroll
-          for (int it = 0; it < (TC_M * 8 + TC_UT - 1) / TC_UT; it++) {
-            if (TC_M * 8 % TC_UT && ut + it * TC_UT >= TC_M * 8) break;   // (uniform per warp)
-            const int i = ut + it * TC_UT, l = i & 7, j = i >> 3, rr = 8 * (j >> 3) + l, p = j & 7;
+#pragma unroll 1
+          for (int i = ut; i < TC_M * 8; i += TC_UT) {
+            const int l = i & 7, j = i >> 3, rr = 8 * (j >> 3) + l, p = j & 7;
             const uint8_t* row = rw + rr * Q4K_BYTES;
             const uint4 w = *reinterpret_cast<const uint4*>(row + 16 + 16 * p);
             // bytes 32g .. 32g + 31: low nibbles -> sub-block 2g, high -> 2g + 1
@@ -591,10 +590,9 @@ __global__ void __launch_bounds__(TcRoles<WF>::WARPS * 32, 1) tc_gemm_kernel(TcA
           }
         } else if constexpr (WF == FMT_Q6K) {
           // thread: row rr, group (lq, k4) of half h: tile m = 2 k4 + lq, values in K-half lq
-#pragma unroll
-          for (int it = 0; it < (TC_M * 8 + TC_UT - 1) / TC_UT; it++) {
-            if (TC_M * 8 % TC_UT && ut + it * TC_UT >= TC_M * 8) break;   // (uniform per warp)
-            const int i = ut + it * TC_UT, l = i & 7, j = i >> 3, rr = 8 * (j >> 3) + l, m = (l + j) & 7, k4 = m >> 1,
+#pragma unroll 1
+          for (int i = ut; i < TC_M * 8; i += TC_UT) {
+            const int l = i & 7, j = i >> 3, rr = 8 * (j >> 3) + l, m = (l + j) & 7, k4 = m >> 1,
                       lq = m & 1;
             const uint8_t* mb = rw + rr * 192;
             const uint4 va = *reinterpret_cast<const uint4*>(mb + 64 * h + 16 * lq + 32 * (k4 & 1));
@@ -626,10 +624,9 @@ __global__ void __launch_bounds__(TcRoles<WF>::WARPS * 32, 1) tc_gemm_kernel(TcA
           // row (or zeros): their products land in columns the epilogue skips.
           // (Rows are 128-byte swizzled: sub-block m of row rr sits in column
           // m ^ (rr % 8), so m = j % 8 keeps a phase's reads distinct.)
-#pragma unroll 4
-          for (int it = 0; it < (TC_M * 8 + TC_UT - 1) / TC_UT; it++) {
-            if (TC_M * 8 % TC_UT && ut + it * TC_UT >= TC_M * 8) break;   // (uniform per warp)
-            const int i = ut + it * TC_UT, l = i & 7, j = i >> 3, rr = 8 * (j >> 3) + l, m = j & 7;
+#pragma unroll 1
+          for (int i = ut; i < TC_M * 8; i += TC_UT) {
+            const int l = i & 7, j = i >> 3, rr = 8 * (j >> 3) + l, m = j & 7;
             const uint4 cv = *reinterpret_cast<const uint4*>(rw + swz(rr, 16 * m));
             const uint32_t cw[4] = {cv.x, cv.y, cv.z, cv.w};
             uint32_t o[8];
