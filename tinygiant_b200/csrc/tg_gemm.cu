@@ -57,15 +57,15 @@ constexpr int TW_MMA = 1;     // lane 0: the MMAs
 constexpr int TW_UNP = 2;     // warps 2 ..: unpack A, stage B, the epilogue's per-step data
 constexpr int TC_NA = 2;      // A/B operand stages
 constexpr int TC_NE = 2;      // epilogue data stages
-// Per format the unpack and epilogue warp counts: Q4_K and Q6_K steps are
-// bound by the epilogue's fp32 fold (16 warps, 4 per lane quarter, up to 8
-// active rows each); MXFP4 steps by decoding the codes (6 unpack warps; 8
-// epilogue warps, up to 16 active rows each).  The epilogue warps follow the
-// unpack warps: warp wid reads TMEM lane quarter wid % 4, and each quarter
-// gets one warp of each group tg = (wid - EPI) / 4.
+// Per format the epilogue warp count: Q4_K and Q6_K steps are bound by the
+// epilogue's fp32 fold (16 warps, 4 per lane quarter, up to 8 active rows
+// each); MXFP4 steps by decoding the codes (8 epilogue warps, up to 16 active
+// rows each).  Six unpack warps for every format.  The epilogue warps follow
+// the unpack warps: warp wid reads TMEM lane quarter wid % 4, and each
+// quarter gets one warp of each group tg = (wid - EPI) / 4.
 template <int WF>
 struct TcRoles {
-  static constexpr int NUNP = WF == FMT_MXFP4 ? 6 : 4;
+  static constexpr int NUNP = 6;
   static constexpr int NEPI = WF == FMT_MXFP4 ? 8 : 16;
   static constexpr int EPI = TW_UNP + NUNP;
   static constexpr int WARPS = EPI + NEPI;
