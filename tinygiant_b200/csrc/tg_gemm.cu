@@ -311,7 +311,7 @@ __device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, const vo
   return true;
 }
 
-template <int WF, int MODE>   // MODE 0: gate/up; 1: down
+template <int WF, int MODE, bool DBG>   // MODE 0: gate/up; 1: down; DBG: the int32 sums test hook is on
 __global__ void __launch_bounds__(TcRoles<WF>::WARPS * 32, 1) tc_gemm_kernel(TcArgs a) {
   using F = TcFmt<WF>;
   using RL = TcRoles<WF>;
@@ -771,7 +771,7 @@ __global__ void __launch_bounds__(TcRoles<WF>::WARPS * 32, 1) tc_gemm_kernel(TcA
                 tc_ld<EW>(tl + (2 * (g2 + gg) + 1) * TC_N, ih2[gg]);
               }
               tc_wait_ld();
-              if (a.dbg) {
+              if (DBG) {
 #pragma unroll
                 for (int gg = 0; gg < GW; gg++)
 #pragma unroll
@@ -817,7 +817,7 @@ __global__ void __launch_bounds__(TcRoles<WF>::WARPS * 32, 1) tc_gemm_kernel(TcA
               tc_ld<1>(tl + (2 * g) * TC_N, il);
               tc_ld<1>(tl + (2 * g + 1) * TC_N, ih);
               tc_wait_ld();
-              if (a.dbg) dbg_put(0, 8 * b + 2 * g, (int)il[0], (int)ih[0]);
+              if (DBG) dbg_put(0, 8 * b + 2 * g, (int)il[0], (int)ih[0]);
               const float4 s4 = sc[g];
               const float flo = i2f_small((int)il[0]), fhi = i2f_small((int)ih[0]);
               const float4 b4 = E.xb4[c0 >> 1][g];
@@ -850,7 +850,7 @@ __global__ void __launch_bounds__(TcRoles<WF>::WARPS * 32, 1) tc_gemm_kernel(TcA
               for (int kk = 0; kk < 2; kk++) {
                 const int k4 = k2 + kk;
                 const uint32_t (&is)[EW] = is2[kk];
-                if (a.dbg)
+                if (DBG)
 #pragma unroll
                   for (int c = 0; c < EW; c++) dbg_put1(c, 16 * b + (2 * h + lq) * 4 + k4, (int)is[c]);
                 const int si = lq + 2 * k4;
@@ -893,7 +893,7 @@ __global__ void __launch_bounds__(TcRoles<WF>::WARPS * 32, 1) tc_gemm_kernel(TcA
             for (int m = 0; m < MB; m++)
               if (m0 + m < nm) tc_ld<EW>(tl + (m0 + m) * TC_N, is[m]);
             tc_wait_ld();
-            if (a.dbg)
+            if (DBG)
 #pragma unroll
               for (int m = 0; m < MB; m++)
                 if (m0 + m < nm)
@@ -1120,7 +1120,10 @@ size_t tc_moe_scratch_bytes(int max_rows, int T, int K, int D, int I) {
 
 template <int WF, int MODE>
 static cudaError_t tc_launch(const TcArgs& a, cudaStream_t s) {
-  const void* fn = reinterpret_cast<const void*>(tc_gemm_kernel<WF, MODE>);
+  // the test hook's stores in a kernel of their own: without them the
+  // epilogue keeps fewer values live
+  const void* fn = a.dbg ? reinterpret_cast<const void*>(tc_gemm_kernel<WF, MODE, true>)
+                         : reinterpret_cast<const void*>(tc_gemm_kernel<WF, MODE, false>);
   const size_t smem = tc_smem(WF, a.K);
   cudaError_t e = ensure_smem(fn, smem);
   if (e != cudaSuccess) return e;
