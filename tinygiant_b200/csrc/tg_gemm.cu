@@ -311,7 +311,9 @@ __device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, const vo
   return true;
 }
 
-template <int WF, int MODE, bool DBG>   // MODE 0: gate/up; 1: down; DBG: the int32 sums test hook is on
+// DIAG: a diagnostics hook is on (the int32 sums of a.dbg, the role counters
+// of a.trace); the kernel without them keeps fewer values live.
+template <int WF, int MODE, bool DIAG>   // MODE 0: gate/up; 1: down
 __global__ void __launch_bounds__(TcRoles<WF>::WARPS * 32, 1) tc_gemm_kernel(TcArgs a) {
   using F = TcFmt<WF>;
   using RL = TcRoles<WF>;
@@ -418,7 +420,7 @@ __global__ void __launch_bounds__(TcRoles<WF>::WARPS * 32, 1) tc_gemm_kernel(TcA
   };
   int issued = 0, tails = 0, mmas = 0;   // producer / MMA thread: for the waits at exit
   // the traced threads: lane 0 of the producer, MMA, first unpack and first epilogue warps
-  const bool trt = a.trace && lane == 0 && (wid == TW_PROD || wid == TW_MMA || wid == TW_UNP || wid == TW_EPI);
+  const bool trt = DIAG && a.trace && lane == 0 && (wid == TW_PROD || wid == TW_MMA || wid == TW_UNP || wid == TW_EPI);
   auto twait = [&](uint64_t* bar, uint32_t parity, int slot) -> bool {
     if (!trt) return tc_wait(bar, parity, abort);
     const long long t0 = clock64();
@@ -426,7 +428,7 @@ __global__ void __launch_bounds__(TcRoles<WF>::WARPS * 32, 1) tc_gemm_kernel(TcA
     sh.tr[slot] += (unsigned long long)(clock64() - t0);
     return r;
   };
-  const long long tstart = clock64();
+  const long long tstart = DIAG ? clock64() : 0;
 
   if (wid == TW_PROD) {
     // ---- producer warp: per unit its row tails (lane 0, once); per block
@@ -771,7 +773,7 @@ __global__ void __launch_bounds__(TcRoles<WF>::WARPS * 32, 1) tc_gemm_kernel(TcA
                 tc_ld<EW>(tl + (2 * (g2 + gg) + 1) * TC_N, ih2[gg]);
               }
               tc_wait_ld();
-              if (DBG) {
+              if (DIAG && a.dbg) {
 #pragma unroll
                 for (int gg = 0; gg < GW; gg++)
 #pragma unroll
@@ -817,7 +819,7 @@ __global__ void __launch_bounds__(TcRoles<WF>::WARPS * 32, 1) tc_gemm_kernel(TcA
               tc_ld<1>(tl + (2 * g) * TC_N, il);
               tc_ld<1>(tl + (2 * g + 1) * TC_N, ih);
               tc_wait_ld();
-              if (DBG) dbg_put(0, 8 * b + 2 * g, (int)il[0], (int)ih[0]);
+              if (DIAG && a.dbg) dbg_put(0, 8 * b + 2 * g, (int)il[0], (int)ih[0]);
               const float4 s4 = sc[g];
               const float flo = i2f_small((int)il[0]), fhi = i2f_small((int)ih[0]);
               const float4 b4 = E.xb4[c0 >> 1][g];
@@ -850,7 +852,7 @@ __global__ void __launch_bounds__(TcRoles<WF>::WARPS * 32, 1) tc_gemm_kernel(TcA
               for (int kk = 0; kk < 2; kk++) {
                 const int k4 = k2 + kk;
                 const uint32_t (&is)[EW] = is2[kk];
-                if (DBG)
+                if (DIAG && a.dbg)
 #pragma unroll
                   for (int c = 0; c < EW; c++) dbg_put1(c, 16 * b + (2 * h + lq) * 4 + k4, (int)is[c]);
                 const int si = lq + 2 * k4;
@@ -893,7 +895,7 @@ __global__ void __launch_bounds__(TcRoles<WF>::WARPS * 32, 1) tc_gemm_kernel(TcA
             for (int m = 0; m < MB; m++)
               if (m0 + m < nm) tc_ld<EW>(tl + (m0 + m) * TC_N, is[m]);
             tc_wait_ld();
-            if (DBG)
+            if (DIAG && a.dbg)
 #pragma unroll
               for (int m = 0; m < MB; m++)
                 if (m0 + m < nm)
@@ -986,7 +988,7 @@ __global__ void __launch_bounds__(TcRoles<WF>::WARPS * 32, 1) tc_gemm_kernel(TcA
   tc_fence_before();
   __syncthreads();
   if (wid == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512));
-  if (a.trace && tid < TC_TR_N) a.trace[(size_t)blockIdx.x * TC_TR_N + tid] = sh.tr[tid];
+  if (DIAG && a.trace && tid < TC_TR_N) a.trace[(size_t)blockIdx.x * TC_TR_N + tid] = sh.tr[tid];
 }
 
 // hq8[row] = Q8 of act(gate + gb, up + ub) over the slot's bias vectors: one
@@ -1120,10 +1122,8 @@ size_t tc_moe_scratch_bytes(int max_rows, int T, int K, int D, int I) {
 
 template <int WF, int MODE>
 static cudaError_t tc_launch(const TcArgs& a, cudaStream_t s) {
-  // the test hook's stores in a kernel of their own: without them the
-  // epilogue keeps fewer values live
-  const void* fn = a.dbg ? reinterpret_cast<const void*>(tc_gemm_kernel<WF, MODE, true>)
-                         : reinterpret_cast<const void*>(tc_gemm_kernel<WF, MODE, false>);
+  const void* fn = a.dbg || a.trace ? reinterpret_cast<const void*>(tc_gemm_kernel<WF, MODE, true>)
+                                     : reinterpret_cast<const void*>(tc_gemm_kernel<WF, MODE, false>);
   const size_t smem = tc_smem(WF, a.K);
   cudaError_t e = ensure_smem(fn, smem);
   if (e != cudaSuccess) return e;
