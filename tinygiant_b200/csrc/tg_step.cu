@@ -231,8 +231,8 @@ __device__ __forceinline__ unsigned long long gtimer() {
 }
 #define TG_MARK(i)                                                                         \
   do {                                                                                     \
-    if (a.trace && (threadIdx.x & 31) == 0)                                                \
-      a.trace[blockIdx.x * 32 + (i)] = (unsigned long long)clock64();                       \
+    if (trace && (threadIdx.x & 31) == 0)                                                  \
+      trace[blockIdx.x * 32 + (i)] = (unsigned long long)clock64();                         \
   } while (0)
 
 // A warp's position in its stream of items: phase 0 = gate/up item a (slot
@@ -290,8 +290,11 @@ static __device__ __noinline__ void step_issue(const StepExpert* sx, const int* 
   }
 }
 
-template <int GF, int DF, int SW>
+// TRACE: the diagnostics hook (a.trace) is on; the kernel without it keeps
+// fewer values live.
+template <int GF, int DF, int SW, bool TRACE>
 __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
+  unsigned long long* const trace = TRACE ? a.trace : nullptr;
   extern __shared__ __align__(128) uint8_t dsm[];
   __shared__ StepShared sh;
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, tid = threadIdx.x;
@@ -310,7 +313,7 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
   StepExpert* sx = reinterpret_cast<StepExpert*>(xa + a.xq_n);   // [xcap] the slots' experts
   StepExpert* etab = sx + a.xcap;                                                 // [E]
   uint64_t* bar = sh.bars[wid];
-  if (a.trace && tid == 0) a.trace[blockIdx.x * 32 + 12] = gtimer();
+  if (trace && tid == 0) trace[blockIdx.x * 32 + 12] = gtimer();
   if (wid == 0) TG_MARK(0);
 
   // ---- Before the preceding kernel completes: the epoch, this warp's router
@@ -488,7 +491,7 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
         }
       }
       if (__all_sync(FULL, ok)) {
-        if (a.trace && t == 0 && lane == 0) a.trace[blockIdx.x * 32 + 19] = it + 1;
+        if (trace && t == 0 && lane == 0) trace[blockIdx.x * 32 + 19] = it + 1;
         break;
       }
       if (it >= a.poll_limit) {
@@ -787,9 +790,9 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
   long long tc = 0;
   auto wait_stage = [&](int stg, int item) -> bool {
     if (dead) return false;
-    if (a.trace) tc = clock64();
+    if (trace) tc = clock64();
     const bool okw = mbar_wait(&bar[stg], (uint32_t)(item / a.nst) & 1u);
-    if (a.trace) {
+    if (trace) {
       const long long t1 = clock64();
       if (lane == 0) tw[3 * tph] += t1 - tc;
       tc = t1;
@@ -804,7 +807,7 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
   auto refill = [&](int stg) {
     __syncwarp();
     long long t0 = 0;
-    if (a.trace) {
+    if (trace) {
       t0 = clock64();
       if (lane == 0) tw[3 * tph + 1] += t0 - tc;
     }
@@ -814,7 +817,7 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
       issue(ic, stg);
       issued++;
     }
-    if (a.trace && lane == 0) tw[3 * tph + 2] += clock64() - t0;
+    if (trace && lane == 0) tw[3 * tph + 2] += clock64() - t0;
   };
 
   // phase A: items gw, gw + NW, ... < nA
@@ -887,7 +890,7 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
     okh = false;
   }
   const int nh = okh ? total * dbpr : 0;   // hidden blocks
-  const long long ta = a.trace ? clock64() : 0;
+  const long long ta = trace ? clock64() : 0;
   if (a.alias_x) __syncthreads();   // xs overlays xa: every warp of this CTA is past phase A
   if (wid == 0) TG_MARK(25);
   if (nh > 4 * SW) {
@@ -938,7 +941,7 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
         if (!seen) seen = tag_is(ld_flag_acquire(a.hflag + q), ep);
         if (__all_sync(FULL, seen)) {
           if (wid == 0 && q0 == 0) TG_MARK(27);
-          if (a.trace && lane == 0) {
+          if (trace && lane == 0) {
             tw[6] += it + 1;
             if (q0 == wid) tw[7] = clock64() - ta;
           }
@@ -990,7 +993,7 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
           }
         }
         if (__all_sync(FULL, ok)) {
-          if (a.trace && lane == 0) {
+          if (trace && lane == 0) {
             tw[6] += it + 1;
             if (q0 == wid) tw[7] = clock64() - ta;
           }
@@ -1105,9 +1108,9 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
 
   if (wid == 0) TG_MARK(8);
   if (wid == SW - 1) TG_MARK(11);
-  if (a.trace && tid == 0) a.trace[blockIdx.x * 32 + 13] = gtimer();
-  if (a.trace && lane == 0)
-    for (int q = 0; q < 8; q++) a.trace[(size_t)gridDim.x * 32 + ((size_t)blockIdx.x * SW_MAX + wid) * 8 + q] = tw[q];
+  if (trace && tid == 0) trace[blockIdx.x * 32 + 13] = gtimer();
+  if (trace && lane == 0)
+    for (int q = 0; q < 8; q++) trace[(size_t)gridDim.x * 32 + ((size_t)blockIdx.x * SW_MAX + wid) * 8 + q] = tw[q];
   // bounded waits for any copies still in flight before the CTA exits
   if (!dead)
     for (int i = j; i < issued; i++) mbar_wait(&bar[i % a.nst], (uint32_t)(i / a.nst) & 1u);
@@ -1141,9 +1144,10 @@ struct StepShape {
   X(FMT_Q80, FMT_Q80)
 
 template <int GF, int DF>
-static const void* step_fn() {
+static const void* step_fn(bool trace) {
   constexpr int SW = GF == FMT_MXFP4 ? SW_MAX : 16;
-  return reinterpret_cast<const void*>(layer_step_kernel<GF, DF, SW>);
+  return trace ? reinterpret_cast<const void*>(layer_step_kernel<GF, DF, SW, true>)
+               : reinterpret_cast<const void*>(layer_step_kernel<GF, DF, SW, false>);
 }
 
 // The step kernel's static shared memory for a format pair (StepShared and
@@ -1154,7 +1158,7 @@ static size_t step_static_smem(int gf, int df) {
   if (!cache[gf][df]) {
     const void* fn = nullptr;
 #define TG_STEP_FN(GFV, DFV) \
-  if (gf == GFV && df == DFV) fn = step_fn<GFV, DFV>();
+  if (gf == GFV && df == DFV) fn = step_fn<GFV, DFV>(false);
     TG_STEP_PAIRS(TG_STEP_FN)
 #undef TG_STEP_FN
     cudaFuncAttributes at{};
@@ -1262,7 +1266,7 @@ static cudaError_t step_launch(StepArgs a, const StepShape& sh, cudaStream_t s) 
   a.sb = sh.sb;
   a.alias_x = sh.alias;
   a.xq_n = sh.xq_n;
-  const void* fn = step_fn<GF, DF>();
+  const void* fn = step_fn<GF, DF>(a.trace != nullptr);
   cudaError_t e = ensure_smem(fn, sh.smem);
   if (e != cudaSuccess) return e;
   static size_t fits = 0;   // largest shared-memory size known to fit one CTA per SM
