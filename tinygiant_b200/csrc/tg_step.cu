@@ -291,14 +291,15 @@ static __device__ __noinline__ void step_issue(const StepExpert* sx, const int* 
 }
 
 // TRACE: the diagnostics hook (a.trace) is on; the kernel without it keeps
-// fewer values live.
-template <int GF, int DF, int SW, bool TRACE>
+// fewer values live.  T1: a one-token step (a.T == 1), the common decode
+// case, compiled with T a constant.
+template <int GF, int DF, int SW, bool TRACE, bool T1>
 __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
   unsigned long long* const trace = TRACE ? a.trace : nullptr;
   extern __shared__ __align__(128) uint8_t dsm[];
   __shared__ StepShared sh;
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, tid = threadIdx.x;
-  const int T = a.T, D = a.D, E = a.E, K = a.top_k, I = a.I;
+  const int T = T1 ? 1 : a.T, D = a.D, E = a.E, K = a.top_k, I = a.I;
   const int G = gridDim.x;
   // work items go to warps CTA-interleaved, so every SM gets an even share
   const int gw = wid * G + blockIdx.x, NW = G * SW;
@@ -1144,10 +1145,11 @@ struct StepShape {
   X(FMT_Q80, FMT_Q80)
 
 template <int GF, int DF>
-static const void* step_fn(bool trace) {
+static const void* step_fn(bool trace, bool t1) {
   constexpr int SW = GF == FMT_MXFP4 ? SW_MAX : 16;
-  return trace ? reinterpret_cast<const void*>(layer_step_kernel<GF, DF, SW, true>)
-               : reinterpret_cast<const void*>(layer_step_kernel<GF, DF, SW, false>);
+  if (trace) return reinterpret_cast<const void*>(layer_step_kernel<GF, DF, SW, true, false>);
+  return t1 ? reinterpret_cast<const void*>(layer_step_kernel<GF, DF, SW, false, true>)
+            : reinterpret_cast<const void*>(layer_step_kernel<GF, DF, SW, false, false>);
 }
 
 // The step kernel's static shared memory for a format pair (StepShared and
@@ -1158,7 +1160,7 @@ static size_t step_static_smem(int gf, int df) {
   if (!cache[gf][df]) {
     const void* fn = nullptr;
 #define TG_STEP_FN(GFV, DFV) \
-  if (gf == GFV && df == DFV) fn = step_fn<GFV, DFV>(false);
+  if (gf == GFV && df == DFV) fn = step_fn<GFV, DFV>(false, false);
     TG_STEP_PAIRS(TG_STEP_FN)
 #undef TG_STEP_FN
     cudaFuncAttributes at{};
@@ -1266,7 +1268,7 @@ static cudaError_t step_launch(StepArgs a, const StepShape& sh, cudaStream_t s) 
   a.sb = sh.sb;
   a.alias_x = sh.alias;
   a.xq_n = sh.xq_n;
-  const void* fn = step_fn<GF, DF>(a.trace != nullptr);
+  const void* fn = step_fn<GF, DF>(a.trace != nullptr, a.T == 1);
   cudaError_t e = ensure_smem(fn, sh.smem);
   if (e != cudaSuccess) return e;
   static size_t fits = 0;   // largest shared-memory size known to fit one CTA per SM
