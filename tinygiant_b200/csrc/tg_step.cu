@@ -292,8 +292,9 @@ static __device__ __noinline__ void step_issue(const StepExpert* sx, const int* 
 
 // TRACE: the diagnostics hook (a.trace) is on; the kernel without it keeps
 // fewer values live.  T1: a one-token step (a.T == 1), the common decode
-// case, compiled with T a constant.
-template <int GF, int DF, int SW, bool TRACE, bool T1>
+// case, compiled with T a constant.  EP: the expert-parallel combine may be
+// on (a.ep_world > 1); without it the kernel has no combine code.
+template <int GF, int DF, int SW, bool TRACE, bool T1, bool EP>
 __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
   unsigned long long* const trace = TRACE ? a.trace : nullptr;
   extern __shared__ __align__(128) uint8_t dsm[];
@@ -1033,7 +1034,7 @@ __global__ void __launch_bounds__(SW * 32, 1) layer_step_kernel(StepArgs a) {
   // shard's part, combined across shards by ep_combine_row.
   auto emit_row = [&](int r, float v) {
     if (dead) return;
-    if (a.ep_world == 1) {
+    if (!EP || a.ep_world == 1) {
       if (lane < T) a.out[(size_t)lane * D + r] = v;
     } else if (!ep_combine_row(a.ep_peers, a.ep_recv, a.ep_rank, a.ep_world, T, D, r, v, ep, a.out,
                                        a.poll_limit)) {
@@ -1145,11 +1146,14 @@ struct StepShape {
   X(FMT_Q80, FMT_Q80)
 
 template <int GF, int DF>
-static const void* step_fn(bool trace, bool t1) {
+static const void* step_fn(bool trace, bool t1, bool ep) {
   constexpr int SW = GF == FMT_MXFP4 ? SW_MAX : 16;
-  if (trace) return reinterpret_cast<const void*>(layer_step_kernel<GF, DF, SW, true, false>);
-  return t1 ? reinterpret_cast<const void*>(layer_step_kernel<GF, DF, SW, false, true>)
-            : reinterpret_cast<const void*>(layer_step_kernel<GF, DF, SW, false, false>);
+  if (trace) return reinterpret_cast<const void*>(layer_step_kernel<GF, DF, SW, true, false, true>);
+  if (ep)
+    return t1 ? reinterpret_cast<const void*>(layer_step_kernel<GF, DF, SW, false, true, true>)
+              : reinterpret_cast<const void*>(layer_step_kernel<GF, DF, SW, false, false, true>);
+  return t1 ? reinterpret_cast<const void*>(layer_step_kernel<GF, DF, SW, false, true, false>)
+            : reinterpret_cast<const void*>(layer_step_kernel<GF, DF, SW, false, false, false>);
 }
 
 // The step kernel's static shared memory for a format pair (StepShared and
@@ -1160,7 +1164,7 @@ static size_t step_static_smem(int gf, int df) {
   if (!cache[gf][df]) {
     const void* fn = nullptr;
 #define TG_STEP_FN(GFV, DFV) \
-  if (gf == GFV && df == DFV) fn = step_fn<GFV, DFV>(false, false);
+  if (gf == GFV && df == DFV) fn = step_fn<GFV, DFV>(false, false, true);
     TG_STEP_PAIRS(TG_STEP_FN)
 #undef TG_STEP_FN
     cudaFuncAttributes at{};
@@ -1268,7 +1272,7 @@ static cudaError_t step_launch(StepArgs a, const StepShape& sh, cudaStream_t s) 
   a.sb = sh.sb;
   a.alias_x = sh.alias;
   a.xq_n = sh.xq_n;
-  const void* fn = step_fn<GF, DF>(a.trace != nullptr, a.T == 1);
+  const void* fn = step_fn<GF, DF>(a.trace != nullptr, a.T == 1, a.ep_world > 1);
   cudaError_t e = ensure_smem(fn, sh.smem);
   if (e != cudaSuccess) return e;
   static size_t fits = 0;   // largest shared-memory size known to fit one CTA per SM
