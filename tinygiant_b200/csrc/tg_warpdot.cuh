@@ -475,7 +475,7 @@ __device__ __forceinline__ float q4k_block_term(const uint8_t* blk, const XQ& xb
   const uint4 h = ld16(blk);
   const float d = f16_fast(h.x & 0xFFFFu), dmin = f16_fast(h.x >> 16);
   float bs = 0.f;
-#pragma unroll 1
+#pragma unroll
   for (int g = 0; g < 4; g++) {
     const uint4 q0 = ld16(blk + 16 + 32 * g), q1 = ld16(blk + 32 + 32 * g);
     const uint4 xa = ld16(xb.qs + 64 * g), xe = ld16(xb.qs + 64 * g + 16);
